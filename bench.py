@@ -1,0 +1,633 @@
+#!/usr/bin/env python
+"""bench.py -- SDPA forward throughput of the sm_100a kernels (and of the reference's CPU path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c5] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 ... bench.py --gpus N
+
+Metric: "SDPA fwd TFLOP/s at 1/2/4/8 B200 and % of dense bf16 tensor peak".
+Default workload C5: causal bf16 SDPA, Q,K,V [B=64, H=32, L=8192, D=128] ~ N(0,1), scale 1/sqrt(128),
+sharded by batch x head across N GPUs (rank r owns batches [r*64/N, (r+1)*64/N)) with no collective
+on the forward path.  A step is one forward over the rank's shard; value = algorithmic causal FLOPs of
+every rank's steps / max-over-ranks device time of the K steps (strong scaling: total work fixed).
+Algorithmic FLOPs = 4 * B * H * D * (number of unmasked (query, key) pairs), L(L+1)/2 pairs per
+(b, h) for causal.
+
+Other workloads (--workload c1|c2-self|c2-cross|c3|c4; single GPU) are the other BASELINE.json
+configs, measured the same way for the tables in BASELINE.md.
+
+Inputs are generated on the GPU from per-batch seeds (identical for every N), larger than the 126 MB
+L2 for c4/c5 (no flush needed); the smaller configs flush L2 with a 256 MB write between steps and
+time each step with its own CUDA events.
+
+Printed (rank 0, one JSON line): value/ms_per_step, e2e (the same metric through the public API with
+host-resident inputs: pinned H2D of the step's Q/K/V and D2H of its O inside the timed region),
+roofline (dominant kernel vs the measured bf16 peak), cpu_baseline (the reference's CPU path --
+stock torch SDPA on the host cores -- on a bounded sample), clocks sampled by nvidia-smi during the
+timed region, gpu_launches, and a parity spot check of sampled slices/rows against that CPU path.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "torch-cmp-patch_b200"))
+sys.path.insert(0, str(ROOT))
+os.environ.setdefault("CMPEXT3_AUTOPATCH", "0")
+
+METRIC = "SDPA fwd TFLOP/s at 1/2/4/8 B200 and % of dense bf16 tensor peak"
+FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0}
+
+WORKLOADS = {
+    "c5": dict(name="C5 causal SDPA bf16 [64,32,8192,128], batch x head shards", kind="sdpa",
+               B=64, H=32, Lq=8192, Lk=8192, D=128, dtype="bf16", causal=True, cross=False),
+    "c4": dict(name="C4 causal prefill SDPA bf16 [4,32,8192,128]", kind="sdpa",
+               B=4, H=32, Lq=8192, Lk=8192, D=128, dtype="bf16", causal=True, cross=False),
+    "c2-self": dict(name="C2 SDXL self-attention SDPA fp16 [2,10,4096,64]", kind="sdpa",
+                    B=2, H=10, Lq=4096, Lk=4096, D=64, dtype="f16", causal=False, cross=False),
+    "c2-cross": dict(name="C2 SDXL cross-attention SDPA fp16 Q [2,10,4096,64] K,V [2,10,77,64]",
+                     kind="sdpa", B=2, H=10, Lq=4096, Lk=77, D=64, dtype="f16", causal=False, cross=True),
+    "c1": dict(name="C1 SD1.5 self-attention SDPA fp32 [2,8,4096,40]", kind="sdpa",
+               B=2, H=8, Lq=4096, Lk=4096, D=40, dtype="f32", causal=False, cross=False),
+    "c3": dict(name="C3 einsum attention bf16 [4,16,2048,64]: scores einsum -> softmax -> values einsum",
+               kind="einsum", B=4, H=16, Lq=2048, Lk=2048, D=64, dtype="bf16", causal=False, cross=False),
+}
+
+
+def causal_pairs(lq: int, lk: int) -> int:
+    """Unmasked (query, key) pairs of a top-left causal mask: row i sees min(i+1, lk) keys."""
+    n = min(lq, lk)
+    return n * (n + 1) // 2 + max(0, lq - lk) * lk
+
+
+def attn_flops(B, H, Lq, Lk, D, causal) -> float:
+    pairs = causal_pairs(Lq, Lk) if causal else Lq * Lk
+    return 4.0 * B * H * D * pairs
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except Exception:  # noqa: BLE001
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic(kernel: str, workload: str) -> dict | None:
+    """DRAM traffic per unit from a committed ncu summary (profiles/traffic.json), if present."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        return json.loads(p.read_text()).get(f"{kernel}:{workload}")
+    except Exception:  # noqa: BLE001
+        return None
+
+
+# ------------------------------------------------------------------------------------------------
+# clocks
+# ------------------------------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi sampling of one GPU (by UUID) every 200 ms while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None):
+        self.uuid = uuid
+        self.proc = None
+        self.lines: list[tuple[float, str]] = []
+        self.t_start = self.t_stop = None
+
+    def start(self):
+        if not self.uuid:
+            return
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.uuid, f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+            return
+        self._reader = threading.Thread(target=self._read, daemon=True)
+        self._reader.start()
+        time.sleep(0.3)
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def mark(self, start: bool):
+        if start:
+            self.t_start = time.time()
+        else:
+            self.t_stop = time.time()
+
+    def stop(self) -> dict | None:
+        if not self.proc:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:  # noqa: BLE001
+            self.proc.kill()
+        rows = []
+        for t, line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                rows.append((t, float(parts[0]), float(parts[1]), parts))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        inside = [r for r in rows if self.t_start and self.t_stop and self.t_start - 0.1 <= r[0] <= self.t_stop + 0.1]
+        window = inside or sorted(rows, key=lambda r: abs(r[0] - (self.t_start or r[0])))[:2]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in window for i in range(4) if r[3][4 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(r[1] for r in window), "sm_max_mhz": max(r[2] for r in window),
+                "reasons": reasons, "samples": len(window),
+                "power_w_max": max(float(r[3][2]) for r in window if r[3][2] not in ("[N/A]", "N/A"))
+                if any(r[3][2] not in ("[N/A]", "N/A") for r in window) else None}
+
+
+# ------------------------------------------------------------------------------------------------
+# inputs
+# ------------------------------------------------------------------------------------------------
+def torch_dtype(name):
+    import torch
+    return {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[name]
+
+
+def make_batch(w: dict, b: int, device, seed: int = 0):
+    """Q, K, V of batch item b ([H, L, D] each), from the item's own seed: identical for any N."""
+    import torch
+    g = torch.Generator(device=device).manual_seed(seed * 1000003 + b)
+    dt = torch_dtype(w["dtype"])
+    H, Lq, Lk, D = w["H"], w["Lq"], w["Lk"], w["D"]
+    q = torch.randn(H, Lq, D, generator=g, device=device).to(dt)
+    if w["cross"]:
+        text = torch.randn(Lk, 2048, generator=g, device=device)
+        wk = torch.randn(2048, H * D, generator=g, device=device) * 0.02
+        wv = torch.randn(2048, H * D, generator=g, device=device) * 0.02
+        k = (text @ wk).view(Lk, H, D).transpose(0, 1).contiguous().to(dt)
+        v = (text @ wv).view(Lk, H, D).transpose(0, 1).contiguous().to(dt)
+    else:
+        k = torch.randn(H, Lk, D, generator=g, device=device).to(dt)
+        v = torch.randn(H, Lk, D, generator=g, device=device).to(dt)
+    return q, k, v
+
+
+def make_inputs(w: dict, b0: int, b1: int, device, seed: int = 0):
+    import torch
+    dt = torch_dtype(w["dtype"])
+    nb = b1 - b0
+    q = torch.empty(nb, w["H"], w["Lq"], w["D"], dtype=dt, device=device)
+    k = torch.empty(nb, w["H"], w["Lk"], w["D"], dtype=dt, device=device)
+    v = torch.empty(nb, w["H"], w["Lk"], w["D"], dtype=dt, device=device)
+    for i, b in enumerate(range(b0, b1)):
+        q[i], k[i], v[i] = make_batch(w, b, device, seed)
+    return q, k, v
+
+
+# ------------------------------------------------------------------------------------------------
+# the reference's CPU path on a bounded sample
+# ------------------------------------------------------------------------------------------------
+def cpu_reference_sample(w: dict, seconds: float, threads: int | None = None) -> dict:
+    """Stock torch CPU SDPA (the op cmpext3's wrapper falls through to for CPU tensors) on row
+    blocks of one (b, h) slice, for about ``seconds``; returns TFLOP/s of algorithmic work."""
+    import torch
+    from oracle import reference_path as RP
+    cores = RP.set_threads(threads)
+    dt = torch_dtype(w["dtype"])
+    g = torch.Generator().manual_seed(12345)
+    Lq, Lk, D = w["Lq"], w["Lk"], w["D"]
+    q = torch.randn(Lq, D, generator=g).to(dt)
+    if w["cross"]:
+        k = (torch.randn(Lk, 2048, generator=g) @ (torch.randn(2048, D, generator=g) * 0.02)).to(dt)
+        v = (torch.randn(Lk, 2048, generator=g) @ (torch.randn(2048, D, generator=g) * 0.02)).to(dt)
+    else:
+        k = torch.randn(Lk, D, generator=g).to(dt)
+        v = torch.randn(Lk, D, generator=g).to(dt)
+    scale = 1.0 / math.sqrt(D)
+    block = 256
+    flops = 0.0
+    rows_done = 0
+    # warm-up (thread pool, kernels) on a small block, not timed
+    RP.sdpa_rows(q[:64], k[:64], v[:64], torch.arange(64), scale=scale, is_causal=w["causal"])
+    t0 = time.perf_counter()
+    starts = list(range(0, Lq, block))
+    order = [starts[(i * 7919) % len(starts)] for i in range(len(starts))]  # spread over the slice
+    i = 0
+    while True:
+        r0 = order[i % len(order)]
+        r1 = min(Lq, r0 + block)
+        rows = torch.arange(r0, r1)
+        kk = Lk if not w["causal"] else min(Lk, r1)
+        with torch.no_grad():
+            RP.sdpa_rows(q[r0:r1], k[:kk], v[:kk], rows, scale=scale, is_causal=w["causal"])
+        if w["causal"]:
+            flops += 4.0 * D * sum(min(r + 1, Lk) for r in range(r0, r1))
+        else:
+            flops += 4.0 * D * (r1 - r0) * Lk
+        rows_done += r1 - r0
+        i += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt_s = time.perf_counter() - t0
+    return {"value": flops / dt_s / 1e12, "unit": "TFLOP/s", "cores": cores, "seconds": dt_s,
+            "rows": rows_done}
+
+
+def cpu_reference_einsum_sample(w: dict, seconds: float, threads: int | None = None) -> dict:
+    """Stock torch CPU einsum -> softmax -> einsum on single (b, h) slices, about ``seconds``."""
+    import torch
+    from oracle import reference_path as RP
+    cores = RP.set_threads(threads)
+    g = torch.Generator().manual_seed(12345)
+    L, D = w["Lq"], w["D"]
+    q, k, v = (torch.randn(1, 1, L, D, generator=g).to(torch.bfloat16) for _ in range(3))
+    RP.einsum_attention(q[:, :, :64], k[:, :, :64], v[:, :, :64])
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        with torch.no_grad():
+            RP.einsum_attention(q, k, v)
+        n += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt_s = time.perf_counter() - t0
+    flops = n * 2 * 2.0 * L * L * D
+    return {"value": flops / dt_s / 1e12, "unit": "TFLOP/s", "cores": cores, "seconds": dt_s, "slices": n}
+
+
+# ------------------------------------------------------------------------------------------------
+# main
+# ------------------------------------------------------------------------------------------------
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="c5", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-verify", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+def config_block(w: dict, key: str, n: int, rank_batches: int) -> dict:
+    cfg = {"workload": w["name"], "B": w["B"], "H": w["H"], "Lq": w["Lq"], "Lk": w["Lk"], "D": w["D"],
+           "causal": w["causal"], "batches_per_rank": rank_batches,
+           "parallelism": f"dp{n} (batch x head shards, no collective on the forward path)"}
+    big = key in ("c4", "c5")
+    cfg["l2"] = ("inputs larger than L2 (no flush)" if big
+                 else "L2 flushed between steps (256 MB write); value from per-step CUDA events")
+    cfg["data"] = "synthetic N(0,1), seeded per batch item on the GPU"
+    return cfg
+
+
+def reference_arm(args, w, key):
+    """--impl reference: the reference's own CPU implementation of the path (stock torch on the
+    host cores, which is what cmpext3 runs for CPU tensors) on the same metric/config."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    n = args.gpus
+    per_step = max(0.5, min(6.0, 100.0 / max(1, args.steps + args.warmup)))
+    sampler = cpu_reference_einsum_sample if w["kind"] == "einsum" else cpu_reference_sample
+    for _ in range(max(0, min(args.warmup, 1))):
+        sampler(w, min(per_step, 1.0))
+    vals = [sampler(w, per_step) for _ in range(args.steps)]
+    value = sum(v["value"] for v in vals) / len(vals)
+    cores = vals[0]["cores"]
+    total_flops = (attn_flops(w["B"], w["H"], w["Lq"], w["Lk"], w["D"], w["causal"])
+                   if w["kind"] == "sdpa" else 2 * 2.0 * w["B"] * w["H"] * w["Lq"] * w["Lk"] * w["D"])
+    sample = ("stock torch CPU scaled_dot_product_attention (the op cmpext3's _patched_sdpa falls "
+              "through to for CPU tensors) on 256-row blocks of one (b,h) slice with an explicit causal "
+              f"mask, ~{per_step:.1f} s per step; value = algorithmic FLOPs of the rows done / time"
+              if w["kind"] == "sdpa" else
+              "stock torch CPU einsum->softmax->einsum on whole (b,h) slices, ~%.1f s per step" % per_step)
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s",
+            "n_gpus": n, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(total_flops / (value * 1e12) * 1e3, 3) if value > 0 else None,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": w["dtype"], "data": "synthetic",
+            "config": config_block(w, key, n, w["B"] // max(1, n)),
+            "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": cores,
+                             "kind": "reference", "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main() -> int:
+    args = parse_args()
+    w = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        return reference_arm(args, w, args.workload)
+
+    import torch
+    import torch.nn.functional as F
+    import torch.distributed as dist
+    import cmpext3
+    from cmpext3 import _native as N
+    from cmpext3 import sharding
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(json.dumps({"error": f"--gpus {args.gpus} but WORLD_SIZE={world}"}), flush=True)
+        return 2
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    distributed = world > 1
+    if distributed:
+        sharding.init_process_group("nccl", timeout_s=300)
+    if w["B"] % world != 0:
+        raise SystemExit(f"workload {args.workload} has B={w['B']}, not divisible by {world} GPUs")
+    b0, b1 = sharding.shard_range(w["B"], rank, world)
+    nb = b1 - b0
+
+    def barrier():
+        if distributed:
+            dist.barrier(device_ids=[local_rank])
+
+    def max_ranks(x: float) -> float:
+        return sharding.max_over_ranks(x, dev) if distributed else x
+
+    peaks, peak_src = load_peaks()
+    q, k, v = make_inputs(w, b0, b1, dev)
+    scale = 1.0 / math.sqrt(w["D"])
+    causal = w["causal"]
+    big = args.workload in ("c4", "c5")
+    flush = None if big else torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    if w["kind"] == "sdpa":
+        step_flops_rank = attn_flops(nb, w["H"], w["Lq"], w["Lk"], w["D"], causal)
+
+        def step():
+            return cmpext3.ops.attention(q, k, v, scale, causal)
+        launches_per_step = 1
+        kernel_name = N.attention_plan(q, k, v, scale, causal)
+    else:
+        # C3: patched torch.einsum -> planner -> patched torch.bmm -> sm_100a bmm kernel; stock softmax
+        cmpext3.enable()
+        step_flops_rank = 2 * 2.0 * nb * w["H"] * w["Lq"] * w["Lk"] * w["D"]
+
+        def step():
+            s = torch.einsum("bhid,bhjd->bhij", q, k)
+            p = torch.softmax(s, dim=-1)
+            return torch.einsum("bhij,bhjd->bhid", p, v)
+        launches_per_step = 2  # two bmm kernels (softmax is stock torch)
+        kernel_name = N.bmm_plan(q.reshape(-1, w["Lq"], w["D"]),
+                                 k.reshape(-1, w["Lk"], w["D"]).transpose(1, 2))
+
+    with torch.no_grad():
+        for _ in range(max(3, args.warmup)):
+            out = step()
+        torch.cuda.synchronize(dev)
+
+        uuid = None
+        try:
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+        except Exception:  # noqa: BLE001
+            pass
+        clocks = ClockSampler(uuid)
+        clocks.start()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+        t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize(dev)
+        clocks.mark(True)
+        t_start.record(stream)
+        for i in range(args.steps):
+            if flush is not None:
+                flush.fill_(float(i))
+            ev[i][0].record(stream)
+            out = step()
+            ev[i][1].record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize(dev)
+        clocks.mark(False)
+        barrier()
+        clock_info = clocks.stop()
+
+        per_step_ms = [a.elapsed_time(b) for a, b in ev]
+        region_ms = t_start.elapsed_time(t_end)
+        busy_ms = sum(per_step_ms)
+        local_ms = region_ms if big else busy_ms
+        total_ms = max_ranks(local_ms)
+        total_flops = step_flops_rank * world * args.steps
+        value = total_flops / (total_ms * 1e-3) / 1e12
+        mean_launch_ms = max_ranks(statistics.mean(per_step_ms))
+
+        # roofline of the dominant kernel
+        if w["kind"] == "sdpa" and w["cross"]:
+            es = torch.tensor([], dtype=q.dtype).element_size()
+            algo_bytes = (q.numel() + k.numel() + v.numel() + out.numel()) * es
+            achieved = algo_bytes / (statistics.mean(per_step_ms) * 1e-3) / 1e9
+            peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+            roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                    "frac": round(achieved / peak, 4), "kernel": kernel_name,
+                    "algorithmic_bytes_per_launch": algo_bytes,
+                    "tflops": round(step_flops_rank / (statistics.mean(per_step_ms) * 1e-3) / 1e12, 2)}
+        elif w["kind"] == "sdpa":
+            achieved = step_flops_rank / (statistics.mean(per_step_ms) * 1e-3) / 1e12
+            sustained = region_ms > 1000.0
+            peak = float(peaks.get("bf16_tflops_sustained" if sustained else "bf16_tflops"))
+            roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+                    "frac": round(achieved / peak, 4), "kernel": kernel_name,
+                    "peak_kind": f"{peak_src} {'sustained' if sustained else 'burst'} cuBLAS bf16",
+                    "frac_of_2250_spec": round(achieved / 2250.0, 4),
+                    "algorithmic_flops_per_launch": step_flops_rank}
+        else:
+            # C3 is HBM-bound on the scores tensor: bytes of both bmms + softmax over the step
+            es = 2
+            score = nb * w["H"] * w["Lq"] * w["Lk"] * es
+            opnd = nb * w["H"] * w["Lq"] * w["D"] * es
+            algo_bytes = (2 * opnd + score) + (2 * score) + (score + 2 * opnd)
+            achieved = algo_bytes / (statistics.mean(per_step_ms) * 1e-3) / 1e9
+            peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+            roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                    "frac": round(achieved / peak, 4), "kernel": kernel_name + " + stock softmax",
+                    "algorithmic_bytes_per_step": algo_bytes}
+        tr = load_traffic("fmha" if w["kind"] == "sdpa" else "bmm", args.workload)
+        roof["traffic"] = None
+        if tr and tr.get("bytes_per_unit"):
+            units = step_flops_rank / tr.get("flops_per_unit", step_flops_rank)
+            roof["traffic"] = round(tr["bytes_per_unit"] * units)
+            roof["traffic_source"] = tr.get("source")
+        roof["note"] = f"peak is {peak_src} ({'MEASURED_PEAKS.json' if peak_src == 'measured' else 'recipe fallback'})"
+
+        # parity spot check: sampled slices / rows of every rank against the CPU path
+        parity = None
+        if not args.no_verify and w["kind"] == "sdpa":
+            parity = verify(w, out, b0, b1, rank, world, dev, scale, distributed)
+
+        # e2e through the public API with host-resident inputs
+        e2e = None
+        if not args.no_e2e and w["kind"] == "sdpa":
+            e2e = end_to_end(w, q, k, v, args.e2e_steps, dev, stream, barrier, max_ranks, world, scale)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        fn = cpu_reference_einsum_sample if w["kind"] == "einsum" else cpu_reference_sample
+        c = fn(w, args.cpu_seconds)
+        cpu = {"value": round(c["value"], 4), "unit": "TFLOP/s", "cores": c["cores"], "kind": "reference",
+               "sample": (f"stock torch CPU SDPA (the reference's CPU path: cmpext3 routes CPU tensors to "
+                          f"it) on {c.get('rows', 0)} query rows of one (b,h) slice in {c['seconds']:.1f} s"
+                          if w["kind"] == "sdpa" else
+                          f"stock torch CPU einsum->softmax->einsum on {c.get('slices')} (b,h) slices in "
+                          f"{c['seconds']:.1f} s")}
+
+    flags = N.device_status()
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic",
+                "config": config_block(w, args.workload, world, nb),
+                "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clock_info,
+                "gpu_launches": launches_per_step * args.steps,
+                "mean_launch_ms": round(mean_launch_ms, 4), "kernel": kernel_name,
+                "parity": parity, "device_flags": flags}
+        print(json.dumps(line), flush=True)
+    if distributed:
+        dist.destroy_process_group()
+    return 0
+
+
+def verify(w, out, b0, b1, rank, world, dev, scale, distributed):
+    """Compare sampled (b, h) slices x sampled rows with the CPU path; gather samples to rank 0."""
+    import torch
+    from cmpext3 import sharding
+    from oracle import reference_path as RP
+    from oracle import sdpa_np
+    nb = b1 - b0
+    # two slices per rank: its first and last (b, h), plus rows spread over the sequence
+    local = [(0, 0), (nb - 1, w["H"] - 1)]
+    samples = torch.stack([out[bi, hi] for bi, hi in local])  # [2, Lq, D]
+    if distributed:
+        allo = sharding.gather_samples(samples)
+    else:
+        allo = samples[None]
+    if rank != 0:
+        return None
+    rows = sorted({0, 1, 127, 128, 129, w["Lq"] // 2, w["Lq"] - 129, w["Lq"] - 1}
+                  | set(torch.randperm(w["Lq"], generator=torch.Generator().manual_seed(7))[:24].tolist()))
+    worst = 0.0
+    checked = []
+    per_rank = w["B"] // world
+    for r in range(world):
+        for s, (bi, hi) in enumerate(local if r == 0 else [(0, 0), (per_rank - 1, w["H"] - 1)]):
+            b = r * per_rank + bi
+            qb, kb, vb = make_batch(w, b, dev)
+            qs, ks, vs = qb[hi].cpu(), kb[hi].cpu(), vb[hi].cpu()
+            ref = RP.sdpa_rows(qs[rows], ks, vs, rows, scale=scale, is_causal=w["causal"])
+            got = allo[r, s][rows].float().cpu()
+            err = sdpa_np.rel_err(got.numpy(), ref.float().numpy())
+            worst = max(worst, err)
+            checked.append([b, hi])
+    tol = {"bf16": 1e-2, "f16": 1e-2, "f32": 1e-4}[w["dtype"]]
+    return {"slices": checked, "rows_per_slice": len(rows), "max_rel": float(f"{worst:.3e}"),
+            "tol": tol, "ok": bool(worst <= tol), "oracle": "stock torch CPU SDPA (reference CPU path)"}
+
+
+def end_to_end(w, q, k, v, steps, dev, stream, barrier, max_ranks, world, scale):
+    """The metric through the public API (patched F.scaled_dot_product_attention) with the step's
+    inputs in pinned host memory and its output read back: H2D + SDPA + D2H per step, in chunks of
+    batch items on three streams so copies in both directions overlap the kernels."""
+    import torch
+    import torch.nn.functional as F
+    import cmpext3
+    nb = q.shape[0]
+    qh = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+    kh = torch.empty(k.shape, dtype=k.dtype, pin_memory=True)
+    vh = torch.empty(v.shape, dtype=v.dtype, pin_memory=True)
+    oh = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+    qh.copy_(q)
+    kh.copy_(k)
+    vh.copy_(v)
+    chunk = max(1, min(nb, 4 if w["Lq"] >= 4096 else nb))
+    nchunks = (nb + chunk - 1) // chunk
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    bufs = [tuple(torch.empty((chunk, *t.shape[1:]), dtype=t.dtype, device=dev) for t in (q, k, v))
+            for _ in range(2)]
+    outs = [None, None]
+    cmpext3.enable()
+
+    def one_step():
+        ready = [torch.cuda.Event() for _ in range(nchunks)]
+        done = [torch.cuda.Event() for _ in range(nchunks)]
+        copied = [torch.cuda.Event() for _ in range(nchunks)]
+        for c in range(nchunks):
+            lo, hi = c * chunk, min(nb, (c + 1) * chunk)
+            bq, bk, bv = bufs[c % 2]
+            with torch.cuda.stream(s_in):
+                if c >= 2:
+                    s_in.wait_event(done[c - 2])  # buffer reuse after its kernel finished
+                bq[: hi - lo].copy_(qh[lo:hi], non_blocking=True)
+                bk[: hi - lo].copy_(kh[lo:hi], non_blocking=True)
+                bv[: hi - lo].copy_(vh[lo:hi], non_blocking=True)
+                ready[c].record(s_in)
+            stream.wait_event(ready[c])
+            if c >= 2:
+                stream.wait_event(copied[c - 2])  # output buffer reuse after its D2H
+            o = F.scaled_dot_product_attention(bq[: hi - lo], bk[: hi - lo], bv[: hi - lo],
+                                               is_causal=w["causal"], scale=scale)
+            outs[c % 2] = o
+            done[c].record(stream)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done[c])
+                oh[lo:hi].copy_(o, non_blocking=True)
+                copied[c].record(s_out)
+        stream.wait_stream(s_out)
+        stream.wait_stream(s_in)
+
+    one_step()
+    torch.cuda.synchronize(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(dev)
+    t0.record(stream)
+    for _ in range(steps):
+        one_step()
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    cmpext3.disable()
+    ms = max_ranks(t0.elapsed_time(t1))
+    flops = attn_flops(nb, w["H"], w["Lq"], w["Lk"], w["D"], w["causal"]) * world * steps
+    es = q.element_size()
+    h2d = (q.numel() + k.numel() + v.numel()) * es * world
+    d2h = q.numel() * es * world
+    return {"value": round(flops / (ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "steps": steps, "ms_per_step": round(ms / steps, 3),
+            "api": "patched F.scaled_dot_product_attention on pinned-host chunks (3 streams)"}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,149 @@
+/*
+ * cmpx_b200.h -- C ABI of the B200 (sm_100a) attention / batched-matmul library.
+ *
+ * This is the drop-in boundary for the hot path of cmpext3 (WifiLast/torch-cmp-patch):
+ * the two native ops that the Python monkeypatch reaches for
+ *   F.scaled_dot_product_attention  -> cmpext3.ops.attention(query, key, value, scale=None, causal=False)
+ *   torch.bmm / matmul / einsum     -> cmpext3.ops.bmm(input, mat2)
+ * In the reference those are pybind11 functions over ATen tensors
+ * (src/main.cpp:2307-2309 `bmm`, src/main.cpp:2353-2358 `attention`, implemented by
+ * custom_bmm_forward src/main.cpp:363-441 and custom_attention_forward src/main.cpp:1603-1774).
+ * Here the boundary is plain C: borrowed device pointers, element strides, sizes, a dtype tag,
+ * the caller's cudaStream_t, and an int status.  Nothing in this header depends on torch.
+ *
+ * Conventions
+ *  - Every entry point returns CMPX_OK (0) or a CMPX_ERR_* code.  A non-zero return means no
+ *    kernel was launched and the output was not touched (the reference's launcher that declined
+ *    silently and left the output unwritten, src/main.cpp:1742-1758, is exactly what this rules out).
+ *  - Work is enqueued on `stream` (a cudaStream_t passed as void*) on the CURRENT device; the
+ *    call does not synchronise and does not allocate device memory.
+ *  - Strides are in elements.  For attention the head_dim must be contiguous (stride 1); for
+ *    bmm one of the two matrix strides of each input must be 1 and C must be row-major.
+ *  - Device-side waits are bounded.  A kernel whose wait runs out sets a bit in the device status
+ *    word, stops early and returns; cmpx_device_status() reads (and clears) that word.
+ */
+#ifndef CMPX_B200_H
+#define CMPX_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CMPX_API __attribute__((visibility("default")))
+#else
+#define CMPX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CMPX_ABI_VERSION 1
+
+/* Element type of every operand of one call (inputs and output share it, as in the reference:
+ * dtype in == dtype out, src/main.cpp:1623-1627, :366-369). */
+typedef enum cmpx_dtype {
+  CMPX_F32 = 0,
+  CMPX_F16 = 1,
+  CMPX_BF16 = 2
+} cmpx_dtype;
+
+typedef enum cmpx_status {
+  CMPX_OK = 0,
+  CMPX_ERR_INVALID_ARGUMENT = 1,  /* null pointer, negative size, shape mismatch */
+  CMPX_ERR_UNSUPPORTED_SHAPE = 2, /* outside the tile table (e.g. head_dim > 128) */
+  CMPX_ERR_UNSUPPORTED_DTYPE = 3,
+  CMPX_ERR_MISALIGNED = 4,        /* pointer/stride not 16-byte aligned for TMA */
+  CMPX_ERR_WORKSPACE = 5,         /* workspace missing or too small */
+  CMPX_ERR_LAUNCH = 6,            /* CUDA launch or tensor-map encode failed */
+  CMPX_ERR_DEVICE = 7,            /* no sm_100 device current, or CUDA runtime error */
+  CMPX_ERR_DEVICE_TIMEOUT = 8     /* reported by cmpx_device_status only */
+} cmpx_status;
+
+/* Scaled-dot-product attention forward:  O = softmax(Q K^T * scale [+ causal mask]) V
+ * Tensors are [batch, heads, len, head_dim] with arbitrary batch/head/len strides and a
+ * contiguous head_dim (the same strided-view contract as the reference's HFMA2 route,
+ * src/main.cpp:1637-1666).  Causal masking is top-left aligned (key j is visible to query i
+ * iff j <= i), which is what torch's is_causal does for len_q != len_k.
+ * Replaces: custom_attention_forward (src/main.cpp:1603-1774) and its launchers
+ * launch_flash_attention_hfma2 (src/cuda/fp16_flash_attention_hfma2.cu:269-286),
+ * launch_attention_fp16 (src/cuda/fp16_attention.cu:328-386),
+ * launch_attention_fp32 (src/cuda/fp32_attention.cu:200-221). */
+typedef struct cmpx_attn_desc {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  int64_t batch, heads, len_q, len_k, head_dim;
+  int64_t q_stride[3]; /* batch, head, row strides of q (elements) */
+  int64_t k_stride[3];
+  int64_t v_stride[3];
+  int64_t o_stride[3];
+  int32_t dtype;       /* cmpx_dtype */
+  int32_t causal;      /* 0 or 1 */
+  double scale;        /* softmax scale; the reference default is 1/sqrt(head_dim) */
+  void* workspace;     /* device scratch of cmpx_attn_workspace_size() bytes (may be NULL if 0) */
+  size_t workspace_bytes;
+} cmpx_attn_desc;
+
+/* Batched matmul  C[b] = A[b] @ B[b],  A: [batch, m, k], B: [batch, k, n], C: [batch, m, n].
+ * Each operand has a batch stride and two matrix strides (row, col).  One of the two matrix
+ * strides of A and of B must be 1 (row-major or column-major view: a transposed operand is
+ * passed as a view, never copied); C must be row-major (col stride 1).
+ * Replaces: custom_bmm_forward (src/main.cpp:363-441) and its per-batch host loop over
+ * launch_matmul_fp32 (src/cuda/fp32_matmul.cu:236-265) / launch_matmul_fp16
+ * (src/cuda/fp16_matmul.cu:373-427). */
+typedef struct cmpx_bmm_desc {
+  const void* a;
+  const void* b;
+  void* c;
+  int64_t batch, m, n, k;
+  int64_t a_stride[3]; /* batch, row (m), col (k) */
+  int64_t b_stride[3]; /* batch, row (k), col (n) */
+  int64_t c_stride[3]; /* batch, row (m), col (n); col must be 1 */
+  int32_t dtype;       /* cmpx_dtype */
+  int32_t reserved;
+} cmpx_bmm_desc;
+
+/* Attention forward.  Replaces cmpext3.ops.attention (src/main.cpp:2353-2358). */
+CMPX_API int cmpx_attn_fwd(const cmpx_attn_desc* desc, void* stream);
+
+/* Bytes of device workspace cmpx_attn_fwd needs for this problem (0 = none).
+ * The workspace must be zero-filled before the call; the kernel leaves it zeroed on return.
+ * No reference counterpart (the reference allocates nothing but the output). */
+CMPX_API size_t cmpx_attn_workspace_size(const cmpx_attn_desc* desc);
+
+/* Batched matmul.  Replaces cmpext3.ops.bmm (src/main.cpp:2307-2309). */
+CMPX_API int cmpx_bmm(const cmpx_bmm_desc* desc, void* stream);
+
+/* Name of the tile-table entry a call would use, written into buf (NUL-terminated).
+ * Returns CMPX_OK or the status the call itself would return.  Replaces the per-signature
+ * decision record of the reference's runtime autoselect (cmpext3/autoselect.py:290-364),
+ * which this library does not need: the kernel choice is a fixed function of the shape. */
+CMPX_API int cmpx_attn_plan(const cmpx_attn_desc* desc, char* buf, size_t buf_len);
+CMPX_API int cmpx_bmm_plan(const cmpx_bmm_desc* desc, char* buf, size_t buf_len);
+
+/* Human-readable text for a status code (static storage). */
+CMPX_API const char* cmpx_status_str(int status);
+
+/* Reads and clears the device status word of the current device after synchronising it.
+ * *flags receives the OR of CMPX_DEVFLAG_* bits raised since the last call.
+ * No reference counterpart (the reference's kernels have no bounded waits). */
+#define CMPX_DEVFLAG_WAIT_TIMEOUT 1u   /* an mbarrier / pipeline wait ran out */
+#define CMPX_DEVFLAG_BAD_ARGS 2u       /* a kernel rejected its own launch arguments */
+CMPX_API int cmpx_device_status(unsigned int* flags);
+
+/* Self-test of the bounded-wait path: launches one CTA that waits on an mbarrier nothing ever
+ * arrives on, for at most timeout_ns nanoseconds, then records CMPX_DEVFLAG_WAIT_TIMEOUT and
+ * returns.  Used by the failure-detection test; never faults, traps or hangs.
+ * No reference counterpart. */
+CMPX_API int cmpx_selftest_wait_timeout(uint64_t timeout_ns, void* stream);
+
+/* Library ABI version (CMPX_ABI_VERSION). */
+CMPX_API int cmpx_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CMPX_B200_H */

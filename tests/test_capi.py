@@ -1,0 +1,139 @@
+"""The C-ABI library without a GPU: it loads, exports every declared symbol, and its host-side logic
+(argument validation, tile-table plan, status strings) behaves -- no compute call is made."""
+from __future__ import annotations
+
+import ctypes
+import math
+import re
+from pathlib import Path
+
+import pytest
+
+from cmpext3 import _native as N
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "cmpx_b200.h"
+
+
+def declared_symbols() -> list[str]:
+    text = HEADER.read_text()
+    return re.findall(r"^CMPX_API\s+[\w\s\*]+?\b(cmpx_\w+)\s*\(", text, flags=re.M)
+
+
+def test_header_declares_the_expected_entry_points():
+    syms = declared_symbols()
+    for name in ("cmpx_attn_fwd", "cmpx_bmm", "cmpx_status_str", "cmpx_attn_plan", "cmpx_bmm_plan",
+                 "cmpx_device_status", "cmpx_attn_workspace_size", "cmpx_abi_version",
+                 "cmpx_selftest_wait_timeout"):
+        assert name in syms
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(N.LIBRARY_PATH))
+    for name in declared_symbols():
+        assert hasattr(lib, name), f"{name} declared in {HEADER.name} but not exported"
+
+
+def test_library_exports_nothing_undeclared():
+    import subprocess
+    out = subprocess.run(["nm", "-D", "--defined-only", str(N.LIBRARY_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    assert exported == set(declared_symbols())
+
+
+def test_abi_version_and_status_strings():
+    assert N.lib.cmpx_abi_version() == 1
+    assert N.lib.cmpx_status_str(0) == b"ok"
+    for code in range(1, 9):
+        assert N.lib.cmpx_status_str(code) not in (b"ok", b"unknown status")
+    assert N.lib.cmpx_status_str(12345) == b"unknown status"
+
+
+def _attn(B=1, H=2, Lq=256, Lk=256, D=128, dtype=2, causal=0, scale=None, ptr=0x10000):
+    d = N.AttnDesc()
+    d.q = d.k = d.v = d.o = ptr
+    d.batch, d.heads, d.len_q, d.len_k, d.head_dim = B, H, Lq, Lk, D
+    for name, L in (("q_stride", Lq), ("k_stride", Lk), ("v_stride", Lk), ("o_stride", Lq)):
+        getattr(d, name)[:] = (H * L * D, L * D, D)
+    d.dtype, d.causal = dtype, causal
+    d.scale = (1 / math.sqrt(D)) if scale is None else scale
+    return d
+
+
+def _plan(d):
+    buf = ctypes.create_string_buffer(128)
+    st = N.lib.cmpx_attn_plan(ctypes.byref(d), buf, 128)
+    return st, buf.value.decode()
+
+
+@pytest.mark.parametrize("cfg,entry", [
+    (dict(B=2, H=8, Lq=4096, Lk=4096, D=40, dtype=0), "attn_f32_simt<D64"),
+    (dict(B=2, H=10, Lq=4096, Lk=4096, D=64, dtype=1), "fmha_sm100<f16,D64"),
+    (dict(B=2, H=10, Lq=4096, Lk=77, D=64, dtype=1), "fmha_sm100<f16,D64"),
+    (dict(B=4, H=32, Lq=8192, Lk=8192, D=128, dtype=2, causal=1), "fmha_sm100<bf16,D128"),
+    (dict(B=64, H=32, Lq=8192, Lk=8192, D=128, dtype=2, causal=1), "fmha_sm100<bf16,D128"),
+])
+def test_tile_table_covers_every_config(cfg, entry):
+    st, name = _plan(_attn(**cfg))
+    assert st == N.OK and name.startswith(entry), (st, name)
+
+
+@pytest.mark.parametrize("mutate,status", [
+    (lambda d: setattr(d, "q", None), N.ERR_INVALID_ARGUMENT),
+    (lambda d: setattr(d, "batch", -1), N.ERR_INVALID_ARGUMENT),
+    (lambda d: setattr(d, "head_dim", 256), N.ERR_UNSUPPORTED_SHAPE),
+    (lambda d: setattr(d, "head_dim", 36), N.ERR_UNSUPPORTED_SHAPE),
+    (lambda d: setattr(d, "dtype", 7), N.ERR_UNSUPPORTED_DTYPE),
+    (lambda d: setattr(d, "scale", float("nan")), N.ERR_INVALID_ARGUMENT),
+    (lambda d: setattr(d, "scale", 0.0), N.ERR_UNSUPPORTED_SHAPE),
+    (lambda d: setattr(d, "len_k", 0), N.ERR_UNSUPPORTED_SHAPE),
+    (lambda d: setattr(d, "q", 0x10008), N.ERR_MISALIGNED),
+    (lambda d: d.k_stride.__setitem__(2, 100), N.ERR_MISALIGNED),
+    (lambda d: setattr(d, "causal", 2), N.ERR_INVALID_ARGUMENT),
+])
+def test_invalid_attention_descriptors_are_rejected_before_launch(mutate, status):
+    d = _attn()
+    mutate(d)
+    assert _plan(d)[0] == status
+    # the launch entry point rejects them the same way, without touching a device
+    assert N.lib.cmpx_attn_fwd(ctypes.byref(d), None) == status
+
+
+def test_null_descriptor_is_rejected():
+    assert N.lib.cmpx_attn_fwd(None, None) == N.ERR_INVALID_ARGUMENT
+    assert N.lib.cmpx_bmm(None, None) == N.ERR_INVALID_ARGUMENT
+
+
+def _bmm(nb=64, m=2048, n=2048, k=64, dtype=2, bt=False, ptr=0x10000):
+    d = N.BmmDesc()
+    d.a = d.b = d.c = ptr
+    d.batch, d.m, d.n, d.k = nb, m, n, k
+    d.a_stride[:] = (m * k, k, 1)
+    d.b_stride[:] = (k * n, 1, k) if bt else (k * n, n, 1)
+    d.c_stride[:] = (m * n, n, 1)
+    d.dtype = dtype
+    return d
+
+
+def _bplan(d):
+    buf = ctypes.create_string_buffer(128)
+    st = N.lib.cmpx_bmm_plan(ctypes.byref(d), buf, 128)
+    return st, buf.value.decode()
+
+
+def test_bmm_plan_for_the_einsum_attention_shapes():
+    st, name = _bplan(_bmm(64, 2048, 2048, 64, bt=True))     # scores: B = K^T view (K-major)
+    assert st == 0 and "128x256" in name and "B:k-major" in name
+    st, name = _bplan(_bmm(64, 2048, 64, 2048, bt=False))    # values: B = V (N-major)
+    assert st == 0 and "128x64" in name and "B:mn-major" in name
+    st, name = _bplan(_bmm(2, 33, 45, 17, dtype=0))
+    assert st == 0 and name.startswith("bmm_f32_simt")
+
+
+def test_bmm_rejects_misaligned_rows():
+    d = _bmm(2, 64, 62, 64)  # N*2 bytes = 124, not a 16-byte multiple
+    assert _bplan(d)[0] == N.ERR_MISALIGNED
+
+
+def test_workspace_size_is_zero_for_now():
+    assert N.lib.cmpx_attn_workspace_size(ctypes.byref(_attn())) == 0

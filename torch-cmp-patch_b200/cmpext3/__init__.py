@@ -1,0 +1,284 @@
+"""cmpext3 (B200 edition) -- drop-in replacement for the attention / batched-matmul hot path of
+cmpext3 (WifiLast/torch-cmp-patch), running hand-written sm_100a kernels.
+
+Importing the package monkeypatches, exactly where the reference does (cmpext3/__init__.py:741-781,
+auto-run at :822-823 of the reference):
+
+    F.scaled_dot_product_attention  -> cmpext3.ops.attention(query, key, value, scale, is_causal)
+    torch.bmm                       -> cmpext3.ops.bmm(input, mat2)
+    torch.matmul (2D / 3D)          -> cmpext3.ops.bmm
+    torch.einsum                    -> einsum_ops planner -> torch.bmm (patched)
+
+with the reference's wrapper signatures, gates and stock bail-outs: stock PyTorch runs when autograd
+is live for an input, when a tensor is not a CUDA fp16/fp32/bf16 tensor, when SDPA gets an
+``attn_mask`` or ``dropout_p > 0`` or a non-4D query, when bmm/matmul get ``out=`` or mixed dtypes, and
+whenever the native op raises ``RuntimeError``/``TypeError`` for an argument outside its tile table.
+
+What changed underneath: the kernels are tcgen05/TMA/TMEM kernels for B200 in a C-ABI library
+(include/cmpx_b200.h), bf16 is computed natively (the reference converted it to fp16 for attention
+and to fp32 for bmm), and the runtime native-versus-stock race is replaced by a fixed tile table
+(see cmpext3.autoselect).  The rest of the reference (linear, conv, norms, activations, TensorRT,
+NVML clock/power changes) is not part of this package; in particular nothing here changes GPU
+clocks or power limits.
+
+    import cmpext3            # patches on import
+    cmpext3.disable(); cmpext3.enable()
+
+Set CMPEXT3_AUTOPATCH=0 to import without patching; CMPEXT3_DISABLE_OPS=attention,bmm,matmul,einsum
+pins named ops to stock; CMPEXT3_VERBOSE=1 logs each new signature's tile-table entry;
+cmpext3.autoselect_report() lists them.
+
+SAFETY: the kernels are forward-only (no autograd); every patched call falls back to stock when
+autograd is live, as in the reference.
+"""
+from __future__ import annotations
+
+import os
+from typing import Any, Callable
+
+import torch
+import torch.nn.functional as F
+
+try:
+    from . import _native as _C
+except ImportError as exc:  # pragma: no cover
+    raise ImportError(
+        "cmpext3 native library not built. Run: python torch-cmp-patch_b200/build.py"
+    ) from exc
+
+# Raw, unpatched access to the native ops (attention, bmm) for manual use.
+ops = _C
+
+from . import autoselect  # noqa: E402
+from . import einsum_ops  # noqa: E402
+
+_SUPPORTED_DTYPES = (torch.float16, torch.float32, torch.bfloat16)
+_ORIGINALS: dict[tuple[Any, str], Callable] = {}
+_ENABLED = False
+
+
+def _grad_safe(*tensors: Any) -> bool:
+    """True if swapping in a kernel with no autograd support is safe."""
+    if hasattr(torch, "is_inference_mode_enabled") and torch.is_inference_mode_enabled():
+        return True
+    if not torch.is_grad_enabled():
+        return True
+    return not any(isinstance(t, torch.Tensor) and t.requires_grad for t in tensors)
+
+
+def _usable(*tensors: Any) -> bool:
+    """True if every tensor argument is a CUDA fp16/fp32/bf16 tensor."""
+    for t in tensors:
+        if isinstance(t, torch.Tensor) and (not t.is_cuda or t.dtype not in _SUPPORTED_DTYPES):
+            return False
+    return True
+
+
+# CMPEXT3_DISABLE_OPS=attention,bmm pins named ops to stock ("attention" is the op name of
+# F.scaled_dot_product_attention, as in the reference).
+_OP_ALIASES = {"scaled_dot_product_attention": "attention"}
+_DISABLED_OPS = frozenset(
+    part.strip() for part in os.environ.get("CMPEXT3_DISABLE_OPS", "").split(",") if part.strip()
+)
+
+
+def _install(target: Any, name: str, wrapper: Callable) -> None:
+    if name in _DISABLED_OPS or _OP_ALIASES.get(name, name) in _DISABLED_OPS:
+        return
+    key = (target, name)
+    if key not in _ORIGINALS:
+        _ORIGINALS[key] = getattr(target, name)
+    _keep_scriptable(wrapper, _ORIGINALS[key])
+    setattr(target, name, wrapper)
+
+
+def _keep_scriptable(wrapper: Callable, original: Callable) -> None:
+    """Make torch.jit.script treat ``wrapper`` as the stock ``original``.
+
+    TorchScript resolves torch.bmm & co. by object identity; a scripted function that calls a
+    patched op would otherwise try to compile the Python wrapper.  C++ builtins are aliased to the
+    wrapper; Python functions get their compiled original (or overloads) cached for the wrapper.
+    """
+    from torch.jit import _builtins, _state
+    op = _builtins._find_builtin(original)
+    if op is not None:
+        _builtins._register_builtin(wrapper, op)
+        return
+    from torch import _jit_internal
+    from torch.jit import _script
+    try:
+        if _jit_internal._get_fn_overloads(_jit_internal._qualified_name(original)):
+            _state._set_jit_overload_cache(wrapper, _script._get_overloads(original))
+        else:
+            _state._set_jit_function_cache(wrapper, torch.jit.script(original))
+    except Exception:  # noqa: BLE001 -- an original that does not script stays as it is
+        pass
+
+
+def _restore(target: Any, name: str) -> None:
+    original = _ORIGINALS.pop((target, name), None)
+    if original is not None:
+        setattr(target, name, original)
+
+
+_DTYPE_TAG = {torch.float16: "fp16", torch.float32: "fp32", torch.bfloat16: "bf16"}
+
+
+def _dispatch(op: str, ref: torch.Tensor, key: tuple, native_call: Callable,
+              stock_call: Callable, plan: Callable[[], str] | None = None) -> Any:
+    """Run the native op for this signature (stock if it declines).
+
+    With the record on (default) the first call per signature notes the tile-table entry, and a
+    signature the kernels decline is remembered as stock (cmpext3.autoselect).  With
+    CMPEXT3_AUTOSELECT=0: kernel, and stock only if it raises.
+    """
+    if autoselect.enabled():
+        try:
+            return autoselect.choose(f"{op} {_DTYPE_TAG.get(ref.dtype, ref.dtype)}", key,
+                                     native_call, stock_call, plan)
+        except TypeError as exc:
+            if "unhashable" not in str(exc):
+                raise
+    try:
+        return native_call()
+    except (RuntimeError, TypeError):
+        return stock_call()
+
+
+# ---------------------------------------------------------------------------------------------
+# Wrappers (signatures and gates as in the reference: __init__.py:423-501, :609-633)
+# ---------------------------------------------------------------------------------------------
+
+def _patched_matmul(input, other, *, out=None):
+    orig = _ORIGINALS[(torch, "matmul")]
+    if out is not None or not (_grad_safe(input, other) and _usable(input, other)):
+        return orig(input, other) if out is None else orig(input, other, out=out)
+    if input.dtype != other.dtype:
+        return orig(input, other)
+    if input.dim() == 2 and other.dim() == 2:
+        native = lambda: _C.bmm(input.unsqueeze(0), other.unsqueeze(0)).squeeze(0)  # noqa: E731
+        plan = lambda: _C.bmm_plan(input.unsqueeze(0), other.unsqueeze(0))  # noqa: E731
+    elif input.dim() == 3 and other.dim() == 3:
+        if _small_bmm_eligible(input, other):
+            return _dispatch("bmm_small", input, (input.shape, input.dtype, other.shape),
+                             lambda: _small_bmm(input, other), lambda: orig(input, other))
+        native = lambda: _C.bmm(input, other)  # noqa: E731
+        plan = lambda: _C.bmm_plan(input, other)  # noqa: E731
+    else:
+        return orig(input, other)
+    return _dispatch("matmul", input, (input.shape, input.dtype, other.shape),
+                     native, lambda: orig(input, other), plan)
+
+
+# Many tiny matrices (M*K*N <= 32768): a broadcast multiply + sum, chunked over the batch, as in
+# the reference (__init__.py:446-464).  Thresholds from the same environment variables.
+_SMALL_BMM_MAX_MKN = int(os.environ.get("CMPEXT3_SMALL_BMM_MAX_MKN", "32768"))
+_SMALL_BMM_CHUNK = int(os.environ.get("CMPEXT3_SMALL_BMM_CHUNK", str(1 << 25)))
+
+
+def _small_bmm_eligible(a: torch.Tensor, b: torch.Tensor) -> bool:
+    return (a.dim() == 3 and b.dim() == 3 and a.size(0) == b.size(0) and a.size(2) == b.size(1)
+            and a.size(1) * a.size(2) * b.size(2) <= _SMALL_BMM_MAX_MKN)
+
+
+def _small_bmm(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    n, m, k = a.shape
+    p = b.size(2)
+    step = max(1, _SMALL_BMM_CHUNK // max(m * k * p, 1))
+    if step >= n:
+        return (a.unsqueeze(-1) * b.unsqueeze(1)).sum(2)
+    out = torch.empty((n, m, p), dtype=a.dtype, device=a.device)
+    for s in range(0, n, step):
+        out[s:s + step] = (a[s:s + step].unsqueeze(-1) * b[s:s + step].unsqueeze(1)).sum(2)
+    return out
+
+
+def _patched_bmm(input, mat2, *, out=None):
+    orig = _ORIGINALS[(torch, "bmm")]
+    if out is not None or not (_grad_safe(input, mat2) and _usable(input, mat2)):
+        return orig(input, mat2) if out is None else orig(input, mat2, out=out)
+    if input.dtype != mat2.dtype:
+        return orig(input, mat2)
+    if _small_bmm_eligible(input, mat2):
+        return _dispatch("bmm_small", input, (input.shape, input.dtype, mat2.shape),
+                         lambda: _small_bmm(input, mat2),
+                         lambda: orig(input, mat2))
+    return _dispatch("bmm", input, (input.shape, input.dtype, mat2.shape),
+                     lambda: _C.bmm(input, mat2),
+                     lambda: orig(input, mat2),
+                     lambda: _C.bmm_plan(input, mat2))
+
+
+def _patched_einsum(*args, **kwargs):
+    """torch.einsum planned as batched matmuls (einsum_ops) so the bmm patch applies."""
+    orig = _ORIGINALS[(torch, "einsum")]
+    if kwargs or len(args) < 2 or not isinstance(args[0], str):
+        return orig(*args, **kwargs)
+    eq = args[0]
+    operands = args[1:]
+    if len(operands) == 1 and isinstance(operands[0], (list, tuple)):
+        operands = tuple(operands[0])
+    if not operands or not all(isinstance(t, torch.Tensor) for t in operands):
+        return orig(*args)
+    if not (_grad_safe(*operands) and _usable(*operands)) or len({t.dtype for t in operands}) != 1:
+        return orig(*args)
+    if einsum_ops.supported(eq, operands) is not None:
+        return orig(*args)
+    return _dispatch("einsum", operands[0],
+                     (eq.replace(" ", ""), tuple(tuple(t.shape) for t in operands)),
+                     lambda: einsum_ops.einsum(eq, operands, bmm=torch.bmm),
+                     lambda: orig(*args))
+
+
+def _patched_sdpa(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=False,
+                  scale=None, **kwargs):
+    orig = _ORIGINALS[(F, "scaled_dot_product_attention")]
+    if (attn_mask is not None or dropout_p != 0.0
+            or query.dim() != 4 or not _grad_safe(query, key, value)
+            or not _usable(query, key, value)):
+        return orig(query, key, value, attn_mask=attn_mask, dropout_p=dropout_p,
+                    is_causal=is_causal, scale=scale, **kwargs)
+    if kwargs.get("enable_gqa") and key.dim() == 4 and key.size(1) != query.size(1):
+        # grouped-query heads are not in the tile table yet: stock handles the head broadcast
+        return orig(query, key, value, attn_mask=attn_mask, dropout_p=dropout_p,
+                    is_causal=is_causal, scale=scale, **kwargs)
+    return _dispatch("attention", query,
+                     (query.shape, query.dtype, key.shape, value.shape, scale, is_causal),
+                     lambda: _C.attention(query, key, value, scale, is_causal),
+                     lambda: orig(query, key, value, attn_mask=attn_mask, dropout_p=dropout_p,
+                                  is_causal=is_causal, scale=scale, **kwargs),
+                     lambda: _C.attention_plan(query, key, value, scale, is_causal))
+
+
+def enable() -> None:
+    """Patch torch / torch.nn.functional so eligible calls run on the sm_100a kernels."""
+    global _ENABLED
+    if _ENABLED:
+        return
+    _install(torch, "matmul", _patched_matmul)
+    _install(torch, "bmm", _patched_bmm)
+    _install(torch, "einsum", _patched_einsum)
+    if hasattr(F, "scaled_dot_product_attention"):
+        _install(F, "scaled_dot_product_attention", _patched_sdpa)
+    _ENABLED = True
+
+
+def disable() -> None:
+    """Restore every patched function to the stock PyTorch implementation."""
+    global _ENABLED
+    for target, name in list(_ORIGINALS.keys()):
+        _restore(target, name)
+    _ENABLED = False
+
+
+def is_enabled() -> bool:
+    return _ENABLED
+
+
+def autoselect_report() -> str:
+    """Every signature seen so far with the tile-table entry (or stock) that served it."""
+    return autoselect.format_report()
+
+
+if os.environ.get("CMPEXT3_AUTOPATCH", "1") != "0":
+    enable()

@@ -1,0 +1,311 @@
+"""cmpext3._native -- the native ops of this path, bound to the C-ABI library with ctypes.
+
+Mirrors the reference's pybind11 module ``cmpext3._native`` for the two ops on this path
+(src/main.cpp:2307-2309 ``bmm(input, mat2)``, src/main.cpp:2353-2358
+``attention(query, key, value, scale=None, causal=False)``): same names, argument names, defaults,
+positional order, dtype in == dtype out, and ``RuntimeError`` for anything the kernels do not
+cover (the monkeypatch turns that into a stock-torch call, as in the reference).
+
+The work is done by ``libcmpx_b200.so`` (include/cmpx_b200.h): this module only checks
+arguments, allocates the output with torch's caching allocator, and passes raw device pointers,
+element strides and the current CUDA stream.  There is no CPU or library fallback in here: if the
+library is missing, importing this module raises ``ImportError``; if a call is outside the tile
+table, it raises ``RuntimeError``.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+from pathlib import Path
+
+import torch
+
+__all__ = ["attention", "bmm", "attention_plan", "bmm_plan", "device_status", "LIBRARY_PATH",
+           "lib", "CmpxError"]
+
+LIBRARY_PATH = Path(os.environ.get("CMPX_LIBRARY", Path(__file__).with_name("libcmpx_b200.so")))
+
+# Status codes (include/cmpx_b200.h)
+OK = 0
+ERR_INVALID_ARGUMENT = 1
+ERR_UNSUPPORTED_SHAPE = 2
+ERR_UNSUPPORTED_DTYPE = 3
+ERR_MISALIGNED = 4
+ERR_WORKSPACE = 5
+ERR_LAUNCH = 6
+ERR_DEVICE = 7
+ERR_DEVICE_TIMEOUT = 8
+
+DEVFLAG_WAIT_TIMEOUT = 1
+DEVFLAG_BAD_ARGS = 2
+
+_DTYPE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+
+class CmpxError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+    def __init__(self, what: str, status: int):
+        self.status = status
+        super().__init__(f"cmpext3 {what}: {_status_str(status)} (status {status})")
+
+
+class AttnDesc(ctypes.Structure):
+    _fields_ = [
+        ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p), ("o", ctypes.c_void_p),
+        ("batch", ctypes.c_int64), ("heads", ctypes.c_int64), ("len_q", ctypes.c_int64),
+        ("len_k", ctypes.c_int64), ("head_dim", ctypes.c_int64),
+        ("q_stride", ctypes.c_int64 * 3), ("k_stride", ctypes.c_int64 * 3),
+        ("v_stride", ctypes.c_int64 * 3), ("o_stride", ctypes.c_int64 * 3),
+        ("dtype", ctypes.c_int32), ("causal", ctypes.c_int32), ("scale", ctypes.c_double),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+class BmmDesc(ctypes.Structure):
+    _fields_ = [
+        ("a", ctypes.c_void_p), ("b", ctypes.c_void_p), ("c", ctypes.c_void_p),
+        ("batch", ctypes.c_int64), ("m", ctypes.c_int64), ("n", ctypes.c_int64), ("k", ctypes.c_int64),
+        ("a_stride", ctypes.c_int64 * 3), ("b_stride", ctypes.c_int64 * 3),
+        ("c_stride", ctypes.c_int64 * 3),
+        ("dtype", ctypes.c_int32), ("reserved", ctypes.c_int32),
+    ]
+
+
+def _load() -> ctypes.CDLL:
+    if not LIBRARY_PATH.exists():
+        raise ImportError(
+            f"cmpext3 native library not built ({LIBRARY_PATH}). "
+            "Run: python torch-cmp-patch_b200/build.py")
+    L = ctypes.CDLL(str(LIBRARY_PATH))
+    L.cmpx_attn_fwd.argtypes = [ctypes.POINTER(AttnDesc), ctypes.c_void_p]
+    L.cmpx_attn_fwd.restype = ctypes.c_int
+    L.cmpx_attn_workspace_size.argtypes = [ctypes.POINTER(AttnDesc)]
+    L.cmpx_attn_workspace_size.restype = ctypes.c_size_t
+    L.cmpx_bmm.argtypes = [ctypes.POINTER(BmmDesc), ctypes.c_void_p]
+    L.cmpx_bmm.restype = ctypes.c_int
+    L.cmpx_attn_plan.argtypes = [ctypes.POINTER(AttnDesc), ctypes.c_char_p, ctypes.c_size_t]
+    L.cmpx_attn_plan.restype = ctypes.c_int
+    L.cmpx_bmm_plan.argtypes = [ctypes.POINTER(BmmDesc), ctypes.c_char_p, ctypes.c_size_t]
+    L.cmpx_bmm_plan.restype = ctypes.c_int
+    L.cmpx_status_str.argtypes = [ctypes.c_int]
+    L.cmpx_status_str.restype = ctypes.c_char_p
+    L.cmpx_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint)]
+    L.cmpx_device_status.restype = ctypes.c_int
+    L.cmpx_selftest_wait_timeout.argtypes = [ctypes.c_uint64, ctypes.c_void_p]
+    L.cmpx_selftest_wait_timeout.restype = ctypes.c_int
+    L.cmpx_abi_version.argtypes = []
+    L.cmpx_abi_version.restype = ctypes.c_int
+    return L
+
+
+lib = _load()
+
+# Debug switch: synchronise after every call and raise if a device-side wait timed out.
+_CHECK = os.environ.get("CMPEXT3_CHECK", "0") not in ("0", "", "false", "False")
+
+
+def _status_str(status: int) -> str:
+    return lib.cmpx_status_str(int(status)).decode()
+
+
+def _stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def device_status() -> int:
+    """Synchronise the current device, return (and clear) its CMPX_DEVFLAG_* bits."""
+    flags = ctypes.c_uint(0)
+    st = lib.cmpx_device_status(ctypes.byref(flags))
+    if st != OK:
+        raise CmpxError("device_status", st)
+    return int(flags.value)
+
+
+def _post_check() -> None:
+    if _CHECK:
+        flags = device_status()
+        if flags:
+            raise CmpxError(f"device flags 0x{flags:x}", ERR_DEVICE_TIMEOUT)
+
+
+# ---------------------------------------------------------------------------------------------
+# attention
+# ---------------------------------------------------------------------------------------------
+
+def _tma_ok(t: torch.Tensor) -> bool:
+    """Strides usable by the 16-bit TMA path: head dim contiguous, other strides 16-byte multiples."""
+    if t.stride(3) != 1 or t.data_ptr() % 16 != 0:
+        return False
+    es = t.element_size()
+    return all(t.stride(i) > 0 and (t.stride(i) * es) % 16 == 0 for i in range(3))
+
+
+def _attn_desc(q, k, v, o, scale: float, causal: bool) -> AttnDesc:
+    d = AttnDesc()
+    d.q, d.k, d.v, d.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr()
+    d.batch, d.heads, d.len_q, d.head_dim = q.shape
+    d.len_k = k.shape[2]
+    for name, t in (("q_stride", q), ("k_stride", k), ("v_stride", v), ("o_stride", o)):
+        getattr(d, name)[:] = (t.stride(0), t.stride(1), t.stride(2))
+    d.dtype = _DTYPE[q.dtype]
+    d.causal = 1 if causal else 0
+    d.scale = float(scale)
+    d.workspace = None
+    d.workspace_bytes = 0
+    return d
+
+
+def _check_attention_args(query, key, value) -> None:
+    for name, t in (("query", query), ("key", key), ("value", value)):
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{name} must be a Tensor")
+        if t.dim() != 4:
+            raise RuntimeError(f"{name} must be 4D (batch, heads, seq, head_dim)")
+        if not t.is_cuda:
+            raise RuntimeError(f"{name} must be a CUDA tensor")
+    if query.dtype not in _DTYPE or key.dtype != query.dtype or value.dtype != query.dtype:
+        raise RuntimeError("query/key/value must share one dtype among float32/float16/bfloat16")
+    if not (query.device == key.device == value.device):
+        raise RuntimeError("query/key/value must be on one device")
+    B, H, _, D = query.shape
+    if key.shape[0] != B or key.shape[1] != H or key.shape[3] != D:
+        raise RuntimeError(f"key shape {tuple(key.shape)} does not match query {tuple(query.shape)}")
+    if tuple(value.shape) != (B, H, key.shape[2], D):
+        raise RuntimeError(f"value shape {tuple(value.shape)} does not match key {tuple(key.shape)}")
+
+
+def _prepare_attention(query, key, value, scale, causal):
+    _check_attention_args(query, key, value)
+    B, H, Lq, D = query.shape
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if query.dtype != torch.float32:
+        # TMA needs 16-byte aligned rows; copy a view that does not have them (the reference makes
+        # such inputs contiguous too, src/main.cpp:1693-1698).
+        query, key, value = (t if _tma_ok(t) else t.contiguous() for t in (query, key, value))
+    else:
+        query, key, value = (t if t.stride(3) == 1 else t.contiguous() for t in (query, key, value))
+    # Output in [B, Lq, H, D] memory viewed as [B, H, Lq, D] -- the layout torch's own CUDA SDPA
+    # returns and the one a model's transpose(1, 2).reshape(B, Lq, H*D) wants.
+    out = torch.empty((B, Lq, H, D), dtype=query.dtype, device=query.device).transpose(1, 2)
+    return query, key, value, out, float(scale)
+
+
+def attention(query, key, value, scale=None, causal=False):
+    """SDPA forward on the sm_100a kernels.  Same contract as the reference's ops.attention."""
+    q, k, v, out, scale = _prepare_attention(query, key, value, scale, causal)
+    desc = _attn_desc(q, k, v, out, scale, bool(causal))
+    with torch.cuda.device(q.device):
+        st = lib.cmpx_attn_fwd(ctypes.byref(desc), _stream_handle(q.device))
+    if st != OK:
+        raise CmpxError("attention", st)
+    _post_check()
+    return out
+
+
+def attention_plan(query, key, value, scale=None, causal=False) -> str:
+    """Name of the tile-table entry ``attention`` would run for these arguments."""
+    q, k, v, out, scale = _prepare_attention(query, key, value, scale, causal)
+    desc = _attn_desc(q, k, v, out, scale, bool(causal))
+    buf = ctypes.create_string_buffer(128)
+    st = lib.cmpx_attn_plan(ctypes.byref(desc), buf, 128)
+    if st != OK:
+        raise CmpxError("attention plan", st)
+    return buf.value.decode()
+
+
+# ---------------------------------------------------------------------------------------------
+# bmm
+# ---------------------------------------------------------------------------------------------
+
+def _mat_ok(t: torch.Tensor) -> bool:
+    """A [batch, r, c] operand the 16-bit TMA path reads in place: row- or column-major matrices
+    with 16-byte aligned leading and batch strides."""
+    if t.data_ptr() % 16 != 0:
+        return False
+    es = t.element_size()
+    s0, s1, s2 = t.stride()
+    lead_ok = (s2 == 1 and (t.shape[1] == 1 or (s1 > 0 and (s1 * es) % 16 == 0))) or \
+              (s1 == 1 and (t.shape[2] == 1 or (s2 > 0 and (s2 * es) % 16 == 0)))
+    batch_ok = t.shape[0] == 1 or (s0 > 0 and (s0 * es) % 16 == 0)
+    return lead_ok and batch_ok
+
+
+def _check_bmm_args(a, b) -> None:
+    for name, t in (("input", a), ("mat2", b)):
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{name} must be a Tensor")
+        if t.dim() != 3:
+            raise RuntimeError(f"{name} must be 3D")
+        if not t.is_cuda:
+            raise RuntimeError(f"{name} must be a CUDA tensor")
+    if a.dtype not in _DTYPE or b.dtype != a.dtype:
+        raise RuntimeError("input/mat2 must share one dtype among float32/float16/bfloat16")
+    if a.device != b.device:
+        raise RuntimeError("input/mat2 must be on one device")
+    if a.shape[0] != b.shape[0]:
+        raise RuntimeError("Batch size mismatch")
+    if a.shape[2] != b.shape[1]:
+        raise RuntimeError("Contracting dimension (K) mismatch")
+
+
+def _prepare_bmm(a, b):
+    _check_bmm_args(a, b)
+    if a.dtype != torch.float32:
+        a = a if _mat_ok(a) else a.contiguous()
+        b = b if _mat_ok(b) else b.contiguous()
+    nb, m, _ = a.shape
+    n = b.shape[2]
+    c = torch.empty((nb, m, n), dtype=a.dtype, device=a.device)
+    return a, b, c
+
+
+def _bmm_desc(a, b, c) -> BmmDesc:
+    d = BmmDesc()
+    d.a, d.b, d.c = a.data_ptr(), b.data_ptr(), c.data_ptr()
+    d.batch, d.m, d.k = a.shape
+    d.n = b.shape[2]
+    d.a_stride[:] = a.stride()
+    d.b_stride[:] = b.stride()
+    d.c_stride[:] = c.stride()
+    d.dtype = _DTYPE[a.dtype]
+    d.reserved = 0
+    return d
+
+
+def bmm(input, mat2):
+    """Batched matmul on the sm_100a kernels.  Same contract as the reference's ops.bmm."""
+    a, b, c = _prepare_bmm(input, mat2)
+    if c.numel() == 0:
+        return c
+    if a.shape[2] == 0:
+        return c.zero_()
+    desc = _bmm_desc(a, b, c)
+    with torch.cuda.device(a.device):
+        st = lib.cmpx_bmm(ctypes.byref(desc), _stream_handle(a.device))
+    if st != OK:
+        raise CmpxError("bmm", st)
+    _post_check()
+    return c
+
+
+def bmm_plan(input, mat2) -> str:
+    """Name of the tile-table entry ``bmm`` would run for these arguments."""
+    a, b, c = _prepare_bmm(input, mat2)
+    desc = _bmm_desc(a, b, c)
+    buf = ctypes.create_string_buffer(128)
+    st = lib.cmpx_bmm_plan(ctypes.byref(desc), buf, 128)
+    if st != OK:
+        raise CmpxError("bmm plan", st)
+    return buf.value.decode()
+
+
+def selftest_wait_timeout(timeout_ns: int, device=None) -> None:
+    """Launch the bounded-wait self-test kernel (see cmpx_selftest_wait_timeout)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        st = lib.cmpx_selftest_wait_timeout(int(timeout_ns), _stream_handle(dev))
+    if st != OK:
+        raise CmpxError("selftest", st)

@@ -1,0 +1,498 @@
+// attn_fwd_sm100.cu -- scaled-dot-product attention forward for fp16 / bf16 on B200 (sm_100a).
+//
+// Computes O = softmax(Q K^T * scale [+ top-left causal mask]) V for [B, H, L, D] views with a
+// contiguous head dim, D <= 128.  This replaces the reference's two fp16 attention kernels
+// (flash_attn_hfma2_kernel, src/cuda/fp16_flash_attention_hfma2.cu:72-243, non-causal; and
+// flash_attention_fp16_optimized, src/cuda/fp16_attention.cu:135-319, causal, D=128) with one
+// tensor-core kernel.  The algorithm is the same online-softmax forward (running row max m,
+// running sum l, O rescaled when m grows, O / l at the end, exp2 domain with the scale folded
+// in); the machinery is Blackwell's:
+//
+//   * one CTA owns two 128-row Q tiles (rows q0 .. q0+255) of one (batch, head);
+//   * warp 8 streams K_j and V_j (128 keys x D) through a ring of shared-memory stages with TMA
+//     (128-byte swizzle, OOB rows/cols zero-filled), Q once;
+//   * warp 9 issues tcgen05.mma: S_t = Q_t K_j^T into TMEM (fp32), then O_t += P_t V_j with P_t
+//     read straight from TMEM (A-from-TMEM form) -- P never touches shared memory;
+//   * warps 0-3 / 4-7 are the softmax warpgroups of tile 0 / tile 1: thread i owns row i, reads
+//     its 128 scores with tcgen05.ld, applies the mask, updates m and l, writes P (16-bit) back
+//     over its scores with tcgen05.st, and rescales its O row in TMEM when the running max grew
+//     by more than 2^8 (otherwise the stale max is kept: exact, since O and l share it);
+//   * the two tiles ping-pong: the tensor core runs tile 1's MMAs while tile 0's softmax runs.
+//   * epilogue: O / l, converted, staged in the (now idle) Q buffer in the swizzled layout and
+//     written with TMA stores that clip rows >= Lq and cols >= D.
+//
+// TMEM columns: S0 [0,128) S1 [128,256) O0 [256,256+DP) O1 [256+DP, 256+2*DP).
+// Every wait is bounded (see cmpx_ptx.cuh); a CTA that gives up drains its in-flight copies
+// and MMAs, frees TMEM, sets the device status word and returns.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <mutex>
+
+#include "cmpx_internal.h"
+#include "cmpx_ptx.cuh"
+
+namespace cmpx {
+
+template <int DP>
+struct FmhaCfg {
+  static constexpr int BM = 128;                    // rows of one Q tile
+  static constexpr int BN = 128;                    // keys per K/V tile
+  static constexpr int NCH = DP / 64;               // 128-byte chunks per row
+  static constexpr int CH_BYTES = 128 * 128;        // one chunk of a 128-row tile
+  static constexpr int QTILE_BYTES = NCH * CH_BYTES;
+  static constexpr int KV_BYTES = NCH * CH_BYTES;
+  static constexpr int NSTAGE = DP == 128 ? 4 : 6;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_KV = 2 * QTILE_BYTES;
+  static constexpr int OFF_BAR = OFF_KV + NSTAGE * KV_BYTES;
+  // barrier slots
+  static constexpr int B_Q = 0;
+  static constexpr int B_FULL = 1;
+  static constexpr int B_EMPTY = B_FULL + NSTAGE;
+  static constexpr int B_SFULL = B_EMPTY + NSTAGE;  // [2]
+  static constexpr int B_PREADY = B_SFULL + 2;      // [2]
+  static constexpr int B_OFINAL = B_PREADY + 2;     // [2]
+  static constexpr int B_DRAIN = B_OFINAL + 2;
+  static constexpr int NBAR = B_DRAIN + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // +1024: runtime alignment slack
+  static constexpr int TM_S0 = 0, TM_S1 = 128, TM_O0 = 256, TM_O1 = 256 + DP;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int THREADS = 320;
+};
+
+struct FmhaParams {
+  int heads;
+  int len_q;
+  int len_k;
+  int n_pairs;        // ceil(len_q / 256)
+  int causal;
+  int neg_scale;      // scale < 0: track the row minimum of raw scores instead of the maximum
+  float scale_log2;   // scale * log2(e)
+  unsigned long long timeout_ns;
+  unsigned int* dev_flags;
+};
+
+template <int DP, bool BF16>
+__global__ void __launch_bounds__(320, 1)
+    fmha_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
+                          const __grid_constant__ CUtensorMap tm_k,
+                          const __grid_constant__ CUtensorMap tm_v,
+                          const __grid_constant__ CUtensorMap tm_o, const FmhaParams p) {
+  using C = FmhaCfg<DP>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t base = (raw_base + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw_base);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const int bh = blockIdx.x;
+  const int b = bh / p.heads;
+  const int h = bh - b * p.heads;
+  const int pair = p.n_pairs - 1 - static_cast<int>(blockIdx.y);  // heavy (late) rows first
+  const int q0 = pair * 256;
+  const int kv_len = p.causal ? min(p.len_k, q0 + 256) : p.len_k;
+  const int n_kv = (kv_len + C::BN - 1) / C::BN;
+
+  const uint32_t sQ = base + C::OFF_Q;
+  const uint32_t sKV = base + C::OFF_KV;
+  auto bar = [&](int i) -> uint32_t { return base + C::OFF_BAR + 8u * i; };
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(C::B_Q), 1);
+    for (int s = 0; s < C::NSTAGE; ++s) {
+      mbar_init(bar(C::B_FULL + s), 1);
+      mbar_init(bar(C::B_EMPTY + s), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar(C::B_SFULL + t), 1);
+      mbar_init(bar(C::B_PREADY + t), 128);
+      mbar_init(bar(C::B_OFINAL + t), 1);
+    }
+    mbar_init(bar(C::B_DRAIN), 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_u32(tmem_holder), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 8 && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+    tma_prefetch_desc(&tm_o);
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem = *tmem_holder;
+  const WaitCtl ctl{abort_flag, p.dev_flags, p.timeout_ns};
+
+  if (warp == 8) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(bar(C::B_Q), 2 * C::QTILE_BYTES);
+      for (int t = 0; t < 2; ++t)
+        for (int c = 0; c < C::NCH; ++c)
+          tma_load_4d(sQ + t * C::QTILE_BYTES + c * C::CH_BYTES, &tm_q, bar(C::B_Q), c * 64,
+                      q0 + t * C::BM, h, b);
+      int issued = 0;
+      bool ok = true;
+      for (int j = 0; ok && j < n_kv; ++j) {
+        for (int which = 0; which < 2; ++which) {
+          const int i = 2 * j + which;
+          const int st = i % C::NSTAGE;
+          const uint32_t rnd = static_cast<uint32_t>(i / C::NSTAGE);
+          if (!mbar_wait(bar(C::B_EMPTY + st), (rnd & 1u) ^ 1u, ctl)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(bar(C::B_FULL + st), C::KV_BYTES);
+          const CUtensorMap* m = which ? &tm_v : &tm_k;
+          for (int c = 0; c < C::NCH; ++c)
+            tma_load_4d(sKV + st * C::KV_BYTES + c * C::CH_BYTES, m, bar(C::B_FULL + st), c * 64,
+                        j * C::BN, h, b);
+          issued = i + 1;
+        }
+      }
+      if (*abort_flag) {
+        // Let every copy still in flight land before shared memory goes away.
+        mbar_wait_drain(bar(C::B_Q), 0, p.timeout_ns);
+        for (int i = max(0, issued - C::NSTAGE); i < issued; ++i)
+          mbar_wait_drain(bar(C::B_FULL + i % C::NSTAGE), static_cast<uint32_t>(i / C::NSTAGE) & 1u,
+                          p.timeout_ns);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdescQK = idesc_f16(128, 128, BF16 ? 1 : 0, 0, 0);
+      constexpr uint32_t kIdescPV = idesc_f16(128, DP, BF16 ? 1 : 0, 0, 1);
+      auto issue_qk = [&](int t, uint32_t k_addr) {
+        const uint32_t q_addr = sQ + t * C::QTILE_BYTES;
+        const uint32_t d_tmem = tmem + (t ? C::TM_S1 : C::TM_S0);
+#pragma unroll
+        for (int k = 0; k < DP / 16; ++k) {
+          const uint32_t off = (k >> 2) * C::CH_BYTES + (k & 3) * 32;
+          umma_ss(d_tmem, smem_desc_sw128(q_addr + off, 16, 1024),
+                  smem_desc_sw128(k_addr + off, 16, 1024), kIdescQK, k > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](int t, uint32_t v_addr, bool acc) {
+        const uint32_t p_tmem = tmem + (t ? C::TM_S1 : C::TM_S0);
+        const uint32_t d_tmem = tmem + (t ? C::TM_O1 : C::TM_O0);
+#pragma unroll
+        for (int k = 0; k < C::BN / 16; ++k) {
+          umma_ts(d_tmem, p_tmem + k * 8, smem_desc_sw128(v_addr + k * 2048, C::CH_BYTES, 1024),
+                  kIdescPV, (acc || k > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(bar(C::B_Q), 0, ctl);
+      if (ok) ok = mbar_wait(bar(C::B_FULL + 0), 0, ctl);  // K_0 is load 0
+      if (ok) {
+        tc_fence_after_sync();
+        issue_qk(0, sKV);
+        umma_commit(bar(C::B_SFULL + 0));
+        issue_qk(1, sKV);
+        umma_commit(bar(C::B_SFULL + 1));
+        umma_commit(bar(C::B_EMPTY + 0));
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int iv = 2 * j + 1, ik = 2 * j + 2;
+        const int stv = iv % C::NSTAGE, stk = ik % C::NSTAGE;
+        const uint32_t pv = static_cast<uint32_t>(iv / C::NSTAGE) & 1u;
+        const uint32_t pk = static_cast<uint32_t>(ik / C::NSTAGE) & 1u;
+        const bool has_next = j + 1 < n_kv;
+        const uint32_t v_addr = sKV + stv * C::KV_BYTES;
+        const uint32_t k_addr = sKV + stk * C::KV_BYTES;
+        if (!mbar_wait(bar(C::B_FULL + stv), pv, ctl)) break;
+        if (!mbar_wait(bar(C::B_PREADY + 0), j & 1, ctl)) break;
+        tc_fence_after_sync();
+        issue_pv(0, v_addr, j > 0);
+        if (has_next) {
+          if (!mbar_wait(bar(C::B_FULL + stk), pk, ctl)) break;
+          tc_fence_after_sync();
+          issue_qk(0, k_addr);
+          umma_commit(bar(C::B_SFULL + 0));
+        } else {
+          umma_commit(bar(C::B_OFINAL + 0));
+        }
+        if (!mbar_wait(bar(C::B_PREADY + 1), j & 1, ctl)) break;
+        tc_fence_after_sync();
+        issue_pv(1, v_addr, j > 0);
+        umma_commit(bar(C::B_EMPTY + stv));
+        if (has_next) {
+          issue_qk(1, k_addr);
+          umma_commit(bar(C::B_SFULL + 1));
+          umma_commit(bar(C::B_EMPTY + stk));
+        } else {
+          umma_commit(bar(C::B_OFINAL + 1));
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax / epilogue
+    const int t = warp >> 2;            // Q tile of this warpgroup
+    const int wq = warp & 3;            // TMEM lane quarter of this warp
+    const int row = wq * 32 + lane;     // row inside the tile
+    const int qrow = q0 + t * C::BM + row;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16);
+    const uint32_t s_tm = lane_base + (t ? C::TM_S1 : C::TM_S0);
+    const uint32_t o_tm = lane_base + (t ? C::TM_O1 : C::TM_O0);
+    const float sl2 = p.scale_log2;
+    const float masked = p.neg_scale ? INFINITY : -INFINITY;  // masked * sl2 == -inf
+    float m_run = -INFINITY;  // running max of s * scale * log2(e)
+    float l_run = 0.f;
+    bool ok = true;
+
+    for (int j = 0; j < n_kv; ++j) {
+      if (!mbar_wait_warp(bar(C::B_SFULL + t), j & 1, ctl)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after_sync();
+      uint32_t sr[128];
+      tmem_ld64(s_tm, *reinterpret_cast<uint32_t(*)[64]>(&sr[0]));
+      tmem_ld64(s_tm + 64, *reinterpret_cast<uint32_t(*)[64]>(&sr[64]));
+      float* s = reinterpret_cast<float*>(sr);
+
+      const int kv0 = j * C::BN;
+      const bool tile_masked =
+          (kv0 + C::BN > p.len_k) || (p.causal && kv0 + C::BN - 1 > q0 + t * C::BM);
+      if (tile_masked) {
+        int lim = p.len_k - kv0;
+        if (p.causal) lim = min(lim, qrow - kv0 + 1);
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (c >= lim) s[c] = masked;
+      }
+      float mx;
+      if (!p.neg_scale) {
+        float a0 = s[0], a1 = s[1], a2 = s[2], a3 = s[3];
+#pragma unroll
+        for (int c = 4; c < 128; c += 4) {
+          a0 = fmaxf(a0, s[c]);
+          a1 = fmaxf(a1, s[c + 1]);
+          a2 = fmaxf(a2, s[c + 2]);
+          a3 = fmaxf(a3, s[c + 3]);
+        }
+        mx = fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
+      } else {
+        float a0 = s[0], a1 = s[1], a2 = s[2], a3 = s[3];
+#pragma unroll
+        for (int c = 4; c < 128; c += 4) {
+          a0 = fminf(a0, s[c]);
+          a1 = fminf(a1, s[c + 1]);
+          a2 = fminf(a2, s[c + 2]);
+          a3 = fminf(a3, s[c + 3]);
+        }
+        mx = fminf(fminf(a0, a1), fminf(a2, a3));
+      }
+      const float m_tile = mx * sl2;
+      const float m_new = fmaxf(m_run, m_tile);
+      float alpha = 1.f;
+      if (m_new - m_run > 8.f) {  // also true on the first tile (m_run = -inf)
+        alpha = ex2_approx(m_run - m_new);
+        m_run = m_new;
+      }
+      const float mb = (m_run == -INFINITY) ? 0.f : m_run;
+      float lsum0 = 0.f, lsum1 = 0.f;
+      uint32_t pk[64];
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float p0 = ex2_approx(fmaf(s[2 * c], sl2, -mb));
+        const float p1 = ex2_approx(fmaf(s[2 * c + 1], sl2, -mb));
+        lsum0 += p0;
+        lsum1 += p1;
+        pk[c] = BF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
+      }
+      l_run = l_run * alpha + (lsum0 + lsum1);
+      tmem_st32(s_tm, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
+      tmem_st32(s_tm + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
+      // O holds PV_{j-1} complete: S_j's commit came after it in issue order.
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+        for (int c = 0; c < DP / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_tm + c * 32, o);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(o_tm + c * 32, o);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before_sync();
+      mbar_arrive(bar(C::B_PREADY + t));
+    }
+
+    if (ok) ok = mbar_wait_warp(bar(C::B_OFINAL + t), 0, ctl);
+    if (ok) {
+      tc_fence_after_sync();
+      const float inv_l = 1.f / l_run;
+      // Stage O_t in the Q_t buffer (all MMAs of tile t are complete).
+      const uint32_t stage = sQ + t * C::QTILE_BYTES;
+#pragma unroll 1
+      for (int c = 0; c < C::NCH; ++c) {
+        const uint32_t row_addr = stage + c * C::CH_BYTES + row * 128;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t o[32];
+          tmem_ld32(o_tm + c * 64 + hh * 32, o);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float lo = __uint_as_float(o[q * 8 + 2 * e]) * inv_l;
+              const float hi = __uint_as_float(o[q * 8 + 2 * e + 1]) * inv_l;
+              w[e] = BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+            }
+            const int chunk = hh * 4 + q;  // 16-byte chunk within the 128-byte row
+            st_shared_v4(row_addr + ((chunk ^ (row & 7)) << 4), w[0], w[1], w[2], w[3]);
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      const int row0 = q0 + t * C::BM + wq * 32;
+      if (lane == 0 && row0 < p.len_q) {
+        for (int c = 0; c < C::NCH; ++c)
+          tma_store_4d(&tm_o, stage + c * C::CH_BYTES + wq * 32 * 128, c * 64, row0, h, b);
+        bulk_commit_group();
+        bulk_wait_group_read0();
+      }
+      __syncwarp();
+    }
+  }
+
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 9) {
+    if (*abort_flag) {
+      if (lane == 0) {
+        umma_commit(bar(C::B_DRAIN));
+        mbar_wait_drain(bar(C::B_DRAIN), 0, p.timeout_ns);
+      }
+      __syncwarp();
+    }
+    tc_fence_after_sync();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// --------------------------------------------------------------------------------------------
+// Host side
+// --------------------------------------------------------------------------------------------
+namespace {
+
+bool stride_ok(int64_t s, int esize) { return s > 0 && ((s * esize) % 16) == 0 && (s * esize) < (1ll << 40); }
+
+template <int DP, bool BF16>
+void* fmha_kernel_ptr() {
+  return reinterpret_cast<void*>(&fmha_fwd_sm100_kernel<DP, BF16>);
+}
+
+}  // namespace
+
+const char* fmha_sm100_plan(const cmpx_attn_desc* d, int* status) {
+  *status = CMPX_OK;
+  if (d->dtype != CMPX_F16 && d->dtype != CMPX_BF16) {
+    *status = CMPX_ERR_UNSUPPORTED_DTYPE;
+    return "none";
+  }
+  if (d->head_dim < 8 || d->head_dim > 128 || (d->head_dim % 8) != 0) {
+    *status = CMPX_ERR_UNSUPPORTED_SHAPE;
+    return "none";
+  }
+  if (d->len_q > (int64_t)256 * 65535 || d->len_k > (1ll << 31) - 256 || d->batch * d->heads > (1ll << 31) - 1) {
+    *status = CMPX_ERR_UNSUPPORTED_SHAPE;
+    return "none";
+  }
+  const void* ptrs[4] = {d->q, d->k, d->v, d->o};
+  for (const void* ptr : ptrs)
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15u) != 0) {
+      *status = CMPX_ERR_MISALIGNED;
+      return "none";
+    }
+  const int64_t* strides[4] = {d->q_stride, d->k_stride, d->v_stride, d->o_stride};
+  for (const int64_t* s : strides)
+    for (int i = 0; i < 3; ++i)
+      if (!stride_ok(s[i], 2)) {
+        *status = CMPX_ERR_MISALIGNED;
+        return "none";
+      }
+  const bool bf = d->dtype == CMPX_BF16;
+  if (d->head_dim <= 64) return bf ? "fmha_sm100<bf16,D64,2x128q,128kv,6st>" : "fmha_sm100<f16,D64,2x128q,128kv,6st>";
+  return bf ? "fmha_sm100<bf16,D128,2x128q,128kv,4st>" : "fmha_sm100<f16,D128,2x128q,128kv,4st>";
+}
+
+namespace {
+
+bool make_bhsd_map(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, int64_t D, int64_t L,
+                   int64_t H, int64_t B, const int64_t* st, uint32_t box_rows) {
+  const uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(L),
+                            static_cast<uint64_t>(H), static_cast<uint64_t>(B)};
+  const uint64_t strides[3] = {static_cast<uint64_t>(st[2]) * 2, static_cast<uint64_t>(st[1]) * 2,
+                               static_cast<uint64_t>(st[0]) * 2};
+  const uint32_t box[4] = {64, box_rows, 1, 1};
+  return encode_tmap(map, dt, 4, ptr, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <int DP, bool BF16>
+int launch_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
+  using C = FmhaCfg<DP>;
+  const CUtensorMapDataType dt =
+      BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap tq, tk, tv, to;
+  if (!make_bhsd_map(&tq, dt, d->q, d->head_dim, d->len_q, d->heads, d->batch, d->q_stride, 128) ||
+      !make_bhsd_map(&tk, dt, d->k, d->head_dim, d->len_k, d->heads, d->batch, d->k_stride, 128) ||
+      !make_bhsd_map(&tv, dt, d->v, d->head_dim, d->len_k, d->heads, d->batch, d->v_stride, 128) ||
+      !make_bhsd_map(&to, dt, d->o, d->head_dim, d->len_q, d->heads, d->batch, d->o_stride, 32))
+    return CMPX_ERR_LAUNCH;
+
+  static std::once_flag once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t attr_err = cudaSuccess;
+  std::call_once(once[dev & 63], [&] {
+    attr_err = cudaFuncSetAttribute(fmha_kernel_ptr<DP, BF16>(),
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess) return CMPX_ERR_LAUNCH;
+
+  FmhaParams p;
+  p.heads = static_cast<int>(d->heads);
+  p.len_q = static_cast<int>(d->len_q);
+  p.len_k = static_cast<int>(d->len_k);
+  p.n_pairs = static_cast<int>((d->len_q + 255) / 256);
+  p.causal = d->causal ? 1 : 0;
+  p.neg_scale = d->scale < 0 ? 1 : 0;
+  p.scale_log2 = static_cast<float>(d->scale * 1.4426950408889634);
+  p.timeout_ns = ctx.timeout_ns;
+  p.dev_flags = ctx.dev_flags;
+  dim3 grid(static_cast<unsigned>(d->batch * d->heads), static_cast<unsigned>(p.n_pairs));
+  fmha_fwd_sm100_kernel<DP, BF16><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, to, p);
+  return cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
+}
+
+}  // namespace
+
+int launch_fmha_sm100(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
+  int st = CMPX_OK;
+  fmha_sm100_plan(d, &st);
+  if (st != CMPX_OK) return st;
+  if (d->len_q == 0) return CMPX_OK;
+  const bool bf = d->dtype == CMPX_BF16;
+  if (d->head_dim <= 64) return bf ? launch_typed<64, true>(d, ctx) : launch_typed<64, false>(d, ctx);
+  return bf ? launch_typed<128, true>(d, ctx) : launch_typed<128, false>(d, ctx);
+}
+
+}  // namespace cmpx

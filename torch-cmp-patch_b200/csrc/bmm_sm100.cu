@@ -1,0 +1,465 @@
+// bmm_sm100.cu -- batched matmul C[b] = A[b] @ B[b] for fp16 / bf16 on B200 (sm_100a).
+//
+// Replaces the reference's bmm path (custom_bmm_forward, src/main.cpp:363-441), which converts
+// bf16 operands to fp32 copies, makes them contiguous, and launches one FMUL/FADD GEMM per batch
+// item from a host loop (gemm_fp32_ga100_kernel, src/cuda/fp32_matmul.cu:31-184; fp16 uses
+// gemm_fp16_sm75 with half2 accumulation, src/cuda/fp16_matmul.cu:143-367).  Here:
+//
+//   * one launch covers every batch item (grid z) and every 128 x BN output tile;
+//   * operands are read in place through rank-3 TMA maps, row-major OR column-major (a transposed
+//     view such as K^T from an einsum plan is a K-major B operand: no copy);
+//   * warp 0 streams 128x64 A and 64xBN B tiles through a ring of 128-byte-swizzled stages,
+//     warp 1 issues tcgen05.mma (M=128, N=BN, K=16 steps) into an fp32 TMEM accumulator,
+//     warps 2-5 drain TMEM -> fp32 -> 16-bit -> swizzled shared staging -> TMA store;
+//   * fp32 accumulation over all of K (the reference's fp16 path accumulates in half);
+//   * ~96 KB shared and <= 256 TMEM columns per CTA so two CTAs share an SM: one CTA's epilogue
+//     (the HBM-bound part for the attention-score shapes) overlaps the other's main loop.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <array>
+#include <cmath>
+#include <mutex>
+#include <string>
+
+#include "cmpx_internal.h"
+#include "cmpx_ptx.cuh"
+
+namespace cmpx {
+
+template <int BN>
+struct BmmCfg {
+  static constexpr int BM = 128, BK = 64;
+  static constexpr int A_BYTES = BM * BK * 2;       // 16 KB
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = BN == 256 ? 2 : (BN == 128 ? 3 : 4);
+  static constexpr int OFF_BAR = STAGES * STAGE_BYTES;
+  // barriers: full[STAGES], empty[STAGES], acc, drain
+  static constexpr int NBAR = 2 * STAGES + 2;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
+  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+  static_assert(STAGES * STAGE_BYTES >= BM * BN * 2, "epilogue staging must fit in the stages");
+};
+
+struct BmmParams {
+  int m, n, k;
+  int n_kblocks;
+  unsigned long long timeout_ns;
+  unsigned int* dev_flags;
+};
+
+template <int BN, bool A_MN, bool B_MN, bool BF16>
+__global__ void __launch_bounds__(192, 2)
+    bmm_sm100_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                     const __grid_constant__ CUtensorMap tm_c, const BmmParams p) {
+  using C = BmmCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t base = (raw_base + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw_base);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN;
+  const int m0 = blockIdx.y * C::BM;
+  const int z = blockIdx.z;
+
+  auto bar = [&](int i) -> uint32_t { return base + C::OFF_BAR + 8u * i; };
+  const int B_FULL = 0, B_EMPTY = C::STAGES, B_ACC = 2 * C::STAGES, B_DRAIN = 2 * C::STAGES + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(bar(B_FULL + s), 1);
+      mbar_init(bar(B_EMPTY + s), 1);
+    }
+    mbar_init(bar(B_ACC), 1);
+    mbar_init(bar(B_DRAIN), 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_holder), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_b);
+    tma_prefetch_desc(&tm_c);
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem = *tmem_holder;
+  const WaitCtl ctl{abort_flag, p.dev_flags, p.timeout_ns};
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < p.n_kblocks; ++kb) {
+        const int st = kb % C::STAGES;
+        const uint32_t rnd = static_cast<uint32_t>(kb / C::STAGES);
+        if (!mbar_wait(bar(B_EMPTY + st), (rnd & 1u) ^ 1u, ctl)) break;
+        const uint32_t sa = base + st * C::STAGE_BYTES;
+        const uint32_t sb = sa + C::A_BYTES;
+        mbar_arrive_expect_tx(bar(B_FULL + st), C::STAGE_BYTES);
+        if (!A_MN) {
+          tma_load_3d(sa, &tm_a, bar(B_FULL + st), kb * C::BK, m0, z);
+        } else {
+          tma_load_3d(sa, &tm_a, bar(B_FULL + st), m0, kb * C::BK, z);
+          tma_load_3d(sa + 8192, &tm_a, bar(B_FULL + st), m0 + 64, kb * C::BK, z);
+        }
+        if (!B_MN) {
+          tma_load_3d(sb, &tm_b, bar(B_FULL + st), kb * C::BK, n0, z);
+        } else {
+#pragma unroll
+          for (int c = 0; c < BN / 64; ++c)
+            tma_load_3d(sb + c * 8192, &tm_b, bar(B_FULL + st), n0 + 64 * c, kb * C::BK, z);
+        }
+        issued = kb + 1;
+      }
+      if (*abort_flag) {
+        for (int i = max(0, issued - C::STAGES); i < issued; ++i)
+          mbar_wait_drain(bar(B_FULL + i % C::STAGES), static_cast<uint32_t>(i / C::STAGES) & 1u,
+                          p.timeout_ns);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdesc = idesc_f16(128, BN, BF16 ? 1 : 0, A_MN ? 1 : 0, B_MN ? 1 : 0);
+      bool ok = true;
+      for (int kb = 0; kb < p.n_kblocks; ++kb) {
+        const int st = kb % C::STAGES;
+        if (!mbar_wait(bar(B_FULL + st), static_cast<uint32_t>(kb / C::STAGES) & 1u, ctl)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after_sync();
+        const uint32_t sa = base + st * C::STAGE_BYTES;
+        const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t da = A_MN ? smem_desc_sw128(sa + k * 2048, 8192, 1024)
+                                   : smem_desc_sw128(sa + k * 32, 16, 1024);
+          const uint64_t db = B_MN ? smem_desc_sw128(sb + k * 2048, 8192, 1024)
+                                   : smem_desc_sw128(sb + k * 32, 16, 1024);
+          umma_ss(tmem, da, db, kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(bar(B_EMPTY + st));
+      }
+      if (ok) umma_commit(bar(B_ACC));
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    if (mbar_wait_warp(bar(B_ACC), 0, ctl)) {
+      tc_fence_after_sync();
+#pragma unroll 1
+      for (int g = 0; g < BN / 32; ++g) {
+        uint32_t acc[32];
+        tmem_ld32(t_lane + g * 32, acc);
+        const uint32_t row_addr = base + (g >> 1) * (128 * 128) + row * 128;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float lo = __uint_as_float(acc[q * 8 + 2 * e]);
+            const float hi = __uint_as_float(acc[q * 8 + 2 * e + 1]);
+            w[e] = BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+          }
+          const int chunk = (g & 1) * 4 + q;
+          st_shared_v4(row_addr + ((chunk ^ (row & 7)) << 4), w[0], w[1], w[2], w[3]);
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      const int r0 = m0 + quarter * 32;
+      if (lane == 0 && r0 < p.m) {
+        for (int c = 0; c < BN / 64; ++c)
+          if (n0 + 64 * c < p.n)
+            tma_store_3d(&tm_c, base + c * (128 * 128) + quarter * 32 * 128, n0 + 64 * c, r0, z);
+        bulk_commit_group();
+        bulk_wait_group_read0();
+      }
+      __syncwarp();
+    }
+  }
+
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    if (*abort_flag) {
+      if (lane == 0) {
+        umma_commit(bar(B_DRAIN));
+        mbar_wait_drain(bar(B_DRAIN), 0, p.timeout_ns);
+      }
+      __syncwarp();
+    }
+    tc_fence_after_sync();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// --------------------------------------------------------------------------------------------
+// Host side
+// --------------------------------------------------------------------------------------------
+namespace {
+
+inline bool s16(int64_t s) { return s > 0 && ((s * 2) % 16) == 0 && (s * 2) < (1ll << 40); }
+
+int pick_bn(int64_t n) { return n >= 256 ? 256 : (n > 64 ? 128 : 64); }
+
+// Name of one tile-table entry (static storage, built once).
+const char* bmm_table_name(bool bf16, int bn, int am, int bm) {
+  static const std::array<std::string, 24> names = [] {
+    std::array<std::string, 24> out;
+    const int bns[3] = {64, 128, 256};
+    for (int t = 0; t < 2; ++t)
+      for (int i = 0; i < 3; ++i)
+        for (int a = 0; a < 2; ++a)
+          for (int b = 0; b < 2; ++b)
+            out[((t * 3 + i) * 2 + a) * 2 + b] =
+                std::string("bmm_sm100<") + (t ? "bf16" : "f16") + ",128x" + std::to_string(bns[i]) +
+                "x64,A:" + (a ? "mn" : "k") + "-major,B:" + (b ? "mn" : "k") + "-major," +
+                std::to_string(bns[i] == 256 ? 2 : (bns[i] == 128 ? 3 : 4)) + "st>";
+    return out;
+  }();
+  const int i = bn == 256 ? 2 : (bn == 128 ? 1 : 0);
+  return names[(((bf16 ? 1 : 0) * 3 + i) * 2 + am) * 2 + bm].c_str();
+}
+
+// Layout of one operand: 0 = K-major (contiguous along K), 1 = MN-major, -1 = unusable.
+int a_major(const cmpx_bmm_desc* d) {
+  if (d->a_stride[2] == 1 && (d->m == 1 || s16(d->a_stride[1])) ) return 0;
+  if (d->a_stride[1] == 1 && (d->k == 1 || s16(d->a_stride[2]))) return 1;
+  return -1;
+}
+int b_major(const cmpx_bmm_desc* d) {
+  if (d->b_stride[1] == 1 && (d->n == 1 || s16(d->b_stride[2]))) return 0;  // contiguous along K
+  if (d->b_stride[2] == 1 && (d->k == 1 || s16(d->b_stride[1]))) return 1;  // contiguous along N
+  return -1;
+}
+
+}  // namespace
+
+const char* bmm_sm100_plan(const cmpx_bmm_desc* d, int* status) {
+  *status = CMPX_OK;
+  if (d->dtype != CMPX_F16 && d->dtype != CMPX_BF16) {
+    *status = CMPX_ERR_UNSUPPORTED_DTYPE;
+    return "none";
+  }
+  if (d->k < 1 || d->m > (int64_t)128 * 65535 || d->n > (1ll << 31) - 256 || d->batch > 65535 ||
+      d->k > (1ll << 31) - 64) {
+    *status = CMPX_ERR_UNSUPPORTED_SHAPE;
+    return "none";
+  }
+  const void* ptrs[3] = {d->a, d->b, d->c};
+  for (const void* ptr : ptrs)
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15u) != 0) {
+      *status = CMPX_ERR_MISALIGNED;
+      return "none";
+    }
+  const int am = a_major(d), bmj = b_major(d);
+  const bool c_ok = d->c_stride[2] == 1 && (d->m == 1 || s16(d->c_stride[1]));
+  const bool batch_ok = d->batch == 1 || (s16(d->a_stride[0]) && s16(d->b_stride[0]) && s16(d->c_stride[0]));
+  if (am < 0 || bmj < 0 || !c_ok || !batch_ok) {
+    *status = CMPX_ERR_MISALIGNED;
+    return "none";
+  }
+  return bmm_table_name(d->dtype == CMPX_BF16, pick_bn(d->n), am, bmj);
+}
+
+namespace {
+
+template <int BN, bool A_MN, bool B_MN, bool BF16>
+int launch_bmm_typed(const cmpx_bmm_desc* d, const LaunchCtx& ctx) {
+  using C = BmmCfg<BN>;
+  const CUtensorMapDataType dt =
+      BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const uint64_t M = d->m, N = d->n, K = d->k, Z = d->batch;
+  CUtensorMap ta, tb, tc;
+  {
+    const uint64_t dims[3] = {A_MN ? M : K, A_MN ? K : M, Z};
+    const uint64_t st[2] = {static_cast<uint64_t>(A_MN ? d->a_stride[2] : d->a_stride[1]) * 2,
+                            static_cast<uint64_t>(d->a_stride[0]) * 2};
+    const uint32_t box[3] = {64, A_MN ? 64u : 128u, 1};
+    if (!encode_tmap(&ta, dt, 3, d->a, dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B)) return CMPX_ERR_LAUNCH;
+  }
+  {
+    const uint64_t dims[3] = {B_MN ? N : K, B_MN ? K : N, Z};
+    const uint64_t st[2] = {static_cast<uint64_t>(B_MN ? d->b_stride[1] : d->b_stride[2]) * 2,
+                            static_cast<uint64_t>(d->b_stride[0]) * 2};
+    const uint32_t box[3] = {64, B_MN ? 64u : static_cast<uint32_t>(BN), 1};
+    if (!encode_tmap(&tb, dt, 3, d->b, dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B)) return CMPX_ERR_LAUNCH;
+  }
+  {
+    const uint64_t dims[3] = {N, M, Z};
+    const uint64_t st[2] = {static_cast<uint64_t>(d->c_stride[1]) * 2,
+                            static_cast<uint64_t>(d->c_stride[0]) * 2};
+    const uint32_t box[3] = {64, 32, 1};
+    if (!encode_tmap(&tc, dt, 3, d->c, dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B)) return CMPX_ERR_LAUNCH;
+  }
+  static std::once_flag once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t attr_err = cudaSuccess;
+  std::call_once(once[dev & 63], [&] {
+    attr_err = cudaFuncSetAttribute(
+        reinterpret_cast<const void*>(&bmm_sm100_kernel<BN, A_MN, B_MN, BF16>),
+        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess) return CMPX_ERR_LAUNCH;
+  BmmParams p;
+  p.m = static_cast<int>(M);
+  p.n = static_cast<int>(N);
+  p.k = static_cast<int>(K);
+  p.n_kblocks = static_cast<int>((K + C::BK - 1) / C::BK);
+  p.timeout_ns = ctx.timeout_ns;
+  p.dev_flags = ctx.dev_flags;
+  dim3 grid(static_cast<unsigned>((N + BN - 1) / BN), static_cast<unsigned>((M + C::BM - 1) / C::BM),
+            static_cast<unsigned>(Z));
+  bmm_sm100_kernel<BN, A_MN, B_MN, BF16><<<grid, 192, C::SMEM_BYTES, ctx.stream>>>(ta, tb, tc, p);
+  return cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
+}
+
+template <int BN, bool BF16>
+int launch_bmm_bn(const cmpx_bmm_desc* d, const LaunchCtx& ctx, int am, int bm) {
+  if (am == 0 && bm == 0) return launch_bmm_typed<BN, false, false, BF16>(d, ctx);
+  if (am == 0 && bm == 1) return launch_bmm_typed<BN, false, true, BF16>(d, ctx);
+  if (am == 1 && bm == 0) return launch_bmm_typed<BN, true, false, BF16>(d, ctx);
+  return launch_bmm_typed<BN, true, true, BF16>(d, ctx);
+}
+
+template <bool BF16>
+int launch_bmm_dt(const cmpx_bmm_desc* d, const LaunchCtx& ctx, int am, int bm) {
+  const int bn = pick_bn(d->n);
+  if (bn == 256) return launch_bmm_bn<256, BF16>(d, ctx, am, bm);
+  if (bn == 128) return launch_bmm_bn<128, BF16>(d, ctx, am, bm);
+  return launch_bmm_bn<64, BF16>(d, ctx, am, bm);
+}
+
+}  // namespace
+
+int launch_bmm_sm100(const cmpx_bmm_desc* d, const LaunchCtx& ctx) {
+  int st = CMPX_OK;
+  bmm_sm100_plan(d, &st);
+  if (st != CMPX_OK) return st;
+  if (d->m == 0 || d->n == 0 || d->batch == 0) return CMPX_OK;
+  const int am = a_major(d), bm = b_major(d);
+  return d->dtype == CMPX_BF16 ? launch_bmm_dt<true>(d, ctx, am, bm) : launch_bmm_dt<false>(d, ctx, am, bm);
+}
+
+// --------------------------------------------------------------------------------------------
+// fp32 batched matmul on the CUDA cores (fp32 FMA, any strides).  128 x 128 output tile per CTA,
+// 256 threads each owning an 8 x 8 block, K staged through shared memory 16 at a time.
+// --------------------------------------------------------------------------------------------
+struct F32BmmParams {
+  const float* a;
+  const float* b;
+  float* c;
+  long long as[3], bs[3], cs[3];
+  int m, n, k;
+};
+
+__global__ void __launch_bounds__(256) bmm_f32_kernel(const F32BmmParams p) {
+  constexpr int BM = 128, BN = 128, BK = 16;
+  __shared__ float sA[BK][BM + 4];
+  __shared__ float sB[BK][BN + 4];
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, z = blockIdx.z;
+  const float* A = p.a + z * p.as[0];
+  const float* B = p.b + z * p.bs[0];
+  float* Cp = p.c + z * p.cs[0];
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  for (int k0 = 0; k0 < p.k; k0 += BK) {
+    for (int idx = tid; idx < BM * BK; idx += 256) {
+      // A: choose the thread->element map so consecutive threads walk the contiguous dim
+      int r, kk;
+      if (p.as[2] == 1) { r = idx / BK; kk = idx % BK; } else { kk = idx / BM; r = idx % BM; }
+      const int gm = m0 + r, gk = k0 + kk;
+      sA[kk][r] = (gm < p.m && gk < p.k) ? A[gm * p.as[1] + gk * p.as[2]] : 0.f;
+      int cc;
+      if (p.bs[2] == 1) { kk = idx / BN; cc = idx % BN; } else { cc = idx / BK; kk = idx % BK; }
+      const int gn = n0 + cc;
+      const int gk2 = k0 + kk;
+      sB[kk][cc] = (gn < p.n && gk2 < p.k) ? B[gk2 * p.bs[1] + gn * p.bs[2]] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      float a[8], bb[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a[i] = sA[kk][ty * 4 + i];
+        a[4 + i] = sA[kk][64 + ty * 4 + i];
+        bb[i] = sB[kk][tx * 4 + i];
+        bb[4 + i] = sB[kk][64 + tx * 4 + i];
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], bb[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int gm = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
+    if (gm >= p.m) continue;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int gn = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4);
+      if (gn < p.n) Cp[gm * p.cs[1] + gn * p.cs[2]] = acc[i][j];
+    }
+  }
+}
+
+const char* bmm_f32_plan(const cmpx_bmm_desc* d, int* status) {
+  *status = CMPX_OK;
+  if (d->dtype != CMPX_F32) {
+    *status = CMPX_ERR_UNSUPPORTED_DTYPE;
+    return "none";
+  }
+  if (d->m > (int64_t)128 * 65535 || d->batch > 65535 || d->n > (1ll << 31) - 256) {
+    *status = CMPX_ERR_UNSUPPORTED_SHAPE;
+    return "none";
+  }
+  return "bmm_f32_simt<128x128x16>";
+}
+
+int launch_bmm_f32(const cmpx_bmm_desc* d, const LaunchCtx& ctx) {
+  int st = CMPX_OK;
+  bmm_f32_plan(d, &st);
+  if (st != CMPX_OK) return st;
+  if (d->m == 0 || d->n == 0 || d->batch == 0) return CMPX_OK;
+  F32BmmParams p;
+  p.a = static_cast<const float*>(d->a);
+  p.b = static_cast<const float*>(d->b);
+  p.c = static_cast<float*>(d->c);
+  for (int i = 0; i < 3; ++i) {
+    p.as[i] = d->a_stride[i];
+    p.bs[i] = d->b_stride[i];
+    p.cs[i] = d->c_stride[i];
+  }
+  p.m = static_cast<int>(d->m);
+  p.n = static_cast<int>(d->n);
+  p.k = static_cast<int>(d->k);
+  dim3 grid(static_cast<unsigned>((d->n + 127) / 128), static_cast<unsigned>((d->m + 127) / 128),
+            static_cast<unsigned>(d->batch));
+  bmm_f32_kernel<<<grid, 256, 0, ctx.stream>>>(p);
+  return cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
+}
+
+}  // namespace cmpx
