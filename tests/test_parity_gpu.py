@@ -29,13 +29,20 @@ pytestmark = pytest.mark.gpu
 G = load()
 
 
-def check(got: torch.Tensor, ref: torch.Tensor, dtype: torch.dtype, what: str = "") -> None:
+def check(got: torch.Tensor, ref: torch.Tensor, dtype: torch.dtype, what: str = "",
+          attention: bool = True) -> None:
+    """The contract: fp16 attention max-abs 2e-3 AND rel 1e-2; fp16 bmm and bf16 rel 1e-2; fp32 rel
+    1e-4.  (max-abs is an attention criterion: attention outputs are averages of N(0,1) values, while
+    bmm outputs grow with sqrt(K) and are judged relative to their peak.)"""
     g = got.detach().float().cpu().numpy()
     r = ref.detach().float().cpu().numpy() if isinstance(ref, torch.Tensor) else np.asarray(ref)
     assert g.shape == r.shape, (what, g.shape, r.shape)
     assert np.isfinite(g).all(), f"{what}: non-finite output"
+    assert np.isfinite(r).all(), f"{what}: the oracle itself is not finite"
     rel = sdpa_np.rel_err(g, r)
-    if dtype == torch.float16:
+    if dtype == torch.float16 and not attention:
+        assert rel <= 1e-2, f"{what}: fp16 rel {rel:.2e}"
+    elif dtype == torch.float16:
         mab = sdpa_np.max_abs(g, r)
         assert mab <= 2e-3 and rel <= 1e-2, f"{what}: fp16 max-abs {mab:.2e} rel {rel:.2e}"
     elif dtype == torch.bfloat16:
@@ -69,7 +76,7 @@ def test_bmm_matches_reference_golden(cuda_device, i):
     got = cmpext3.ops.bmm(a.to(cuda_device), b.to(cuda_device))
     torch.cuda.synchronize()
     assert got.dtype == a.dtype
-    check(got, _golden_tensor(f"bmm/{name}/c"), a.dtype, name)
+    check(got, _golden_tensor(f"bmm/{name}/c"), a.dtype, name, attention=False)
 
 
 def test_einsum_attention_matches_reference_golden(cuda_device, patched):
@@ -79,7 +86,7 @@ def test_einsum_attention_matches_reference_golden(cuda_device, patched):
         p = torch.softmax(s, dim=-1)
         o = torch.einsum("bhij,bhjd->bhid", p, v)
     torch.cuda.synchronize()
-    check(s, _golden_tensor("einsum_attn/s"), torch.bfloat16, "scores")
+    check(s, _golden_tensor("einsum_attn/s"), torch.bfloat16, "scores", attention=False)
     check(o, _golden_tensor("einsum_attn/o"), torch.bfloat16, "values")
     entries = [d.entry for d in cmpext3.autoselect.report() if d.use_native]
     assert any("bmm_sm100" in (e or "") for e in entries), cmpext3.autoselect_report()
@@ -151,7 +158,20 @@ def test_attention_strided_blhd_views(cuda_device, dtype):
 def test_attention_scales(cuda_device, scale):
     q, k, v = _rand_qkv(1, 2, 160, 200, 128, torch.bfloat16, seed=11)
     _run_and_check(cuda_device, q, k, v, scale, False, f"scale {scale}")
-    _run_and_check(cuda_device, q, k, v, scale, True, f"scale {scale} causal")
+    if scale > 0:
+        _run_and_check(cuda_device, q, k, v, scale, True, f"scale {scale} causal")
+
+
+def test_negative_scale_causal_against_float64(cuda_device):
+    """Stock torch CPU SDPA returns NaN for every row when scale < 0 and is_causal (its masked
+    scores become +inf), so the reference's CPU path has no usable answer there.  The kernel's
+    answer is checked against the float64 restatement instead."""
+    q, k, v = _rand_qkv(1, 2, 160, 200, 128, torch.bfloat16, seed=11)
+    stock = RP.sdpa(q, k, v, scale=-0.2, is_causal=True)
+    assert torch.isnan(stock).all(), "stock CPU SDPA changed behaviour: compare against it directly"
+    got = cmpext3.ops.attention(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), -0.2, True)
+    ref = sdpa_np.sdpa(q.float().numpy(), k.float().numpy(), v.float().numpy(), scale=-0.2, causal=True)
+    check(got, ref, torch.bfloat16, "scale -0.2 causal vs float64")
 
 
 def test_attention_large_logits_stay_finite(cuda_device):
@@ -228,7 +248,7 @@ def test_bmm_sweep(cuda_device, dtype, shape, bt):
         return
     got = cmpext3.ops.bmm(a.to(cuda_device), b.to(cuda_device))
     torch.cuda.synchronize()
-    check(got, RP.bmm(a, b), dtype, f"bmm {shape} bt={bt}")
+    check(got, RP.bmm(a, b), dtype, f"bmm {shape} bt={bt}", attention=False)
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
@@ -238,7 +258,7 @@ def test_bmm_transposed_a(cuda_device, dtype):
     b = torch.randn(3, 200, 72, generator=g).to(dtype)
     got = cmpext3.ops.bmm(a.to(cuda_device), b.to(cuda_device))
     torch.cuda.synchronize()
-    check(got, RP.bmm(a, b), dtype, "bmm A^T")
+    check(got, RP.bmm(a, b), dtype, "bmm A^T", attention=False)
 
 
 def test_patched_sdpa_end_to_end(cuda_device, patched):
@@ -258,7 +278,7 @@ def test_patched_matmul_2d(cuda_device, patched):
     b = torch.randn(192, 320, generator=g).to(torch.bfloat16)
     with torch.no_grad():
         got = torch.matmul(a.to(cuda_device), b.to(cuda_device))
-    check(got, a.float() @ b.float(), torch.bfloat16, "matmul 2d")
+    check(got, a.float() @ b.float(), torch.bfloat16, "matmul 2d", attention=False)
 
 
 def test_unsupported_shape_falls_back_to_stock(cuda_device, patched):

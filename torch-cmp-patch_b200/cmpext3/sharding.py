@@ -61,9 +61,10 @@ def gather_samples(local: torch.Tensor) -> torch.Tensor | None:
     other than 0 get None.
     """
     world = dist.get_world_size()
-    out = torch.empty((world, *local.shape), dtype=local.dtype, device=local.device)
-    dist.all_gather_into_tensor(out, local.contiguous())
-    return out if dist.get_rank() == 0 else None
+    local = local.contiguous()
+    out = torch.empty((world * local.shape[0], *local.shape[1:]), dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(out, local)
+    return out.view(world, *local.shape) if dist.get_rank() == 0 else None
 
 
 def max_over_ranks(value: float, device: torch.device | None = None) -> float:

@@ -34,6 +34,10 @@
 #include "cmpx_internal.h"
 #include "cmpx_ptx.cuh"
 
+#ifndef CMPX_FMHA_EMU
+#define CMPX_FMHA_EMU 0  // column pairs (of every 8) whose exp2 runs on the FMA pipe (polynomial)
+#endif
+
 namespace cmpx {
 
 template <int DP>
@@ -61,7 +65,10 @@ struct FmhaCfg {
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // +1024: runtime alignment slack
   static constexpr int TM_S0 = 0, TM_S1 = 128, TM_O0 = 256, TM_O1 = 256 + DP;
   static constexpr int TMEM_COLS = 512;
+  // Warp roles: 0-3 softmax/epilogue of tile 0, 4-7 of tile 1 (thread = row), 8 TMA producer,
+  // 9 MMA issuer.
   static constexpr int THREADS = 320;
+  static constexpr int W_TMA = 8, W_MMA = 9;
 };
 
 struct FmhaParams {
@@ -91,10 +98,11 @@ __global__ void __launch_bounds__(320, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  const int bh = blockIdx.x;
-  const int b = bh / p.heads;
-  const int h = bh - b * p.heads;
-  const int pair = p.n_pairs - 1 - static_cast<int>(blockIdx.y);  // heavy (late) rows first
+  // Grid (pair, head, batch): the CTAs of one (b, h) are dispatched together, so the K/V tiles
+  // they all stream stay in L2; within a head the heavy (late, causal) row pairs go first.
+  const int pair = p.n_pairs - 1 - static_cast<int>(blockIdx.x);
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
   const int q0 = pair * 256;
   const int kv_len = p.causal ? min(p.len_k, q0 + 256) : p.len_k;
   const int n_kv = (kv_len + C::BN - 1) / C::BN;
@@ -120,11 +128,11 @@ __global__ void __launch_bounds__(320, 1)
     *abort_flag = 0;
     fence_mbarrier_init();
   }
-  if (warp == 9) {
+  if (warp == C::W_MMA) {
     tmem_alloc(smem_u32(tmem_holder), C::TMEM_COLS);
     tmem_relinquish();
   }
-  if (warp == 8 && lane == 0) {
+  if (warp == C::W_TMA && lane == 0) {
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
@@ -136,105 +144,109 @@ __global__ void __launch_bounds__(320, 1)
   const uint32_t tmem = *tmem_holder;
   const WaitCtl ctl{abort_flag, p.dev_flags, p.timeout_ns};
 
-  if (warp == 8) {
-    // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      mbar_arrive_expect_tx(bar(C::B_Q), 2 * C::QTILE_BYTES);
-      for (int t = 0; t < 2; ++t)
-        for (int c = 0; c < C::NCH; ++c)
-          tma_load_4d(sQ + t * C::QTILE_BYTES + c * C::CH_BYTES, &tm_q, bar(C::B_Q), c * 64,
-                      q0 + t * C::BM, h, b);
-      int issued = 0;
-      bool ok = true;
-      for (int j = 0; ok && j < n_kv; ++j) {
-        for (int which = 0; which < 2; ++which) {
-          const int i = 2 * j + which;
-          const int st = i % C::NSTAGE;
-          const uint32_t rnd = static_cast<uint32_t>(i / C::NSTAGE);
-          if (!mbar_wait(bar(C::B_EMPTY + st), (rnd & 1u) ^ 1u, ctl)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(bar(C::B_FULL + st), C::KV_BYTES);
-          const CUtensorMap* m = which ? &tm_v : &tm_k;
+  if (warp >= 8) {
+    if (warp == C::W_TMA) {
+      // ---------------------------------------------------------------- TMA producer
+      if (lane == 0) {
+        mbar_arrive_expect_tx(bar(C::B_Q), 2 * C::QTILE_BYTES);
+        for (int t = 0; t < 2; ++t)
           for (int c = 0; c < C::NCH; ++c)
-            tma_load_4d(sKV + st * C::KV_BYTES + c * C::CH_BYTES, m, bar(C::B_FULL + st), c * 64,
-                        j * C::BN, h, b);
-          issued = i + 1;
+            tma_load_4d(sQ + t * C::QTILE_BYTES + c * C::CH_BYTES, &tm_q, bar(C::B_Q), c * 64,
+                        q0 + t * C::BM, h, b);
+        int issued = 0;
+        bool ok = true;
+        for (int j = 0; ok && j < n_kv; ++j) {
+          for (int which = 0; which < 2; ++which) {
+            const int i = 2 * j + which;
+            const int st = i % C::NSTAGE;
+            const uint32_t rnd = static_cast<uint32_t>(i / C::NSTAGE);
+            if (!mbar_wait(bar(C::B_EMPTY + st), (rnd & 1u) ^ 1u, ctl)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(bar(C::B_FULL + st), C::KV_BYTES);
+            const CUtensorMap* m = which ? &tm_v : &tm_k;
+            for (int c = 0; c < C::NCH; ++c)
+              tma_load_4d(sKV + st * C::KV_BYTES + c * C::CH_BYTES, m, bar(C::B_FULL + st), c * 64,
+                          j * C::BN, h, b);
+            issued = i + 1;
+          }
+        }
+        if (*abort_flag) {
+          // Let every copy still in flight land before shared memory goes away.
+          mbar_wait_drain(bar(C::B_Q), 0, p.timeout_ns);
+          for (int i = max(0, issued - C::NSTAGE); i < issued; ++i)
+            mbar_wait_drain(bar(C::B_FULL + i % C::NSTAGE), static_cast<uint32_t>(i / C::NSTAGE) & 1u,
+                            p.timeout_ns);
         }
       }
-      if (*abort_flag) {
-        // Let every copy still in flight land before shared memory goes away.
-        mbar_wait_drain(bar(C::B_Q), 0, p.timeout_ns);
-        for (int i = max(0, issued - C::NSTAGE); i < issued; ++i)
-          mbar_wait_drain(bar(C::B_FULL + i % C::NSTAGE), static_cast<uint32_t>(i / C::NSTAGE) & 1u,
-                          p.timeout_ns);
-      }
-    }
-  } else if (warp == 9) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t kIdescQK = idesc_f16(128, 128, BF16 ? 1 : 0, 0, 0);
-      constexpr uint32_t kIdescPV = idesc_f16(128, DP, BF16 ? 1 : 0, 0, 1);
-      auto issue_qk = [&](int t, uint32_t k_addr) {
-        const uint32_t q_addr = sQ + t * C::QTILE_BYTES;
-        const uint32_t d_tmem = tmem + (t ? C::TM_S1 : C::TM_S0);
+    } else if (warp == C::W_MMA) {
+      // ---------------------------------------------------------------- MMA issuer
+      if (lane == 0) {
+        constexpr uint32_t kIdescQK = idesc_f16(128, 128, BF16 ? 1 : 0, 0, 0);
+        constexpr uint32_t kIdescPV = idesc_f16(128, DP, BF16 ? 1 : 0, 0, 1);
+        auto issue_qk = [&](int t, uint32_t k_addr) {
+          const uint32_t q_addr = sQ + t * C::QTILE_BYTES;
+          const uint32_t d_tmem = tmem + (t ? C::TM_S1 : C::TM_S0);
 #pragma unroll
-        for (int k = 0; k < DP / 16; ++k) {
-          const uint32_t off = (k >> 2) * C::CH_BYTES + (k & 3) * 32;
-          umma_ss(d_tmem, smem_desc_sw128(q_addr + off, 16, 1024),
-                  smem_desc_sw128(k_addr + off, 16, 1024), kIdescQK, k > 0 ? 1u : 0u);
-        }
-      };
-      auto issue_pv = [&](int t, uint32_t v_addr, bool acc) {
-        const uint32_t p_tmem = tmem + (t ? C::TM_S1 : C::TM_S0);
-        const uint32_t d_tmem = tmem + (t ? C::TM_O1 : C::TM_O0);
+          for (int k = 0; k < DP / 16; ++k) {
+            const uint32_t off = (k >> 2) * C::CH_BYTES + (k & 3) * 32;
+            umma_ss(d_tmem, smem_desc_sw128(q_addr + off, 16, 1024),
+                    smem_desc_sw128(k_addr + off, 16, 1024), kIdescQK, k > 0 ? 1u : 0u);
+          }
+        };
+        // P_t (16-bit, two keys per column) lives in the first 64 columns of S_t.
+        auto issue_pv = [&](int t, uint32_t v_addr, bool acc) {
+          const uint32_t p_tmem = tmem + (t ? C::TM_S1 : C::TM_S0);
+          const uint32_t d_tmem = tmem + (t ? C::TM_O1 : C::TM_O0);
 #pragma unroll
-        for (int k = 0; k < C::BN / 16; ++k) {
-          umma_ts(d_tmem, p_tmem + k * 8, smem_desc_sw128(v_addr + k * 2048, C::CH_BYTES, 1024),
-                  kIdescPV, (acc || k > 0) ? 1u : 0u);
-        }
-      };
-      bool ok = mbar_wait(bar(C::B_Q), 0, ctl);
-      if (ok) ok = mbar_wait(bar(C::B_FULL + 0), 0, ctl);  // K_0 is load 0
-      if (ok) {
-        tc_fence_after_sync();
-        issue_qk(0, sKV);
-        umma_commit(bar(C::B_SFULL + 0));
-        issue_qk(1, sKV);
-        umma_commit(bar(C::B_SFULL + 1));
-        umma_commit(bar(C::B_EMPTY + 0));
-      }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int iv = 2 * j + 1, ik = 2 * j + 2;
-        const int stv = iv % C::NSTAGE, stk = ik % C::NSTAGE;
-        const uint32_t pv = static_cast<uint32_t>(iv / C::NSTAGE) & 1u;
-        const uint32_t pk = static_cast<uint32_t>(ik / C::NSTAGE) & 1u;
-        const bool has_next = j + 1 < n_kv;
-        const uint32_t v_addr = sKV + stv * C::KV_BYTES;
-        const uint32_t k_addr = sKV + stk * C::KV_BYTES;
-        if (!mbar_wait(bar(C::B_FULL + stv), pv, ctl)) break;
-        if (!mbar_wait(bar(C::B_PREADY + 0), j & 1, ctl)) break;
-        tc_fence_after_sync();
-        issue_pv(0, v_addr, j > 0);
-        if (has_next) {
-          if (!mbar_wait(bar(C::B_FULL + stk), pk, ctl)) break;
+          for (int k = 0; k < C::BN / 16; ++k) {
+            umma_ts(d_tmem, p_tmem + k * 8,
+                    smem_desc_sw128(v_addr + k * 2048, C::CH_BYTES, 1024), kIdescPV,
+                    (acc || k > 0) ? 1u : 0u);
+          }
+        };
+        bool ok = mbar_wait(bar(C::B_Q), 0, ctl);
+        if (ok) ok = mbar_wait(bar(C::B_FULL + 0), 0, ctl);  // K_0 is load 0
+        if (ok) {
           tc_fence_after_sync();
-          issue_qk(0, k_addr);
+          issue_qk(0, sKV);
           umma_commit(bar(C::B_SFULL + 0));
-        } else {
-          umma_commit(bar(C::B_OFINAL + 0));
-        }
-        if (!mbar_wait(bar(C::B_PREADY + 1), j & 1, ctl)) break;
-        tc_fence_after_sync();
-        issue_pv(1, v_addr, j > 0);
-        umma_commit(bar(C::B_EMPTY + stv));
-        if (has_next) {
-          issue_qk(1, k_addr);
+          issue_qk(1, sKV);
           umma_commit(bar(C::B_SFULL + 1));
-          umma_commit(bar(C::B_EMPTY + stk));
-        } else {
-          umma_commit(bar(C::B_OFINAL + 1));
+          umma_commit(bar(C::B_EMPTY + 0));
+        }
+        for (int j = 0; ok && j < n_kv; ++j) {
+          const int iv = 2 * j + 1, ik = 2 * j + 2;
+          const int stv = iv % C::NSTAGE, stk = ik % C::NSTAGE;
+          const uint32_t pv = static_cast<uint32_t>(iv / C::NSTAGE) & 1u;
+          const uint32_t pk = static_cast<uint32_t>(ik / C::NSTAGE) & 1u;
+          const bool has_next = j + 1 < n_kv;
+          const uint32_t v_addr = sKV + stv * C::KV_BYTES;
+          const uint32_t k_addr = sKV + stk * C::KV_BYTES;
+          if (!mbar_wait(bar(C::B_FULL + stv), pv, ctl)) break;
+          if (!mbar_wait(bar(C::B_PREADY + 0), j & 1, ctl)) break;
+          tc_fence_after_sync();
+          issue_pv(0, v_addr, j > 0);
+          if (has_next) {
+            if (!mbar_wait(bar(C::B_FULL + stk), pk, ctl)) break;
+            tc_fence_after_sync();
+            issue_qk(0, k_addr);
+            umma_commit(bar(C::B_SFULL + 0));
+          } else {
+            umma_commit(bar(C::B_OFINAL + 0));
+          }
+          if (!mbar_wait(bar(C::B_PREADY + 1), j & 1, ctl)) break;
+          tc_fence_after_sync();
+          issue_pv(1, v_addr, j > 0);
+          umma_commit(bar(C::B_EMPTY + stv));
+          if (has_next) {
+            issue_qk(1, k_addr);
+            umma_commit(bar(C::B_SFULL + 1));
+            umma_commit(bar(C::B_EMPTY + stk));
+          } else {
+            umma_commit(bar(C::B_OFINAL + 1));
+          }
         }
       }
     }
@@ -254,69 +266,79 @@ __global__ void __launch_bounds__(320, 1)
     bool ok = true;
 
     for (int j = 0; j < n_kv; ++j) {
-      if (!mbar_wait_warp(bar(C::B_SFULL + t), j & 1, ctl)) {
+      if (!mbar_wait_all(bar(C::B_SFULL + t), j & 1, ctl)) {
         ok = false;
         break;
       }
       tc_fence_after_sync();
       uint32_t sr[128];
-      tmem_ld64(s_tm, *reinterpret_cast<uint32_t(*)[64]>(&sr[0]));
-      tmem_ld64(s_tm + 64, *reinterpret_cast<uint32_t(*)[64]>(&sr[64]));
+      tmem_ld128(s_tm, sr);
       float* s = reinterpret_cast<float*>(sr);
 
       const int kv0 = j * C::BN;
-      const bool tile_masked =
-          (kv0 + C::BN > p.len_k) || (p.causal && kv0 + C::BN - 1 > q0 + t * C::BM);
-      if (tile_masked) {
-        int lim = p.len_k - kv0;
+      const bool masked_tile = (kv0 + C::BN > p.len_k) || (p.causal && kv0 + C::BN - 1 > q0 + t * C::BM);
+      int lim = 128;
+      if (masked_tile) {
+        lim = p.len_k - kv0;
         if (p.causal) lim = min(lim, qrow - kv0 + 1);
 #pragma unroll
         for (int c = 0; c < 128; ++c)
           if (c >= lim) s[c] = masked;
       }
+      // Row extreme (max; min for a negative scale): 3-input max/min, 8 chains.
       float mx;
-      if (!p.neg_scale) {
-        float a0 = s[0], a1 = s[1], a2 = s[2], a3 = s[3];
+      {
+        float a[8];
 #pragma unroll
-        for (int c = 4; c < 128; c += 4) {
-          a0 = fmaxf(a0, s[c]);
-          a1 = fmaxf(a1, s[c + 1]);
-          a2 = fmaxf(a2, s[c + 2]);
-          a3 = fmaxf(a3, s[c + 3]);
-        }
-        mx = fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
-      } else {
-        float a0 = s[0], a1 = s[1], a2 = s[2], a3 = s[3];
+        for (int i = 0; i < 8; ++i) a[i] = s[i];
+        if (!p.neg_scale) {
 #pragma unroll
-        for (int c = 4; c < 128; c += 4) {
-          a0 = fminf(a0, s[c]);
-          a1 = fminf(a1, s[c + 1]);
-          a2 = fminf(a2, s[c + 2]);
-          a3 = fminf(a3, s[c + 3]);
+          for (int c = 8; c < 128; c += 16)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) a[i] = fmax3(a[i], s[c + 2 * i], s[c + 2 * i + 1]);
+          mx = fmax3(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
+        } else {
+#pragma unroll
+          for (int c = 8; c < 128; c += 16)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) a[i] = fmin3(a[i], s[c + 2 * i], s[c + 2 * i + 1]);
+          mx = fmin3(fmin3(a[0], a[1], a[2]), fmin3(a[3], a[4], a[5]), fminf(a[6], a[7]));
         }
-        mx = fminf(fminf(a0, a1), fminf(a2, a3));
       }
-      const float m_tile = mx * sl2;
-      const float m_new = fmaxf(m_run, m_tile);
+      const float m_new = fmaxf(m_run, mx * sl2);
       float alpha = 1.f;
       if (m_new - m_run > 8.f) {  // also true on the first tile (m_run = -inf)
         alpha = ex2_approx(m_run - m_new);
         m_run = m_new;
       }
-      const float mb = (m_run == -INFINITY) ? 0.f : m_run;
-      float lsum0 = 0.f, lsum1 = 0.f;
+      const float nmb = (m_run == -INFINITY) ? 0.f : -m_run;
+      // p = 2^(s * scale*log2(e) - m).  CMPX_FMHA_EMU of every 8 column pairs take the packed
+      // polynomial exp2 on the FMA pipe, the rest MUFU ex2 with scalar FFMA / FADD.
+      float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
       uint32_t pk[64];
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
-        const float p0 = ex2_approx(fmaf(s[2 * c], sl2, -mb));
-        const float p1 = ex2_approx(fmaf(s[2 * c + 1], sl2, -mb));
-        lsum0 += p0;
-        lsum1 += p1;
+        float p0, p1;
+        if ((c & 7) >= 8 - CMPX_FMHA_EMU) {
+          const uint64_t pv = exp2_poly3_x2(f2_fma(f2_pack(s[2 * c], s[2 * c + 1]),
+                                                   f2_pack(sl2, sl2), f2_pack(nmb, nmb)));
+          f2_unpack(pv, p0, p1);
+        } else {
+          p0 = ex2_approx(fmaf(s[2 * c], sl2, nmb));
+          p1 = ex2_approx(fmaf(s[2 * c + 1], sl2, nmb));
+        }
+        if (c & 1) {
+          l2 += p0;
+          l3 += p1;
+        } else {
+          l0 += p0;
+          l1 += p1;
+        }
         pk[c] = BF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
       }
-      l_run = l_run * alpha + (lsum0 + lsum1);
       tmem_st32(s_tm, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
       tmem_st32(s_tm + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
+      l_run = l_run * alpha + ((l0 + l1) + (l2 + l3));
       // O holds PV_{j-1} complete: S_j's commit came after it in issue order.
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
@@ -333,7 +355,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_arrive(bar(C::B_PREADY + t));
     }
 
-    if (ok) ok = mbar_wait_warp(bar(C::B_OFINAL + t), 0, ctl);
+    if (ok) ok = mbar_wait_all(bar(C::B_OFINAL + t), 0, ctl);
     if (ok) {
       tc_fence_after_sync();
       const float inv_l = 1.f / l_run;
@@ -375,7 +397,7 @@ __global__ void __launch_bounds__(320, 1)
 
   tc_fence_before_sync();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == C::W_MMA) {
     if (*abort_flag) {
       if (lane == 0) {
         umma_commit(bar(C::B_DRAIN));
@@ -412,7 +434,7 @@ const char* fmha_sm100_plan(const cmpx_attn_desc* d, int* status) {
     *status = CMPX_ERR_UNSUPPORTED_SHAPE;
     return "none";
   }
-  if (d->len_q > (int64_t)256 * 65535 || d->len_k > (1ll << 31) - 256 || d->batch * d->heads > (1ll << 31) - 1) {
+  if (d->len_q > (1ll << 31) - 256 || d->len_k > (1ll << 31) - 256 || d->heads > 65535 || d->batch > 65535) {
     *status = CMPX_ERR_UNSUPPORTED_SHAPE;
     return "none";
   }
@@ -478,7 +500,8 @@ int launch_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   p.scale_log2 = static_cast<float>(d->scale * 1.4426950408889634);
   p.timeout_ns = ctx.timeout_ns;
   p.dev_flags = ctx.dev_flags;
-  dim3 grid(static_cast<unsigned>(d->batch * d->heads), static_cast<unsigned>(p.n_pairs));
+  dim3 grid(static_cast<unsigned>(p.n_pairs), static_cast<unsigned>(d->heads),
+            static_cast<unsigned>(d->batch));
   fmha_fwd_sm100_kernel<DP, BF16><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, to, p);
   return cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
 }

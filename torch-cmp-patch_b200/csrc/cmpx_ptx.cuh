@@ -67,21 +67,35 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps (up to hint_ns) until the phase completes
+// instead of spinning, so waiting warps do not take issue slots from working ones.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+constexpr uint32_t kWaitSliceNs = 500000;  // one suspended try_wait: at most 0.5 ms
+
 // Wait until the phase with the given parity has completed.  Returns false if the CTA abort
 // word was raised by another role, or if this wait ran past ctl.timeout_ns (in which case it
 // raises the abort word and the device flag itself).  Call from ONE lane.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtl& ctl) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
-  for (uint32_t n = 1;; ++n) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((n & 31u) == 0) {
-      if (*ctl.abort) return false;
-      if (global_timer_ns() - t0 > ctl.timeout_ns) {
-        *ctl.abort = 1;
-        atomicOr(ctl.dev_flags, 1u /* CMPX_DEVFLAG_WAIT_TIMEOUT */);
-        return false;
-      }
+  while (true) {
+    if (mbar_try_wait_sleep(bar, parity, kWaitSliceNs)) return true;
+    if (*ctl.abort) return false;
+    if (global_timer_ns() - t0 > ctl.timeout_ns) {
+      *ctl.abort = 1;
+      atomicOr(ctl.dev_flags, 1u /* CMPX_DEVFLAG_WAIT_TIMEOUT */);
+      return false;
     }
   }
 }
@@ -92,9 +106,9 @@ __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity,
                                                 unsigned long long timeout_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
-  for (uint32_t n = 1;; ++n) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((n & 31u) == 0 && global_timer_ns() - t0 > timeout_ns) return false;
+  while (true) {
+    if (mbar_try_wait_sleep(bar, parity, kWaitSliceNs)) return true;
+    if (global_timer_ns() - t0 > timeout_ns) return false;
   }
 }
 
@@ -104,6 +118,13 @@ __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, co
   if (lane_id() == 0) ok = mbar_wait(bar, parity, ctl) ? 1 : 0;
   ok = __shfl_sync(0xffffffffu, ok, 0);
   return ok != 0;
+}
+
+// Warp-uniform wait with a fast path: every lane tests the phase once (no branch divergence
+// when it is already complete); otherwise lane 0 waits, sleeping between tests, and broadcasts.
+__device__ __forceinline__ bool mbar_wait_all(uint32_t bar, uint32_t parity, const WaitCtl& ctl) {
+  if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+  return mbar_wait_warp(bar, parity, ctl);
 }
 
 // ----------------------------------------------------------------------------------------
@@ -281,6 +302,16 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
 }
 #undef CMPX_R8
 
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, uint32_t (&r)[128]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x128.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95,%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%128];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]), "=r"(r[64]), "=r"(r[65]), "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]), "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]), "=r"(r[78]), "=r"(r[79]), "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]), "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]), "=r"(r[88]), "=r"(r[89]), "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]), "=r"(r[96]), "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]), "=r"(r[102]), "=r"(r[103]), "=r"(r[104]), "=r"(r[105]), "=r"(r[106]), "=r"(r[107]), "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]), "=r"(r[112]), "=r"(r[113]), "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]), "=r"(r[119]), "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]), "=r"(r[126]), "=r"(r[127])
+      : "r"(taddr)
+      : "memory");
+}
+
 #define CMPX_W8(b) "r"(r[b + 0]), "r"(r[b + 1]), "r"(r[b + 2]), "r"(r[b + 3]), "r"(r[b + 4]), \
                    "r"(r[b + 5]), "r"(r[b + 6]), "r"(r[b + 7])
 
@@ -313,6 +344,83 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): two floats in one 64-bit register pair.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// Three-input max / min (sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x evaluated on the FMA / integer pipes instead of the MUFU unit, so that part of a softmax
+// tile's exponentials can run beside the MUFU ones.  Cody-Waite split x = n + f with n = rint(x)
+// (the 1.5 * 2^23 round-to-nearest addition) and |f| <= 0.5, then a degree-3 minimax polynomial for
+// 2^f on [-0.5, 0.5] (coefficients fitted here by a Remez exchange on the relative error; max
+// relative error 7.5e-5, below half an ulp of bf16 and fp16), and n added to the exponent field.
+// x is clamped to >= -125 (2^-125 stands in for 0 for masked scores); x <= 8 in the callers.
+__device__ __forceinline__ float exp2_poly3(float x) {
+  x = fmaxf(x, -125.f);
+  const float kRound = 12582912.f;  // 1.5 * 2^23
+  const float t = x + kRound;
+  const float f = x - (t - kRound);
+  float p = fmaf(0.0551716685295105f, f, 0.2426111251115799f);
+  p = fmaf(p, f, 0.6932609677314758f);
+  p = fmaf(p, f, 0.9999280571937561f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+// Packed form of exp2_poly3 for two values at once (the polynomial in f32x2 arithmetic).
+__device__ __forceinline__ uint64_t exp2_poly3_x2(uint64_t xv) {
+  float x0, x1;
+  f2_unpack(xv, x0, x1);
+  xv = f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+  const uint64_t kRound = f2_pack(12582912.f, 12582912.f);
+  const uint64_t t = f2_add(xv, kRound);
+  const uint64_t f = f2_sub(xv, f2_sub(t, kRound));
+  uint64_t p = f2_fma(f2_pack(0.0551716685295105f, 0.0551716685295105f), f,
+                      f2_pack(0.2426111251115799f, 0.2426111251115799f));
+  p = f2_fma(p, f, f2_pack(0.6932609677314758f, 0.6932609677314758f));
+  p = f2_fma(p, f, f2_pack(0.9999280571937561f, 0.9999280571937561f));
+  float p0, p1, t0, t1;
+  f2_unpack(p, p0, p1);
+  f2_unpack(t, t0, t1);
+  return f2_pack(__int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23)),
+                 __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23)));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
