@@ -11,17 +11,19 @@
 //   * one CTA owns two 128-row Q tiles (rows q0 .. q0+255) of one (batch, head);
 //   * warp 8 streams K_j and V_j (128 keys x D) through a ring of shared-memory stages with TMA
 //     (128-byte swizzle, OOB rows/cols zero-filled), Q once;
-//   * warp 9 issues tcgen05.mma: S_t = Q_t K_j^T into TMEM (fp32), then O_t += P_t V_j with P_t
-//     read straight from TMEM (A-from-TMEM form) -- P never touches shared memory;
+//   * warp 9 issues tcgen05.mma: S = Q_t K_j^T into TMEM (fp32; one S buffer the two tiles take
+//     in turns), then O_t += P_t V_j with P_t read straight from TMEM (A-from-TMEM form) -- P never
+//     touches shared memory;
 //   * warps 0-3 / 4-7 are the softmax warpgroups of tile 0 / tile 1: thread i owns row i, reads
-//     its 128 scores with tcgen05.ld, applies the mask, updates m and l, writes P (16-bit) back
-//     over its scores with tcgen05.st, and rescales its O row in TMEM when the running max grew
-//     by more than 2^8 (otherwise the stale max is kept: exact, since O and l share it);
-//   * the two tiles ping-pong: the tensor core runs tile 1's MMAs while tile 0's softmax runs.
+//     its 128 scores with tcgen05.ld and releases S at once, applies the mask, updates m and l,
+//     writes P (16-bit) into its tile's P buffer with tcgen05.st, and rescales its O row in TMEM
+//     when the running max grew by more than 2^8 (otherwise the stale max is kept: exact, since O
+//     and l share it);
+//   * the QK of one tile runs while the other tile's softmax -- and its own exponentials -- run.
 //   * epilogue: O / l, converted, staged in the (now idle) Q buffer in the swizzled layout and
 //     written with TMA stores that clip rows >= Lq and cols >= D.
 //
-// TMEM columns: S0 [0,128) S1 [128,256) O0 [256,256+DP) O1 [256+DP, 256+2*DP).
+// TMEM columns: S [0,128) (shared by the two tiles), P0 [128,192), P1 [192,256), O0, O1.
 // Every wait is bounded (see cmpx_ptx.cuh); a CTA that gives up drains its in-flight copies
 // and MMAs, frees TMEM, sets the device status word and returns.
 #include <cuda.h>
@@ -56,14 +58,17 @@ struct FmhaCfg {
   static constexpr int B_Q = 0;
   static constexpr int B_FULL = 1;
   static constexpr int B_EMPTY = B_FULL + NSTAGE;
-  static constexpr int B_SFULL = B_EMPTY + NSTAGE;  // [2]
-  static constexpr int B_PREADY = B_SFULL + 2;      // [2]
-  static constexpr int B_OFINAL = B_PREADY + 2;     // [2]
-  static constexpr int B_DRAIN = B_OFINAL + 2;
+  static constexpr int B_SFULL = B_EMPTY + NSTAGE;  // [2] S holds tile t's scores
+  static constexpr int B_SFREE = B_SFULL + 2;       // [2] tile t's softmax has read S
+  static constexpr int B_PREADY = B_SFREE + 2;      // [2] P_t written
+  static constexpr int B_PVDONE = B_PREADY + 2;     // [2] O_t += P_t V complete
+  static constexpr int B_DRAIN = B_PVDONE + 2;
   static constexpr int NBAR = B_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // +1024: runtime alignment slack
-  static constexpr int TM_S0 = 0, TM_S1 = 128, TM_O0 = 256, TM_O1 = 256 + DP;
+  // One S buffer shared by the two Q tiles (their QKs alternate), a P buffer per tile, an O
+  // accumulator per tile: S [0,128) P0 [128,192) P1 [192,256) O0 [256,256+DP) O1 [256+DP, 256+2DP).
+  static constexpr int TM_S = 0, TM_P0 = 128, TM_P1 = 192, TM_O0 = 256, TM_O1 = 256 + DP;
   static constexpr int TMEM_COLS = 512;
   // Warp roles: 0-3 softmax/epilogue of tile 0, 4-7 of tile 1 (thread = row), 8 TMA producer,
   // 9 MMA issuer.
@@ -82,6 +87,49 @@ struct FmhaParams {
   unsigned long long timeout_ns;
   unsigned int* dev_flags;
 };
+
+// One pass over a row's 128 scores: p = 2^(s*sl2 + nmb) packed to 16-bit and stored to TMEM
+// (4 chunks of 16 columns at p_tm), the row sum of p, and the maximum of s*sl2 + nmb.
+// CMPX_FMHA_EMU of every 8 column pairs use the packed polynomial exp2 on the FMA pipe.
+template <bool BF16>
+__device__ __forceinline__ void exp_pass(const float* s, float sl2, float nmb, uint32_t p_tm,
+                                         float& l_out, float& xmax_out) {
+  float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
+  float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      const int cc = q * 16 + c;
+      float p0, p1;
+      if ((cc & 7) >= 8 - CMPX_FMHA_EMU) {
+        const uint64_t xv = f2_fma(f2_pack(s[2 * cc], s[2 * cc + 1]), f2_pack(sl2, sl2), f2_pack(nmb, nmb));
+        float x0, x1;
+        f2_unpack(xv, x0, x1);
+        if (c & 1) a1 = fmax3(a1, x0, x1); else a0 = fmax3(a0, x0, x1);
+        f2_unpack(exp2_poly3_x2(xv), p0, p1);
+      } else {
+        const float x0 = fmaf(s[2 * cc], sl2, nmb);
+        const float x1 = fmaf(s[2 * cc + 1], sl2, nmb);
+        if (c & 1) a3 = fmax3(a3, x0, x1); else a2 = fmax3(a2, x0, x1);
+        p0 = ex2_approx(x0);
+        p1 = ex2_approx(x1);
+      }
+      if (c & 1) {
+        l2 += p0;
+        l3 += p1;
+      } else {
+        l0 += p0;
+        l1 += p1;
+      }
+      pk[c] = BF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
+    }
+    tmem_st16(p_tm + q * 16, pk);
+  }
+  l_out = (l0 + l1) + (l2 + l3);
+  xmax_out = fmax3(fmaxf(a0, a1), a2, a3);
+}
 
 template <int DP, bool BF16>
 __global__ void __launch_bounds__(320, 1)
@@ -121,8 +169,9 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(C::B_SFULL + t), 1);
+      mbar_init(bar(C::B_SFREE + t), 128);
       mbar_init(bar(C::B_PREADY + t), 128);
-      mbar_init(bar(C::B_OFINAL + t), 1);
+      mbar_init(bar(C::B_PVDONE + t), 1);
     }
     mbar_init(bar(C::B_DRAIN), 1);
     *abort_flag = 0;
@@ -187,17 +236,16 @@ __global__ void __launch_bounds__(320, 1)
         constexpr uint32_t kIdescPV = idesc_f16(128, DP, BF16 ? 1 : 0, 0, 1);
         auto issue_qk = [&](int t, uint32_t k_addr) {
           const uint32_t q_addr = sQ + t * C::QTILE_BYTES;
-          const uint32_t d_tmem = tmem + (t ? C::TM_S1 : C::TM_S0);
 #pragma unroll
           for (int k = 0; k < DP / 16; ++k) {
             const uint32_t off = (k >> 2) * C::CH_BYTES + (k & 3) * 32;
-            umma_ss(d_tmem, smem_desc_sw128(q_addr + off, 16, 1024),
+            umma_ss(tmem + C::TM_S, smem_desc_sw128(q_addr + off, 16, 1024),
                     smem_desc_sw128(k_addr + off, 16, 1024), kIdescQK, k > 0 ? 1u : 0u);
           }
         };
-        // P_t (16-bit, two keys per column) lives in the first 64 columns of S_t.
+        // P_t: 16-bit, two keys per 32-bit column, 64 columns.
         auto issue_pv = [&](int t, uint32_t v_addr, bool acc) {
-          const uint32_t p_tmem = tmem + (t ? C::TM_S1 : C::TM_S0);
+          const uint32_t p_tmem = tmem + (t ? C::TM_P1 : C::TM_P0);
           const uint32_t d_tmem = tmem + (t ? C::TM_O1 : C::TM_O0);
 #pragma unroll
           for (int k = 0; k < C::BN / 16; ++k) {
@@ -206,46 +254,59 @@ __global__ void __launch_bounds__(320, 1)
                     (acc || k > 0) ? 1u : 0u);
           }
         };
+        // K_j is ring load 2j, V_j is load 2j+1.
+        auto stage_of = [&](int load) -> uint32_t { return sKV + (load % C::NSTAGE) * C::KV_BYTES; };
+        auto full_bar = [&](int load) -> uint32_t { return bar(C::B_FULL + load % C::NSTAGE); };
+        auto empty_bar = [&](int load) -> uint32_t { return bar(C::B_EMPTY + load % C::NSTAGE); };
+        auto round_par = [&](int load) -> uint32_t { return static_cast<uint32_t>(load / C::NSTAGE) & 1u; };
+        // Issue order per key tile j (each step waits only for what it reads or overwrites):
+        //   QK_1(j) once tile 0 has read S(j);  PV_1(j-1) once P_1(j-1) is written;
+        //   QK_0(j+1) once tile 1 has read S(j);  PV_0(j) once P_0(j) is written.
+        // The QKs of one tile overlap the other tile's softmax AND its own exponentials (S is
+        // released as soon as it is in registers), so the tensor pipe waits only on the slower of
+        // the two softmaxes, not on softmax + MMA latency in series.
         bool ok = mbar_wait(bar(C::B_Q), 0, ctl);
-        if (ok) ok = mbar_wait(bar(C::B_FULL + 0), 0, ctl);  // K_0 is load 0
+        if (ok) ok = mbar_wait(full_bar(0), 0, ctl);
         if (ok) {
           tc_fence_after_sync();
-          issue_qk(0, sKV);
+          issue_qk(0, stage_of(0));
           umma_commit(bar(C::B_SFULL + 0));
-          issue_qk(1, sKV);
-          umma_commit(bar(C::B_SFULL + 1));
-          umma_commit(bar(C::B_EMPTY + 0));
         }
         for (int j = 0; ok && j < n_kv; ++j) {
-          const int iv = 2 * j + 1, ik = 2 * j + 2;
-          const int stv = iv % C::NSTAGE, stk = ik % C::NSTAGE;
-          const uint32_t pv = static_cast<uint32_t>(iv / C::NSTAGE) & 1u;
-          const uint32_t pk = static_cast<uint32_t>(ik / C::NSTAGE) & 1u;
-          const bool has_next = j + 1 < n_kv;
-          const uint32_t v_addr = sKV + stv * C::KV_BYTES;
-          const uint32_t k_addr = sKV + stk * C::KV_BYTES;
-          if (!mbar_wait(bar(C::B_FULL + stv), pv, ctl)) break;
-          if (!mbar_wait(bar(C::B_PREADY + 0), j & 1, ctl)) break;
+          const int lk = 2 * j, lv = 2 * j + 1, lk1 = 2 * j + 2, lv0 = 2 * j - 1;
+          if (!(ok = mbar_wait(bar(C::B_SFREE + 0), j & 1, ctl))) break;
           tc_fence_after_sync();
-          issue_pv(0, v_addr, j > 0);
-          if (has_next) {
-            if (!mbar_wait(bar(C::B_FULL + stk), pk, ctl)) break;
+          issue_qk(1, stage_of(lk));
+          umma_commit(bar(C::B_SFULL + 1));
+          umma_commit(empty_bar(lk));  // K_j done
+          if (j > 0) {
+            if (!(ok = mbar_wait(bar(C::B_PREADY + 1), (j - 1) & 1, ctl))) break;
             tc_fence_after_sync();
-            issue_qk(0, k_addr);
-            umma_commit(bar(C::B_SFULL + 0));
-          } else {
-            umma_commit(bar(C::B_OFINAL + 0));
+            issue_pv(1, stage_of(lv0), j > 1);
+            umma_commit(bar(C::B_PVDONE + 1));
+            umma_commit(empty_bar(lv0));  // V_{j-1} done
           }
-          if (!mbar_wait(bar(C::B_PREADY + 1), j & 1, ctl)) break;
+          if (j + 1 < n_kv) {
+            if (!(ok = mbar_wait(bar(C::B_SFREE + 1), j & 1, ctl))) break;
+            if (!(ok = mbar_wait(full_bar(lk1), round_par(lk1), ctl))) break;
+            tc_fence_after_sync();
+            issue_qk(0, stage_of(lk1));
+            umma_commit(bar(C::B_SFULL + 0));
+          }
+          if (!(ok = mbar_wait(full_bar(lv), round_par(lv), ctl))) break;
+          if (!(ok = mbar_wait(bar(C::B_PREADY + 0), j & 1, ctl))) break;
           tc_fence_after_sync();
-          issue_pv(1, v_addr, j > 0);
-          umma_commit(bar(C::B_EMPTY + stv));
-          if (has_next) {
-            issue_qk(1, k_addr);
-            umma_commit(bar(C::B_SFULL + 1));
-            umma_commit(bar(C::B_EMPTY + stk));
-          } else {
-            umma_commit(bar(C::B_OFINAL + 1));
+          issue_pv(0, stage_of(lv), j > 0);
+          umma_commit(bar(C::B_PVDONE + 0));
+        }
+        if (ok) {
+          const int j = n_kv - 1, lv = 2 * j + 1;
+          ok = mbar_wait(bar(C::B_PREADY + 1), j & 1, ctl);
+          if (ok) {
+            tc_fence_after_sync();
+            issue_pv(1, stage_of(lv), j > 0);
+            umma_commit(bar(C::B_PVDONE + 1));
+            umma_commit(empty_bar(lv));
           }
         }
       }
@@ -257,7 +318,8 @@ __global__ void __launch_bounds__(320, 1)
     const int row = wq * 32 + lane;     // row inside the tile
     const int qrow = q0 + t * C::BM + row;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16);
-    const uint32_t s_tm = lane_base + (t ? C::TM_S1 : C::TM_S0);
+    const uint32_t s_tm = lane_base + C::TM_S;
+    const uint32_t p_tm = lane_base + (t ? C::TM_P1 : C::TM_P0);
     const uint32_t o_tm = lane_base + (t ? C::TM_O1 : C::TM_O0);
     const float sl2 = p.scale_log2;
     const float masked = p.neg_scale ? INFINITY : -INFINITY;  // masked * sl2 == -inf
@@ -274,6 +336,8 @@ __global__ void __launch_bounds__(320, 1)
       uint32_t sr[128];
       tmem_ld128(s_tm, sr);
       float* s = reinterpret_cast<float*>(sr);
+      tc_fence_before_sync();
+      mbar_arrive(bar(C::B_SFREE + t));  // S is in registers: the other tile's QK may overwrite it
 
       const int kv0 = j * C::BN;
       const bool masked_tile = (kv0 + C::BN > p.len_k) || (p.causal && kv0 + C::BN - 1 > q0 + t * C::BM);
@@ -285,77 +349,51 @@ __global__ void __launch_bounds__(320, 1)
         for (int c = 0; c < 128; ++c)
           if (c >= lim) s[c] = masked;
       }
-      // Row extreme (max; min for a negative scale): 3-input max/min, 8 chains.
-      float mx;
-      {
-        float a[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) a[i] = s[i];
-        if (!p.neg_scale) {
-#pragma unroll
-          for (int c = 8; c < 128; c += 16)
-#pragma unroll
-            for (int i = 0; i < 8; ++i) a[i] = fmax3(a[i], s[c + 2 * i], s[c + 2 * i + 1]);
-          mx = fmax3(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
-        } else {
-#pragma unroll
-          for (int c = 8; c < 128; c += 16)
-#pragma unroll
-            for (int i = 0; i < 8; ++i) a[i] = fmin3(a[i], s[c + 2 * i], s[c + 2 * i + 1]);
-          mx = fmin3(fmin3(a[0], a[1], a[2]), fmin3(a[3], a[4], a[5]), fminf(a[6], a[7]));
+      // P_t and O_t are free once PV_t(j-1) has completed (usually long done by now).
+      if (j > 0) {
+        if (!mbar_wait_all(bar(C::B_PVDONE + t), (j - 1) & 1, ctl)) {
+          ok = false;
+          break;
         }
+        tc_fence_after_sync();
       }
-      const float m_new = fmaxf(m_run, mx * sl2);
+      // Fast pass: exponentiate against the running max m_run straight away, x = s*scale*log2e - m,
+      // taking this tile's row maximum of x in the same pass (independent of the exp2 chain).
+      // P goes to TMEM in 16-column chunks as it is produced.  Only when some row's maximum grew
+      // by more than 2^8 (always on a row's first tile) does the warp redo the tile against the
+      // new maximum, rescaling l and O with it; otherwise the stale maximum stays (exact: O, l
+      // and P share it).
+      const float m_used = (m_run == -INFINITY) ? 0.f : m_run;
+      float l_tile, xmax;
+      exp_pass<BF16>(s, sl2, -m_used, p_tm, l_tile, xmax);
+      const float m_tile = xmax + m_used;  // row max of s*scale*log2e in this tile
       float alpha = 1.f;
-      if (m_new - m_run > 8.f) {  // also true on the first tile (m_run = -inf)
-        alpha = ex2_approx(m_run - m_new);
-        m_run = m_new;
-      }
-      const float nmb = (m_run == -INFINITY) ? 0.f : -m_run;
-      // p = 2^(s * scale*log2(e) - m).  CMPX_FMHA_EMU of every 8 column pairs take the packed
-      // polynomial exp2 on the FMA pipe, the rest MUFU ex2 with scalar FFMA / FADD.
-      float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
-      uint32_t pk[64];
-#pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        float p0, p1;
-        if ((c & 7) >= 8 - CMPX_FMHA_EMU) {
-          const uint64_t pv = exp2_poly3_x2(f2_fma(f2_pack(s[2 * c], s[2 * c + 1]),
-                                                   f2_pack(sl2, sl2), f2_pack(nmb, nmb)));
-          f2_unpack(pv, p0, p1);
-        } else {
-          p0 = ex2_approx(fmaf(s[2 * c], sl2, nmb));
-          p1 = ex2_approx(fmaf(s[2 * c + 1], sl2, nmb));
+      if (__any_sync(0xffffffffu, m_tile - m_run > 8.f)) {
+        if (m_tile - m_run > 8.f) {  // (m_run = -inf, m_tile finite: first tile of the row)
+          alpha = ex2_approx(m_run - m_tile);
+          m_run = m_tile;
         }
-        if (c & 1) {
-          l2 += p0;
-          l3 += p1;
-        } else {
-          l0 += p0;
-          l1 += p1;
-        }
-        pk[c] = BF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
-      }
-      tmem_st32(s_tm, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
-      tmem_st32(s_tm + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
-      l_run = l_run * alpha + ((l0 + l1) + (l2 + l3));
-      // O holds PV_{j-1} complete: S_j's commit came after it in issue order.
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        tmem_st_wait();  // the redo overwrites the fast pass's P columns
+        float xm;
+        exp_pass<BF16>(s, sl2, (m_run == -INFINITY) ? 0.f : -m_run, p_tm, l_tile, xm);
+        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-        for (int c = 0; c < DP / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(o_tm + c * 32, o);
+          for (int c = 0; c < DP / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(o_tm + c * 32, o);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st32(o_tm + c * 32, o);
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(o_tm + c * 32, o);
+          }
         }
       }
+      l_run = l_run * alpha + l_tile;
       tmem_st_wait();
       tc_fence_before_sync();
       mbar_arrive(bar(C::B_PREADY + t));
     }
 
-    if (ok) ok = mbar_wait_all(bar(C::B_OFINAL + t), 0, ctl);
+    if (ok) ok = mbar_wait_all(bar(C::B_PVDONE + t), (n_kv - 1) & 1, ctl);
     if (ok) {
       tc_fence_after_sync();
       const float inv_l = 1.f / l_run;
