@@ -108,8 +108,10 @@ typedef struct cmpx_bmm_desc {
 /* Attention forward.  Replaces cmpext3.ops.attention (src/main.cpp:2353-2358). */
 CMPX_API int cmpx_attn_fwd(const cmpx_attn_desc* desc, void* stream);
 
-/* Bytes of device workspace cmpx_attn_fwd needs for this problem (0 = none).
- * The workspace must be zero-filled before the call; the kernel leaves it zeroed on return.
+/* Bytes of device workspace cmpx_attn_fwd needs for this problem (0 = none; 256 for the 16-bit
+ * kernels, which keep the work counters of their persistent schedule there).  The workspace must be
+ * 16-byte aligned and zero-filled before the first call; every call leaves it zeroed on return, so a
+ * workspace can be reused by calls that do not overlap on the GPU (one per stream).
  * No reference counterpart (the reference allocates nothing but the output). */
 CMPX_API size_t cmpx_attn_workspace_size(const cmpx_attn_desc* desc);
 

@@ -135,5 +135,14 @@ def test_bmm_rejects_misaligned_rows():
     assert _bplan(d)[0] == N.ERR_MISALIGNED
 
 
-def test_workspace_size_is_zero_for_now():
-    assert N.lib.cmpx_attn_workspace_size(ctypes.byref(_attn())) == 0
+def test_workspace_contract():
+    assert N.lib.cmpx_attn_workspace_size(ctypes.byref(_attn(dtype=2))) == 256
+    assert N.lib.cmpx_attn_workspace_size(ctypes.byref(_attn(dtype=1))) == 256
+    assert N.lib.cmpx_attn_workspace_size(ctypes.byref(_attn(dtype=0))) == 0
+    assert N.lib.cmpx_attn_workspace_size(None) == 0
+    d = _attn(dtype=2)  # valid shape, no workspace: rejected before any device work
+    assert N.lib.cmpx_attn_fwd(ctypes.byref(d), None) == N.ERR_WORKSPACE
+    d.workspace, d.workspace_bytes = 0x10000, 8  # too small
+    assert N.lib.cmpx_attn_fwd(ctypes.byref(d), None) == N.ERR_WORKSPACE
+    d.workspace, d.workspace_bytes = 0x10004, 256  # misaligned
+    assert N.lib.cmpx_attn_fwd(ctypes.byref(d), None) == N.ERR_WORKSPACE

@@ -198,7 +198,11 @@ def test_attention_output_layout_and_every_element_written(cuda_device):
     out = torch.full((2, 300, 3, 128), float("nan"), dtype=torch.bfloat16, device=cuda_device).transpose(1, 2)
     desc = N._attn_desc(qd, kd, vd, out, 1 / math.sqrt(128), True)
     import ctypes
+    ws = torch.zeros(N.lib.cmpx_attn_workspace_size(ctypes.byref(desc)), dtype=torch.uint8, device=cuda_device)
+    desc.workspace, desc.workspace_bytes = ws.data_ptr(), ws.numel()
     assert N.lib.cmpx_attn_fwd(ctypes.byref(desc), N._stream_handle(cuda_device)) == 0
+    torch.cuda.synchronize()
+    assert int(ws.count_nonzero()) == 0, "the kernel must leave its workspace zeroed"
     torch.cuda.synchronize()
     assert torch.isfinite(out.float()).all()
     ref = RP.sdpa(q, k, v, is_causal=True)

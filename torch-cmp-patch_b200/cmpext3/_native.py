@@ -193,12 +193,32 @@ def _prepare_attention(query, key, value, scale, causal):
     return query, key, value, out, float(scale)
 
 
+# Zero-filled workspaces, one per (device, stream): the kernels leave them zeroed, and calls on one
+# stream never overlap, so each stream reuses its own.
+_WORKSPACES: dict = {}
+
+
+def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    key = (device.index, stream)
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+        _WORKSPACES[key] = ws
+    return ws
+
+
 def attention(query, key, value, scale=None, causal=False):
     """SDPA forward on the sm_100a kernels.  Same contract as the reference's ops.attention."""
     q, k, v, out, scale = _prepare_attention(query, key, value, scale, causal)
     desc = _attn_desc(q, k, v, out, scale, bool(causal))
     with torch.cuda.device(q.device):
-        st = lib.cmpx_attn_fwd(ctypes.byref(desc), _stream_handle(q.device))
+        stream = _stream_handle(q.device)
+        need = lib.cmpx_attn_workspace_size(ctypes.byref(desc))
+        if need:
+            ws = _workspace(q.device, stream, need)
+            desc.workspace = ws.data_ptr()
+            desc.workspace_bytes = ws.numel()
+        st = lib.cmpx_attn_fwd(ctypes.byref(desc), stream)
     if st != OK:
         raise CmpxError("attention", st)
     _post_check()

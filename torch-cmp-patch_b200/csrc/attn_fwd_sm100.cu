@@ -29,6 +29,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <mutex>
@@ -53,27 +54,34 @@ struct FmhaCfg {
   static constexpr int NSTAGE = DP == 128 ? 4 : 6;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_KV = 2 * QTILE_BYTES;
-  static constexpr int OFF_BAR = OFF_KV + NSTAGE * KV_BYTES;
+  static constexpr int OFF_OST = OFF_KV + NSTAGE * KV_BYTES;   // O staging (one tile) for TMA stores
+  static constexpr int OFF_BAR = OFF_OST + QTILE_BYTES;
   // barrier slots
-  static constexpr int B_Q = 0;
-  static constexpr int B_FULL = 1;
+  static constexpr int B_QFULL = 0;                 // Q of the current item landed
+  static constexpr int B_QEMPTY = 1;                // last QK of an item done: Q may be reloaded
+  static constexpr int B_FULL = 2;
   static constexpr int B_EMPTY = B_FULL + NSTAGE;
   static constexpr int B_SFULL = B_EMPTY + NSTAGE;  // [2] S holds tile t's scores
   static constexpr int B_SFREE = B_SFULL + 2;       // [2] tile t's softmax has read S
   static constexpr int B_PREADY = B_SFREE + 2;      // [2] P_t written
   static constexpr int B_PVDONE = B_PREADY + 2;     // [2] O_t += P_t V complete
-  static constexpr int B_DRAIN = B_PVDONE + 2;
+  static constexpr int B_OFREE = B_PVDONE + 2;      // [2] epilogue has read O_t
+  static constexpr int B_ITFULL = B_OFREE + 2;      // [2] work-item slot written
+  static constexpr int B_ITEMPTY = B_ITFULL + 2;    // [2] work-item slot read by every consumer
+  static constexpr int B_OST = B_ITEMPTY + 2;       // [2 tile][4 quarter] staging rows free for tile t
+  static constexpr int B_DRAIN = B_OST + 8;
   static constexpr int NBAR = B_DRAIN + 1;
-  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-  static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // +1024: runtime alignment slack
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // tmem base, abort word, item slots [2]
+  static constexpr int SMEM_BYTES = OFF_MISC + 32 + 1024;  // +1024: runtime alignment slack
   // One S buffer shared by the two Q tiles (their QKs alternate), a P buffer per tile, an O
   // accumulator per tile: S [0,128) P0 [128,192) P1 [192,256) O0 [256,256+DP) O1 [256+DP, 256+2DP).
   static constexpr int TM_S = 0, TM_P0 = 128, TM_P1 = 192, TM_O0 = 256, TM_O1 = 256 + DP;
   static constexpr int TMEM_COLS = 512;
-  // Warp roles: 0-3 softmax/epilogue of tile 0, 4-7 of tile 1 (thread = row), 8 TMA producer,
-  // 9 MMA issuer.
+  // Warp roles: 0-3 softmax/epilogue of tile 0, 4-7 of tile 1 (thread = row), 8 TMA producer
+  // (and work fetch), 9 MMA issuer.
   static constexpr int THREADS = 320;
   static constexpr int W_TMA = 8, W_MMA = 9;
+  static constexpr int ITEM_CONSUMERS = 1 + 8;  // MMA lane 0 + lane 0 of each softmax warp
 };
 
 struct FmhaParams {
@@ -81,9 +89,14 @@ struct FmhaParams {
   int len_q;
   int len_k;
   int n_pairs;        // ceil(len_q / 256)
+  int n_items;        // n_pairs * heads * batch
   int causal;
-  int neg_scale;      // scale < 0: track the row minimum of raw scores instead of the maximum
+  int neg_scale;      // scale < 0: masked scores are +inf so that masked * scale = -inf
   float scale_log2;   // scale * log2(e)
+  void* o;            // output [B, H, Lq, D] view
+  long long os_b, os_h, os_s;  // its strides (elements)
+  int head_dim;
+  unsigned int* work;          // [0] next work item, [1] CTAs finished (both 0 at launch and exit)
   unsigned long long timeout_ns;
   unsigned int* dev_flags;
 };
@@ -131,6 +144,9 @@ __device__ __forceinline__ void exp_pass(const float* s, float sl2, float nmb, u
   xmax_out = fmax3(fmaxf(a0, a1), a2, a3);
 }
 
+// Work item w (persistent schedule): bh = w / n_pairs, pair = n_pairs - 1 - w % n_pairs.  The items
+// of one (b, h) are consecutive, so the CTAs busy at any moment share a few heads' K/V in L2, and
+// within a head the heavy (late, causal) row pairs go first.
 template <int DP, bool BF16>
 __global__ void __launch_bounds__(320, 1)
     fmha_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -146,23 +162,16 @@ __global__ void __launch_bounds__(320, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Grid (pair, head, batch): the CTAs of one (b, h) are dispatched together, so the K/V tiles
-  // they all stream stay in L2; within a head the heavy (late, causal) row pairs go first.
-  const int pair = p.n_pairs - 1 - static_cast<int>(blockIdx.x);
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
-  const int q0 = pair * 256;
-  const int kv_len = p.causal ? min(p.len_k, q0 + 256) : p.len_k;
-  const int n_kv = (kv_len + C::BN - 1) / C::BN;
-
   const uint32_t sQ = base + C::OFF_Q;
   const uint32_t sKV = base + C::OFF_KV;
   auto bar = [&](int i) -> uint32_t { return base + C::OFF_BAR + 8u * i; };
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+  volatile int* item_slot = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);  // [2]
 
   if (threadIdx.x == 0) {
-    mbar_init(bar(C::B_Q), 1);
+    mbar_init(bar(C::B_QFULL), 1);
+    mbar_init(bar(C::B_QEMPTY), 1);
     for (int s = 0; s < C::NSTAGE; ++s) {
       mbar_init(bar(C::B_FULL + s), 1);
       mbar_init(bar(C::B_EMPTY + s), 1);
@@ -172,7 +181,11 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(bar(C::B_SFREE + t), 128);
       mbar_init(bar(C::B_PREADY + t), 128);
       mbar_init(bar(C::B_PVDONE + t), 1);
+      mbar_init(bar(C::B_OFREE + t), 128);
+      mbar_init(bar(C::B_ITFULL + t), 1);
+      mbar_init(bar(C::B_ITEMPTY + t), C::ITEM_CONSUMERS);
     }
+    for (int i = 0; i < 8; ++i) mbar_init(bar(C::B_OST + i), 1);
     mbar_init(bar(C::B_DRAIN), 1);
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -193,43 +206,67 @@ __global__ void __launch_bounds__(320, 1)
   const uint32_t tmem = *tmem_holder;
   const WaitCtl ctl{abort_flag, p.dev_flags, p.timeout_ns};
 
+  // Item k of this CTA: wait for its slot, read it, release the slot (consumers only).
+  auto next_item = [&](int k, int& w) -> bool {
+    const int slot = k & 1;
+    if (!mbar_wait(bar(C::B_ITFULL + slot), static_cast<uint32_t>(k >> 1) & 1u, ctl)) return false;
+    w = item_slot[slot];
+    mbar_arrive(bar(C::B_ITEMPTY + slot));
+    return true;
+  };
+  auto item_geometry = [&](int w, int& b, int& h, int& q0, int& n_kv) {
+    const int bh = w / p.n_pairs;
+    const int pair = p.n_pairs - 1 - (w - bh * p.n_pairs);
+    b = bh / p.heads;
+    h = bh - b * p.heads;
+    q0 = pair * 256;
+    const int kv_len = p.causal ? min(p.len_k, q0 + 256) : p.len_k;
+    n_kv = (kv_len + C::BN - 1) / C::BN;
+  };
+
   if (warp >= 8) {
     if (warp == C::W_TMA) {
-      // ---------------------------------------------------------------- TMA producer
+      // ---------------------------------------------------------------- work fetch + TMA producer
       if (lane == 0) {
-        mbar_arrive_expect_tx(bar(C::B_Q), 2 * C::QTILE_BYTES);
-        for (int t = 0; t < 2; ++t)
-          for (int c = 0; c < C::NCH; ++c)
-            tma_load_4d(sQ + t * C::QTILE_BYTES + c * C::CH_BYTES, &tm_q, bar(C::B_Q), c * 64,
-                        q0 + t * C::BM, h, b);
-        int issued = 0;
+        int load = 0;  // K/V ring loads issued so far (K_j and V_j of every item, in order)
         bool ok = true;
-        for (int j = 0; ok && j < n_kv; ++j) {
-          for (int which = 0; which < 2; ++which) {
-            const int i = 2 * j + which;
-            const int st = i % C::NSTAGE;
-            const uint32_t rnd = static_cast<uint32_t>(i / C::NSTAGE);
-            if (!mbar_wait(bar(C::B_EMPTY + st), (rnd & 1u) ^ 1u, ctl)) {
-              ok = false;
-              break;
-            }
-            mbar_arrive_expect_tx(bar(C::B_FULL + st), C::KV_BYTES);
-            const CUtensorMap* m = which ? &tm_v : &tm_k;
+        for (int k = 0; ok; ++k) {
+          const int slot = k & 1;
+          if (!(ok = mbar_wait(bar(C::B_ITEMPTY + slot), (static_cast<uint32_t>(k >> 1) & 1u) ^ 1u, ctl))) break;
+          const int wi = static_cast<int>(atomicAdd(p.work, 1u));
+          const int w = wi < p.n_items ? wi : -1;
+          item_slot[slot] = w;
+          mbar_arrive(bar(C::B_ITFULL + slot));
+          if (w < 0) break;
+          int b, h, q0, n_kv;
+          item_geometry(w, b, h, q0, n_kv);
+          if (k > 0 && !(ok = mbar_wait(bar(C::B_QEMPTY), static_cast<uint32_t>(k - 1) & 1u, ctl))) break;
+          mbar_arrive_expect_tx(bar(C::B_QFULL), 2 * C::QTILE_BYTES);
+          for (int t = 0; t < 2; ++t)
             for (int c = 0; c < C::NCH; ++c)
-              tma_load_4d(sKV + st * C::KV_BYTES + c * C::CH_BYTES, m, bar(C::B_FULL + st), c * 64,
-                          j * C::BN, h, b);
-            issued = i + 1;
+              tma_load_4d(sQ + t * C::QTILE_BYTES + c * C::CH_BYTES, &tm_q, bar(C::B_QFULL), c * 64,
+                          q0 + t * C::BM, h, b);
+          for (int j = 0; ok && j < n_kv; ++j) {
+            for (int which = 0; which < 2; ++which, ++load) {
+              const int st = load % C::NSTAGE;
+              const uint32_t rnd = static_cast<uint32_t>(load / C::NSTAGE);
+              if (!(ok = mbar_wait(bar(C::B_EMPTY + st), (rnd & 1u) ^ 1u, ctl))) break;
+              mbar_arrive_expect_tx(bar(C::B_FULL + st), C::KV_BYTES);
+              const CUtensorMap* m = which ? &tm_v : &tm_k;
+              for (int c = 0; c < C::NCH; ++c)
+                tma_load_4d(sKV + st * C::KV_BYTES + c * C::CH_BYTES, m, bar(C::B_FULL + st), c * 64,
+                            j * C::BN, h, b);
+            }
           }
         }
         if (*abort_flag) {
           // Let every copy still in flight land before shared memory goes away.
-          mbar_wait_drain(bar(C::B_Q), 0, p.timeout_ns);
-          for (int i = max(0, issued - C::NSTAGE); i < issued; ++i)
+          for (int i = max(0, load - C::NSTAGE); i < load; ++i)
             mbar_wait_drain(bar(C::B_FULL + i % C::NSTAGE), static_cast<uint32_t>(i / C::NSTAGE) & 1u,
                             p.timeout_ns);
         }
       }
-    } else if (warp == C::W_MMA) {
+    } else {
       // ---------------------------------------------------------------- MMA issuer
       if (lane == 0) {
         constexpr uint32_t kIdescQK = idesc_f16(128, 128, BF16 ? 1 : 0, 0, 0);
@@ -254,60 +291,81 @@ __global__ void __launch_bounds__(320, 1)
                     (acc || k > 0) ? 1u : 0u);
           }
         };
-        // K_j is ring load 2j, V_j is load 2j+1.
         auto stage_of = [&](int load) -> uint32_t { return sKV + (load % C::NSTAGE) * C::KV_BYTES; };
         auto full_bar = [&](int load) -> uint32_t { return bar(C::B_FULL + load % C::NSTAGE); };
         auto empty_bar = [&](int load) -> uint32_t { return bar(C::B_EMPTY + load % C::NSTAGE); };
         auto round_par = [&](int load) -> uint32_t { return static_cast<uint32_t>(load / C::NSTAGE) & 1u; };
-        // Issue order per key tile j (each step waits only for what it reads or overwrites):
-        //   QK_1(j) once tile 0 has read S(j);  PV_1(j-1) once P_1(j-1) is written;
-        //   QK_0(j+1) once tile 1 has read S(j);  PV_0(j) once P_0(j) is written.
-        // The QKs of one tile overlap the other tile's softmax AND its own exponentials (S is
-        // released as soon as it is in registers), so the tensor pipe waits only on the slower of
-        // the two softmaxes, not on softmax + MMA latency in series.
-        bool ok = mbar_wait(bar(C::B_Q), 0, ctl);
-        if (ok) ok = mbar_wait(full_bar(0), 0, ctl);
-        if (ok) {
+        // Barrier phase counters carried across items.
+        uint32_t n_sfree0 = 0, n_sfree1 = 0, n_pready0 = 0, n_pready1 = 0;
+        int base_load = 0;
+        bool ok = true;
+        // Issue order per key tile j of an item (each step waits only for what it reads or
+        // overwrites):  QK_1(j) once tile 0 has read S(j);  PV_1(j-1) once P_1(j-1) is written;
+        // QK_0(j+1) once tile 1 has read S(j);  PV_0(j) once P_0(j) is written.  The QKs of one
+        // tile overlap the other tile's softmax and its own exponentials (S is released as soon as
+        // it is in registers).
+        for (int k = 0; ok; ++k) {
+          int w;
+          if (!(ok = next_item(k, w))) break;
+          if (w < 0) break;
+          int b, h, q0, n_kv;
+          item_geometry(w, b, h, q0, n_kv);
+          (void)b; (void)h; (void)q0;
+          if (!(ok = mbar_wait(bar(C::B_QFULL), static_cast<uint32_t>(k) & 1u, ctl))) break;
+          // S is free once tile 1's softmax read the previous item's last S.
+          if (k > 0 && !(ok = mbar_wait(bar(C::B_SFREE + 1), (n_sfree1++) & 1u, ctl))) break;
+          if (!(ok = mbar_wait(full_bar(base_load), round_par(base_load), ctl))) break;
           tc_fence_after_sync();
-          issue_qk(0, stage_of(0));
+          issue_qk(0, stage_of(base_load));
           umma_commit(bar(C::B_SFULL + 0));
-        }
-        for (int j = 0; ok && j < n_kv; ++j) {
-          const int lk = 2 * j, lv = 2 * j + 1, lk1 = 2 * j + 2, lv0 = 2 * j - 1;
-          if (!(ok = mbar_wait(bar(C::B_SFREE + 0), j & 1, ctl))) break;
-          tc_fence_after_sync();
-          issue_qk(1, stage_of(lk));
-          umma_commit(bar(C::B_SFULL + 1));
-          umma_commit(empty_bar(lk));  // K_j done
-          if (j > 0) {
-            if (!(ok = mbar_wait(bar(C::B_PREADY + 1), (j - 1) & 1, ctl))) break;
+          for (int j = 0; ok && j < n_kv; ++j) {
+            const int lk = base_load + 2 * j, lv = lk + 1, lk1 = lk + 2, lv0 = lk - 1;
+            if (!(ok = mbar_wait(bar(C::B_SFREE + 0), (n_sfree0++) & 1u, ctl))) break;
             tc_fence_after_sync();
-            issue_pv(1, stage_of(lv0), j > 1);
-            umma_commit(bar(C::B_PVDONE + 1));
-            umma_commit(empty_bar(lv0));  // V_{j-1} done
+            issue_qk(1, stage_of(lk));
+            umma_commit(bar(C::B_SFULL + 1));
+            umma_commit(empty_bar(lk));  // K_j done
+            if (j + 1 == n_kv) umma_commit(bar(C::B_QEMPTY));  // last QK of the item
+            if (j > 0) {
+              if (!(ok = mbar_wait(bar(C::B_PREADY + 1), (n_pready1++) & 1u, ctl))) break;
+              // The item's first PV_1 overwrites O_1: the previous item's epilogue must have read it.
+              if (j == 1 && k > 0 &&
+                  !(ok = mbar_wait(bar(C::B_OFREE + 1), static_cast<uint32_t>(k - 1) & 1u, ctl)))
+                break;
+              tc_fence_after_sync();
+              issue_pv(1, stage_of(lv0), j > 1);
+              umma_commit(bar(C::B_PVDONE + 1));
+              umma_commit(empty_bar(lv0));  // V_{j-1} done
+            }
+            if (j + 1 < n_kv) {
+              if (!(ok = mbar_wait(bar(C::B_SFREE + 1), (n_sfree1++) & 1u, ctl))) break;
+              if (!(ok = mbar_wait(full_bar(lk1), round_par(lk1), ctl))) break;
+              tc_fence_after_sync();
+              issue_qk(0, stage_of(lk1));
+              umma_commit(bar(C::B_SFULL + 0));
+            }
+            if (!(ok = mbar_wait(full_bar(lv), round_par(lv), ctl))) break;
+            if (!(ok = mbar_wait(bar(C::B_PREADY + 0), (n_pready0++) & 1u, ctl))) break;
+            if (j == 0 && k > 0 &&
+                !(ok = mbar_wait(bar(C::B_OFREE + 0), static_cast<uint32_t>(k - 1) & 1u, ctl)))
+              break;
+            tc_fence_after_sync();
+            issue_pv(0, stage_of(lv), j > 0);
+            umma_commit(bar(C::B_PVDONE + 0));
           }
-          if (j + 1 < n_kv) {
-            if (!(ok = mbar_wait(bar(C::B_SFREE + 1), j & 1, ctl))) break;
-            if (!(ok = mbar_wait(full_bar(lk1), round_par(lk1), ctl))) break;
+          if (!ok) break;
+          {
+            const int lv = base_load + 2 * (n_kv - 1) + 1;
+            if (!(ok = mbar_wait(bar(C::B_PREADY + 1), (n_pready1++) & 1u, ctl))) break;
+            if (n_kv == 1 && k > 0 &&
+                !(ok = mbar_wait(bar(C::B_OFREE + 1), static_cast<uint32_t>(k - 1) & 1u, ctl)))
+              break;
             tc_fence_after_sync();
-            issue_qk(0, stage_of(lk1));
-            umma_commit(bar(C::B_SFULL + 0));
-          }
-          if (!(ok = mbar_wait(full_bar(lv), round_par(lv), ctl))) break;
-          if (!(ok = mbar_wait(bar(C::B_PREADY + 0), j & 1, ctl))) break;
-          tc_fence_after_sync();
-          issue_pv(0, stage_of(lv), j > 0);
-          umma_commit(bar(C::B_PVDONE + 0));
-        }
-        if (ok) {
-          const int j = n_kv - 1, lv = 2 * j + 1;
-          ok = mbar_wait(bar(C::B_PREADY + 1), j & 1, ctl);
-          if (ok) {
-            tc_fence_after_sync();
-            issue_pv(1, stage_of(lv), j > 0);
+            issue_pv(1, stage_of(lv), n_kv > 1);
             umma_commit(bar(C::B_PVDONE + 1));
             umma_commit(empty_bar(lv));
           }
+          base_load += 2 * n_kv;
         }
       }
     }
@@ -316,89 +374,100 @@ __global__ void __launch_bounds__(320, 1)
     const int t = warp >> 2;            // Q tile of this warpgroup
     const int wq = warp & 3;            // TMEM lane quarter of this warp
     const int row = wq * 32 + lane;     // row inside the tile
-    const int qrow = q0 + t * C::BM + row;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16);
     const uint32_t s_tm = lane_base + C::TM_S;
     const uint32_t p_tm = lane_base + (t ? C::TM_P1 : C::TM_P0);
     const uint32_t o_tm = lane_base + (t ? C::TM_O1 : C::TM_O0);
     const float sl2 = p.scale_log2;
     const float masked = p.neg_scale ? INFINITY : -INFINITY;  // masked * sl2 == -inf
-    float m_run = -INFINITY;  // running max of s * scale * log2(e)
-    float l_run = 0.f;
+    uint32_t n_sfull = 0, n_pvdone = 0;  // barrier phase counters carried across items
     bool ok = true;
 
-    for (int j = 0; j < n_kv; ++j) {
-      if (!mbar_wait_all(bar(C::B_SFULL + t), j & 1, ctl)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after_sync();
-      uint32_t sr[128];
-      tmem_ld128(s_tm, sr);
-      float* s = reinterpret_cast<float*>(sr);
-      tc_fence_before_sync();
-      mbar_arrive(bar(C::B_SFREE + t));  // S is in registers: the other tile's QK may overwrite it
+    for (int k = 0; ok; ++k) {
+      int w = -1;
+      if (lane == 0) ok = next_item(k, w);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      w = __shfl_sync(0xffffffffu, w, 0);
+      if (!ok || w < 0) break;
+      int b, h, q0, n_kv;
+      item_geometry(w, b, h, q0, n_kv);
+      const int qrow = q0 + t * C::BM + row;
+      float m_run = -INFINITY;  // running max of s * scale * log2(e)
+      float l_run = 0.f;
 
-      const int kv0 = j * C::BN;
-      const bool masked_tile = (kv0 + C::BN > p.len_k) || (p.causal && kv0 + C::BN - 1 > q0 + t * C::BM);
-      int lim = 128;
-      if (masked_tile) {
-        lim = p.len_k - kv0;
-        if (p.causal) lim = min(lim, qrow - kv0 + 1);
-#pragma unroll
-        for (int c = 0; c < 128; ++c)
-          if (c >= lim) s[c] = masked;
-      }
-      // P_t and O_t are free once PV_t(j-1) has completed (usually long done by now).
-      if (j > 0) {
-        if (!mbar_wait_all(bar(C::B_PVDONE + t), (j - 1) & 1, ctl)) {
+      for (int j = 0; j < n_kv; ++j) {
+        if (!mbar_wait_all(bar(C::B_SFULL + t), (n_sfull++) & 1u, ctl)) {
           ok = false;
           break;
         }
         tc_fence_after_sync();
-      }
-      // Fast pass: exponentiate against the running max m_run straight away, x = s*scale*log2e - m,
-      // taking this tile's row maximum of x in the same pass (independent of the exp2 chain).
-      // P goes to TMEM in 16-column chunks as it is produced.  Only when some row's maximum grew
-      // by more than 2^8 (always on a row's first tile) does the warp redo the tile against the
-      // new maximum, rescaling l and O with it; otherwise the stale maximum stays (exact: O, l
-      // and P share it).
-      const float m_used = (m_run == -INFINITY) ? 0.f : m_run;
-      float l_tile, xmax;
-      exp_pass<BF16>(s, sl2, -m_used, p_tm, l_tile, xmax);
-      const float m_tile = xmax + m_used;  // row max of s*scale*log2e in this tile
-      float alpha = 1.f;
-      if (__any_sync(0xffffffffu, m_tile - m_run > 8.f)) {
-        if (m_tile - m_run > 8.f) {  // (m_run = -inf, m_tile finite: first tile of the row)
-          alpha = ex2_approx(m_run - m_tile);
-          m_run = m_tile;
-        }
-        tmem_st_wait();  // the redo overwrites the fast pass's P columns
-        float xm;
-        exp_pass<BF16>(s, sl2, (m_run == -INFINITY) ? 0.f : -m_run, p_tm, l_tile, xm);
-        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll 1
-          for (int c = 0; c < DP / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(o_tm + c * 32, o);
+        uint32_t sr[128];
+        tmem_ld128(s_tm, sr);
+        float* s = reinterpret_cast<float*>(sr);
+        tc_fence_before_sync();
+        mbar_arrive(bar(C::B_SFREE + t));  // S is in registers: the other tile's QK may overwrite it
+
+        const int kv0 = j * C::BN;
+        if ((kv0 + C::BN > p.len_k) || (p.causal && kv0 + C::BN - 1 > q0 + t * C::BM)) {
+          int lim = p.len_k - kv0;
+          if (p.causal) lim = min(lim, qrow - kv0 + 1);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st32(o_tm + c * 32, o);
+          for (int c = 0; c < 128; ++c)
+            if (c >= lim) s[c] = masked;
+        }
+        // P_t and O_t are free once PV_t(j-1) has completed (usually long done by now).
+        if (j > 0) {
+          if (!mbar_wait_all(bar(C::B_PVDONE + t), (n_pvdone++) & 1u, ctl)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+        }
+        // Fast pass against the running max, row max of x found in the same pass; redo only when
+        // some row's max grew by more than 2^8 (always on a row's first tile).
+        const float m_used = (m_run == -INFINITY) ? 0.f : m_run;
+        float l_tile, xmax;
+        exp_pass<BF16>(s, sl2, -m_used, p_tm, l_tile, xmax);
+        const float m_tile = xmax + m_used;  // row max of s*scale*log2e in this tile
+        float alpha = 1.f;
+        if (__any_sync(0xffffffffu, m_tile - m_run > 8.f)) {
+          if (m_tile - m_run > 8.f) {  // (m_run = -inf, m_tile finite: first tile of the row)
+            alpha = ex2_approx(m_run - m_tile);
+            m_run = m_tile;
+          }
+          tmem_st_wait();  // the redo overwrites the fast pass's P columns
+          float xm;
+          exp_pass<BF16>(s, sl2, (m_run == -INFINITY) ? 0.f : -m_run, p_tm, l_tile, xm);
+          if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+            for (int c = 0; c < DP / 32; ++c) {
+              uint32_t o[32];
+              tmem_ld32(o_tm + c * 32, o);
+#pragma unroll
+              for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+              tmem_st32(o_tm + c * 32, o);
+            }
           }
         }
+        l_run = l_run * alpha + l_tile;
+        tmem_st_wait();
+        tc_fence_before_sync();
+        mbar_arrive(bar(C::B_PREADY + t));
       }
-      l_run = l_run * alpha + l_tile;
-      tmem_st_wait();
-      tc_fence_before_sync();
-      mbar_arrive(bar(C::B_PREADY + t));
-    }
+      if (!ok) break;
 
-    if (ok) ok = mbar_wait_all(bar(C::B_PVDONE + t), (n_kv - 1) & 1, ctl);
-    if (ok) {
+      // Epilogue: O_t / l, 16-bit, staged in shared memory (swizzled) and written with TMA stores
+      // that clip rows >= Lq and columns >= D.  The staging buffer holds one tile: the two tiles
+      // take turns per 32-row quarter (tile 0 of item k waits for tile 1 of item k-1 and vice versa).
+      if (!(ok = mbar_wait_all(bar(C::B_PVDONE + t), (n_pvdone++) & 1u, ctl))) break;
       tc_fence_after_sync();
       const float inv_l = 1.f / l_run;
-      // Stage O_t in the Q_t buffer (all MMAs of tile t are complete).
-      const uint32_t stage = sQ + t * C::QTILE_BYTES;
+      const uint32_t turn_bar = bar(C::B_OST + t * 4 + wq);
+      if (t == 1 || k > 0) {
+        const uint32_t par = t == 1 ? static_cast<uint32_t>(k) & 1u : static_cast<uint32_t>(k - 1) & 1u;
+        if (!(ok = mbar_wait_all(turn_bar, par, ctl))) break;
+      }
+      const uint32_t stage = base + C::OFF_OST;
 #pragma unroll 1
       for (int c = 0; c < C::NCH; ++c) {
         const uint32_t row_addr = stage + c * C::CH_BYTES + row * 128;
@@ -406,28 +475,35 @@ __global__ void __launch_bounds__(320, 1)
         for (int hh = 0; hh < 2; ++hh) {
           uint32_t o[32];
           tmem_ld32(o_tm + c * 64 + hh * 32, o);
+          if (c == C::NCH - 1 && hh == 1) {
+            tc_fence_before_sync();
+            mbar_arrive(bar(C::B_OFREE + t));  // O_t is read: the next item may overwrite it
+          }
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            uint32_t w[4];
+            uint32_t wv[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const float lo = __uint_as_float(o[q * 8 + 2 * e]) * inv_l;
               const float hi = __uint_as_float(o[q * 8 + 2 * e + 1]) * inv_l;
-              w[e] = BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+              wv[e] = BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
             }
             const int chunk = hh * 4 + q;  // 16-byte chunk within the 128-byte row
-            st_shared_v4(row_addr + ((chunk ^ (row & 7)) << 4), w[0], w[1], w[2], w[3]);
+            st_shared_v4(row_addr + ((chunk ^ (row & 7)) << 4), wv[0], wv[1], wv[2], wv[3]);
           }
         }
       }
       fence_proxy_async_smem();
       __syncwarp();
-      const int row0 = q0 + t * C::BM + wq * 32;
-      if (lane == 0 && row0 < p.len_q) {
-        for (int c = 0; c < C::NCH; ++c)
-          tma_store_4d(&tm_o, stage + c * C::CH_BYTES + wq * 32 * 128, c * 64, row0, h, b);
-        bulk_commit_group();
-        bulk_wait_group_read0();
+      if (lane == 0) {
+        const int row0 = q0 + t * C::BM + wq * 32;
+        if (row0 < p.len_q) {
+          for (int c = 0; c < C::NCH; ++c)
+            tma_store_4d(&tm_o, stage + c * C::CH_BYTES + wq * 32 * 128, c * 64, row0, h, b);
+          bulk_commit_group();
+          bulk_wait_group_read0();
+        }
+        mbar_arrive(bar(C::B_OST + (1 - t) * 4 + wq));  // these staging rows are free again
       }
       __syncwarp();
     }
@@ -445,6 +521,14 @@ __global__ void __launch_bounds__(320, 1)
     }
     tc_fence_after_sync();
     tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+  // The last CTA to finish puts the work counters back to zero for the next launch.
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(p.work + 1, 1u) == gridDim.x - 1) {
+      atomicExch(p.work, 0u);
+      atomicExch(p.work + 1, 0u);
+    }
   }
 }
 
@@ -489,9 +573,14 @@ const char* fmha_sm100_plan(const cmpx_attn_desc* d, int* status) {
         *status = CMPX_ERR_MISALIGNED;
         return "none";
       }
+  if (((d->len_q + 255) / 256) * d->heads * d->batch > (1ll << 30)) {
+    *status = CMPX_ERR_UNSUPPORTED_SHAPE;
+    return "none";
+  }
   const bool bf = d->dtype == CMPX_BF16;
-  if (d->head_dim <= 64) return bf ? "fmha_sm100<bf16,D64,2x128q,128kv,6st>" : "fmha_sm100<f16,D64,2x128q,128kv,6st>";
-  return bf ? "fmha_sm100<bf16,D128,2x128q,128kv,4st>" : "fmha_sm100<f16,D128,2x128q,128kv,4st>";
+  if (d->head_dim <= 64)
+    return bf ? "fmha_sm100<bf16,D64,2x128q,128kv,6st,persistent>" : "fmha_sm100<f16,D64,2x128q,128kv,6st,persistent>";
+  return bf ? "fmha_sm100<bf16,D128,2x128q,128kv,4st,persistent>" : "fmha_sm100<f16,D128,2x128q,128kv,4st,persistent>";
 }
 
 namespace {
@@ -533,13 +622,19 @@ int launch_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   p.len_q = static_cast<int>(d->len_q);
   p.len_k = static_cast<int>(d->len_k);
   p.n_pairs = static_cast<int>((d->len_q + 255) / 256);
+  p.n_items = static_cast<int>(p.n_pairs * d->heads * d->batch);
   p.causal = d->causal ? 1 : 0;
   p.neg_scale = d->scale < 0 ? 1 : 0;
   p.scale_log2 = static_cast<float>(d->scale * 1.4426950408889634);
+  p.o = d->o;
+  p.os_b = d->o_stride[0];
+  p.os_h = d->o_stride[1];
+  p.os_s = d->o_stride[2];
+  p.head_dim = static_cast<int>(d->head_dim);
+  p.work = static_cast<unsigned int*>(d->workspace);
   p.timeout_ns = ctx.timeout_ns;
   p.dev_flags = ctx.dev_flags;
-  dim3 grid(static_cast<unsigned>(p.n_pairs), static_cast<unsigned>(d->heads),
-            static_cast<unsigned>(d->batch));
+  const int grid = std::min(p.n_items, std::max(1, ctx.num_sms));
   fmha_fwd_sm100_kernel<DP, BF16><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, to, p);
   return cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
 }

@@ -26,6 +26,7 @@ __device__ unsigned int g_dev_flags;
 namespace {
 
 constexpr int kMaxDevices = 64;
+constexpr size_t kAttnWorkspaceBytes = 256;
 
 struct DeviceState {
   std::once_flag once;
@@ -207,8 +208,9 @@ const char* cmpx_status_str(int status) {
 }
 
 size_t cmpx_attn_workspace_size(const cmpx_attn_desc* desc) {
-  (void)desc;
-  return 0;
+  // The persistent 16-bit kernel keeps two work counters (next item, CTAs finished).
+  if (!desc || (desc->dtype != CMPX_F16 && desc->dtype != CMPX_BF16)) return 0;
+  return kAttnWorkspaceBytes;
 }
 
 int cmpx_attn_plan(const cmpx_attn_desc* desc, char* buf, size_t buf_len) {
@@ -230,6 +232,10 @@ int cmpx_attn_fwd(const cmpx_attn_desc* desc, void* stream) {
   attn_plan_impl(desc, &st);
   if (st != CMPX_OK) return st;
   if (desc->batch == 0 || desc->heads == 0 || desc->len_q == 0) return CMPX_OK;
+  if (cmpx_attn_workspace_size(desc) > 0 &&
+      (!desc->workspace || desc->workspace_bytes < cmpx_attn_workspace_size(desc) ||
+       (reinterpret_cast<uintptr_t>(desc->workspace) & 15u) != 0))
+    return CMPX_ERR_WORKSPACE;
   LaunchCtx ctx;
   st = device_ctx(&ctx, static_cast<cudaStream_t>(stream));
   if (st != CMPX_OK) return st;
