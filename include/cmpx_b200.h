@@ -115,6 +115,20 @@ CMPX_API int cmpx_attn_fwd(const cmpx_attn_desc* desc, void* stream);
  * No reference counterpart (the reference allocates nothing but the output). */
 CMPX_API size_t cmpx_attn_workspace_size(const cmpx_attn_desc* desc);
 
+/* Attention forward that allocates nothing, for callers that cannot obtain device memory at the
+ * time of the call (a serving process whose pool owns the whole GPU, code running inside an
+ * allocator callback, stacks that only allocate at start-up -- cudaMalloc may also synchronise the
+ * device).  Same descriptor and results as cmpx_attn_fwd, but the workspace fields are ignored: the
+ * kernel's scratch (its work counters) lives in a fixed 256-byte array inside the library, which
+ * every GPU that loads the library keeps until the process exits.  A call whose scratch need
+ * (cmpx_attn_workspace_size) exceeds 256 bytes returns CMPX_ERR_WORKSPACE.  The first call on a
+ * device looks up that array's device address (cudaGetSymbolAddress); make that first call before
+ * capturing the stream into a graph.  Each call clears the counters it needs with an enqueued
+ * memset.  All calls share the one array, so calls whose work overlaps on the GPU (different
+ * streams without ordering between them) race on it: serialise them.
+ * No counterpart in the reference. */
+CMPX_API int cmpx_attn_fwd_noalloc(const cmpx_attn_desc* desc, void* stream);
+
 /* Batched matmul.  Replaces cmpext3.ops.bmm (src/main.cpp:2307-2309). */
 CMPX_API int cmpx_bmm(const cmpx_bmm_desc* desc, void* stream);
 
