@@ -102,46 +102,63 @@ struct FmhaParams {
 };
 
 // One pass over a row's 128 scores: p = 2^(s*sl2 + nmb) packed to 16-bit and stored to TMEM
-// (4 chunks of 16 columns at p_tm), the row sum of p, and the maximum of s*sl2 + nmb.
-// CMPX_FMHA_EMU of every 8 column pairs use the packed polynomial exp2 on the FMA pipe.
+// (4 chunks of 16 columns at p_tm), and the row sum of p.  x = s*sl2 + nmb is formed and the sum
+// accumulated two keys at a time with packed f32x2 arithmetic; exponentials on MUFU
+// (CMPX_FMHA_EMU of every 8 column pairs on the FMA pipe instead), 16-bit packing per pair.
 template <bool BF16>
-__device__ __forceinline__ void exp_pass(const float* s, float sl2, float nmb, uint32_t p_tm,
-                                         float& l_out, float& xmax_out) {
-  float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
-  float a0 = -INFINITY, a1 = -INFINITY, a2 = -INFINITY, a3 = -INFINITY;
+__device__ __forceinline__ float exp_pass(const float* s, float sl2, float nmb, uint32_t p_tm) {
+  uint64_t la = f2_pack(0.f, 0.f), lb = la;
+  const uint64_t sl2x2 = f2_pack(sl2, sl2), nmbx2 = f2_pack(nmb, nmb);
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     uint32_t pk[16];
 #pragma unroll
     for (int c = 0; c < 16; ++c) {
       const int cc = q * 16 + c;
+      const uint64_t xv = f2_fma(f2_pack(s[2 * cc], s[2 * cc + 1]), sl2x2, nmbx2);
       float p0, p1;
       if ((cc & 7) >= 8 - CMPX_FMHA_EMU) {
-        const uint64_t xv = f2_fma(f2_pack(s[2 * cc], s[2 * cc + 1]), f2_pack(sl2, sl2), f2_pack(nmb, nmb));
-        float x0, x1;
-        f2_unpack(xv, x0, x1);
-        if (c & 1) a1 = fmax3(a1, x0, x1); else a0 = fmax3(a0, x0, x1);
         f2_unpack(exp2_poly3_x2(xv), p0, p1);
       } else {
-        const float x0 = fmaf(s[2 * cc], sl2, nmb);
-        const float x1 = fmaf(s[2 * cc + 1], sl2, nmb);
-        if (c & 1) a3 = fmax3(a3, x0, x1); else a2 = fmax3(a2, x0, x1);
+        float x0, x1;
+        f2_unpack(xv, x0, x1);
         p0 = ex2_approx(x0);
         p1 = ex2_approx(x1);
       }
-      if (c & 1) {
-        l2 += p0;
-        l3 += p1;
-      } else {
-        l0 += p0;
-        l1 += p1;
-      }
+      if (c & 1)
+        lb = f2_add(lb, f2_pack(p0, p1));
+      else
+        la = f2_add(la, f2_pack(p0, p1));
       pk[c] = BF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
     }
     tmem_st16(p_tm + q * 16, pk);
   }
-  l_out = (l0 + l1) + (l2 + l3);
-  xmax_out = fmax3(fmaxf(a0, a1), a2, a3);
+  float a0, a1;
+  f2_unpack(f2_add(la, lb), a0, a1);
+  return a0 + a1;
+}
+
+// Row maximum / minimum of 128 values: 8 independent chains, the first 16 values seed them in pairs,
+// the other 112 follow two at a time with the 3-input form.
+__device__ __forceinline__ float row_max128(const float* s) {
+  float a[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a[i] = fmaxf(s[2 * i], s[2 * i + 1]);
+#pragma unroll
+  for (int c = 16; c < 128; c += 16)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = fmax3(a[i], s[c + 2 * i], s[c + 2 * i + 1]);
+  return fmax3(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
+}
+__device__ __forceinline__ float row_min128(const float* s) {
+  float a[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a[i] = fminf(s[2 * i], s[2 * i + 1]);
+#pragma unroll
+  for (int c = 16; c < 128; c += 16)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = fmin3(a[i], s[c + 2 * i], s[c + 2 * i + 1]);
+  return fmin3(fmin3(a[0], a[1], a[2]), fmin3(a[3], a[4], a[5]), fminf(a[6], a[7]));
 }
 
 // Work item w (persistent schedule): bh = w / n_pairs, pair = n_pairs - 1 - w % n_pairs.  The items
@@ -423,21 +440,27 @@ __global__ void __launch_bounds__(320, 1)
           }
           tc_fence_after_sync();
         }
-        // Fast pass against the running max, row max of x found in the same pass; redo only when
-        // some row's max grew by more than 2^8 (always on a row's first tile).
-        const float m_used = (m_run == -INFINITY) ? 0.f : m_run;
-        float l_tile, xmax;
-        exp_pass<BF16>(s, sl2, -m_used, p_tm, l_tile, xmax);
-        const float m_tile = xmax + m_used;  // row max of s*scale*log2e in this tile
+        // Fast pass against the running max m_run.  Any p above 2^8 (a key more than 8 above
+        // m_run in log2 units) forces the tile's row sum above 256, so a row sum <= 256 proves the
+        // stale max is usable (exact: O, l and P share it).  Otherwise -- and on a row's first
+        // tile, where m_run is still -inf -- the warp takes the slow path: exact tile max, new
+        // running max, P recomputed, l and O rescaled.  After a slow pass m_run is the true running
+        // max, so later triggers are rare.  (Key 0 is never masked, so m_run is finite after j = 0.)
+        float l_tile = 0.f;
         float alpha = 1.f;
-        if (__any_sync(0xffffffffu, m_tile - m_run > 8.f)) {
-          if (m_tile - m_run > 8.f) {  // (m_run = -inf, m_tile finite: first tile of the row)
+        bool slow = (j == 0);
+        if (!slow) {
+          l_tile = exp_pass<BF16>(s, sl2, -m_run, p_tm);
+          slow = __any_sync(0xffffffffu, !(l_tile <= 256.f));
+          if (slow) tmem_st_wait();  // the redo overwrites the fast pass's P columns
+        }
+        if (slow) {
+          const float m_tile = (p.neg_scale ? row_min128(s) : row_max128(s)) * sl2;
+          if (m_tile > m_run) {  // (always on the first tile: m_run = -inf, m_tile finite)
             alpha = ex2_approx(m_run - m_tile);
             m_run = m_tile;
           }
-          tmem_st_wait();  // the redo overwrites the fast pass's P columns
-          float xm;
-          exp_pass<BF16>(s, sl2, (m_run == -INFINITY) ? 0.f : -m_run, p_tm, l_tile, xm);
+          l_tile = exp_pass<BF16>(s, sl2, -m_run, p_tm);
           if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
             for (int c = 0; c < DP / 32; ++c) {
