@@ -81,7 +81,7 @@ struct FmhaCfg {
   // (and work fetch), 9 MMA issuer.
   static constexpr int THREADS = 320;
   static constexpr int W_TMA = 8, W_MMA = 9;
-  static constexpr int ITEM_CONSUMERS = 1 + 8;  // MMA lane 0 + lane 0 of each softmax warp
+  static constexpr int ITEM_CONSUMERS = 1 + 8;  // lane 0 of the MMA warp and of each softmax warp
 };
 
 struct FmhaParams {
@@ -231,6 +231,15 @@ __global__ void __launch_bounds__(320, 1)
     mbar_arrive(bar(C::B_ITEMPTY + slot));
     return true;
   };
+  // Same for a whole warp: a warp-wide wait, every lane reads the slot, lane 0 releases it.
+  auto next_item_warp = [&](int k, int& w) -> bool {
+    const int slot = k & 1;
+    if (!mbar_wait_all(bar(C::B_ITFULL + slot), static_cast<uint32_t>(k >> 1) & 1u, ctl)) return false;
+    w = item_slot[slot];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar(C::B_ITEMPTY + slot));
+    return true;
+  };
   auto item_geometry = [&](int w, int& b, int& h, int& q0, int& n_kv) {
     const int bh = w / p.n_pairs;
     const int pair = p.n_pairs - 1 - (w - bh * p.n_pairs);
@@ -285,7 +294,9 @@ __global__ void __launch_bounds__(320, 1)
       }
     } else {
       // ---------------------------------------------------------------- MMA issuer
-      if (lane == 0) {
+      // The whole warp runs this loop with warp-uniform control flow (waits are warp-wide and
+      // return one verdict); one elected lane issues each MMA and commit (the *_w helpers).
+      {
         constexpr uint32_t kIdescQK = idesc_f16(128, 128, BF16 ? 1 : 0, 0, 0);
         constexpr uint32_t kIdescPV = idesc_f16(128, DP, BF16 ? 1 : 0, 0, 1);
         auto issue_qk = [&](int t, uint32_t k_addr) {
@@ -293,8 +304,8 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
           for (int k = 0; k < DP / 16; ++k) {
             const uint32_t off = (k >> 2) * C::CH_BYTES + (k & 3) * 32;
-            umma_ss(tmem + C::TM_S, smem_desc_sw128(q_addr + off, 16, 1024),
-                    smem_desc_sw128(k_addr + off, 16, 1024), kIdescQK, k > 0 ? 1u : 0u);
+            umma_ss_w(tmem + C::TM_S, smem_desc_sw128(q_addr + off, 16, 1024),
+                      smem_desc_sw128(k_addr + off, 16, 1024), kIdescQK, k > 0 ? 1u : 0u);
           }
         };
         // P_t: 16-bit, two keys per 32-bit column, 64 columns.
@@ -303,9 +314,9 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t d_tmem = tmem + (t ? C::TM_O1 : C::TM_O0);
 #pragma unroll
           for (int k = 0; k < C::BN / 16; ++k) {
-            umma_ts(d_tmem, p_tmem + k * 8,
-                    smem_desc_sw128(v_addr + k * 2048, C::CH_BYTES, 1024), kIdescPV,
-                    (acc || k > 0) ? 1u : 0u);
+            umma_ts_w(d_tmem, p_tmem + k * 8,
+                      smem_desc_sw128(v_addr + k * 2048, C::CH_BYTES, 1024), kIdescPV,
+                      (acc || k > 0) ? 1u : 0u);
           }
         };
         auto stage_of = [&](int load) -> uint32_t { return sKV + (load % C::NSTAGE) * C::KV_BYTES; };
@@ -323,64 +334,64 @@ __global__ void __launch_bounds__(320, 1)
         // it is in registers).
         for (int k = 0; ok; ++k) {
           int w;
-          if (!(ok = next_item(k, w))) break;
+          if (!(ok = next_item_warp(k, w))) break;
           if (w < 0) break;
           int b, h, q0, n_kv;
           item_geometry(w, b, h, q0, n_kv);
           (void)b; (void)h; (void)q0;
-          if (!(ok = mbar_wait(bar(C::B_QFULL), static_cast<uint32_t>(k) & 1u, ctl))) break;
+          if (!(ok = mbar_wait_all(bar(C::B_QFULL), static_cast<uint32_t>(k) & 1u, ctl))) break;
           // S is free once tile 1's softmax read the previous item's last S.
-          if (k > 0 && !(ok = mbar_wait(bar(C::B_SFREE + 1), (n_sfree1++) & 1u, ctl))) break;
-          if (!(ok = mbar_wait(full_bar(base_load), round_par(base_load), ctl))) break;
+          if (k > 0 && !(ok = mbar_wait_all(bar(C::B_SFREE + 1), (n_sfree1++) & 1u, ctl))) break;
+          if (!(ok = mbar_wait_all(full_bar(base_load), round_par(base_load), ctl))) break;
           tc_fence_after_sync();
           issue_qk(0, stage_of(base_load));
-          umma_commit(bar(C::B_SFULL + 0));
+          umma_commit_w(bar(C::B_SFULL + 0));
           for (int j = 0; ok && j < n_kv; ++j) {
             const int lk = base_load + 2 * j, lv = lk + 1, lk1 = lk + 2, lv0 = lk - 1;
-            if (!(ok = mbar_wait(bar(C::B_SFREE + 0), (n_sfree0++) & 1u, ctl))) break;
+            if (!(ok = mbar_wait_all(bar(C::B_SFREE + 0), (n_sfree0++) & 1u, ctl))) break;
             tc_fence_after_sync();
             issue_qk(1, stage_of(lk));
-            umma_commit(bar(C::B_SFULL + 1));
-            umma_commit(empty_bar(lk));  // K_j done
-            if (j + 1 == n_kv) umma_commit(bar(C::B_QEMPTY));  // last QK of the item
+            umma_commit_w(bar(C::B_SFULL + 1));
+            umma_commit_w(empty_bar(lk));  // K_j done
+            if (j + 1 == n_kv) umma_commit_w(bar(C::B_QEMPTY));  // last QK of the item
             if (j > 0) {
-              if (!(ok = mbar_wait(bar(C::B_PREADY + 1), (n_pready1++) & 1u, ctl))) break;
+              if (!(ok = mbar_wait_all(bar(C::B_PREADY + 1), (n_pready1++) & 1u, ctl))) break;
               // The item's first PV_1 overwrites O_1: the previous item's epilogue must have read it.
               if (j == 1 && k > 0 &&
-                  !(ok = mbar_wait(bar(C::B_OFREE + 1), static_cast<uint32_t>(k - 1) & 1u, ctl)))
+                  !(ok = mbar_wait_all(bar(C::B_OFREE + 1), static_cast<uint32_t>(k - 1) & 1u, ctl)))
                 break;
               tc_fence_after_sync();
               issue_pv(1, stage_of(lv0), j > 1);
-              umma_commit(bar(C::B_PVDONE + 1));
-              umma_commit(empty_bar(lv0));  // V_{j-1} done
+              umma_commit_w(bar(C::B_PVDONE + 1));
+              umma_commit_w(empty_bar(lv0));  // V_{j-1} done
             }
             if (j + 1 < n_kv) {
-              if (!(ok = mbar_wait(bar(C::B_SFREE + 1), (n_sfree1++) & 1u, ctl))) break;
-              if (!(ok = mbar_wait(full_bar(lk1), round_par(lk1), ctl))) break;
+              if (!(ok = mbar_wait_all(bar(C::B_SFREE + 1), (n_sfree1++) & 1u, ctl))) break;
+              if (!(ok = mbar_wait_all(full_bar(lk1), round_par(lk1), ctl))) break;
               tc_fence_after_sync();
               issue_qk(0, stage_of(lk1));
-              umma_commit(bar(C::B_SFULL + 0));
+              umma_commit_w(bar(C::B_SFULL + 0));
             }
-            if (!(ok = mbar_wait(full_bar(lv), round_par(lv), ctl))) break;
-            if (!(ok = mbar_wait(bar(C::B_PREADY + 0), (n_pready0++) & 1u, ctl))) break;
+            if (!(ok = mbar_wait_all(full_bar(lv), round_par(lv), ctl))) break;
+            if (!(ok = mbar_wait_all(bar(C::B_PREADY + 0), (n_pready0++) & 1u, ctl))) break;
             if (j == 0 && k > 0 &&
-                !(ok = mbar_wait(bar(C::B_OFREE + 0), static_cast<uint32_t>(k - 1) & 1u, ctl)))
+                !(ok = mbar_wait_all(bar(C::B_OFREE + 0), static_cast<uint32_t>(k - 1) & 1u, ctl)))
               break;
             tc_fence_after_sync();
             issue_pv(0, stage_of(lv), j > 0);
-            umma_commit(bar(C::B_PVDONE + 0));
+            umma_commit_w(bar(C::B_PVDONE + 0));
           }
           if (!ok) break;
           {
             const int lv = base_load + 2 * (n_kv - 1) + 1;
-            if (!(ok = mbar_wait(bar(C::B_PREADY + 1), (n_pready1++) & 1u, ctl))) break;
+            if (!(ok = mbar_wait_all(bar(C::B_PREADY + 1), (n_pready1++) & 1u, ctl))) break;
             if (n_kv == 1 && k > 0 &&
-                !(ok = mbar_wait(bar(C::B_OFREE + 1), static_cast<uint32_t>(k - 1) & 1u, ctl)))
+                !(ok = mbar_wait_all(bar(C::B_OFREE + 1), static_cast<uint32_t>(k - 1) & 1u, ctl)))
               break;
             tc_fence_after_sync();
             issue_pv(1, stage_of(lv), n_kv > 1);
-            umma_commit(bar(C::B_PVDONE + 1));
-            umma_commit(empty_bar(lv));
+            umma_commit_w(bar(C::B_PVDONE + 1));
+            umma_commit_w(empty_bar(lv));
           }
           base_load += 2 * n_kv;
         }
@@ -536,10 +547,9 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   if (warp == C::W_MMA) {
     if (*abort_flag) {
-      if (lane == 0) {
-        umma_commit(bar(C::B_DRAIN));
-        mbar_wait_drain(bar(C::B_DRAIN), 0, p.timeout_ns);
-      }
+      __syncwarp();
+      umma_commit_w(bar(C::B_DRAIN));  // same election as the MMAs: tracks all of them
+      if (lane == 0) mbar_wait_drain(bar(C::B_DRAIN), 0, p.timeout_ns);
       __syncwarp();
     }
     tc_fence_after_sync();
