@@ -78,10 +78,10 @@ struct FmhaCfg {
   static constexpr int TM_S = 0, TM_P0 = 128, TM_P1 = 192, TM_O0 = 256, TM_O1 = 256 + DP;
   static constexpr int TMEM_COLS = 512;
   // Warp roles: 0-3 softmax/epilogue of tile 0, 4-7 of tile 1 (thread = row), 8 TMA producer
-  // (and work fetch), 9 MMA issuer.
-  static constexpr int THREADS = 320;
-  static constexpr int W_TMA = 8, W_MMA = 9;
-  static constexpr int ITEM_CONSUMERS = 1 + 8;  // lane 0 of the MMA warp and of each softmax warp
+  // (and work fetch), 9 QK issuer (and TMEM owner), 10 PV issuer.
+  static constexpr int THREADS = 352;
+  static constexpr int W_TMA = 8, W_MMA = 9, W_PV = 10;
+  static constexpr int ITEM_CONSUMERS = 2 + 8;  // lane 0 of each MMA warp and of each softmax warp
 };
 
 struct FmhaParams {
@@ -165,7 +165,7 @@ __device__ __forceinline__ float row_min128(const float* s) {
 // of one (b, h) are consecutive, so the CTAs busy at any moment share a few heads' K/V in L2, and
 // within a head the heavy (late, causal) row pairs go first.
 template <int DP, bool BF16>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(352, 1)
     fmha_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v,
@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(bar(C::B_ITEMPTY + t), C::ITEM_CONSUMERS);
     }
     for (int i = 0; i < 8; ++i) mbar_init(bar(C::B_OST + i), 1);
-    mbar_init(bar(C::B_DRAIN), 1);
+    mbar_init(bar(C::B_DRAIN), 2);  // one commit from each MMA warp
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -293,12 +293,26 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
     } else {
-      // ---------------------------------------------------------------- MMA issuer
-      // The whole warp runs this loop with warp-uniform control flow (waits are warp-wide and
-      // return one verdict); one elected lane issues each MMA and commit (the *_w helpers).
-      {
-        constexpr uint32_t kIdescQK = idesc_f16(128, 128, BF16 ? 1 : 0, 0, 0);
-        constexpr uint32_t kIdescPV = idesc_f16(128, DP, BF16 ? 1 : 0, 0, 1);
+      // ---------------------------------------------------------------- MMA issuers
+      // Two issuing warps feed the one tensor pipe: W_MMA issues the QK products, W_PV the PV
+      // products.  The pipe's queue is only a few MMAs deep and every MMA issue costs the issuing
+      // thread a good part of an MMA's execution time, so one warp alone lets the pipe drain
+      // while it does the bookkeeping (barrier waits, commits) between two products; with two,
+      // one warp's MMAs keep the pipe busy while the other waits.  Each warp runs its loop with
+      // warp-uniform control flow (waits are warp-wide and return one verdict) and one elected
+      // lane issues its MMAs and commits (the *_w helpers).  The two streams touch disjoint TMEM
+      // (QK: S;  PV: P_t, O_t); every cross-dependency goes through an mbarrier.
+      constexpr uint32_t kIdescQK = idesc_f16(128, 128, BF16 ? 1 : 0, 0, 0);
+      constexpr uint32_t kIdescPV = idesc_f16(128, DP, BF16 ? 1 : 0, 0, 1);
+      auto stage_of = [&](int load) -> uint32_t { return sKV + (load % C::NSTAGE) * C::KV_BYTES; };
+      auto full_bar = [&](int load) -> uint32_t { return bar(C::B_FULL + load % C::NSTAGE); };
+      auto empty_bar = [&](int load) -> uint32_t { return bar(C::B_EMPTY + load % C::NSTAGE); };
+      auto round_par = [&](int load) -> uint32_t { return static_cast<uint32_t>(load / C::NSTAGE) & 1u; };
+      int base_load = 0;  // K/V ring loads of the items before this one (K_j = +2j, V_j = +2j+1)
+      bool ok = true;
+      if (warp == C::W_MMA) {
+        // QK_t(j) = Q_t K_j^T into S.  Order per key tile j:  QK_1(j) once tile 0 has read S(j);
+        // QK_0(j+1) once tile 1 has read S(j).
         auto issue_qk = [&](int t, uint32_t k_addr) {
           const uint32_t q_addr = sQ + t * C::QTILE_BYTES;
 #pragma unroll
@@ -308,30 +322,7 @@ __global__ void __launch_bounds__(320, 1)
                       smem_desc_sw128(k_addr + off, 16, 1024), kIdescQK, k > 0 ? 1u : 0u);
           }
         };
-        // P_t: 16-bit, two keys per 32-bit column, 64 columns.
-        auto issue_pv = [&](int t, uint32_t v_addr, bool acc) {
-          const uint32_t p_tmem = tmem + (t ? C::TM_P1 : C::TM_P0);
-          const uint32_t d_tmem = tmem + (t ? C::TM_O1 : C::TM_O0);
-#pragma unroll
-          for (int k = 0; k < C::BN / 16; ++k) {
-            umma_ts_w(d_tmem, p_tmem + k * 8,
-                      smem_desc_sw128(v_addr + k * 2048, C::CH_BYTES, 1024), kIdescPV,
-                      (acc || k > 0) ? 1u : 0u);
-          }
-        };
-        auto stage_of = [&](int load) -> uint32_t { return sKV + (load % C::NSTAGE) * C::KV_BYTES; };
-        auto full_bar = [&](int load) -> uint32_t { return bar(C::B_FULL + load % C::NSTAGE); };
-        auto empty_bar = [&](int load) -> uint32_t { return bar(C::B_EMPTY + load % C::NSTAGE); };
-        auto round_par = [&](int load) -> uint32_t { return static_cast<uint32_t>(load / C::NSTAGE) & 1u; };
-        // Barrier phase counters carried across items.
-        uint32_t n_sfree0 = 0, n_sfree1 = 0, n_pready0 = 0, n_pready1 = 0;
-        int base_load = 0;
-        bool ok = true;
-        // Issue order per key tile j of an item (each step waits only for what it reads or
-        // overwrites):  QK_1(j) once tile 0 has read S(j);  PV_1(j-1) once P_1(j-1) is written;
-        // QK_0(j+1) once tile 1 has read S(j);  PV_0(j) once P_0(j) is written.  The QKs of one
-        // tile overlap the other tile's softmax and its own exponentials (S is released as soon as
-        // it is in registers).
+        uint32_t n_sfree0 = 0, n_sfree1 = 0;  // barrier phase counters carried across items
         for (int k = 0; ok; ++k) {
           int w;
           if (!(ok = next_item_warp(k, w))) break;
@@ -347,31 +338,48 @@ __global__ void __launch_bounds__(320, 1)
           issue_qk(0, stage_of(base_load));
           umma_commit_w(bar(C::B_SFULL + 0));
           for (int j = 0; ok && j < n_kv; ++j) {
-            const int lk = base_load + 2 * j, lv = lk + 1, lk1 = lk + 2, lv0 = lk - 1;
+            const int lk = base_load + 2 * j, lk1 = lk + 2;
             if (!(ok = mbar_wait_all(bar(C::B_SFREE + 0), (n_sfree0++) & 1u, ctl))) break;
             tc_fence_after_sync();
             issue_qk(1, stage_of(lk));
             umma_commit_w(bar(C::B_SFULL + 1));
             umma_commit_w(empty_bar(lk));  // K_j done
-            if (j + 1 == n_kv) umma_commit_w(bar(C::B_QEMPTY));  // last QK of the item
-            if (j > 0) {
-              if (!(ok = mbar_wait_all(bar(C::B_PREADY + 1), (n_pready1++) & 1u, ctl))) break;
-              // The item's first PV_1 overwrites O_1: the previous item's epilogue must have read it.
-              if (j == 1 && k > 0 &&
-                  !(ok = mbar_wait_all(bar(C::B_OFREE + 1), static_cast<uint32_t>(k - 1) & 1u, ctl)))
-                break;
-              tc_fence_after_sync();
-              issue_pv(1, stage_of(lv0), j > 1);
-              umma_commit_w(bar(C::B_PVDONE + 1));
-              umma_commit_w(empty_bar(lv0));  // V_{j-1} done
+            if (j + 1 == n_kv) {
+              umma_commit_w(bar(C::B_QEMPTY));  // last QK of the item
+              break;
             }
-            if (j + 1 < n_kv) {
-              if (!(ok = mbar_wait_all(bar(C::B_SFREE + 1), (n_sfree1++) & 1u, ctl))) break;
-              if (!(ok = mbar_wait_all(full_bar(lk1), round_par(lk1), ctl))) break;
-              tc_fence_after_sync();
-              issue_qk(0, stage_of(lk1));
-              umma_commit_w(bar(C::B_SFULL + 0));
-            }
+            if (!(ok = mbar_wait_all(bar(C::B_SFREE + 1), (n_sfree1++) & 1u, ctl))) break;
+            if (!(ok = mbar_wait_all(full_bar(lk1), round_par(lk1), ctl))) break;
+            tc_fence_after_sync();
+            issue_qk(0, stage_of(lk1));
+            umma_commit_w(bar(C::B_SFULL + 0));
+          }
+          base_load += 2 * n_kv;
+        }
+      } else {
+        // O_t += P_t V_j, P_t from TMEM (16-bit, two keys per 32-bit column).  Order per key tile
+        // j: PV_0(j) once P_0(j) is written, PV_1(j) once P_1(j) is written; the first PV_t of an
+        // item overwrites O_t, so it also waits for the previous item's epilogue to have read O_t.
+        auto issue_pv = [&](int t, uint32_t v_addr, bool acc) {
+          const uint32_t p_tmem = tmem + (t ? C::TM_P1 : C::TM_P0);
+          const uint32_t d_tmem = tmem + (t ? C::TM_O1 : C::TM_O0);
+#pragma unroll
+          for (int k = 0; k < C::BN / 16; ++k) {
+            umma_ts_w(d_tmem, p_tmem + k * 8,
+                      smem_desc_sw128(v_addr + k * 2048, C::CH_BYTES, 1024), kIdescPV,
+                      (acc || k > 0) ? 1u : 0u);
+          }
+        };
+        uint32_t n_pready0 = 0, n_pready1 = 0;
+        for (int k = 0; ok; ++k) {
+          int w;
+          if (!(ok = next_item_warp(k, w))) break;
+          if (w < 0) break;
+          int b, h, q0, n_kv;
+          item_geometry(w, b, h, q0, n_kv);
+          (void)b; (void)h; (void)q0;
+          for (int j = 0; ok && j < n_kv; ++j) {
+            const int lv = base_load + 2 * j + 1;
             if (!(ok = mbar_wait_all(full_bar(lv), round_par(lv), ctl))) break;
             if (!(ok = mbar_wait_all(bar(C::B_PREADY + 0), (n_pready0++) & 1u, ctl))) break;
             if (j == 0 && k > 0 &&
@@ -380,18 +388,14 @@ __global__ void __launch_bounds__(320, 1)
             tc_fence_after_sync();
             issue_pv(0, stage_of(lv), j > 0);
             umma_commit_w(bar(C::B_PVDONE + 0));
-          }
-          if (!ok) break;
-          {
-            const int lv = base_load + 2 * (n_kv - 1) + 1;
             if (!(ok = mbar_wait_all(bar(C::B_PREADY + 1), (n_pready1++) & 1u, ctl))) break;
-            if (n_kv == 1 && k > 0 &&
+            if (j == 0 && k > 0 &&
                 !(ok = mbar_wait_all(bar(C::B_OFREE + 1), static_cast<uint32_t>(k - 1) & 1u, ctl)))
               break;
             tc_fence_after_sync();
-            issue_pv(1, stage_of(lv), n_kv > 1);
+            issue_pv(1, stage_of(lv), j > 0);
             umma_commit_w(bar(C::B_PVDONE + 1));
-            umma_commit_w(empty_bar(lv));
+            umma_commit_w(empty_bar(lv));  // V_j done (read by both tiles' PVs)
           }
           base_load += 2 * n_kv;
         }
@@ -545,13 +549,14 @@ __global__ void __launch_bounds__(320, 1)
 
   tc_fence_before_sync();
   __syncthreads();
+  if (*abort_flag && (warp == C::W_MMA || warp == C::W_PV)) {
+    // Each issuing warp commits to DRAIN (same election as its MMAs, so the commit tracks all of
+    // them); the TMEM owner waits for both before giving TMEM back.
+    umma_commit_w(bar(C::B_DRAIN));
+    if (warp == C::W_MMA && lane == 0) mbar_wait_drain(bar(C::B_DRAIN), 0, p.timeout_ns);
+    __syncwarp();
+  }
   if (warp == C::W_MMA) {
-    if (*abort_flag) {
-      __syncwarp();
-      umma_commit_w(bar(C::B_DRAIN));  // same election as the MMAs: tracks all of them
-      if (lane == 0) mbar_wait_drain(bar(C::B_DRAIN), 0, p.timeout_ns);
-      __syncwarp();
-    }
     tc_fence_after_sync();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
