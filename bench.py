@@ -22,7 +22,7 @@ time each step with its own CUDA events.
 Printed (rank 0, one JSON line): value/ms_per_step, e2e (the same metric through the public API with
 host-resident inputs: pinned H2D of the step's Q/K/V and D2H of its O inside the timed region),
 roofline (dominant kernel vs the measured bf16 peak), cpu_baseline (the reference's CPU path --
-stock torch SDPA on the host cores -- on a bounded sample), clocks sampled by nvidia-smi during the
+stock torch SDPA on the host cores -- on a bounded sample), clocks sampled (NVML, every 5 ms) during the
 timed region, gpu_launches, and a parity spot check of sampled slices/rows against that CPU path.
 """
 from __future__ import annotations
@@ -99,20 +99,66 @@ def load_traffic(kernel: str, workload: str) -> dict | None:
 # clocks
 # ------------------------------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi sampling of one GPU (by UUID) every 200 ms while the timed region runs."""
+    """SM clock, power and clock-event (throttle) reasons of one GPU, sampled while the timed
+    region runs.  Primary source: NVML (the counters nvidia-smi prints) polled every 5 ms from a
+    thread, so that even a timed region of a few tens of milliseconds holds several samples;
+    fallback when NVML cannot be opened: nvidia-smi -lms 200.  Read-only: nothing is set."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+    PERIOD_S = 0.005
 
     def __init__(self, uuid: str | None):
         self.uuid = uuid
         self.proc = None
+        self.nvml = None
+        self.handle = None
         self.lines: list[tuple[float, str]] = []
+        self.samples: list[tuple[float, float, float, float | None, set]] = []
         self.t_start = self.t_stop = None
+        self._halt = threading.Event()
+
+    def _open_nvml(self) -> bool:
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.handle = pynvml.nvmlDeviceGetHandleByUUID(self.uuid)
+            self.nvml = pynvml
+            return True
+        except Exception:  # noqa: BLE001
+            self.nvml = None
+            return False
+
+    def _nvml_loop(self):
+        nv = self.nvml
+        bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+        max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(self.handle, nv.NVML_CLOCK_SM))
+        while not self._halt.is_set():
+            try:
+                mhz = float(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                try:
+                    watts = nv.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
+                except Exception:  # noqa: BLE001
+                    watts = None
+                self.samples.append((time.time(), mhz, max_mhz, watts,
+                                     {name for name, bit in bits.items() if mask & bit}))
+            except Exception:  # noqa: BLE001
+                pass
+            self._halt.wait(self.PERIOD_S)
 
     def start(self):
         if not self.uuid:
+            return
+        if self._open_nvml():
+            self._thread = threading.Thread(target=self._nvml_loop, daemon=True)
+            self._thread.start()
+            time.sleep(0.05)
             return
         try:
             self.proc = subprocess.Popen(
@@ -136,7 +182,24 @@ class ClockSampler:
         else:
             self.t_stop = time.time()
 
+    def _summary(self, window, source) -> dict:
+        watts = [r[3] for r in window if r[3] is not None]
+        return {"sm_mhz": statistics.median(r[1] for r in window), "sm_max_mhz": max(r[2] for r in window),
+                "reasons": sorted(set().union(*(r[4] for r in window))), "samples": len(window),
+                "power_w_max": max(watts) if watts else None, "source": source}
+
     def stop(self) -> dict | None:
+        if self.nvml is not None:
+            self._halt.set()
+            self._thread.join(timeout=2)
+            try:
+                self.nvml.nvmlShutdown()
+            except Exception:  # noqa: BLE001
+                pass
+            inside = [r for r in self.samples if self.t_start and self.t_stop and self.t_start <= r[0] <= self.t_stop]
+            if not inside:
+                return None
+            return self._summary(inside, f"nvml every {self.PERIOD_S * 1e3:.0f} ms")
         if not self.proc:
             return None
         time.sleep(0.25)
@@ -151,19 +214,16 @@ class ClockSampler:
             if len(parts) < 8:
                 continue
             try:
-                rows.append((t, float(parts[0]), float(parts[1]), parts))
+                watts = float(parts[2]) if parts[2] not in ("[N/A]", "N/A") else None
+                rows.append((t, float(parts[0]), float(parts[1]), watts,
+                             {self.REASONS[i] for i in range(4) if parts[4 + i].lower() == "active"}))
             except ValueError:
                 continue
         if not rows:
             return None
         inside = [r for r in rows if self.t_start and self.t_stop and self.t_start - 0.1 <= r[0] <= self.t_stop + 0.1]
         window = inside or sorted(rows, key=lambda r: abs(r[0] - (self.t_start or r[0])))[:2]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in window for i in range(4) if r[3][4 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(r[1] for r in window), "sm_max_mhz": max(r[2] for r in window),
-                "reasons": reasons, "samples": len(window),
-                "power_w_max": max(float(r[3][2]) for r in window if r[3][2] not in ("[N/A]", "N/A"))
-                if any(r[3][2] not in ("[N/A]", "N/A") for r in window) else None}
+        return self._summary(window, "nvidia-smi every 200 ms")
 
 
 # ------------------------------------------------------------------------------------------------
