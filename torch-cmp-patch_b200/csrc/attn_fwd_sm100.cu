@@ -101,36 +101,49 @@ struct FmhaParams {
   unsigned int* dev_flags;
 };
 
-// One pass over a row's 128 scores: p = 2^(s*sl2 + nmb) packed to 16-bit and stored to TMEM
-// (4 chunks of 16 columns at p_tm), and the row sum of p.  x = s*sl2 + nmb is formed and the sum
+// One chunk (16 column pairs = 32 keys) of a row's exponentials: p = 2^(s*sl2 + nmb) packed to
+// 16-bit pairs in pk, the row sum accumulated in la/lb.  x = s*sl2 + nmb is formed and the sum
 // accumulated two keys at a time with packed f32x2 arithmetic; exponentials on MUFU
-// (CMPX_FMHA_EMU of every 8 column pairs on the FMA pipe instead), 16-bit packing per pair.
+// (CMPX_FMHA_EMU of every 8 column pairs on the FMA pipe instead).
 template <bool BF16>
-__device__ __forceinline__ float exp_pass(const float* s, float sl2, float nmb, uint32_t p_tm) {
+__device__ __forceinline__ void exp_chunk(const float* s, int q, uint64_t sl2x2, uint64_t nmbx2,
+                                          uint64_t& la, uint64_t& lb, uint32_t (&pk)[16]) {
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {
+    const int cc = q * 16 + c;
+    const uint64_t xv = f2_fma(f2_pack(s[2 * cc], s[2 * cc + 1]), sl2x2, nmbx2);
+    float p0, p1;
+    if ((cc & 7) >= 8 - CMPX_FMHA_EMU) {
+      f2_unpack(exp2_poly3_x2(xv), p0, p1);
+    } else {
+      float x0, x1;
+      f2_unpack(xv, x0, x1);
+      p0 = ex2_approx(x0);
+      p1 = ex2_approx(x1);
+    }
+    if (c & 1)
+      lb = f2_add(lb, f2_pack(p0, p1));
+    else
+      la = f2_add(la, f2_pack(p0, p1));
+    pk[c] = BF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
+  }
+}
+
+// One pass over a row's 128 scores: the four chunks' P stored to TMEM (16 columns each at p_tm);
+// returns the row sum of p.  before_store() runs after the first chunk is computed and before
+// anything is stored: the wait for the P buffer to be free (the previous PV) overlaps the first
+// quarter of the exponentials instead of preceding them.
+template <bool BF16, class BeforeStore>
+__device__ __forceinline__ float exp_pass(const float* s, float sl2, float nmb, uint32_t p_tm,
+                                          BeforeStore&& before_store) {
   uint64_t la = f2_pack(0.f, 0.f), lb = la;
   const uint64_t sl2x2 = f2_pack(sl2, sl2), nmbx2 = f2_pack(nmb, nmb);
+  uint32_t pk[16];
+  exp_chunk<BF16>(s, 0, sl2x2, nmbx2, la, lb, pk);
+  before_store();
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    uint32_t pk[16];
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      const int cc = q * 16 + c;
-      const uint64_t xv = f2_fma(f2_pack(s[2 * cc], s[2 * cc + 1]), sl2x2, nmbx2);
-      float p0, p1;
-      if ((cc & 7) >= 8 - CMPX_FMHA_EMU) {
-        f2_unpack(exp2_poly3_x2(xv), p0, p1);
-      } else {
-        float x0, x1;
-        f2_unpack(xv, x0, x1);
-        p0 = ex2_approx(x0);
-        p1 = ex2_approx(x1);
-      }
-      if (c & 1)
-        lb = f2_add(lb, f2_pack(p0, p1));
-      else
-        la = f2_add(la, f2_pack(p0, p1));
-      pk[c] = BF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
-    }
+    if (q > 0) exp_chunk<BF16>(s, q, sl2x2, nmbx2, la, lb, pk);
     tmem_st16(p_tm + q * 16, pk);
   }
   float a0, a1;
@@ -447,25 +460,28 @@ __global__ void __launch_bounds__(352, 1)
           for (int c = 0; c < 128; ++c)
             if (c >= lim) s[c] = masked;
         }
-        // P_t and O_t are free once PV_t(j-1) has completed (usually long done by now).
-        if (j > 0) {
-          if (!mbar_wait_all(bar(C::B_PVDONE + t), (n_pvdone++) & 1u, ctl)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after_sync();
-        }
         // Fast pass against the running max m_run.  Any p above 2^8 (a key more than 8 above
         // m_run in log2 units) forces the tile's row sum above 256, so a row sum <= 256 proves the
         // stale max is usable (exact: O, l and P share it).  Otherwise -- and on a row's first
         // tile, where m_run is still -inf -- the warp takes the slow path: exact tile max, new
         // running max, P recomputed, l and O rescaled.  After a slow pass m_run is the true running
         // max, so later triggers are rare.  (Key 0 is never masked, so m_run is finite after j = 0.)
+        // P_t and O_t are free once PV_t(j-1) has completed: the fast pass waits for that between
+        // computing and storing its first half (no wait at j = 0: the previous item's epilogue
+        // already waited for its last PV).
         float l_tile = 0.f;
         float alpha = 1.f;
         bool slow = (j == 0);
         if (!slow) {
-          l_tile = exp_pass<BF16>(s, sl2, -m_run, p_tm);
+          bool pv_ok = true;
+          l_tile = exp_pass<BF16>(s, sl2, -m_run, p_tm, [&] {
+            pv_ok = mbar_wait_all(bar(C::B_PVDONE + t), (n_pvdone++) & 1u, ctl);
+            tc_fence_after_sync();
+          });
+          if (!pv_ok) {
+            ok = false;
+            break;
+          }
           slow = __any_sync(0xffffffffu, !(l_tile <= 256.f));
           if (slow) tmem_st_wait();  // the redo overwrites the fast pass's P columns
         }
@@ -475,7 +491,7 @@ __global__ void __launch_bounds__(352, 1)
             alpha = ex2_approx(m_run - m_tile);
             m_run = m_tile;
           }
-          l_tile = exp_pass<BF16>(s, sl2, -m_run, p_tm);
+          l_tile = exp_pass<BF16>(s, sl2, -m_run, p_tm, [] {});
           if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
             for (int c = 0; c < DP / 32; ++c) {
