@@ -197,9 +197,16 @@ class ClockSampler:
             except Exception:  # noqa: BLE001
                 pass
             inside = [r for r in self.samples if self.t_start and self.t_stop and self.t_start <= r[0] <= self.t_stop]
+            source = f"nvml every {self.PERIOD_S * 1e3:.0f} ms"
+            if not inside and self.samples and self.t_start and self.t_stop:
+                # timed region shorter than the sampling period: the samples just before and after it
+                before = [r for r in self.samples if r[0] < self.t_start][-1:]
+                after = [r for r in self.samples if r[0] > self.t_stop][:1]
+                inside = before + after
+                source += " (timed region shorter than the period: nearest samples before/after)"
             if not inside:
                 return None
-            return self._summary(inside, f"nvml every {self.PERIOD_S * 1e3:.0f} ms")
+            return self._summary(inside, source)
         if not self.proc:
             return None
         time.sleep(0.25)
