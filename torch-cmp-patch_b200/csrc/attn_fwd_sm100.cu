@@ -37,8 +37,13 @@
 #include "cmpx_internal.h"
 #include "cmpx_ptx.cuh"
 
+// Column pairs (of every 8) whose exp2 runs on the FMA pipe (polynomial) instead of MUFU, for
+// head dims <= 64 and for larger ones.
+#ifndef CMPX_FMHA_EMU64
+#define CMPX_FMHA_EMU64 0
+#endif
 #ifndef CMPX_FMHA_EMU
-#define CMPX_FMHA_EMU 0  // column pairs (of every 8) whose exp2 runs on the FMA pipe (polynomial)
+#define CMPX_FMHA_EMU 0
 #endif
 
 namespace cmpx {
@@ -80,6 +85,7 @@ struct FmhaCfg {
   // Warp roles: 0-3 softmax/epilogue of tile 0, 4-7 of tile 1 (thread = row), 8 TMA producer
   // (and work fetch), 9 QK issuer (and TMEM owner), 10 PV issuer.
   static constexpr int THREADS = 352;
+  static constexpr int EMU = DP <= 64 ? CMPX_FMHA_EMU64 : CMPX_FMHA_EMU;
   static constexpr int W_TMA = 8, W_MMA = 9, W_PV = 10;
   static constexpr int ITEM_CONSUMERS = 2 + 8;  // lane 0 of each MMA warp and of each softmax warp
 };
@@ -103,9 +109,9 @@ struct FmhaParams {
 
 // One chunk (16 column pairs = 32 keys) of a row's exponentials: p = 2^(s*sl2 + nmb) packed to
 // 16-bit pairs in pk, the row sum accumulated in la/lb.  x = s*sl2 + nmb is formed and the sum
-// accumulated two keys at a time with packed f32x2 arithmetic; exponentials on MUFU
-// (CMPX_FMHA_EMU of every 8 column pairs on the FMA pipe instead).
-template <bool BF16>
+// accumulated two keys at a time with packed f32x2 arithmetic; exponentials on MUFU (EMU of every
+// 8 column pairs on the FMA pipe instead).
+template <bool BF16, int EMU>
 __device__ __forceinline__ void exp_chunk(const float* s, int q, uint64_t sl2x2, uint64_t nmbx2,
                                           uint64_t& la, uint64_t& lb, uint32_t (&pk)[16]) {
 #pragma unroll
@@ -113,7 +119,7 @@ __device__ __forceinline__ void exp_chunk(const float* s, int q, uint64_t sl2x2,
     const int cc = q * 16 + c;
     const uint64_t xv = f2_fma(f2_pack(s[2 * cc], s[2 * cc + 1]), sl2x2, nmbx2);
     float p0, p1;
-    if ((cc & 7) >= 8 - CMPX_FMHA_EMU) {
+    if ((cc & 7) >= 8 - EMU) {
       f2_unpack(exp2_poly3_x2(xv), p0, p1);
     } else {
       float x0, x1;
@@ -133,17 +139,17 @@ __device__ __forceinline__ void exp_chunk(const float* s, int q, uint64_t sl2x2,
 // returns the row sum of p.  before_store() runs after the first chunk is computed and before
 // anything is stored: the wait for the P buffer to be free (the previous PV) overlaps the first
 // quarter of the exponentials instead of preceding them.
-template <bool BF16, class BeforeStore>
+template <bool BF16, int EMU, class BeforeStore>
 __device__ __forceinline__ float exp_pass(const float* s, float sl2, float nmb, uint32_t p_tm,
                                           BeforeStore&& before_store) {
   uint64_t la = f2_pack(0.f, 0.f), lb = la;
   const uint64_t sl2x2 = f2_pack(sl2, sl2), nmbx2 = f2_pack(nmb, nmb);
   uint32_t pk[16];
-  exp_chunk<BF16>(s, 0, sl2x2, nmbx2, la, lb, pk);
+  exp_chunk<BF16, EMU>(s, 0, sl2x2, nmbx2, la, lb, pk);
   before_store();
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    if (q > 0) exp_chunk<BF16>(s, q, sl2x2, nmbx2, la, lb, pk);
+    if (q > 0) exp_chunk<BF16, EMU>(s, q, sl2x2, nmbx2, la, lb, pk);
     tmem_st16(p_tm + q * 16, pk);
   }
   float a0, a1;
@@ -474,7 +480,7 @@ __global__ void __launch_bounds__(352, 1)
         bool slow = (j == 0);
         if (!slow) {
           bool pv_ok = true;
-          l_tile = exp_pass<BF16>(s, sl2, -m_run, p_tm, [&] {
+          l_tile = exp_pass<BF16, C::EMU>(s, sl2, -m_run, p_tm, [&] {
             pv_ok = mbar_wait_all(bar(C::B_PVDONE + t), (n_pvdone++) & 1u, ctl);
             tc_fence_after_sync();
           });
@@ -491,7 +497,7 @@ __global__ void __launch_bounds__(352, 1)
             alpha = ex2_approx(m_run - m_tile);
             m_run = m_tile;
           }
-          l_tile = exp_pass<BF16>(s, sl2, -m_run, p_tm, [] {});
+          l_tile = exp_pass<BF16, C::EMU>(s, sl2, -m_run, p_tm, [] {});
           if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
             for (int c = 0; c < DP / 32; ++c) {
@@ -631,13 +637,12 @@ const char* fmha_sm100_plan(const cmpx_attn_desc* d, int* status) {
     *status = CMPX_ERR_UNSUPPORTED_SHAPE;
     return "none";
   }
+  if (fmha_short_eligible(d)) return fmha_short_name(d);
   const bool bf = d->dtype == CMPX_BF16;
   if (d->head_dim <= 64)
     return bf ? "fmha_sm100<bf16,D64,2x128q,128kv,6st,persistent>" : "fmha_sm100<f16,D64,2x128q,128kv,6st,persistent>";
   return bf ? "fmha_sm100<bf16,D128,2x128q,128kv,4st,persistent>" : "fmha_sm100<f16,D128,2x128q,128kv,4st,persistent>";
 }
-
-namespace {
 
 bool make_bhsd_map(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, int64_t D, int64_t L,
                    int64_t H, int64_t B, const int64_t* st, uint32_t box_rows) {
@@ -648,6 +653,8 @@ bool make_bhsd_map(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, in
   const uint32_t box[4] = {64, box_rows, 1, 1};
   return encode_tmap(map, dt, 4, ptr, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
+
+namespace {
 
 template <int DP, bool BF16>
 int launch_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
@@ -700,6 +707,7 @@ int launch_fmha_sm100(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   fmha_sm100_plan(d, &st);
   if (st != CMPX_OK) return st;
   if (d->len_q == 0) return CMPX_OK;
+  if (fmha_short_eligible(d)) return launch_fmha_short(d, ctx);
   const bool bf = d->dtype == CMPX_BF16;
   if (d->head_dim <= 64) return bf ? launch_typed<64, true>(d, ctx) : launch_typed<64, false>(d, ctx);
   return bf ? launch_typed<128, true>(d, ctx) : launch_typed<128, false>(d, ctx);

@@ -23,10 +23,19 @@ bool encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const vo
                  const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                  CUtensorMapSwizzle swizzle);
 
+// 4-D TMA map over a [B, H, L, D] 16-bit tensor with element strides st = {b, h, l} (D
+// contiguous): box = 64 head-dim elements (128 bytes, 128-byte swizzle) x box_rows rows.
+bool make_bhsd_map(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, int64_t D, int64_t L,
+                   int64_t H, int64_t B, const int64_t* st, uint32_t box_rows);
+
 // ---- attention ----
 // Tile-table lookups: return a static name and whether the kernel supports the call.
 const char* fmha_sm100_plan(const cmpx_attn_desc* d, int* status);
 int launch_fmha_sm100(const cmpx_attn_desc* d, const LaunchCtx& ctx);
+// Short key sequences (non-causal, 1 <= Lk <= 128): one key tile, Q tiles streamed.
+bool fmha_short_eligible(const cmpx_attn_desc* d);
+const char* fmha_short_name(const cmpx_attn_desc* d);
+int launch_fmha_short(const cmpx_attn_desc* d, const LaunchCtx& ctx);
 
 const char* attn_f32_plan(const cmpx_attn_desc* d, int* status);
 int launch_attn_f32(const cmpx_attn_desc* d, const LaunchCtx& ctx);
