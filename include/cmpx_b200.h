@@ -132,6 +132,25 @@ CMPX_API int cmpx_attn_fwd_noalloc(const cmpx_attn_desc* desc, void* stream);
 /* Batched matmul.  Replaces cmpext3.ops.bmm (src/main.cpp:2307-2309). */
 CMPX_API int cmpx_bmm(const cmpx_bmm_desc* desc, void* stream);
 
+/* Row softmax over the last dimension:  y[r, :] = softmax(x[r, :]) for r < rows, computed in
+ * fp32 (max, exp, sum) and rounded once to the output dtype (dtype in == dtype out), which is what
+ * torch.softmax(x, dim=-1) returns for a fp16 / bf16 / fp32 tensor.  Rows are `cols` contiguous
+ * elements apart by x_row_stride / y_row_stride (elements).
+ * No counterpart among the reference's native ops: the reference leaves softmax stock
+ * (cmpext3/__init__.py:133-138).  It serves the einsum-attention chain
+ * einsum('bhid,bhjd->bhij') -> softmax(-1) -> einsum('bhij,bhjd->bhid') (cmpext3/einsum_ops.py:69-121),
+ * whose softmax over the score tensor dominates that chain when it runs stock. */
+typedef struct cmpx_softmax_desc {
+  const void* x;
+  void* y;
+  int64_t rows, cols;
+  int64_t x_row_stride, y_row_stride;
+  int32_t dtype; /* cmpx_dtype */
+  int32_t reserved;
+} cmpx_softmax_desc;
+
+CMPX_API int cmpx_softmax_rows(const cmpx_softmax_desc* desc, void* stream);
+
 /* Name of the tile-table entry a call would use, written into buf (NUL-terminated).
  * Returns CMPX_OK or the status the call itself would return.  Replaces the per-signature
  * decision record of the reference's runtime autoselect (cmpext3/autoselect.py:290-364),

@@ -43,6 +43,13 @@ def einsum(eq: str, *operands: torch.Tensor) -> torch.Tensor:
     return _EINSUM(eq, *operands)
 
 
+def softmax(x: torch.Tensor, dim: int = -1) -> torch.Tensor:
+    """Stock CPU softmax: the reference never patches softmax (cmpext3/__init__.py:133-138), so
+    its einsum-attention chain always runs this op."""
+    assert x.device.type == "cpu"
+    return _SOFTMAX(x, dim=dim)
+
+
 def einsum_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
     """The einsum-routed attention workload: scores einsum -> softmax (stock) -> values einsum."""
     s = einsum("bhid,bhjd->bhij", q, k)

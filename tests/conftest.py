@@ -43,9 +43,13 @@ import torch.nn.functional as F  # noqa: E402
 
 import cmpext3  # noqa: E402
 
-STOCK_UNPATCHED = {(F, "softmax"): F.softmax, (torch, "softmax"): torch.softmax}
+# Ops this package leaves alone (the reference's other patches -- linear, conv, norms -- are out of
+# this hot path's scope).  softmax is patched, but diverts only the attention chain's softmax.
+STOCK_UNPATCHED = {(F, "linear"): F.linear, (torch, "baddbmm"): torch.baddbmm,
+                   (F, "layer_norm"): F.layer_norm}
+STOCK_SOFTMAX = {"torch": torch.softmax, "F": F.softmax, "Tensor": torch.Tensor.softmax}
 
-NATIVE_OPS = ["attention", "bmm", "attention_plan", "bmm_plan"]
+NATIVE_OPS = ["attention", "bmm", "attention_plan", "bmm_plan", "softmax"]
 
 
 def pytest_configure(config):

@@ -11,7 +11,7 @@ import torch
 import torch.nn.functional as F
 
 import cmpext3
-from conftest import STOCK_UNPATCHED, force_eligible
+from conftest import STOCK_SOFTMAX, STOCK_UNPATCHED, force_eligible
 
 
 def assert_called_once_with_tensors(mock_fn, *expected_args, **expected_kwargs):
@@ -237,6 +237,80 @@ class TestBmm:
         b = torch.randn(2, 128, 64)
         torch.bmm(a, b)
         native.bmm.assert_not_called()
+
+
+class TestSoftmax:
+    """softmax is diverted only for the last dimension of a tensor a patched einsum / bmm / matmul
+    returned (the middle step of an attention chain); every other softmax runs stock."""
+
+    CALLS = {
+        "torch": lambda x, **kw: torch.softmax(x, -1, **kw),
+        "F": lambda x, **kw: F.softmax(x, dim=-1, **kw),
+        "Tensor": lambda x, **kw: x.softmax(-1, **kw),
+    }
+
+    @pytest.mark.parametrize("form", ["torch", "F", "Tensor"])
+    def test_softmax_of_einsum_scores_routes_to_native(self, patched, native, monkeypatch, form):
+        force_eligible(monkeypatch)
+        q, k = torch.randn(1, 2, 64, 32), torch.randn(1, 2, 96, 32)
+        native.bmm.return_value = torch.zeros(2, 64, 96)
+        s = torch.einsum("bhid,bhjd->bhij", q, k)
+        native.softmax.return_value = torch.ones(1, 2, 64, 96)
+        got = self.CALLS[form](s)
+        native.softmax.assert_called_once()
+        assert native.softmax.call_args[0][0] is s and native.softmax.call_args[0][1] == -1
+        assert torch.equal(got, torch.ones(1, 2, 64, 96))
+
+    @pytest.mark.parametrize("form", ["torch", "F", "Tensor"])
+    def test_softmax_of_any_other_tensor_is_stock(self, patched, native, monkeypatch, form):
+        force_eligible(monkeypatch)
+        x = torch.randn(3, 5, 7)
+        got = self.CALLS[form](x)
+        native.softmax.assert_not_called()
+        assert torch.equal(got, STOCK_SOFTMAX["torch"](x, -1))
+
+    def test_other_dim_or_dtype_is_stock(self, patched, native, monkeypatch):
+        force_eligible(monkeypatch)
+        native.bmm.return_value = torch.randn(2, 8, 6)
+        s = torch.bmm(torch.randn(2, 8, 4), torch.randn(2, 4, 6))
+        torch.softmax(s, 1)
+        torch.softmax(s, -1, dtype=torch.float64)
+        F.softmax(s)  # implicit dim: stock (with torch's warning)
+        native.softmax.assert_not_called()
+
+    def test_declined_native_softmax_falls_back_to_stock(self, patched, native, monkeypatch):
+        force_eligible(monkeypatch)
+        native.bmm.return_value = torch.randn(2, 8, 6)
+        s = torch.bmm(torch.randn(2, 8, 4), torch.randn(2, 4, 6))
+        native.softmax.side_effect = RuntimeError("outside the tile table")
+        got = torch.softmax(s, -1)
+        assert torch.allclose(got, STOCK_SOFTMAX["torch"](s, -1))
+
+    def test_einsum_softmax_einsum_chain(self, patched, native, monkeypatch):
+        force_eligible(monkeypatch)
+        q, k, v = torch.randn(1, 2, 64, 32), torch.randn(1, 2, 96, 32), torch.randn(1, 2, 96, 32)
+        native.bmm.side_effect = lambda a, b: a @ b  # Tensor.__matmul__ is not patched
+        native.softmax.side_effect = lambda x, dim: STOCK_SOFTMAX["torch"](x, dim)
+        s = torch.einsum("bhid,bhjd->bhij", q, k)
+        o = torch.einsum("bhij,bhjd->bhid", torch.softmax(s, dim=-1), v)
+        assert native.bmm.call_count == 2 and native.softmax.call_count == 1
+        ref = STOCK_SOFTMAX["torch"](q @ k.transpose(-1, -2), -1) @ v
+        assert torch.allclose(o, ref, atol=1e-5)
+
+    def test_disable_restores_every_softmax(self):
+        cmpext3.enable()
+        cmpext3.disable()
+        assert torch.softmax is STOCK_SOFTMAX["torch"]
+        assert F.softmax is STOCK_SOFTMAX["F"]
+        assert torch.Tensor.softmax is STOCK_SOFTMAX["Tensor"]
+
+    def test_dead_products_leave_the_registry(self, patched, native, monkeypatch):
+        force_eligible(monkeypatch)
+        native.bmm.side_effect = lambda a, b: torch.zeros(a.shape[0], a.shape[1], b.shape[2])
+        before = len(cmpext3._PRODUCED)
+        for _ in range(50):
+            torch.bmm(torch.randn(2, 3, 4), torch.randn(2, 4, 5))
+        assert len(cmpext3._PRODUCED) <= before + 1
 
 
 class TestEinsum:

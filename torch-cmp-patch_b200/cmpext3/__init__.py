@@ -9,6 +9,14 @@ auto-run at :822-823 of the reference):
     torch.matmul (2D / 3D)          -> cmpext3.ops.bmm
     torch.einsum                    -> einsum_ops planner -> torch.bmm (patched)
 
+and, beyond the reference, the middle step of an einsum / bmm attention chain
+(``einsum('bhid,bhjd->bhij') -> softmax(-1) -> einsum('bhij,bhjd->bhid')``):
+
+    torch.softmax / F.softmax / Tensor.softmax over the last dimension of a tensor that one of the
+    patched einsum / bmm / matmul calls above returned -> cmpext3.ops.softmax
+
+(every other softmax stays stock, as in the reference, which does not patch softmax at all).
+
 with the reference's wrapper signatures, gates and stock bail-outs: stock PyTorch runs when autograd
 is live for an input, when a tensor is not a CUDA fp16/fp32/bf16 tensor, when SDPA gets an
 ``attn_mask`` or ``dropout_p > 0`` or a non-4D query, when bmm/matmul get ``out=`` or mixed dtypes, and
@@ -24,8 +32,8 @@ clocks or power limits.
     import cmpext3            # patches on import
     cmpext3.disable(); cmpext3.enable()
 
-Set CMPEXT3_AUTOPATCH=0 to import without patching; CMPEXT3_DISABLE_OPS=attention,bmm,matmul,einsum
-pins named ops to stock; CMPEXT3_VERBOSE=1 logs each new signature's tile-table entry;
+Set CMPEXT3_AUTOPATCH=0 to import without patching; CMPEXT3_DISABLE_OPS=attention,bmm,matmul,einsum,
+softmax pins named ops to stock; CMPEXT3_VERBOSE=1 logs each new signature's tile-table entry;
 cmpext3.autoselect_report() lists them.
 
 SAFETY: the kernels are forward-only (no autograd); every patched call falls back to stock when
@@ -34,6 +42,7 @@ autograd is live, as in the reference.
 from __future__ import annotations
 
 import os
+import weakref
 from typing import Any, Callable
 
 import torch
@@ -166,8 +175,8 @@ def _patched_matmul(input, other, *, out=None):
         plan = lambda: _C.bmm_plan(input, other)  # noqa: E731
     else:
         return orig(input, other)
-    return _dispatch("matmul", input, (input.shape, input.dtype, other.shape),
-                     native, lambda: orig(input, other), plan)
+    return _note_product(_dispatch("matmul", input, (input.shape, input.dtype, other.shape),
+                                   native, lambda: orig(input, other), plan))
 
 
 # Many tiny matrices (M*K*N <= 32768): a broadcast multiply + sum, chunked over the batch, as in
@@ -203,10 +212,32 @@ def _patched_bmm(input, mat2, *, out=None):
         return _dispatch("bmm_small", input, (input.shape, input.dtype, mat2.shape),
                          lambda: _small_bmm(input, mat2),
                          lambda: orig(input, mat2))
-    return _dispatch("bmm", input, (input.shape, input.dtype, mat2.shape),
-                     lambda: _C.bmm(input, mat2),
-                     lambda: orig(input, mat2),
-                     lambda: _C.bmm_plan(input, mat2))
+    return _note_product(_dispatch("bmm", input, (input.shape, input.dtype, mat2.shape),
+                                   lambda: _C.bmm(input, mat2),
+                                   lambda: orig(input, mat2),
+                                   lambda: _C.bmm_plan(input, mat2)))
+
+
+# Tensors returned by the patched einsum / bmm / matmul, keyed by id and held weakly: a softmax
+# over the last dimension of one of them is the middle step of an attention chain, and only such a
+# softmax is diverted to the native row-softmax kernel.
+_PRODUCED: dict[int, weakref.ref] = {}
+
+
+def _note_product(t: Any) -> Any:
+    if isinstance(t, torch.Tensor):
+        key = id(t)
+
+        def _forget(ref, key=key):
+            if _PRODUCED.get(key) is ref:
+                del _PRODUCED[key]
+        _PRODUCED[key] = weakref.ref(t, _forget)
+    return t
+
+
+def _is_product(t: Any) -> bool:
+    ref = _PRODUCED.get(id(t))
+    return ref is not None and ref() is t
 
 
 def _patched_einsum(*args, **kwargs):
@@ -224,10 +255,39 @@ def _patched_einsum(*args, **kwargs):
         return orig(*args)
     if einsum_ops.supported(eq, operands) is not None:
         return orig(*args)
-    return _dispatch("einsum", operands[0],
-                     (eq.replace(" ", ""), tuple(tuple(t.shape) for t in operands)),
-                     lambda: einsum_ops.einsum(eq, operands, bmm=torch.bmm),
-                     lambda: orig(*args))
+    return _note_product(_dispatch("einsum", operands[0],
+                                   (eq.replace(" ", ""), tuple(tuple(t.shape) for t in operands)),
+                                   lambda: einsum_ops.einsum(eq, operands, bmm=torch.bmm),
+                                   lambda: orig(*args)))
+
+
+def _softmax(input, dim, dtype, stock_call: Callable):
+    """Native row softmax for the last dimension of a tensor a patched einsum / bmm / matmul
+    returned (same dtype out); stock otherwise."""
+    if (isinstance(input, torch.Tensor) and dim is not None and (dtype is None or dtype == input.dtype)
+            and input.dim() > 0 and isinstance(dim, int) and dim in (-1, input.dim() - 1)
+            and _is_product(input) and _grad_safe(input) and _usable(input)):
+        return _dispatch("softmax", input, (tuple(input.shape), input.dtype),
+                         lambda: _C.softmax(input, -1), stock_call)
+    return stock_call()
+
+
+def _patched_torch_softmax(input, dim, dtype=None, **kwargs):
+    orig = _ORIGINALS[(torch, "softmax")]
+    if kwargs:
+        return orig(input, dim, dtype=dtype, **kwargs)
+    return _softmax(input, dim, dtype, lambda: orig(input, dim, dtype=dtype))
+
+
+def _patched_f_softmax(input, dim=None, _stacklevel=3, dtype=None):
+    orig = _ORIGINALS[(F, "softmax")]
+    return _softmax(input, dim, dtype,
+                    lambda: orig(input, dim=dim, _stacklevel=_stacklevel, dtype=dtype))
+
+
+def _patched_tensor_softmax(self, dim, dtype=None):
+    orig = _ORIGINALS[(torch.Tensor, "softmax")]
+    return _softmax(self, dim, dtype, lambda: orig(self, dim, dtype=dtype))
 
 
 def _patched_sdpa(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=False,
@@ -260,6 +320,9 @@ def enable() -> None:
     _install(torch, "einsum", _patched_einsum)
     if hasattr(F, "scaled_dot_product_attention"):
         _install(F, "scaled_dot_product_attention", _patched_sdpa)
+    _install(torch, "softmax", _patched_torch_softmax)
+    _install(F, "softmax", _patched_f_softmax)
+    _install(torch.Tensor, "softmax", _patched_tensor_softmax)
     _ENABLED = True
 
 

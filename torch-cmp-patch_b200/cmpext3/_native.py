@@ -73,6 +73,13 @@ class BmmDesc(ctypes.Structure):
     ]
 
 
+class SoftmaxDesc(ctypes.Structure):
+    _fields_ = [("x", ctypes.c_void_p), ("y", ctypes.c_void_p),
+                ("rows", ctypes.c_int64), ("cols", ctypes.c_int64),
+                ("x_row_stride", ctypes.c_int64), ("y_row_stride", ctypes.c_int64),
+                ("dtype", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+
+
 def _load() -> ctypes.CDLL:
     if not LIBRARY_PATH.exists():
         raise ImportError(
@@ -89,6 +96,8 @@ def _load() -> ctypes.CDLL:
     L.cmpx_attn_plan.restype = ctypes.c_int
     L.cmpx_bmm_plan.argtypes = [ctypes.POINTER(BmmDesc), ctypes.c_char_p, ctypes.c_size_t]
     L.cmpx_bmm_plan.restype = ctypes.c_int
+    L.cmpx_softmax_rows.argtypes = [ctypes.POINTER(SoftmaxDesc), ctypes.c_void_p]
+    L.cmpx_softmax_rows.restype = ctypes.c_int
     L.cmpx_status_str.argtypes = [ctypes.c_int]
     L.cmpx_status_str.restype = ctypes.c_char_p
     L.cmpx_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint)]
@@ -320,6 +329,38 @@ def bmm_plan(input, mat2) -> str:
     if st != OK:
         raise CmpxError("bmm plan", st)
     return buf.value.decode()
+
+
+# ---------------------------------------------------------------------------------------------
+# softmax over the last dimension (the einsum-attention chain's middle step)
+# ---------------------------------------------------------------------------------------------
+
+def softmax(input, dim=-1):
+    """torch.softmax(input, dim=-1) on the sm_100a row-softmax kernel (fp32 arithmetic, output in
+    the input's dtype).  Only the last dimension; the rows must be contiguous."""
+    if not isinstance(input, torch.Tensor):
+        raise TypeError("input must be a Tensor")
+    if not input.is_cuda or input.dtype not in _DTYPE:
+        raise RuntimeError("input must be a CUDA float32/float16/bfloat16 tensor")
+    if input.dim() == 0 or dim not in (-1, input.dim() - 1):
+        raise RuntimeError("only the last dimension is supported")
+    x = input if input.is_contiguous() else input.contiguous()
+    y = torch.empty_like(x, memory_format=torch.contiguous_format)
+    if x.numel() == 0:
+        return y
+    cols = x.shape[-1]
+    d = SoftmaxDesc()
+    d.x, d.y = x.data_ptr(), y.data_ptr()
+    d.rows, d.cols = x.numel() // cols, cols
+    d.x_row_stride = d.y_row_stride = cols
+    d.dtype = _DTYPE[x.dtype]
+    d.reserved = 0
+    with torch.cuda.device(x.device):
+        st = lib.cmpx_softmax_rows(ctypes.byref(d), _stream_handle(x.device))
+    if st != OK:
+        raise CmpxError("softmax", st)
+    _post_check()
+    return y
 
 
 def selftest_wait_timeout(timeout_ns: int, device=None) -> None:

@@ -255,6 +255,17 @@ int cmpx_bmm(const cmpx_bmm_desc* desc, void* stream) {
   return launch_bmm_sm100(desc, ctx);
 }
 
+int cmpx_softmax_rows(const cmpx_softmax_desc* desc, void* stream) {
+  int st = CMPX_OK;
+  softmax_rows_plan(desc, &st);
+  if (st != CMPX_OK) return st;
+  if (desc->rows == 0) return CMPX_OK;
+  LaunchCtx ctx;
+  st = device_ctx(&ctx, static_cast<cudaStream_t>(stream));
+  if (st != CMPX_OK) return st;
+  return launch_softmax_rows(desc, ctx);
+}
+
 int cmpx_device_status(unsigned int* flags) {
   if (!flags) return CMPX_ERR_INVALID_ARGUMENT;
   LaunchCtx ctx;

@@ -47,6 +47,10 @@ int launch_bmm_sm100(const cmpx_bmm_desc* d, const LaunchCtx& ctx);
 const char* bmm_f32_plan(const cmpx_bmm_desc* d, int* status);
 int launch_bmm_f32(const cmpx_bmm_desc* d, const LaunchCtx& ctx);
 
+// ---- row softmax (einsum-attention chain) ----
+const char* softmax_rows_plan(const cmpx_softmax_desc* d, int* status);
+int launch_softmax_rows(const cmpx_softmax_desc* d, const LaunchCtx& ctx);
+
 // ---- self test ----
 int launch_wait_selftest(uint64_t timeout_ns, const LaunchCtx& ctx);
 
