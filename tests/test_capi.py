@@ -135,7 +135,7 @@ def _bplan(d):
 
 def test_bmm_plan_for_the_einsum_attention_shapes():
     st, name = _bplan(_bmm(64, 2048, 2048, 64, bt=True))     # scores: B = K^T view (K-major)
-    assert st == 0 and "128x256" in name and "B:k-major" in name
+    assert st == 0 and "128x128" in name and "B:k-major" in name
     st, name = _bplan(_bmm(64, 2048, 64, 2048, bt=False))    # values: B = V (N-major)
     assert st == 0 and "128x64" in name and "B:mn-major" in name
     st, name = _bplan(_bmm(2, 33, 45, 17, dtype=0))

@@ -5,18 +5,22 @@
 // item from a host loop (gemm_fp32_ga100_kernel, src/cuda/fp32_matmul.cu:31-184; fp16 uses
 // gemm_fp16_sm75 with half2 accumulation, src/cuda/fp16_matmul.cu:143-367).  Here:
 //
-//   * one launch covers every batch item (grid z) and every 128 x BN output tile;
+//   * one persistent launch: a CTA per SM walks the 128 x BN output tiles of every batch item
+//     (flattened, n fastest);
 //   * operands are read in place through rank-3 TMA maps, row-major OR column-major (a transposed
 //     view such as K^T from an einsum plan is a K-major B operand: no copy);
-//   * warp 0 streams 128x64 A and 64xBN B tiles through a ring of 128-byte-swizzled stages,
-//     warp 1 issues tcgen05.mma (M=128, N=BN, K=16 steps) into an fp32 TMEM accumulator,
-//     warps 2-5 drain TMEM -> fp32 -> 16-bit -> swizzled shared staging -> TMA store;
-//   * fp32 accumulation over all of K (the reference's fp16 path accumulates in half);
-//   * ~96 KB shared and <= 256 TMEM columns per CTA so two CTAs share an SM: one CTA's epilogue
-//     (the HBM-bound part for the attention-score shapes) overlaps the other's main loop.
+//   * warp 0 streams 128x64 A and 64xBN B tiles through a ring of 128-byte-swizzled stages that
+//     runs across tile boundaries; warp 1 issues tcgen05.mma (M=128, N=BN, K=16 steps) into one of
+//     two fp32 TMEM accumulators, so tile i+1's MMAs run while tile i is drained; warps 2-9 drain
+//     TMEM -> fp32 -> 16-bit -> swizzled shared staging -> TMA stores (two warps per TMEM lane
+//     quarter, each taking every other 64-column chunk);
+//   * fp32 accumulation over all of K (the reference's fp16 path accumulates in half).
+//   For the attention-score shape (K = 64: one k-block per tile, 64 KB of output per tile) the
+//   kernel is an HBM write stream; the double accumulator keeps the stores going back to back.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <array>
 #include <cmath>
 #include <mutex>
@@ -33,25 +37,33 @@ struct BmmCfg {
   static constexpr int A_BYTES = BM * BK * 2;       // 16 KB
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = BN == 256 ? 2 : (BN == 128 ? 3 : 4);
-  static constexpr int OFF_BAR = STAGES * STAGE_BYTES;
-  // barriers: full[STAGES], empty[STAGES], acc, drain
-  static constexpr int NBAR = 2 * STAGES + 2;
+  static constexpr int STAGES = BN == 128 ? 4 : 6;
+  static constexpr int CHUNKS = BN / 64;            // 64-column (128-byte) chunks of a C tile
+  static constexpr int SLOT_BYTES = 32 * 128;       // one warp's 32 rows of one chunk
+  static constexpr int STAGING_BYTES = 4 * CHUNKS * SLOT_BYTES;      // [quarter][chunk] slots
+  static constexpr int OFF_STAGING = STAGES * STAGE_BYTES;           // two staging buffers
+  static constexpr int OFF_BAR = OFF_STAGING + 2 * STAGING_BYTES;
+  static constexpr int B_FULL = 0, B_EMPTY = STAGES;                 // [STAGES] each
+  static constexpr int B_ACCF = 2 * STAGES, B_ACCE = 2 * STAGES + 2;  // [2] each
+  static constexpr int B_DRAIN = 2 * STAGES + 4;
+  static constexpr int NBAR = 2 * STAGES + 5;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
-  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
-  static_assert(STAGES * STAGE_BYTES >= BM * BN * 2, "epilogue staging must fit in the stages");
+  static constexpr int TMEM_COLS = 2 * BN;          // two accumulators (128 / 256 columns)
+  static constexpr int THREADS = 320;               // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+  static constexpr int EPI_WARPS = 8;
 };
 
 struct BmmParams {
   int m, n, k;
   int n_kblocks;
+  int tiles_m, tiles_n, n_tiles;
   unsigned long long timeout_ns;
   unsigned int* dev_flags;
 };
 
 template <int BN, bool A_MN, bool B_MN, bool BF16>
-__global__ void __launch_bounds__(192, 2)
+__global__ void __launch_bounds__(320, 1)
     bmm_sm100_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                      const __grid_constant__ CUtensorMap tm_c, const BmmParams p) {
   using C = BmmCfg<BN>;
@@ -61,22 +73,29 @@ __global__ void __launch_bounds__(192, 2)
   uint8_t* smem = smem_raw + (base - raw_base);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN;
-  const int m0 = blockIdx.y * C::BM;
-  const int z = blockIdx.z;
 
   auto bar = [&](int i) -> uint32_t { return base + C::OFF_BAR + 8u * i; };
-  const int B_FULL = 0, B_EMPTY = C::STAGES, B_ACC = 2 * C::STAGES, B_DRAIN = 2 * C::STAGES + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+  // Tile t of the flattened (batch, m tile, n tile) order, n fastest: consecutive tiles share A.
+  auto decode = [&](int t, int& z, int& m0, int& n0) {
+    const int nt = t % p.tiles_n;
+    const int r = t / p.tiles_n;
+    m0 = (r % p.tiles_m) * C::BM;
+    z = r / p.tiles_m;
+    n0 = nt * BN;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(bar(B_FULL + s), 1);
-      mbar_init(bar(B_EMPTY + s), 1);
+      mbar_init(bar(C::B_FULL + s), 1);
+      mbar_init(bar(C::B_EMPTY + s), 1);
     }
-    mbar_init(bar(B_ACC), 1);
-    mbar_init(bar(B_DRAIN), 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar(C::B_ACCF + b), 1);
+      mbar_init(bar(C::B_ACCE + b), C::EPI_WARPS);
+    }
+    mbar_init(bar(C::B_DRAIN), 1);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -98,46 +117,55 @@ __global__ void __launch_bounds__(192, 2)
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      int issued = 0;
-      for (int kb = 0; kb < p.n_kblocks; ++kb) {
-        const int st = kb % C::STAGES;
-        const uint32_t rnd = static_cast<uint32_t>(kb / C::STAGES);
-        if (!mbar_wait(bar(B_EMPTY + st), (rnd & 1u) ^ 1u, ctl)) break;
-        const uint32_t sa = base + st * C::STAGE_BYTES;
-        const uint32_t sb = sa + C::A_BYTES;
-        mbar_arrive_expect_tx(bar(B_FULL + st), C::STAGE_BYTES);
-        if (!A_MN) {
-          tma_load_3d(sa, &tm_a, bar(B_FULL + st), kb * C::BK, m0, z);
-        } else {
-          tma_load_3d(sa, &tm_a, bar(B_FULL + st), m0, kb * C::BK, z);
-          tma_load_3d(sa + 8192, &tm_a, bar(B_FULL + st), m0 + 64, kb * C::BK, z);
-        }
-        if (!B_MN) {
-          tma_load_3d(sb, &tm_b, bar(B_FULL + st), kb * C::BK, n0, z);
-        } else {
+      int it = 0;  // k-blocks issued so far, over all of this CTA's tiles (ring position)
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.n_tiles; t += gridDim.x) {
+        int z, m0, n0;
+        decode(t, z, m0, n0);
+        for (int kb = 0; kb < p.n_kblocks; ++kb, ++it) {
+          const int st = it % C::STAGES;
+          const uint32_t rnd = static_cast<uint32_t>(it / C::STAGES);
+          if (!(ok = mbar_wait(bar(C::B_EMPTY + st), (rnd & 1u) ^ 1u, ctl))) break;
+          const uint32_t sa = base + st * C::STAGE_BYTES;
+          const uint32_t sb = sa + C::A_BYTES;
+          mbar_arrive_expect_tx(bar(C::B_FULL + st), C::STAGE_BYTES);
+          if (!A_MN) {
+            tma_load_3d(sa, &tm_a, bar(C::B_FULL + st), kb * C::BK, m0, z);
+          } else {
+            tma_load_3d(sa, &tm_a, bar(C::B_FULL + st), m0, kb * C::BK, z);
+            tma_load_3d(sa + 8192, &tm_a, bar(C::B_FULL + st), m0 + 64, kb * C::BK, z);
+          }
+          if (!B_MN) {
+            tma_load_3d(sb, &tm_b, bar(C::B_FULL + st), kb * C::BK, n0, z);
+          } else {
 #pragma unroll
-          for (int c = 0; c < BN / 64; ++c)
-            tma_load_3d(sb + c * 8192, &tm_b, bar(B_FULL + st), n0 + 64 * c, kb * C::BK, z);
+            for (int c = 0; c < BN / 64; ++c)
+              tma_load_3d(sb + c * 8192, &tm_b, bar(C::B_FULL + st), n0 + 64 * c, kb * C::BK, z);
+          }
         }
-        issued = kb + 1;
       }
       if (*abort_flag) {
-        for (int i = max(0, issued - C::STAGES); i < issued; ++i)
-          mbar_wait_drain(bar(B_FULL + i % C::STAGES), static_cast<uint32_t>(i / C::STAGES) & 1u,
+        // Let every copy still in flight land before shared memory goes away.
+        for (int i = max(0, it - C::STAGES); i < it; ++i)
+          mbar_wait_drain(bar(C::B_FULL + i % C::STAGES), static_cast<uint32_t>(i / C::STAGES) & 1u,
                           p.timeout_ns);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t kIdesc = idesc_f16(128, BN, BF16 ? 1 : 0, A_MN ? 1 : 0, B_MN ? 1 : 0);
-      bool ok = true;
-      for (int kb = 0; kb < p.n_kblocks; ++kb) {
-        const int st = kb % C::STAGES;
-        if (!mbar_wait(bar(B_FULL + st), static_cast<uint32_t>(kb / C::STAGES) & 1u, ctl)) {
-          ok = false;
-          break;
-        }
+    // Warp-uniform control flow, one elected lane issues (the *_w helpers).  Accumulator b of
+    // tile i alternates so tile i+1's MMAs overlap tile i's epilogue.
+    constexpr uint32_t kIdesc = idesc_f16(128, BN, BF16 ? 1 : 0, A_MN ? 1 : 0, B_MN ? 1 : 0);
+    int it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x, i = 0; ok && t < p.n_tiles; t += gridDim.x, ++i) {
+      const int b = i & 1;
+      if (!(ok = mbar_wait_all(bar(C::B_ACCE + b), (static_cast<uint32_t>(i >> 1) & 1u) ^ 1u, ctl))) break;
+      tc_fence_after_sync();
+      const uint32_t d_tmem = tmem + b * BN;
+      for (int kb = 0; kb < p.n_kblocks; ++kb, ++it) {
+        const int st = it % C::STAGES;
+        if (!(ok = mbar_wait_all(bar(C::B_FULL + st), static_cast<uint32_t>(it / C::STAGES) & 1u, ctl))) break;
         tc_fence_after_sync();
         const uint32_t sa = base + st * C::STAGE_BYTES;
         const uint32_t sb = sa + C::A_BYTES;
@@ -147,59 +175,80 @@ __global__ void __launch_bounds__(192, 2)
                                    : smem_desc_sw128(sa + k * 32, 16, 1024);
           const uint64_t db = B_MN ? smem_desc_sw128(sb + k * 2048, 8192, 1024)
                                    : smem_desc_sw128(sb + k * 32, 16, 1024);
-          umma_ss(tmem, da, db, kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
+          umma_ss_w(d_tmem, da, db, kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
         }
-        umma_commit(bar(B_EMPTY + st));
+        umma_commit_w(bar(C::B_EMPTY + st));
       }
-      if (ok) umma_commit(bar(B_ACC));
+      if (ok) umma_commit_w(bar(C::B_ACCF + b));
     }
   } else {
-    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    // ------------------------------------------------------------------ epilogue (warps 2..9)
+    // Warp w reads TMEM lane quarter w % 4 (rows quarter*32 ..) and the 64-column chunks
+    // c = half, half + 2, ... of each tile; each (quarter, chunk) has its own staging slot, stored
+    // with one TMA store (clipped at M and N).  Two staging buffers alternate by tile, so writing
+    // tile i's rows only waits for tile i-2's stores to have read theirs.
     const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
+    const int half = (warp - 2) >> 2;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    if (mbar_wait_warp(bar(B_ACC), 0, ctl)) {
+    bool ok = true;
+    for (int t = blockIdx.x, i = 0; ok && t < p.n_tiles; t += gridDim.x, ++i) {
+      const int b = i & 1;
+      int z, m0, n0;
+      decode(t, z, m0, n0);
+      if (!(ok = mbar_wait_all(bar(C::B_ACCF + b), static_cast<uint32_t>(i >> 1) & 1u, ctl))) break;
       tc_fence_after_sync();
+      const uint32_t staging = base + C::OFF_STAGING + b * C::STAGING_BYTES;
+      if (i > 1) {  // this buffer's slots: tile i-2's stores (one group per tile) must have read them
+        if (lane == 0) bulk_wait_group_read1();
+        __syncwarp();
+      }
 #pragma unroll 1
-      for (int g = 0; g < BN / 32; ++g) {
-        uint32_t acc[32];
-        tmem_ld32(t_lane + g * 32, acc);
-        const uint32_t row_addr = base + (g >> 1) * (128 * 128) + row * 128;
+      for (int c = half; c < C::CHUNKS; c += 2) {
+        const uint32_t slot = staging + (quarter * C::CHUNKS + c) * C::SLOT_BYTES;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint32_t w[4];
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t acc[32];
+          tmem_ld32(t_lane + b * BN + c * 64 + hh * 32, acc);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float lo = __uint_as_float(acc[q * 8 + 2 * e]);
-            const float hi = __uint_as_float(acc[q * 8 + 2 * e + 1]);
-            w[e] = BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+          for (int q = 0; q < 4; ++q) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float lo = __uint_as_float(acc[q * 8 + 2 * e]);
+              const float hi = __uint_as_float(acc[q * 8 + 2 * e + 1]);
+              w[e] = BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+            }
+            const int chunk = hh * 4 + q;  // 16-byte chunk within the 128-byte row
+            st_shared_v4(slot + lane * 128 + ((chunk ^ (lane & 7)) << 4), w[0], w[1], w[2], w[3]);
           }
-          const int chunk = (g & 1) * 4 + q;
-          st_shared_v4(row_addr + ((chunk ^ (row & 7)) << 4), w[0], w[1], w[2], w[3]);
         }
       }
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(C::B_ACCE + b));  // accumulator b read: tile i+2 may reuse it
       fence_proxy_async_smem();
       __syncwarp();
       const int r0 = m0 + quarter * 32;
-      if (lane == 0 && r0 < p.m) {
-        for (int c = 0; c < BN / 64; ++c)
-          if (n0 + 64 * c < p.n)
-            tma_store_3d(&tm_c, base + c * (128 * 128) + quarter * 32 * 128, n0 + 64 * c, r0, z);
+      if (lane == 0) {
+        if (r0 < p.m) {
+          for (int c = half; c < C::CHUNKS; c += 2)
+            if (n0 + 64 * c < p.n)
+              tma_store_3d(&tm_c, staging + (quarter * C::CHUNKS + c) * C::SLOT_BYTES, n0 + 64 * c, r0, z);
+        }
         bulk_commit_group();
-        bulk_wait_group_read0();
       }
       __syncwarp();
     }
+    if (lane == 0) bulk_wait_group0();  // every store of this warp complete before exit
   }
 
   tc_fence_before_sync();
   __syncthreads();
   if (warp == 1) {
     if (*abort_flag) {
-      if (lane == 0) {
-        umma_commit(bar(B_DRAIN));
-        mbar_wait_drain(bar(B_DRAIN), 0, p.timeout_ns);
-      }
+      __syncwarp();
+      umma_commit_w(bar(C::B_DRAIN));  // same election as the MMAs: tracks all of them
+      if (lane == 0) mbar_wait_drain(bar(C::B_DRAIN), 0, p.timeout_ns);
       __syncwarp();
     }
     tc_fence_after_sync();
@@ -214,25 +263,25 @@ namespace {
 
 inline bool s16(int64_t s) { return s > 0 && ((s * 2) % 16) == 0 && (s * 2) < (1ll << 40); }
 
-int pick_bn(int64_t n) { return n >= 256 ? 256 : (n > 64 ? 128 : 64); }
+int pick_bn(int64_t n) { return n > 64 ? 128 : 64; }
 
 // Name of one tile-table entry (static storage, built once).
 const char* bmm_table_name(bool bf16, int bn, int am, int bm) {
-  static const std::array<std::string, 24> names = [] {
-    std::array<std::string, 24> out;
-    const int bns[3] = {64, 128, 256};
+  static const std::array<std::string, 16> names = [] {
+    std::array<std::string, 16> out;
+    const int bns[2] = {64, 128};
     for (int t = 0; t < 2; ++t)
-      for (int i = 0; i < 3; ++i)
+      for (int i = 0; i < 2; ++i)
         for (int a = 0; a < 2; ++a)
           for (int b = 0; b < 2; ++b)
-            out[((t * 3 + i) * 2 + a) * 2 + b] =
+            out[((t * 2 + i) * 2 + a) * 2 + b] =
                 std::string("bmm_sm100<") + (t ? "bf16" : "f16") + ",128x" + std::to_string(bns[i]) +
                 "x64,A:" + (a ? "mn" : "k") + "-major,B:" + (b ? "mn" : "k") + "-major," +
-                std::to_string(bns[i] == 256 ? 2 : (bns[i] == 128 ? 3 : 4)) + "st>";
+                std::to_string(bns[i] == 128 ? 4 : 6) + "st,persistent>";
     return out;
   }();
-  const int i = bn == 256 ? 2 : (bn == 128 ? 1 : 0);
-  return names[(((bf16 ? 1 : 0) * 3 + i) * 2 + am) * 2 + bm].c_str();
+  const int i = bn == 128 ? 1 : 0;
+  return names[(((bf16 ? 1 : 0) * 2 + i) * 2 + am) * 2 + bm].c_str();
 }
 
 // Layout of one operand: 0 = K-major (contiguous along K), 1 = MN-major, -1 = unusable.
@@ -321,11 +370,15 @@ int launch_bmm_typed(const cmpx_bmm_desc* d, const LaunchCtx& ctx) {
   p.n = static_cast<int>(N);
   p.k = static_cast<int>(K);
   p.n_kblocks = static_cast<int>((K + C::BK - 1) / C::BK);
+  p.tiles_m = static_cast<int>((M + C::BM - 1) / C::BM);
+  p.tiles_n = static_cast<int>((N + BN - 1) / BN);
+  const int64_t n_tiles = static_cast<int64_t>(p.tiles_m) * p.tiles_n * static_cast<int64_t>(Z);
+  if (n_tiles > (1ll << 31) - 1) return CMPX_ERR_UNSUPPORTED_SHAPE;
+  p.n_tiles = static_cast<int>(n_tiles);
   p.timeout_ns = ctx.timeout_ns;
   p.dev_flags = ctx.dev_flags;
-  dim3 grid(static_cast<unsigned>((N + BN - 1) / BN), static_cast<unsigned>((M + C::BM - 1) / C::BM),
-            static_cast<unsigned>(Z));
-  bmm_sm100_kernel<BN, A_MN, B_MN, BF16><<<grid, 192, C::SMEM_BYTES, ctx.stream>>>(ta, tb, tc, p);
+  const int grid = static_cast<int>(std::min<int64_t>(n_tiles, std::max(1, ctx.num_sms)));
+  bmm_sm100_kernel<BN, A_MN, B_MN, BF16><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(ta, tb, tc, p);
   return cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
 }
 
@@ -340,7 +393,6 @@ int launch_bmm_bn(const cmpx_bmm_desc* d, const LaunchCtx& ctx, int am, int bm) 
 template <bool BF16>
 int launch_bmm_dt(const cmpx_bmm_desc* d, const LaunchCtx& ctx, int am, int bm) {
   const int bn = pick_bn(d->n);
-  if (bn == 256) return launch_bmm_bn<256, BF16>(d, ctx, am, bm);
   if (bn == 128) return launch_bmm_bn<128, BF16>(d, ctx, am, bm);
   return launch_bmm_bn<64, BF16>(d, ctx, am, bm);
 }
