@@ -67,7 +67,7 @@ def _plan(d):
 
 
 @pytest.mark.parametrize("cfg,entry", [
-    (dict(B=2, H=8, Lq=4096, Lk=4096, D=40, dtype=0), "attn_f32_simt<D64"),
+    (dict(B=2, H=8, Lq=4096, Lk=4096, D=40, dtype=0), "attn_tf32x3_sm100<D64"),
     (dict(B=2, H=10, Lq=4096, Lk=4096, D=64, dtype=1), "fmha_sm100<f16,D64"),
     (dict(B=2, H=10, Lq=4096, Lk=77, D=64, dtype=1), "fmha_sm100_short<f16,D64"),
     (dict(B=4, H=32, Lq=8192, Lk=8192, D=128, dtype=2, causal=1), "fmha_sm100<bf16,D128"),
@@ -86,6 +86,17 @@ def test_tile_table_covers_every_config(cfg, entry):
     (dict(Lq=300, Lk=77, D=64, dtype=2, causal=1), "fmha_sm100<bf16,D64"),  # causal: general kernel
 ])
 def test_short_key_sequences_take_the_streamed_kernel(cfg, entry):
+    st, name = _plan(_attn(**cfg))
+    assert st == N.OK and name.startswith(entry), (st, name)
+
+
+@pytest.mark.parametrize("cfg,entry", [
+    (dict(D=40, dtype=0), "attn_tf32x3_sm100"),
+    (dict(D=64, dtype=0, causal=1), "attn_tf32x3_sm100"),
+    (dict(D=100, dtype=0), "attn_f32_simt<D128"),                       # head dim above 64
+    (dict(D=37, dtype=0), "attn_f32_simt<D64"),                         # rows not 16-byte aligned
+])
+def test_fp32_tile_table(cfg, entry):
     st, name = _plan(_attn(**cfg))
     assert st == N.OK and name.startswith(entry), (st, name)
 

@@ -14,7 +14,9 @@
 //   * P goes through shared memory (key-major) and O += P V accumulates 4 rows x 4*NC columns
 //     per thread; O is rescaled by exp2(m_old - m_new) whenever the row max moves;
 //   * causal masking (top-left aligned) and the ragged last key tile are masked to -inf.
-// Supports any head_dim <= 128 and arbitrary batch/head/row strides (contiguous head dim).
+// Supports any head_dim <= 128 and arbitrary batch/head/row strides (contiguous head dim).  Calls
+// with head_dim <= 64 and 16-byte aligned operands go to the tensor-core 3xTF32 kernel instead
+// (attn_tf32x3_sm100.cu); this kernel serves the rest.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -203,6 +205,7 @@ const char* attn_f32_plan(const cmpx_attn_desc* d, int* status) {
     *status = CMPX_ERR_UNSUPPORTED_SHAPE;
     return "none";
   }
+  if (attn_tf32x3_eligible(d)) return "attn_tf32x3_sm100<D64,128q,64kv,persistent>";
   return d->head_dim <= 64 ? "attn_f32_simt<D64,64q,64kv>" : "attn_f32_simt<D128,64q,64kv>";
 }
 
@@ -248,6 +251,7 @@ int launch_attn_f32(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   attn_f32_plan(d, &st);
   if (st != CMPX_OK) return st;
   if (d->len_q == 0) return CMPX_OK;
+  if (attn_tf32x3_eligible(d)) return launch_attn_tf32x3(d, ctx);
   return d->head_dim <= 64 ? launch_f32_typed<64>(d, ctx) : launch_f32_typed<128>(d, ctx);
 }
 

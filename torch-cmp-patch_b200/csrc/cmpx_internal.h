@@ -39,6 +39,9 @@ int launch_fmha_short(const cmpx_attn_desc* d, const LaunchCtx& ctx);
 
 const char* attn_f32_plan(const cmpx_attn_desc* d, int* status);
 int launch_attn_f32(const cmpx_attn_desc* d, const LaunchCtx& ctx);
+// fp32 on the tensor cores (3xTF32), head_dim <= 64 with 16-byte aligned pointers / strides.
+bool attn_tf32x3_eligible(const cmpx_attn_desc* d);
+int launch_attn_tf32x3(const cmpx_attn_desc* d, const LaunchCtx& ctx);
 
 // ---- batched matmul ----
 const char* bmm_sm100_plan(const cmpx_bmm_desc* d, int* status);

@@ -275,6 +275,29 @@ __device__ __forceinline__ void umma_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint
       : "memory");
 }
 
+// kind::tf32 forms (fp32 operands, the tensor core reads their top 19 bits), warp-collective.
+__device__ __forceinline__ void umma_ss_tf32_w(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                               uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred e, p;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_ts_tf32_w(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                               uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred e, p;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 __device__ __forceinline__ void umma_commit_w(uint32_t bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\t"
@@ -308,6 +331,13 @@ __host__ __device__ constexpr uint32_t idesc_f16(int m, int n, int ab_bf16, int 
          | (static_cast<uint32_t>(b_mn) << 16)     // B major
          | (static_cast<uint32_t>(n >> 3) << 17)   // N / 8
          | (static_cast<uint32_t>(m >> 4) << 24);  // M / 16
+}
+
+// Instruction descriptor for kind::tf32 (A and B format code 2) with fp32 accumulation.
+__host__ __device__ constexpr uint32_t idesc_tf32(int m, int n, int a_mn, int b_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(a_mn) << 15) |
+         (static_cast<uint32_t>(b_mn) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
 }
 
 // ----------------------------------------------------------------------------------------
