@@ -11,18 +11,23 @@
 //
 //   * a CTA owns a 128-row Q tile of one (batch, head) at a time (persistent, items strided over
 //     the grid); keys stream in 64-key tiles;
-//   * warp 0: TMA of Q (once per item) and K, V tiles (fp32, 128-byte swizzle, OOB zero-filled)
-//     into a 2-stage ring;
-//   * warps 2-5 ("converter"): Q and K split in place into hi (truncated) and lo parts; V
-//     transposed into V^T hi / lo (the K-major B operand of P V);
+//   * warp 0: TMA of Q (once per item, into a staging tile) and K, V tiles (fp32, 128-byte
+//     swizzle, OOB zero-filled) into a 3-stage ring;
+//   * warps 2-5 ("converter", thread = row for Q): Q split into hi / lo and written to TMEM (the
+//     QK products read A from TMEM); V transposed into V^T hi / lo (the K-major B operand of P V),
+//     then K split in place into hi and lo (lo over the raw V, already consumed) -- 64 KB a stage;
 //   * warp 1: tcgen05.mma kind::tf32 -- S = Qh Kh^T + Qh Kl^T + Ql Kh^T into one of two TMEM S
-//     buffers, the next tile's S issued before this tile's P V; O += Ph Vh + Ph Vl + Pl Vh with
-//     P read from TMEM;
+//     buffers, O += Ph Vh + Ph Vl + Pl Vh with P read from TMEM.  The warp polls the inputs of the
+//     next S and of the pending P V and issues whichever is ready first, so neither waits behind
+//     the other's loads;
 //   * warps 6-9 (thread = row): exact tile max, running max moved only when a tile's max exceeds
 //     it by more than 2^64 (fp32 keeps p = 2^(x - m) exact far beyond that; O, l and P share m,
-//     so the result is the same), p in fp32, split into Ph / Pl in TMEM; the epilogue writes O / l.
+//     so the result is the same), p in fp32, split into Ph (written over the tile's own S buffer)
+//     and Pl (one of two buffers); the epilogue writes O / l.  Tile j's S buffer is reused by tile
+//     j+2 only after PV(j) is done, so storing P never waits for a PV.
 //
-// TMEM columns: S0 [0,64), S1 [64,128), Ph [128,192), Pl [192,256), O [256,320).
+// TMEM columns: S0 / Ph0 [0,64), S1 / Ph1 [64,128), Pl0 [128,192), Pl1 [192,256), O [256,320),
+// Qh [320,384), Ql [384,448).
 // Every wait is bounded (cmpx_ptx.cuh); a CTA that gives up drains its copies and MMAs, frees
 // TMEM, raises the device status word and returns.
 #include <cuda.h>
@@ -40,29 +45,33 @@ namespace cmpx {
 struct X3Cfg {
   static constexpr int BM = 128, BN = 64, DP = 64;  // query rows, keys per tile, padded head dim
   static constexpr int QCH = BM * 128;              // one 32-column (128-byte) chunk of a Q tile
-  static constexpr int Q_BYTES = 2 * QCH;           // 32 KB
+  static constexpr int Q_BYTES = 2 * QCH;           // 32 KB staging tile
   static constexpr int KCH = BN * 128;              // one chunk of a K / V / V^T tile (64 rows)
   static constexpr int T_BYTES = 2 * KCH;           // 16 KB
-  static constexpr int NS = 2;                      // K/V ring stages
-  static constexpr int ST_K = 0, ST_KL = T_BYTES, ST_V = 2 * T_BYTES, ST_VTH = 3 * T_BYTES,
-                       ST_VTL = 4 * T_BYTES;
-  static constexpr int STAGE_BYTES = 5 * T_BYTES;   // 80 KB
-  static constexpr int OFF_Q = 0, OFF_QL = Q_BYTES, OFF_ST = 2 * Q_BYTES;
+  static constexpr int NS = 3;                      // K/V ring stages
+  // stage slots: K (hi in place) | raw V, then K lo | V^T hi | V^T lo
+  static constexpr int ST_K = 0, ST_B = T_BYTES, ST_VTH = 2 * T_BYTES, ST_VTL = 3 * T_BYTES;
+  static constexpr int STAGE_BYTES = 4 * T_BYTES;   // 64 KB
+  static constexpr int OFF_Q = 0, OFF_ST = Q_BYTES;
   static constexpr int OFF_BAR = OFF_ST + NS * STAGE_BYTES;
-  static constexpr int B_QFULL = 0, B_QCONV = 1, B_QEMPTY = 2;
-  static constexpr int B_FULL = 3;                  // [NS]
+  static constexpr int B_QFULL = 0;                 // Q staging tile landed
+  static constexpr int B_QFREE = 1;                 // converter has read it (count 128)
+  static constexpr int B_QEMPTY = 2;                // last S product of the item done: TMEM Q free
+  static constexpr int B_QCONV = 3;                 // Q hi / lo in TMEM (count 128)
+  static constexpr int B_FULL = 4;                  // [NS]
   static constexpr int B_CONV = B_FULL + NS;        // [NS] count 128
   static constexpr int B_EMPTY = B_CONV + NS;       // [NS]
-  static constexpr int B_SFULL = B_EMPTY + NS;      // [2]
-  static constexpr int B_SFREE = B_SFULL + 2;       // [2] count 128
-  static constexpr int B_PREADY = B_SFREE + 2;      // count 128
-  static constexpr int B_PVDONE = B_PREADY + 1;
-  static constexpr int B_OFREE = B_PVDONE + 1;      // count 128
-  static constexpr int B_DRAIN = B_OFREE + 1;
+  static constexpr int B_SFULL = B_EMPTY + NS;      // [2] S buffer b holds its tile's scores
+  static constexpr int B_PREADY = B_SFULL + 2;      // [2] P of buffer b written (count 128)
+  static constexpr int B_PVD = B_PREADY + 2;        // [2] P V of buffer b's tile done
+  static constexpr int B_OFREE = B_PVD + 2;         // count 128
+  static constexpr int B_VREAD = B_OFREE + 1;      // converter threads have read a stage's raw V (128)
+  static constexpr int B_DRAIN = B_VREAD + 1;
   static constexpr int NBAR = B_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
-  static constexpr int TM_S0 = 0, TM_S1 = 64, TM_PH = 128, TM_PL = 192, TM_O = 256;
+  static constexpr int TM_S0 = 0, TM_S1 = 64, TM_PL0 = 128, TM_PL1 = 192, TM_O = 256, TM_QH = 320,
+                       TM_QL = 384;
   static constexpr int TMEM_COLS = 512;
   static constexpr int THREADS = 320;
   static constexpr int W_TMA = 0, W_MMA = 1;
@@ -107,7 +116,7 @@ __global__ void __launch_bounds__(320, 1)
   auto bar = [&](int i) -> uint32_t { return base + C::OFF_BAR + 8u * i; };
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
-  const uint32_t sQ = base + C::OFF_Q, sQL = base + C::OFF_QL;
+  const uint32_t sQ = base + C::OFF_Q;
   auto stage = [&](int load) -> uint32_t { return base + C::OFF_ST + (load % C::NS) * C::STAGE_BYTES; };
 
   // Item w -> (b, h, q0, number of 64-key tiles); causal items heaviest-first within a head.
@@ -123,8 +132,9 @@ __global__ void __launch_bounds__(320, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(bar(C::B_QFULL), 1);
-    mbar_init(bar(C::B_QCONV), 128);
+    mbar_init(bar(C::B_QFREE), 128);
     mbar_init(bar(C::B_QEMPTY), 1);
+    mbar_init(bar(C::B_QCONV), 128);
     for (int s = 0; s < C::NS; ++s) {
       mbar_init(bar(C::B_FULL + s), 1);
       mbar_init(bar(C::B_CONV + s), 128);
@@ -132,11 +142,11 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar(C::B_SFULL + b), 1);
-      mbar_init(bar(C::B_SFREE + b), 128);
+      mbar_init(bar(C::B_PREADY + b), 128);
+      mbar_init(bar(C::B_PVD + b), 1);
     }
-    mbar_init(bar(C::B_PREADY), 128);
-    mbar_init(bar(C::B_PVDONE), 1);
     mbar_init(bar(C::B_OFREE), 128);
+    mbar_init(bar(C::B_VREAD), 128);
     mbar_init(bar(C::B_DRAIN), 1);
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -164,7 +174,8 @@ __global__ void __launch_bounds__(320, 1)
       for (int k = 0, w = blockIdx.x; ok && w < p.n_items; ++k, w += gridDim.x) {
         int b, h, q0, n_kv;
         geometry(w, b, h, q0, n_kv);
-        if (k > 0 && !(ok = mbar_wait(bar(C::B_QEMPTY), static_cast<uint32_t>(k - 1) & 1u, ctl))) break;
+        // the staging tile is free once the converter has read the previous item's Q
+        if (k > 0 && !(ok = mbar_wait(bar(C::B_QFREE), static_cast<uint32_t>(k - 1) & 1u, ctl))) break;
         mbar_arrive_expect_tx(bar(C::B_QFULL), C::Q_BYTES);
         for (int c = 0; c < 2; ++c) tma_load_4d(sQ + c * C::QCH, &tm_q, bar(C::B_QFULL), c * 32, q0, h, b);
         for (int j = 0; ok && j < n_kv; ++j, ++load) {
@@ -174,7 +185,7 @@ __global__ void __launch_bounds__(320, 1)
           mbar_arrive_expect_tx(bar(C::B_FULL + st), 2 * C::T_BYTES);
           for (int c = 0; c < 2; ++c) {
             tma_load_4d(sb + C::ST_K + c * C::KCH, &tm_k, bar(C::B_FULL + st), c * 32, j * C::BN, h, b);
-            tma_load_4d(sb + C::ST_V + c * C::KCH, &tm_v, bar(C::B_FULL + st), c * 32, j * C::BN, h, b);
+            tma_load_4d(sb + C::ST_B + c * C::KCH, &tm_v, bar(C::B_FULL + st), c * 32, j * C::BN, h, b);
           }
         }
       }
@@ -185,31 +196,30 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else if (warp == C::W_MMA) {
     // ------------------------------------------------------------------ MMA issuer (warp-uniform)
-    constexpr uint32_t kIdesc = idesc_tf32(128, 64, 0, 0);
+    constexpr uint32_t kIdesc = idesc_tf32(128, 64, 0, 0);  // K-major A (TMEM) and B
     int load_base = 0;  // ring position of the item's first K/V tile
     int g = 0;          // tiles of all earlier items (S buffer and barrier phase bookkeeping)
     bool ok = true;
-    // One S product: S_b = Qh Kh^T + Qh Kl^T + Ql Kh^T.
+    // One S product: S_b = Qh Kh^T + Qh Kl^T + Ql Kh^T (Q from TMEM).
     auto issue_qk = [&](uint32_t sb, uint32_t s_tmem) {
-      const uint32_t kh = sb + C::ST_K, kl = sb + C::ST_KL;
+      const uint32_t kh = sb + C::ST_K, kl = sb + C::ST_B;
 #pragma unroll 1
       for (int part = 0; part < 3; ++part) {
-        const uint32_t qa = part == 2 ? sQL : sQ;
+        const uint32_t qa = tmem + (part == 2 ? C::TM_QL : C::TM_QH);
         const uint32_t kb = part == 1 ? kl : kh;
         for (int s = 0; s < p.qk_steps; ++s) {
-          const uint32_t qoff = (s >> 2) * C::QCH + (s & 3) * 32;
           const uint32_t koff = (s >> 2) * C::KCH + (s & 3) * 32;
-          umma_ss_tf32_w(s_tmem, smem_desc_sw128(qa + qoff, 16, 1024), smem_desc_sw128(kb + koff, 16, 1024),
-                         kIdesc, (part > 0 || s > 0) ? 1u : 0u);
+          umma_ts_tf32_w(s_tmem, qa + s * 8, smem_desc_sw128(kb + koff, 16, 1024), kIdesc,
+                         (part > 0 || s > 0) ? 1u : 0u);
         }
       }
     };
-    // O (+)= Ph Vh + Ph Vl + Pl Vh over the tile's 64 keys (8 K-steps of 8).
-    auto issue_pv = [&](uint32_t sb, bool acc) {
+    // O (+)= Ph Vh + Ph Vl + Pl Vh over the tile's 64 keys (8 K-steps of 8); P of buffer pb.
+    auto issue_pv = [&](uint32_t sb, int pb, bool acc) {
       const uint32_t vh = sb + C::ST_VTH, vl = sb + C::ST_VTL;
 #pragma unroll 1
       for (int part = 0; part < 3; ++part) {
-        const uint32_t pa = tmem + (part == 2 ? C::TM_PL : C::TM_PH);
+        const uint32_t pa = tmem + (part == 2 ? (pb ? C::TM_PL1 : C::TM_PL0) : (pb ? C::TM_S1 : C::TM_S0));
         const uint32_t vb = part == 1 ? vl : vh;
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
@@ -219,65 +229,118 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
     };
+    // Warp-uniform non-blocking test of one barrier phase.
+    auto ready = [&](uint32_t b, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, mbar_test_wait(b, parity));
+    };
     for (int k = 0, w = blockIdx.x; ok && w < p.n_items; ++k, w += gridDim.x) {
       int b, h, q0, n_kv;
       geometry(w, b, h, q0, n_kv);
       (void)b; (void)h; (void)q0;
       if (!(ok = mbar_wait_all(bar(C::B_QCONV), static_cast<uint32_t>(k) & 1u, ctl))) break;
-      auto do_pv = [&](int jj) -> bool {
-        const int gj = g + jj;
-        if (!mbar_wait_all(bar(C::B_PREADY), static_cast<uint32_t>(gj) & 1u, ctl)) return false;
-        // The item's first PV overwrites O: the previous item's epilogue must have read it.
-        if (jj == 0 && k > 0 && !mbar_wait_all(bar(C::B_OFREE), static_cast<uint32_t>(k - 1) & 1u, ctl))
-          return false;
-        tc_fence_after_sync();
-        issue_pv(stage(load_base + jj), jj > 0);
-        umma_commit_w(bar(C::B_PVDONE));
-        umma_commit_w(bar(C::B_EMPTY + (load_base + jj) % C::NS));
-        return true;
-      };
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int gj = g + j, ld = load_base + j, bs = gj & 1;
-        if (!(ok = mbar_wait_all(bar(C::B_CONV + ld % C::NS), static_cast<uint32_t>(ld / C::NS) & 1u, ctl))) break;
-        // S buffer bs is free once the softmax of its previous tile (gj - 2) has read it.
-        if (!(ok = mbar_wait_all(bar(C::B_SFREE + bs), (static_cast<uint32_t>(gj >> 1) & 1u) ^ 1u, ctl))) break;
-        tc_fence_after_sync();
-        issue_qk(stage(ld), tmem + (bs ? C::TM_S1 : C::TM_S0));
-        umma_commit_w(bar(C::B_SFULL + bs));
-        if (j + 1 == n_kv) umma_commit_w(bar(C::B_QEMPTY));  // last product reading Q
-        if (j > 0 && !(ok = do_pv(j - 1))) break;
+      // Issue S(nq) and PV(np) in whichever order their inputs become ready.
+      int nq = 0, np = 0;
+      uint64_t t_idle = global_timer_ns();
+      while (np < n_kv) {
+        bool progress = false;
+        if (nq < n_kv) {
+          const int ld = load_base + nq, gq = g + nq, bs = gq & 1;
+          // K/V tile converted; buffer bs (tile gq-2's S, then P) consumed by PV(gq-2).
+          if (ready(bar(C::B_CONV + ld % C::NS), static_cast<uint32_t>(ld / C::NS) & 1u) &&
+              (gq < 2 || ready(bar(C::B_PVD + bs), static_cast<uint32_t>((gq - 2) >> 1) & 1u))) {
+            tc_fence_after_sync();
+            issue_qk(stage(ld), tmem + (bs ? C::TM_S1 : C::TM_S0));
+            umma_commit_w(bar(C::B_SFULL + bs));
+            if (nq + 1 == n_kv) umma_commit_w(bar(C::B_QEMPTY));  // last product reading Q
+            ++nq;
+            progress = true;
+          }
+        }
+        if (np < nq) {
+          const int gp = g + np, pb = gp & 1;
+          // P written; the item's first PV overwrites O: the previous epilogue must have read it.
+          if (ready(bar(C::B_PREADY + pb), static_cast<uint32_t>(gp >> 1) & 1u) &&
+              (np > 0 || k == 0 || ready(bar(C::B_OFREE), static_cast<uint32_t>(k - 1) & 1u))) {
+            tc_fence_after_sync();
+            issue_pv(stage(load_base + np), pb, np > 0);
+            umma_commit_w(bar(C::B_PVD + pb));
+            umma_commit_w(bar(C::B_EMPTY + (load_base + np) % C::NS));
+            ++np;
+            progress = true;
+          }
+        }
+        if (progress) {
+          t_idle = global_timer_ns();
+        } else {
+          if (*abort_flag) {
+            ok = false;
+            break;
+          }
+          if (global_timer_ns() - t_idle > p.timeout_ns) {
+            if (lane == 0) {
+              *abort_flag = 1;
+              atomicOr(p.dev_flags, 1u /* CMPX_DEVFLAG_WAIT_TIMEOUT */);
+            }
+            ok = false;
+            break;
+          }
+          __nanosleep(64);
+        }
       }
-      if (ok) ok = do_pv(n_kv - 1);
       g += n_kv;
       load_base += n_kv;
     }
   } else if (warp < 6) {
     // ------------------------------------------------------------------ converter (warps 2-5)
     const int tid = threadIdx.x - 64;  // 0..127
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;  // Q row of this thread = TMEM lane it writes
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     int load = 0;
     bool ok = true;
     for (int k = 0, w = blockIdx.x; ok && w < p.n_items; ++k, w += gridDim.x) {
       int b, h, q0, n_kv;
       geometry(w, b, h, q0, n_kv);
+      // Q: this thread's row from the staging tile -> hi / lo -> TMEM.
       if (!(ok = mbar_wait_all(bar(C::B_QFULL), static_cast<uint32_t>(k) & 1u, ctl))) break;
-      // Q (32 KB) -> hi in place, lo alongside (same swizzled layout: the split is elementwise).
-#pragma unroll 4
-      for (int v = tid; v < C::Q_BYTES / 16; v += 128) split_v4(sQ + v * 16, sQ + v * 16, sQL + v * 16);
-      fence_proxy_async_smem();
+      uint32_t q[64];
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const uint32_t addr = sQ + c * C::QCH + row * 128 + ((u ^ (row & 7)) << 4);
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(q[c * 32 + u * 4]), "=r"(q[c * 32 + u * 4 + 1]), "=r"(q[c * 32 + u * 4 + 2]),
+                         "=r"(q[c * 32 + u * 4 + 3])
+                       : "r"(addr));
+        }
+      mbar_arrive(bar(C::B_QFREE));  // the staging tile may take the next item's Q
+      // TMEM Q is free once the previous item's last S product is done.
+      if (k > 0 && !(ok = mbar_wait_all(bar(C::B_QEMPTY), static_cast<uint32_t>(k - 1) & 1u, ctl))) break;
+      tc_fence_after_sync();
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t hi[32], lo[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          hi[e] = tf32_trunc(q[hh * 32 + e]);
+          lo[e] = __float_as_uint(__uint_as_float(q[hh * 32 + e]) - __uint_as_float(hi[e]));
+        }
+        tmem_st32(lane_base + C::TM_QH + hh * 32, hi);
+        tmem_st32(lane_base + C::TM_QL + hh * 32, lo);
+      }
+      tmem_st_wait();
+      tc_fence_before_sync();
       mbar_arrive(bar(C::B_QCONV));
       for (int j = 0; ok && j < n_kv; ++j, ++load) {
         const int st = load % C::NS;
         if (!(ok = mbar_wait_all(bar(C::B_FULL + st), static_cast<uint32_t>(load / C::NS) & 1u, ctl))) break;
         const uint32_t sb = stage(load);
-        // K -> hi in place, lo alongside.
-#pragma unroll 4
-        for (int v = tid; v < C::T_BYTES / 16; v += 128)
-          split_v4(sb + C::ST_K + v * 16, sb + C::ST_K + v * 16, sb + C::ST_KL + v * 16);
-        // V [key][d] -> V^T [d][key] hi / lo (K-major B operand: rows d, 64 keys in two 128-byte
-        // chunks).  Thread -> (d = tid % 64, keys half*32 .. half*32+31).
+        // V [key][d] (slot B) -> V^T [d][key] hi / lo (K-major B operand: rows d, 64 keys in two
+        // 128-byte chunks).  Thread -> (d = tid % 64, keys half*32 .. half*32+31).
         {
           const int d = tid & 63, half = tid >> 6;
-          const uint32_t vsrc = sb + C::ST_V + (d >> 5) * C::KCH + (d & 3) * 4;
+          const uint32_t vsrc = sb + C::ST_B + (d >> 5) * C::KCH + (d & 3) * 4;
           const int du = (d & 31) >> 2;  // 16-byte unit of column d inside its 128-byte row
           const uint32_t dst_row = half * C::KCH + d * 128;
 #pragma unroll
@@ -297,6 +360,13 @@ __global__ void __launch_bounds__(320, 1)
                          __float_as_uint(__uint_as_float(x[3]) - __uint_as_float(h3)));
           }
         }
+        // Every converter thread has read the raw V: slot B may now take K lo (a bounded wait on
+        // an mbarrier, one phase per stage conversion, rather than a named barrier).
+        mbar_arrive(bar(C::B_VREAD));
+        if (!(ok = mbar_wait_all(bar(C::B_VREAD), static_cast<uint32_t>(load) & 1u, ctl))) break;
+#pragma unroll 4
+        for (int v = tid; v < C::T_BYTES / 16; v += 128)
+          split_v4(sb + C::ST_K + v * 16, sb + C::ST_K + v * 16, sb + C::ST_B + v * 16);
         fence_proxy_async_smem();
         mbar_arrive(bar(C::B_CONV + st));
       }
@@ -323,7 +393,6 @@ __global__ void __launch_bounds__(320, 1)
         tmem_ld64(lane_base + (bs ? C::TM_S1 : C::TM_S0), sr);
         float* s = reinterpret_cast<float*>(sr);
         tc_fence_before_sync();
-        mbar_arrive(bar(C::B_SFREE + bs));
         const int kv0 = j * C::BN;
         if (kv0 + C::BN > p.len_k || (p.causal && kv0 + C::BN - 1 > q0)) {
           int lim = p.len_k - kv0;
@@ -332,14 +401,25 @@ __global__ void __launch_bounds__(320, 1)
           for (int c = 0; c < 64; ++c)
             if (c >= lim) s[c] = masked;
         }
-        float mx = s[0];
+        float a8[8];
         if (p.neg_scale) {
 #pragma unroll
-          for (int c = 1; c < 64; ++c) mx = fminf(mx, s[c]);
+          for (int e = 0; e < 8; ++e) a8[e] = fminf(s[e], s[8 + e]);
+#pragma unroll
+          for (int c = 16; c < 64; c += 16)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) a8[e] = fmin3(a8[e], s[c + e], s[c + 8 + e]);
         } else {
 #pragma unroll
-          for (int c = 1; c < 64; ++c) mx = fmaxf(mx, s[c]);
+          for (int e = 0; e < 8; ++e) a8[e] = fmaxf(s[e], s[8 + e]);
+#pragma unroll
+          for (int c = 16; c < 64; c += 16)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) a8[e] = fmax3(a8[e], s[c + e], s[c + 8 + e]);
         }
+        const float mx = p.neg_scale
+                             ? fmin3(fmin3(a8[0], a8[1], a8[2]), fmin3(a8[3], a8[4], a8[5]), fminf(a8[6], a8[7]))
+                             : fmax3(fmax3(a8[0], a8[1], a8[2]), fmax3(a8[3], a8[4], a8[5]), fmaxf(a8[6], a8[7]));
         const float m_tile = mx * sl2;
         float alpha = 1.f;
         if (m_run == -INFINITY || m_tile > m_run + 64.f) {
@@ -348,31 +428,38 @@ __global__ void __launch_bounds__(320, 1)
           m_run = m_new;
         }
         const float nm = (m_run == -INFINITY) ? 0.f : -m_run;
-        float l0 = 0.f, l1 = 0.f;
+        const uint64_t sl2x2 = f2_pack(sl2, sl2), nmx2 = f2_pack(nm, nm);
+        uint64_t la = f2_pack(0.f, 0.f), lb = la;
 #pragma unroll
         for (int c = 0; c < 64; c += 2) {
-          s[c] = ex2_approx(fmaf(s[c], sl2, nm));
-          s[c + 1] = ex2_approx(fmaf(s[c + 1], sl2, nm));
-          l0 += s[c];
-          l1 += s[c + 1];
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(s[c], s[c + 1]), sl2x2, nmx2), x0, x1);
+          s[c] = ex2_approx(x0);
+          s[c + 1] = ex2_approx(x1);
+          if (c & 2)
+            lb = f2_add(lb, f2_pack(s[c], s[c + 1]));
+          else
+            la = f2_add(la, f2_pack(s[c], s[c + 1]));
         }
+        float l0, l1;
+        f2_unpack(f2_add(la, lb), l0, l1);
         l_run = l_run * alpha + (l0 + l1);
-        // P buffers and O are free once the previous tile's PV is done (none before the first).
-        if (j > 0) {
-          if (!(ok = mbar_wait_all(bar(C::B_PVDONE), static_cast<uint32_t>(gj - 1) & 1u, ctl))) break;
+        // O moves only in the (rare) rescale: it needs the previous tile's PV done.  Storing P needs
+        // no wait: buffer bs was last read by PV(gj-2), which completed before QK(gj) was issued.
+        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+          const int gprev = gj - 1;
+          if (!(ok = mbar_wait_all(bar(C::B_PVD + (gprev & 1)), static_cast<uint32_t>(gprev >> 1) & 1u, ctl))) break;
           tc_fence_after_sync();
-          if (__any_sync(0xffffffffu, alpha != 1.f)) {
-            uint32_t o[64];
-            tmem_ld64(lane_base + C::TM_O, o);
+          uint32_t o[64];
+          tmem_ld64(lane_base + C::TM_O, o);
 #pragma unroll
-            for (int e = 0; e < 64; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          for (int e = 0; e < 64; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              uint32_t part[32];
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t part[32];
 #pragma unroll
-              for (int e = 0; e < 32; ++e) part[e] = o[hh * 32 + e];
-              tmem_st32(lane_base + C::TM_O + hh * 32, part);
-            }
+            for (int e = 0; e < 32; ++e) part[e] = o[hh * 32 + e];
+            tmem_st32(lane_base + C::TM_O + hh * 32, part);
           }
         }
 #pragma unroll
@@ -384,16 +471,17 @@ __global__ void __launch_bounds__(320, 1)
             ph[e] = tf32_trunc(bits);
             pl[e] = __float_as_uint(s[hh * 32 + e] - __uint_as_float(ph[e]));
           }
-          tmem_st32(lane_base + C::TM_PH + hh * 32, ph);
-          tmem_st32(lane_base + C::TM_PL + hh * 32, pl);
+          tmem_st32(lane_base + (bs ? C::TM_S1 : C::TM_S0) + hh * 32, ph);
+          tmem_st32(lane_base + (bs ? C::TM_PL1 : C::TM_PL0) + hh * 32, pl);
         }
         tmem_st_wait();
         tc_fence_before_sync();
-        mbar_arrive(bar(C::B_PREADY));
+        mbar_arrive(bar(C::B_PREADY + bs));
       }
       if (!ok) break;
       // Epilogue: O / l, fp32, straight to global memory (this thread's row).
-      if (!(ok = mbar_wait_all(bar(C::B_PVDONE), static_cast<uint32_t>(g + n_kv - 1) & 1u, ctl))) break;
+      const int glast = g + n_kv - 1;
+      if (!(ok = mbar_wait_all(bar(C::B_PVD + (glast & 1)), static_cast<uint32_t>(glast >> 1) & 1u, ctl))) break;
       tc_fence_after_sync();
       uint32_t o[64];
       tmem_ld64(lane_base + C::TM_O, o);
