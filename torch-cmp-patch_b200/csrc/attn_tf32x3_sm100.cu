@@ -200,32 +200,39 @@ __global__ void __launch_bounds__(320, 1)
     int load_base = 0;  // ring position of the item's first K/V tile
     int g = 0;          // tiles of all earlier items (S buffer and barrier phase bookkeeping)
     bool ok = true;
-    // One S product: S_b = Qh Kh^T + Qh Kl^T + Ql Kh^T (Q from TMEM).
+    // Issue loops are fully unrolled with compile-time offsets added to descriptors built once
+    // per product (the start address sits in the low bits: no carry for shared-memory
+    // addresses), so each MMA costs the issuing warp about one MMA slot.
+    // One S product: S_b = Qh Kh^T + Qh Kl^T + Ql Kh^T (Q from TMEM), qk_steps K-steps of 8.
     auto issue_qk = [&](uint32_t sb, uint32_t s_tmem) {
-      const uint32_t kh = sb + C::ST_K, kl = sb + C::ST_B;
-#pragma unroll 1
+      const uint64_t dkh = smem_desc_sw128(sb + C::ST_K, 16, 1024);
+      const uint64_t dkl = smem_desc_sw128(sb + C::ST_B, 16, 1024);
+      const int steps = p.qk_steps;
+#pragma unroll
       for (int part = 0; part < 3; ++part) {
-        const uint32_t qa = tmem + (part == 2 ? C::TM_QL : C::TM_QH);
-        const uint32_t kb = part == 1 ? kl : kh;
-        for (int s = 0; s < p.qk_steps; ++s) {
-          const uint32_t koff = (s >> 2) * C::KCH + (s & 3) * 32;
-          umma_ts_tf32_w(s_tmem, qa + s * 8, smem_desc_sw128(kb + koff, 16, 1024), kIdesc,
-                         (part > 0 || s > 0) ? 1u : 0u);
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+          if (s < steps) {
+            const uint64_t koff = static_cast<uint64_t>(((s >> 2) * C::KCH + (s & 3) * 32) >> 4);
+            umma_ts_tf32_w(s_tmem, tmem + (part == 2 ? C::TM_QL : C::TM_QH) + s * 8,
+                           (part == 1 ? dkl : dkh) + koff, kIdesc, (part > 0 || s > 0) ? 1u : 0u);
+          }
         }
       }
     };
     // O (+)= Ph Vh + Ph Vl + Pl Vh over the tile's 64 keys (8 K-steps of 8); P of buffer pb.
     auto issue_pv = [&](uint32_t sb, int pb, bool acc) {
-      const uint32_t vh = sb + C::ST_VTH, vl = sb + C::ST_VTL;
-#pragma unroll 1
+      const uint64_t dvh = smem_desc_sw128(sb + C::ST_VTH, 16, 1024);
+      const uint64_t dvl = smem_desc_sw128(sb + C::ST_VTL, 16, 1024);
+      const uint32_t ph = tmem + (pb ? C::TM_S1 : C::TM_S0), pl = tmem + (pb ? C::TM_PL1 : C::TM_PL0);
+      const uint32_t acc0 = acc ? 1u : 0u;
+#pragma unroll
       for (int part = 0; part < 3; ++part) {
-        const uint32_t pa = tmem + (part == 2 ? (pb ? C::TM_PL1 : C::TM_PL0) : (pb ? C::TM_S1 : C::TM_S0));
-        const uint32_t vb = part == 1 ? vl : vh;
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
-          const uint32_t voff = (s >> 2) * C::KCH + (s & 3) * 32;
-          umma_ts_tf32_w(tmem + C::TM_O, pa + s * 8, smem_desc_sw128(vb + voff, 16, 1024), kIdesc,
-                         (acc || part > 0 || s > 0) ? 1u : 0u);
+          const uint64_t voff = static_cast<uint64_t>(((s >> 2) * C::KCH + (s & 3) * 32) >> 4);
+          umma_ts_tf32_w(tmem + C::TM_O, (part == 2 ? pl : ph) + s * 8, (part == 1 ? dvl : dvh) + voff,
+                         kIdesc, (part > 0 || s > 0) ? 1u : acc0);
         }
       }
     };
