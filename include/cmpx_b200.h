@@ -38,7 +38,7 @@
 extern "C" {
 #endif
 
-#define CMPX_ABI_VERSION 1
+#define CMPX_ABI_VERSION 2  /* 2: cmpx_attn_desc.heads_kv (grouped-query attention) */
 
 /* Element type of every operand of one call (inputs and output share it, as in the reference:
  * dtype in == dtype out, src/main.cpp:1623-1627, :366-369). */
@@ -65,6 +65,8 @@ typedef enum cmpx_status {
  * contiguous head_dim (the same strided-view contract as the reference's HFMA2 route,
  * src/main.cpp:1637-1666).  Causal masking is top-left aligned (key j is visible to query i
  * iff j <= i), which is what torch's is_causal does for len_q != len_k.
+ * Grouped-query attention: k and v may have heads_kv heads (a divisor of heads); query head h then
+ * reads key/value head h / (heads / heads_kv), as torch's enable_gqa=True does.
  * Replaces: custom_attention_forward (src/main.cpp:1603-1774) and its launchers
  * launch_flash_attention_hfma2 (src/cuda/fp16_flash_attention_hfma2.cu:269-286),
  * launch_attention_fp16 (src/cuda/fp16_attention.cu:328-386),
@@ -84,6 +86,7 @@ typedef struct cmpx_attn_desc {
   double scale;        /* softmax scale; the reference default is 1/sqrt(head_dim) */
   void* workspace;     /* device scratch of cmpx_attn_workspace_size() bytes (may be NULL if 0) */
   size_t workspace_bytes;
+  int64_t heads_kv;    /* heads of k and v: 0 or heads = one per query head, else a divisor of heads */
 } cmpx_attn_desc;
 
 /* Batched matmul  C[b] = A[b] @ B[b],  A: [batch, m, k], B: [batch, k, n], C: [batch, m, n].

@@ -42,7 +42,7 @@ def test_library_exports_nothing_undeclared():
 
 
 def test_abi_version_and_status_strings():
-    assert N.lib.cmpx_abi_version() == 1
+    assert N.lib.cmpx_abi_version() == 2
     assert N.lib.cmpx_status_str(0) == b"ok"
     for code in range(1, 9):
         assert N.lib.cmpx_status_str(code) not in (b"ok", b"unknown status")
@@ -90,6 +90,14 @@ def test_short_key_sequences_take_the_streamed_kernel(cfg, entry):
     assert st == N.OK and name.startswith(entry), (st, name)
 
 
+@pytest.mark.parametrize("heads_kv", [0, 1, 2, 4, 8])
+def test_grouped_query_heads_are_accepted(heads_kv):
+    d = _attn(H=8, D=128)
+    d.heads_kv = heads_kv
+    st, name = _plan(d)
+    assert st == N.OK and name.startswith("fmha_sm100<bf16,D128"), (st, name)
+
+
 @pytest.mark.parametrize("cfg,entry", [
     (dict(D=40, dtype=0), "attn_tf32x3_sm100"),
     (dict(D=64, dtype=0, causal=1), "attn_tf32x3_sm100"),
@@ -113,6 +121,8 @@ def test_fp32_tile_table(cfg, entry):
     (lambda d: setattr(d, "q", 0x10008), N.ERR_MISALIGNED),
     (lambda d: d.k_stride.__setitem__(2, 100), N.ERR_MISALIGNED),
     (lambda d: setattr(d, "causal", 2), N.ERR_INVALID_ARGUMENT),
+    (lambda d: setattr(d, "heads_kv", 3), N.ERR_INVALID_ARGUMENT),   # does not divide heads=2
+    (lambda d: setattr(d, "heads_kv", -1), N.ERR_INVALID_ARGUMENT),
 ])
 def test_invalid_attention_descriptors_are_rejected_before_launch(mutate, status):
     d = _attn()

@@ -411,13 +411,22 @@ class TestScaledDotProductAttention:
         native.attention.assert_called_once()
         assert got.shape == q.shape
 
-    def test_gqa_heads_go_to_stock(self, patched, native, monkeypatch):
+    def test_gqa_heads_go_to_native(self, patched, native, monkeypatch):
         force_eligible(monkeypatch)
         q = torch.randn(1, 4, 3, 8)
         k, v = torch.randn(1, 2, 3, 8), torch.randn(1, 2, 3, 8)
+        native.attention.return_value = torch.zeros(1, 4, 3, 8)
         got = F.scaled_dot_product_attention(q, k, v, enable_gqa=True)
+        native.attention.assert_called_once()
+        assert native.attention.call_args[0][1] is k and got.shape == q.shape
+
+    def test_unequal_heads_without_enable_gqa_stay_stock(self, patched, native, monkeypatch):
+        force_eligible(monkeypatch)
+        q = torch.randn(1, 4, 3, 8)
+        k, v = torch.randn(1, 2, 3, 8), torch.randn(1, 2, 3, 8)
+        with pytest.raises(RuntimeError):  # torch's own shape error, as without the patch
+            F.scaled_dot_product_attention(q, k, v)
         native.attention.assert_not_called()
-        assert got.shape == q.shape
 
 
 class TestDispatchRecord:

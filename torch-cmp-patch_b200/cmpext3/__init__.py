@@ -298,8 +298,8 @@ def _patched_sdpa(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=Fa
             or not _usable(query, key, value)):
         return orig(query, key, value, attn_mask=attn_mask, dropout_p=dropout_p,
                     is_causal=is_causal, scale=scale, **kwargs)
-    if kwargs.get("enable_gqa") and key.dim() == 4 and key.size(1) != query.size(1):
-        # grouped-query heads are not in the tile table yet: stock handles the head broadcast
+    if key.dim() == 4 and key.size(1) != query.size(1) and not kwargs.get("enable_gqa"):
+        # unequal head counts without enable_gqa: torch's own error / behaviour
         return orig(query, key, value, attn_mask=attn_mask, dropout_p=dropout_p,
                     is_causal=is_causal, scale=scale, **kwargs)
     return _dispatch("attention", query,

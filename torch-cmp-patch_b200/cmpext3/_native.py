@@ -60,6 +60,7 @@ class AttnDesc(ctypes.Structure):
         ("v_stride", ctypes.c_int64 * 3), ("o_stride", ctypes.c_int64 * 3),
         ("dtype", ctypes.c_int32), ("causal", ctypes.c_int32), ("scale", ctypes.c_double),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+        ("heads_kv", ctypes.c_int64),
     ]
 
 
@@ -163,6 +164,7 @@ def _attn_desc(q, k, v, o, scale: float, causal: bool) -> AttnDesc:
     d.scale = float(scale)
     d.workspace = None
     d.workspace_bytes = 0
+    d.heads_kv = k.shape[1]
     return d
 
 
@@ -179,9 +181,12 @@ def _check_attention_args(query, key, value) -> None:
     if not (query.device == key.device == value.device):
         raise RuntimeError("query/key/value must be on one device")
     B, H, _, D = query.shape
-    if key.shape[0] != B or key.shape[1] != H or key.shape[3] != D:
+    Hkv = key.shape[1]
+    # Hkv < H: grouped-query attention (query head h reads key/value head h // (H // Hkv)), the
+    # semantics of torch's enable_gqa=True; the reference's op takes equal head counts only.
+    if key.shape[0] != B or key.shape[3] != D or Hkv < 1 or H % Hkv != 0:
         raise RuntimeError(f"key shape {tuple(key.shape)} does not match query {tuple(query.shape)}")
-    if tuple(value.shape) != (B, H, key.shape[2], D):
+    if tuple(value.shape) != (B, Hkv, key.shape[2], D):
         raise RuntimeError(f"value shape {tuple(value.shape)} does not match key {tuple(key.shape)}")
 
 

@@ -33,6 +33,7 @@ struct F32AttnParams {
   float* o;
   long long qs[3], ks[3], vs[3], os[3];
   int heads, len_q, len_k, head_dim, causal;
+  int group;  // query heads per key/value head (grouped-query attention)
   float scale_log2;
 };
 
@@ -71,8 +72,8 @@ __global__ void __launch_bounds__(256) attn_fwd_f32_kernel(const F32AttnParams p
   const int D = p.head_dim;
 
   const float* qb = p.q + b * p.qs[0] + h * p.qs[1];
-  const float* kb = p.k + b * p.ks[0] + h * p.ks[1];
-  const float* vb = p.v + b * p.vs[0] + h * p.vs[1];
+  const float* kb = p.k + b * p.ks[0] + (h / p.group) * p.ks[1];
+  const float* vb = p.v + b * p.vs[0] + (h / p.group) * p.vs[1];
   float* ob = p.o + b * p.os[0] + h * p.os[1];
 
   // Q tile, transposed, pre-multiplied by scale*log2(e) so scores come out in the exp2 domain.
@@ -234,6 +235,7 @@ int launch_f32_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
     p.os[i] = d->o_stride[i];
   }
   p.heads = static_cast<int>(d->heads);
+  p.group = attn_group(d);
   p.len_q = static_cast<int>(d->len_q);
   p.len_k = static_cast<int>(d->len_k);
   p.head_dim = static_cast<int>(d->head_dim);

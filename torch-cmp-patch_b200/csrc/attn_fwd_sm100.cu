@@ -102,6 +102,7 @@ struct FmhaParams {
   void* o;            // output [B, H, Lq, D] view
   long long os_b, os_h, os_s;  // its strides (elements)
   int head_dim;
+  int group;                   // query heads per key/value head (grouped-query attention)
   unsigned int* work;          // [0] next work item, [1] CTAs finished (both 0 at launch and exit)
   unsigned long long timeout_ns;
   unsigned int* dev_flags;
@@ -300,7 +301,7 @@ __global__ void __launch_bounds__(352, 1)
               const CUtensorMap* m = which ? &tm_v : &tm_k;
               for (int c = 0; c < C::NCH; ++c)
                 tma_load_4d(sKV + st * C::KV_BYTES + c * C::CH_BYTES, m, bar(C::B_FULL + st), c * 64,
-                            j * C::BN, h, b);
+                            j * C::BN, h / p.group, b);
             }
           }
         }
@@ -663,8 +664,8 @@ int launch_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
       BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap tq, tk, tv, to;
   if (!make_bhsd_map(&tq, dt, d->q, d->head_dim, d->len_q, d->heads, d->batch, d->q_stride, 128) ||
-      !make_bhsd_map(&tk, dt, d->k, d->head_dim, d->len_k, d->heads, d->batch, d->k_stride, 128) ||
-      !make_bhsd_map(&tv, dt, d->v, d->head_dim, d->len_k, d->heads, d->batch, d->v_stride, 128) ||
+      !make_bhsd_map(&tk, dt, d->k, d->head_dim, d->len_k, attn_heads_kv(d), d->batch, d->k_stride, 128) ||
+      !make_bhsd_map(&tv, dt, d->v, d->head_dim, d->len_k, attn_heads_kv(d), d->batch, d->v_stride, 128) ||
       !make_bhsd_map(&to, dt, d->o, d->head_dim, d->len_q, d->heads, d->batch, d->o_stride, 32))
     return CMPX_ERR_LAUNCH;
 
@@ -692,6 +693,7 @@ int launch_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   p.os_h = d->o_stride[1];
   p.os_s = d->o_stride[2];
   p.head_dim = static_cast<int>(d->head_dim);
+  p.group = attn_group(d);
   p.work = static_cast<unsigned int*>(d->workspace);
   p.timeout_ns = ctx.timeout_ns;
   p.dev_flags = ctx.dev_flags;

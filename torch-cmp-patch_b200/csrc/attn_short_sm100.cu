@@ -72,6 +72,7 @@ struct ShortParams {
   int n_tiles;    // n_qt * heads * batch
   int pv_steps;   // ceil(len_k / 16): K=16 steps of P V that hold keys
   int neg_scale;  // scale < 0: masked scores are +inf so that masked * scale = -inf
+  int group;      // query heads per key/value head (grouped-query attention)
   float scale_log2;
   unsigned long long timeout_ns;
   unsigned int* dev_flags;
@@ -173,8 +174,8 @@ __global__ void __launch_bounds__(320, 1)
             break;
           mbar_arrive_expect_tx(bar(C::B_KVFULL), 2 * C::TILE_BYTES);
           for (int c = 0; c < C::NCH; ++c) {
-            tma_load_4d(base + C::OFF_K + c * C::CH_BYTES, &tm_k, bar(C::B_KVFULL), c * 64, 0, h, b);
-            tma_load_4d(base + C::OFF_V + c * C::CH_BYTES, &tm_v, bar(C::B_KVFULL), c * 64, 0, h, b);
+            tma_load_4d(base + C::OFF_K + c * C::CH_BYTES, &tm_k, bar(C::B_KVFULL), c * 64, 0, h / p.group, b);
+            tma_load_4d(base + C::OFF_V + c * C::CH_BYTES, &tm_v, bar(C::B_KVFULL), c * 64, 0, h / p.group, b);
           }
           ++kv_round;
         }
@@ -447,8 +448,8 @@ int launch_short_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
       BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap tq, tk, tv, to;
   if (!make_bhsd_map(&tq, dt, d->q, d->head_dim, d->len_q, d->heads, d->batch, d->q_stride, 128) ||
-      !make_bhsd_map(&tk, dt, d->k, d->head_dim, d->len_k, d->heads, d->batch, d->k_stride, 128) ||
-      !make_bhsd_map(&tv, dt, d->v, d->head_dim, d->len_k, d->heads, d->batch, d->v_stride, 128) ||
+      !make_bhsd_map(&tk, dt, d->k, d->head_dim, d->len_k, attn_heads_kv(d), d->batch, d->k_stride, 128) ||
+      !make_bhsd_map(&tv, dt, d->v, d->head_dim, d->len_k, attn_heads_kv(d), d->batch, d->v_stride, 128) ||
       !make_bhsd_map(&to, dt, d->o, d->head_dim, d->len_q, d->heads, d->batch, d->o_stride, 32))
     return CMPX_ERR_LAUNCH;
 
@@ -470,6 +471,7 @@ int launch_short_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   p.n_tiles = static_cast<int>(p.n_qt * d->heads * d->batch);
   p.pv_steps = static_cast<int>((d->len_k + 15) / 16);
   p.neg_scale = d->scale < 0 ? 1 : 0;
+  p.group = attn_group(d);
   p.scale_log2 = static_cast<float>(d->scale * 1.4426950408889634);
   p.timeout_ns = ctx.timeout_ns;
   p.dev_flags = ctx.dev_flags;

@@ -82,6 +82,7 @@ struct X3Params {
   int n_qt, n_items;
   int qk_steps;   // ceil(head_dim / 8): K=8 steps of Q K^T
   int causal, neg_scale;
+  int group;      // query heads per key/value head (grouped-query attention)
   float scale_log2;
   float* o;
   long long os_b, os_h, os_s;
@@ -184,8 +185,8 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t sb = stage(load);
           mbar_arrive_expect_tx(bar(C::B_FULL + st), 2 * C::T_BYTES);
           for (int c = 0; c < 2; ++c) {
-            tma_load_4d(sb + C::ST_K + c * C::KCH, &tm_k, bar(C::B_FULL + st), c * 32, j * C::BN, h, b);
-            tma_load_4d(sb + C::ST_B + c * C::KCH, &tm_v, bar(C::B_FULL + st), c * 32, j * C::BN, h, b);
+            tma_load_4d(sb + C::ST_K + c * C::KCH, &tm_k, bar(C::B_FULL + st), c * 32, j * C::BN, h / p.group, b);
+            tma_load_4d(sb + C::ST_B + c * C::KCH, &tm_v, bar(C::B_FULL + st), c * 32, j * C::BN, h / p.group, b);
           }
         }
       }
@@ -565,8 +566,8 @@ int launch_attn_tf32x3(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   using C = X3Cfg;
   CUtensorMap tq, tk, tv;
   if (!make_map_f32(&tq, d->q, d->head_dim, d->len_q, d->heads, d->batch, d->q_stride, C::BM) ||
-      !make_map_f32(&tk, d->k, d->head_dim, d->len_k, d->heads, d->batch, d->k_stride, C::BN) ||
-      !make_map_f32(&tv, d->v, d->head_dim, d->len_k, d->heads, d->batch, d->v_stride, C::BN))
+      !make_map_f32(&tk, d->k, d->head_dim, d->len_k, attn_heads_kv(d), d->batch, d->k_stride, C::BN) ||
+      !make_map_f32(&tv, d->v, d->head_dim, d->len_k, attn_heads_kv(d), d->batch, d->v_stride, C::BN))
     return CMPX_ERR_LAUNCH;
   static std::once_flag once[64];
   int dev = 0;
@@ -587,6 +588,7 @@ int launch_attn_tf32x3(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   p.qk_steps = static_cast<int>((d->head_dim + 7) / 8);
   p.causal = d->causal ? 1 : 0;
   p.neg_scale = d->scale < 0 ? 1 : 0;
+  p.group = attn_group(d);
   p.scale_log2 = static_cast<float>(d->scale * 1.4426950408889634);
   p.o = static_cast<float*>(d->o);
   p.os_b = d->o_stride[0];

@@ -94,6 +94,9 @@ bool attn_desc_valid(const cmpx_attn_desc* d) {
   if (!d || !d->q || !d->k || !d->v || !d->o) return false;
   if (d->batch < 0 || d->heads < 0 || d->len_q < 0 || d->len_k < 0 || d->head_dim <= 0) return false;
   if (!std::isfinite(d->scale)) return false;
+  // grouped-query attention: heads_kv (0 = heads) must divide heads
+  if (d->heads_kv < 0 || (d->heads_kv > 0 && (d->heads_kv > d->heads || d->heads % d->heads_kv != 0)))
+    return false;
   return true;
 }
 

@@ -29,6 +29,13 @@ bool make_bhsd_map(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, in
                    int64_t H, int64_t B, const int64_t* st, uint32_t box_rows);
 
 // ---- attention ----
+// Key/value heads of a call (heads_kv = 0 means one per query head) and the query-head group size.
+inline int64_t attn_heads_kv(const cmpx_attn_desc* d) { return d->heads_kv > 0 ? d->heads_kv : d->heads; }
+inline int attn_group(const cmpx_attn_desc* d) {
+  const int64_t hk = attn_heads_kv(d);
+  return hk > 0 ? static_cast<int>(d->heads / hk) : 1;
+}
+
 // Tile-table lookups: return a static name and whether the kernel supports the call.
 const char* fmha_sm100_plan(const cmpx_attn_desc* d, int* status);
 int launch_fmha_sm100(const cmpx_attn_desc* d, const LaunchCtx& ctx);
