@@ -121,7 +121,9 @@ def _status_str(status: int) -> str:
 
 
 def _stream_handle(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """Raw cudaStream_t of the current torch stream on `device` (no Stream object is built)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    return torch._C._cuda_getCurrentRawStream(idx)
 
 
 def device_status() -> int:
@@ -146,26 +148,22 @@ def _post_check() -> None:
 
 def _tma_ok(t: torch.Tensor) -> bool:
     """Strides usable by the 16-bit TMA path: head dim contiguous, other strides 16-byte multiples."""
-    if t.stride(3) != 1 or t.data_ptr() % 16 != 0:
+    s0, s1, s2, s3 = t.stride()
+    if s3 != 1 or t.data_ptr() % 16 != 0:
         return False
     es = t.element_size()
-    return all(t.stride(i) > 0 and (t.stride(i) * es) % 16 == 0 for i in range(3))
+    return s0 > 0 and s1 > 0 and s2 > 0 and (s0 * es) % 16 == 0 and (s1 * es) % 16 == 0 and (s2 * es) % 16 == 0
 
 
-def _attn_desc(q, k, v, o, scale: float, causal: bool) -> AttnDesc:
-    d = AttnDesc()
-    d.q, d.k, d.v, d.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr()
-    d.batch, d.heads, d.len_q, d.head_dim = q.shape
-    d.len_k = k.shape[2]
-    for name, t in (("q_stride", q), ("k_stride", k), ("v_stride", v), ("o_stride", o)):
-        getattr(d, name)[:] = (t.stride(0), t.stride(1), t.stride(2))
-    d.dtype = _DTYPE[q.dtype]
-    d.causal = 1 if causal else 0
-    d.scale = float(scale)
-    d.workspace = None
-    d.workspace_bytes = 0
-    d.heads_kv = k.shape[1]
-    return d
+def _attn_desc(q, k, v, o, scale: float, causal: bool, workspace=None) -> AttnDesc:
+    B, H, Lq, D = q.shape
+    qs, ks, vs, os_ = q.stride(), k.stride(), v.stride(), o.stride()
+    return AttnDesc(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), B, H, Lq, k.shape[2], D,
+                    (ctypes.c_int64 * 3)(*qs[:3]), (ctypes.c_int64 * 3)(*ks[:3]),
+                    (ctypes.c_int64 * 3)(*vs[:3]), (ctypes.c_int64 * 3)(*os_[:3]),
+                    _DTYPE[q.dtype], 1 if causal else 0, float(scale),
+                    None if workspace is None else workspace.data_ptr(),
+                    0 if workspace is None else workspace.numel(), k.shape[1])
 
 
 def _check_attention_args(query, key, value) -> None:
@@ -224,15 +222,16 @@ def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
 def attention(query, key, value, scale=None, causal=False):
     """SDPA forward on the sm_100a kernels.  Same contract as the reference's ops.attention."""
     q, k, v, out, scale = _prepare_attention(query, key, value, scale, causal)
-    desc = _attn_desc(q, k, v, out, scale, bool(causal))
-    with torch.cuda.device(q.device):
-        stream = _stream_handle(q.device)
-        need = lib.cmpx_attn_workspace_size(ctypes.byref(desc))
-        if need:
-            ws = _workspace(q.device, stream, need)
-            desc.workspace = ws.data_ptr()
-            desc.workspace_bytes = ws.numel()
+    dev = q.device
+    stream = _stream_handle(dev)
+    # The 16-bit kernels keep their work counters in a 256-byte workspace (the fp32 ones need none;
+    # an unneeded workspace is ignored): one zero-filled buffer per (device, stream).
+    desc = _attn_desc(q, k, v, out, scale, bool(causal), _workspace(dev, stream, 256))
+    if dev.index == torch.cuda.current_device():
         st = lib.cmpx_attn_fwd(ctypes.byref(desc), stream)
+    else:
+        with torch.cuda.device(dev):
+            st = lib.cmpx_attn_fwd(ctypes.byref(desc), stream)
     if st != OK:
         raise CmpxError("attention", st)
     _post_check()
