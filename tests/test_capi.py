@@ -43,6 +43,9 @@ def test_library_exports_nothing_undeclared():
 
 def test_abi_version_and_status_strings():
     assert N.lib.cmpx_abi_version() == 2
+    header = HEADER.read_text()
+    m = re.search(r"#define CMPX_ABI_VERSION (\d+)", header)
+    assert m and int(m.group(1)) == N.ABI_VERSION == N.lib.cmpx_abi_version()
     assert N.lib.cmpx_status_str(0) == b"ok"
     for code in range(1, 9):
         assert N.lib.cmpx_status_str(code) not in (b"ok", b"unknown status")

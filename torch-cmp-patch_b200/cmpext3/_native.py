@@ -81,6 +81,10 @@ class SoftmaxDesc(ctypes.Structure):
                 ("dtype", ctypes.c_int32), ("reserved", ctypes.c_int32)]
 
 
+# CMPX_ABI_VERSION of include/cmpx_b200.h that the ctypes structures above mirror.
+ABI_VERSION = 2
+
+
 def _load() -> ctypes.CDLL:
     if not LIBRARY_PATH.exists():
         raise ImportError(
@@ -107,6 +111,10 @@ def _load() -> ctypes.CDLL:
     L.cmpx_selftest_wait_timeout.restype = ctypes.c_int
     L.cmpx_abi_version.argtypes = []
     L.cmpx_abi_version.restype = ctypes.c_int
+    if L.cmpx_abi_version() != ABI_VERSION:
+        raise ImportError(
+            f"{LIBRARY_PATH} has ABI version {L.cmpx_abi_version()}, this binding expects "
+            f"{ABI_VERSION} (the descriptor layouts above). Rebuild: python torch-cmp-patch_b200/build.py")
     return L
 
 

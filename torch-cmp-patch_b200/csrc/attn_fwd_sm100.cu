@@ -269,6 +269,11 @@ __global__ void __launch_bounds__(352, 1)
     const int kv_len = p.causal ? min(p.len_k, q0 + 256) : p.len_k;
     n_kv = (kv_len + C::BN - 1) / C::BN;
   };
+  // Key tiles tile 0 of an item takes part in: under the causal mask its rows (q0 .. q0+127) see no
+  // key of a last tile that starts past q0 + 127, so QK_0, its softmax and PV_0 skip that tile.
+  auto tile0_kv = [&](int q0, int n_kv) -> int {
+    return (p.causal && (n_kv - 1) * C::BN > q0 + C::BM - 1) ? n_kv - 1 : n_kv;
+  };
 
   if (warp >= 8) {
     if (warp == C::W_TMA) {
@@ -332,7 +337,7 @@ __global__ void __launch_bounds__(352, 1)
       bool ok = true;
       if (warp == C::W_MMA) {
         // QK_t(j) = Q_t K_j^T into S.  Order per key tile j:  QK_1(j) once tile 0 has read S(j);
-        // QK_0(j+1) once tile 1 has read S(j).
+        // QK_0(j+1) once tile 1 has read S(j).  Tile 0 stops after n_kv0 key tiles (tile0_kv).
         auto issue_qk = [&](int t, uint32_t k_addr) {
           const uint32_t q_addr = sQ + t * C::QTILE_BYTES;
 #pragma unroll
@@ -349,7 +354,8 @@ __global__ void __launch_bounds__(352, 1)
           if (w < 0) break;
           int b, h, q0, n_kv;
           item_geometry(w, b, h, q0, n_kv);
-          (void)b; (void)h; (void)q0;
+          (void)b; (void)h;
+          const int n_kv0 = tile0_kv(q0, n_kv);
           if (!(ok = mbar_wait_all(bar(C::B_QFULL), static_cast<uint32_t>(k) & 1u, ctl))) break;
           // S is free once tile 1's softmax read the previous item's last S.
           if (k > 0 && !(ok = mbar_wait_all(bar(C::B_SFREE + 1), (n_sfree1++) & 1u, ctl))) break;
@@ -359,7 +365,7 @@ __global__ void __launch_bounds__(352, 1)
           umma_commit_w(bar(C::B_SFULL + 0));
           for (int j = 0; ok && j < n_kv; ++j) {
             const int lk = base_load + 2 * j, lk1 = lk + 2;
-            if (!(ok = mbar_wait_all(bar(C::B_SFREE + 0), (n_sfree0++) & 1u, ctl))) break;
+            if (j < n_kv0 && !(ok = mbar_wait_all(bar(C::B_SFREE + 0), (n_sfree0++) & 1u, ctl))) break;
             tc_fence_after_sync();
             issue_qk(1, stage_of(lk));
             umma_commit_w(bar(C::B_SFULL + 1));
@@ -370,9 +376,11 @@ __global__ void __launch_bounds__(352, 1)
             }
             if (!(ok = mbar_wait_all(bar(C::B_SFREE + 1), (n_sfree1++) & 1u, ctl))) break;
             if (!(ok = mbar_wait_all(full_bar(lk1), round_par(lk1), ctl))) break;
-            tc_fence_after_sync();
-            issue_qk(0, stage_of(lk1));
-            umma_commit_w(bar(C::B_SFULL + 0));
+            if (j + 1 < n_kv0) {
+              tc_fence_after_sync();
+              issue_qk(0, stage_of(lk1));
+              umma_commit_w(bar(C::B_SFULL + 0));
+            }
           }
           base_load += 2 * n_kv;
         }
@@ -397,17 +405,20 @@ __global__ void __launch_bounds__(352, 1)
           if (w < 0) break;
           int b, h, q0, n_kv;
           item_geometry(w, b, h, q0, n_kv);
-          (void)b; (void)h; (void)q0;
+          (void)b; (void)h;
+          const int n_kv0 = tile0_kv(q0, n_kv);
           for (int j = 0; ok && j < n_kv; ++j) {
             const int lv = base_load + 2 * j + 1;
             if (!(ok = mbar_wait_all(full_bar(lv), round_par(lv), ctl))) break;
-            if (!(ok = mbar_wait_all(bar(C::B_PREADY + 0), (n_pready0++) & 1u, ctl))) break;
-            if (j == 0 && k > 0 &&
-                !(ok = mbar_wait_all(bar(C::B_OFREE + 0), static_cast<uint32_t>(k - 1) & 1u, ctl)))
-              break;
-            tc_fence_after_sync();
-            issue_pv(0, stage_of(lv), j > 0);
-            umma_commit_w(bar(C::B_PVDONE + 0));
+            if (j < n_kv0) {
+              if (!(ok = mbar_wait_all(bar(C::B_PREADY + 0), (n_pready0++) & 1u, ctl))) break;
+              if (j == 0 && k > 0 &&
+                  !(ok = mbar_wait_all(bar(C::B_OFREE + 0), static_cast<uint32_t>(k - 1) & 1u, ctl)))
+                break;
+              tc_fence_after_sync();
+              issue_pv(0, stage_of(lv), j > 0);
+              umma_commit_w(bar(C::B_PVDONE + 0));
+            }
             if (!(ok = mbar_wait_all(bar(C::B_PREADY + 1), (n_pready1++) & 1u, ctl))) break;
             if (j == 0 && k > 0 &&
                 !(ok = mbar_wait_all(bar(C::B_OFREE + 1), static_cast<uint32_t>(k - 1) & 1u, ctl)))
@@ -444,10 +455,11 @@ __global__ void __launch_bounds__(352, 1)
       int b, h, q0, n_kv;
       item_geometry(w, b, h, q0, n_kv);
       const int qrow = q0 + t * C::BM + row;
+      const int n_kv_t = t == 0 ? tile0_kv(q0, n_kv) : n_kv;
       float m_run = -INFINITY;  // running max of s * scale * log2(e)
       float l_run = 0.f;
 
-      for (int j = 0; j < n_kv; ++j) {
+      for (int j = 0; j < n_kv_t; ++j) {
         if (!mbar_wait_all(bar(C::B_SFULL + t), (n_sfull++) & 1u, ctl)) {
           ok = false;
           break;
