@@ -456,8 +456,9 @@ def main() -> int:
 
         def step():
             return cmpext3.ops.attention(q, k, v, scale, causal)
-        launches_per_step = 1
         kernel_name = N.attention_plan(q, k, v, scale, causal)
+        # a tail-split schedule launches the attention kernel and the kernel merging the split ranges
+        launches_per_step = 2 if "+tail-split" in kernel_name else 1
     else:
         # C3: patched torch.einsum -> planner -> patched torch.bmm -> sm_100a bmm kernel; patched
         # torch.softmax of the scores (a patched einsum's product) -> sm_100a row-softmax kernel

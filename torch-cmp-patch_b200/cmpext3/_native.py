@@ -93,6 +93,8 @@ def _load() -> ctypes.CDLL:
     L = ctypes.CDLL(str(LIBRARY_PATH))
     L.cmpx_attn_fwd.argtypes = [ctypes.POINTER(AttnDesc), ctypes.c_void_p]
     L.cmpx_attn_fwd.restype = ctypes.c_int
+    L.cmpx_attn_fwd_noalloc.argtypes = [ctypes.POINTER(AttnDesc), ctypes.c_void_p]
+    L.cmpx_attn_fwd_noalloc.restype = ctypes.c_int
     L.cmpx_attn_workspace_size.argtypes = [ctypes.POINTER(AttnDesc)]
     L.cmpx_attn_workspace_size.restype = ctypes.c_size_t
     L.cmpx_bmm.argtypes = [ctypes.POINTER(BmmDesc), ctypes.c_void_p]
@@ -232,9 +234,14 @@ def attention(query, key, value, scale=None, causal=False):
     q, k, v, out, scale = _prepare_attention(query, key, value, scale, causal)
     dev = q.device
     stream = _stream_handle(dev)
-    # The 16-bit kernels keep their work counters in a 256-byte workspace (the fp32 ones need none;
-    # an unneeded workspace is ignored): one zero-filled buffer per (device, stream).
-    desc = _attn_desc(q, k, v, out, scale, bool(causal), _workspace(dev, stream, 256))
+    # The 16-bit kernels keep their work counters (and, for a non-causal call whose last wave of
+    # work is partial, the split key ranges' partial results) in a workspace; the fp32 ones need
+    # none.  One zero-filled buffer per (device, stream), grown on demand.
+    desc = _attn_desc(q, k, v, out, scale, bool(causal))
+    nbytes = lib.cmpx_attn_workspace_size(ctypes.byref(desc))
+    if nbytes:
+        ws = _workspace(dev, stream, nbytes)
+        desc.workspace, desc.workspace_bytes = ws.data_ptr(), ws.numel()
     if dev.index == torch.cuda.current_device():
         st = lib.cmpx_attn_fwd(ctypes.byref(desc), stream)
     else:

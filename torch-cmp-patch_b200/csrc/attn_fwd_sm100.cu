@@ -48,6 +48,9 @@
 
 namespace cmpx {
 
+// Most key ranges one item of the tail split is cut into.
+constexpr int kMaxSplit = 8;
+
 template <int DP>
 struct FmhaCfg {
   static constexpr int BM = 128;                    // rows of one Q tile
@@ -104,6 +107,15 @@ struct FmhaParams {
   int head_dim;
   int group;                   // query heads per key/value head (grouped-query attention)
   unsigned int* work;          // [0] next work item, [1] CTAs finished (both 0 at launch and exit)
+  // Tail split (non-causal): work items 0 .. n_whole-1 are whole (row pair, head) items; each item
+  // after them is cut into `split` key ranges, one work item each (n_work items in all).  The
+  // range's partial O (fp32, not normalised) and its row max / sum go to part_o / part_ml, and
+  // fmha_split_merge_kernel merges them.
+  int n_whole;
+  int split;
+  int n_work;
+  float* part_ml;              // [n_work - n_whole][2][128] (m, l) pairs
+  float* part_o;               // [n_work - n_whole][2][128][DP]
   unsigned long long timeout_ns;
   unsigned int* dev_flags;
 };
@@ -181,15 +193,127 @@ __device__ __forceinline__ float row_min128(const float* s) {
   return fmin3(fmin3(a[0], a[1], a[2]), fmin3(a[3], a[4], a[5]), fminf(a[6], a[7]));
 }
 
+// Epilogue of one key range of a split item, for the calling warp's 32 rows of tile t (thread =
+// row): the row's O (fp32, scaled by 2^-m) and (m, l) go to the range's slot, and O_t is released
+// (ofree_bar).  fmha_split_merge_kernel, launched next on the stream, merges the ranges.
+// (Not inlined: its registers stay out of the softmax loop's allocation.)
+template <int DP>
+__device__ __noinline__ void fmha_split_epilogue(float* part_o, float* part_ml, int part, int t,
+                                                 int row, float m_run, float l_run, uint32_t o_tm,
+                                                 uint32_t ofree_bar) {
+  const size_t slot = (static_cast<size_t>(part) * 2 + t) * 128 + row;
+  float* po = part_o + slot * DP;
+#pragma unroll 1
+  for (int c = 0; c < DP / 32; ++c) {
+    uint32_t o[32];
+    tmem_ld32(o_tm + c * 32, o);
+    if (c == DP / 32 - 1) {
+      tc_fence_before_sync();
+      mbar_arrive(ofree_bar);  // O_t is read: the next item may overwrite it
+    }
+#pragma unroll
+    for (int e = 0; e < 32; e += 4)
+      *reinterpret_cast<uint4*>(po + c * 32 + e) = make_uint4(o[e], o[e + 1], o[e + 2], o[e + 3]);
+  }
+  reinterpret_cast<float2*>(part_ml)[slot] = make_float2(m_run, l_run);
+}
+
+// Merge of the split items' key ranges: for each of their rows, O = sum_r 2^(m_r - M) O_r /
+// sum_r 2^(m_r - M) l_r with M = max_r m_r -- the online-softmax rescale step applied across
+// ranges instead of across key tiles -- written as the 16-bit output row.  A warp takes 2 rows
+// (one after the other in the row order of the ranges' slots); lane l takes columns
+// [l*CPL, (l+1)*CPL) of every range's row, so every load is one contiguous row.  Spread over
+// ~rows/32 CTAs, the merge costs a round trip or two to L2 per warp; done by the last range's own
+// CTA it was bound by the loads one SM can keep in flight.
+template <int DP, bool BF16>
+__global__ void __launch_bounds__(128) fmha_split_merge_kernel(const __grid_constant__ FmhaParams p) {
+  constexpr int CPL = DP / 32;  // fp32 columns per lane: 2 or 4
+  constexpr int ROWS = 2;       // rows per warp
+  const int lane = threadIdx.x & 31;
+  const int col = lane * CPL;
+  const int split = p.split;
+  const int n_rows = (p.n_items - p.n_whole) * 256;
+  const int r0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * ROWS;
+  float2 ml[ROWS][kMaxSplit];
+  float o[ROWS][kMaxSplit][CPL];
+#pragma unroll
+  for (int i = 0; i < ROWS; ++i) {
+    const int gr = min(r0 + i, n_rows - 1);  // (rows past the end repeat the last; not stored)
+    const int item = p.n_whole + gr / 256;
+    const int tr = gr % 256;
+    const size_t slot0 = (static_cast<size_t>(item - p.n_whole) * split * 2 + tr / 128) * 128 + tr % 128;
+#pragma unroll
+    for (int r = 0; r < kMaxSplit; ++r) {
+      const size_t slot = slot0 + static_cast<size_t>(r) * 2 * 128;
+      if (r < split) {
+        ml[i][r] = __ldcg(reinterpret_cast<const float2*>(p.part_ml) + slot);
+        if constexpr (CPL == 2) {
+          const float2 x = ld_cg_f2(p.part_o + slot * DP + col);
+          o[i][r][0] = x.x;
+          o[i][r][1] = x.y;
+        } else {
+          const float4 x = ld_cg_f4(p.part_o + slot * DP + col);
+          o[i][r][0] = x.x;
+          o[i][r][1] = x.y;
+          o[i][r][2] = x.z;
+          o[i][r][3] = x.w;
+        }
+      } else {
+        ml[i][r] = make_float2(-INFINITY, 0.f);
+#pragma unroll
+        for (int e = 0; e < CPL; ++e) o[i][r][e] = 0.f;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < ROWS; ++i) {
+    const int gr = r0 + i;
+    if (gr >= n_rows) break;
+    const int item = p.n_whole + gr / 256;
+    const int bh = item / p.n_pairs;
+    const int pair = p.n_pairs - 1 - (item - bh * p.n_pairs);
+    const int b = bh / p.heads;
+    const int h = bh - b * p.heads;
+    const int qrow = pair * 256 + gr % 256;
+    if (qrow >= p.len_q || col >= p.head_dim) continue;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < kMaxSplit; ++r) mx = fmaxf(mx, ml[i][r].x);
+    float a[CPL];
+#pragma unroll
+    for (int e = 0; e < CPL; ++e) a[e] = 0.f;
+    float lsum = 0.f;
+#pragma unroll
+    for (int r = 0; r < kMaxSplit; ++r) {
+      const float w = r < split ? ex2_approx(ml[i][r].x - mx) : 0.f;
+      lsum += w * ml[i][r].y;
+#pragma unroll
+      for (int e = 0; e < CPL; ++e) a[e] += w * o[i][r][e];
+    }
+    const float inv = 1.f / lsum;
+    uint16_t* dst = static_cast<uint16_t*>(p.o) + b * p.os_b + h * p.os_h +
+                    static_cast<long long>(qrow) * p.os_s + col;
+    const uint32_t lo = BF16 ? pack_bf16x2(a[0] * inv, a[1] * inv) : pack_f16x2(a[0] * inv, a[1] * inv);
+    if constexpr (CPL == 2) {
+      *reinterpret_cast<uint32_t*>(dst) = lo;
+    } else {
+      const uint32_t hi = BF16 ? pack_bf16x2(a[2] * inv, a[3] * inv) : pack_f16x2(a[2] * inv, a[3] * inv);
+      *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
+    }
+  }
+}
+
 // Work item w (persistent schedule): bh = w / n_pairs, pair = n_pairs - 1 - w % n_pairs.  The items
 // of one (b, h) are consecutive, so the CTAs busy at any moment share a few heads' K/V in L2, and
-// within a head the heavy (late, causal) row pairs go first.
-template <int DP, bool BF16>
+// within a head the heavy (late, causal) row pairs go first.  SPLIT: the launch has a tail split
+// (a separate instantiation, so that launches without one run the unsplit code unchanged).
+template <int DP, bool BF16, bool SPLIT>
 __global__ void __launch_bounds__(352, 1)
     fmha_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v,
-                          const __grid_constant__ CUtensorMap tm_o, const FmhaParams p) {
+                          const __grid_constant__ CUtensorMap tm_o,
+                          const __grid_constant__ FmhaParams p) {
   using C = FmhaCfg<DP>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
@@ -260,14 +384,34 @@ __global__ void __launch_bounds__(352, 1)
     if (lane == 0) mbar_arrive(bar(C::B_ITEMPTY + slot));
     return true;
   };
-  auto item_geometry = [&](int w, int& b, int& h, int& q0, int& n_kv) {
-    const int bh = w / p.n_pairs;
-    const int pair = p.n_pairs - 1 - (w - bh * p.n_pairs);
-    b = bh / p.heads;
-    h = bh - b * p.heads;
-    q0 = pair * 256;
-    const int kv_len = p.causal ? min(p.len_k, q0 + 256) : p.len_k;
-    n_kv = (kv_len + C::BN - 1) / C::BN;
+  // Work item w -> (b, h, rows q0 .. q0+255, key tiles [j0, j1) of the item's n_kv); part >= 0 is
+  // the index of a split item's key range among all ranges (-1: whole item).
+  struct Work {
+    int b, h, q0, n_kv, j0, j1, item, part;
+  };
+  auto work_geometry = [&](int w) -> Work {
+    Work g;
+    g.item = w;
+    g.part = -1;
+    if (SPLIT && w >= p.n_whole) {
+      g.part = w - p.n_whole;
+      g.item = p.n_whole + g.part / p.split;
+    }
+    const int bh = g.item / p.n_pairs;
+    const int pair = p.n_pairs - 1 - (g.item - bh * p.n_pairs);
+    g.b = bh / p.heads;
+    g.h = bh - g.b * p.heads;
+    g.q0 = pair * 256;
+    const int kv_len = p.causal ? min(p.len_k, g.q0 + 256) : p.len_k;
+    g.n_kv = (kv_len + C::BN - 1) / C::BN;
+    g.j0 = 0;
+    g.j1 = g.n_kv;
+    if (SPLIT && g.part >= 0) {  // (the host splits only non-causal calls, with n_kv >= 4 * split)
+      const int r = g.part - (g.item - p.n_whole) * p.split;
+      g.j0 = r * g.n_kv / p.split;
+      g.j1 = (r + 1) * g.n_kv / p.split;
+    }
+    return g;
   };
   // Key tiles tile 0 of an item takes part in: under the causal mask its rows (q0 .. q0+127) see no
   // key of a last tile that starts past q0 + 127, so QK_0, its softmax and PV_0 skip that tile.
@@ -281,23 +425,32 @@ __global__ void __launch_bounds__(352, 1)
       if (lane == 0) {
         int load = 0;  // K/V ring loads issued so far (K_j and V_j of every item, in order)
         bool ok = true;
+        bool took_range = false;
         for (int k = 0; ok; ++k) {
           const int slot = k & 1;
           if (!(ok = mbar_wait(bar(C::B_ITEMPTY + slot), (static_cast<uint32_t>(k >> 1) & 1u) ^ 1u, ctl))) break;
+          // Whole items come from the shared counter.  The split items' key ranges (never more
+          // than CTAs) are dealt one per CTA, range blockIdx.x: drawn from the counter, a CTA
+          // whose producer runs ahead -- it takes its next item as soon as it has issued the
+          // current one's loads, which for a short range is early -- would take several.
           const int wi = static_cast<int>(atomicAdd(p.work, 1u));
-          const int w = wi < p.n_items ? wi : -1;
+          int w = wi < p.n_whole ? wi : -1;
+          if (SPLIT && w < 0 && !took_range && static_cast<int>(blockIdx.x) < p.n_work - p.n_whole) {
+            w = p.n_whole + static_cast<int>(blockIdx.x);
+            took_range = true;
+          }
           item_slot[slot] = w;
           mbar_arrive(bar(C::B_ITFULL + slot));
           if (w < 0) break;
-          int b, h, q0, n_kv;
-          item_geometry(w, b, h, q0, n_kv);
+          const Work g = work_geometry(w);
+          const int b = g.b, h = g.h, q0 = g.q0;
           if (k > 0 && !(ok = mbar_wait(bar(C::B_QEMPTY), static_cast<uint32_t>(k - 1) & 1u, ctl))) break;
           mbar_arrive_expect_tx(bar(C::B_QFULL), 2 * C::QTILE_BYTES);
           for (int t = 0; t < 2; ++t)
             for (int c = 0; c < C::NCH; ++c)
               tma_load_4d(sQ + t * C::QTILE_BYTES + c * C::CH_BYTES, &tm_q, bar(C::B_QFULL), c * 64,
                           q0 + t * C::BM, h, b);
-          for (int j = 0; ok && j < n_kv; ++j) {
+          for (int j = g.j0; ok && j < g.j1; ++j) {
             for (int which = 0; which < 2; ++which, ++load) {
               const int st = load % C::NSTAGE;
               const uint32_t rnd = static_cast<uint32_t>(load / C::NSTAGE);
@@ -352,10 +505,8 @@ __global__ void __launch_bounds__(352, 1)
           int w;
           if (!(ok = next_item_warp(k, w))) break;
           if (w < 0) break;
-          int b, h, q0, n_kv;
-          item_geometry(w, b, h, q0, n_kv);
-          (void)b; (void)h;
-          const int n_kv0 = tile0_kv(q0, n_kv);
+          const Work g = work_geometry(w);
+          const int n_kv0 = tile0_kv(g.q0, g.n_kv);  // (split items are non-causal: n_kv0 = n_kv)
           if (!(ok = mbar_wait_all(bar(C::B_QFULL), static_cast<uint32_t>(k) & 1u, ctl))) break;
           // S is free once tile 1's softmax read the previous item's last S.
           if (k > 0 && !(ok = mbar_wait_all(bar(C::B_SFREE + 1), (n_sfree1++) & 1u, ctl))) break;
@@ -363,14 +514,14 @@ __global__ void __launch_bounds__(352, 1)
           tc_fence_after_sync();
           issue_qk(0, stage_of(base_load));
           umma_commit_w(bar(C::B_SFULL + 0));
-          for (int j = 0; ok && j < n_kv; ++j) {
-            const int lk = base_load + 2 * j, lk1 = lk + 2;
+          for (int j = g.j0; ok && j < g.j1; ++j) {
+            const int lk = base_load + 2 * (j - g.j0), lk1 = lk + 2;
             if (j < n_kv0 && !(ok = mbar_wait_all(bar(C::B_SFREE + 0), (n_sfree0++) & 1u, ctl))) break;
             tc_fence_after_sync();
             issue_qk(1, stage_of(lk));
             umma_commit_w(bar(C::B_SFULL + 1));
             umma_commit_w(empty_bar(lk));  // K_j done
-            if (j + 1 == n_kv) {
+            if (j + 1 == g.j1) {
               umma_commit_w(bar(C::B_QEMPTY));  // last QK of the item
               break;
             }
@@ -382,7 +533,7 @@ __global__ void __launch_bounds__(352, 1)
               umma_commit_w(bar(C::B_SFULL + 0));
             }
           }
-          base_load += 2 * n_kv;
+          base_load += 2 * (g.j1 - g.j0);
         }
       } else {
         // O_t += P_t V_j, P_t from TMEM (16-bit, two keys per 32-bit column).  Order per key tile
@@ -403,32 +554,30 @@ __global__ void __launch_bounds__(352, 1)
           int w;
           if (!(ok = next_item_warp(k, w))) break;
           if (w < 0) break;
-          int b, h, q0, n_kv;
-          item_geometry(w, b, h, q0, n_kv);
-          (void)b; (void)h;
-          const int n_kv0 = tile0_kv(q0, n_kv);
-          for (int j = 0; ok && j < n_kv; ++j) {
-            const int lv = base_load + 2 * j + 1;
+          const Work g = work_geometry(w);
+          const int n_kv0 = tile0_kv(g.q0, g.n_kv);
+          for (int j = g.j0; ok && j < g.j1; ++j) {
+            const int lv = base_load + 2 * (j - g.j0) + 1;
             if (!(ok = mbar_wait_all(full_bar(lv), round_par(lv), ctl))) break;
             if (j < n_kv0) {
               if (!(ok = mbar_wait_all(bar(C::B_PREADY + 0), (n_pready0++) & 1u, ctl))) break;
-              if (j == 0 && k > 0 &&
+              if (j == g.j0 && k > 0 &&
                   !(ok = mbar_wait_all(bar(C::B_OFREE + 0), static_cast<uint32_t>(k - 1) & 1u, ctl)))
                 break;
               tc_fence_after_sync();
-              issue_pv(0, stage_of(lv), j > 0);
+              issue_pv(0, stage_of(lv), j > g.j0);
               umma_commit_w(bar(C::B_PVDONE + 0));
             }
             if (!(ok = mbar_wait_all(bar(C::B_PREADY + 1), (n_pready1++) & 1u, ctl))) break;
-            if (j == 0 && k > 0 &&
+            if (j == g.j0 && k > 0 &&
                 !(ok = mbar_wait_all(bar(C::B_OFREE + 1), static_cast<uint32_t>(k - 1) & 1u, ctl)))
               break;
             tc_fence_after_sync();
-            issue_pv(1, stage_of(lv), j > 0);
+            issue_pv(1, stage_of(lv), j > g.j0);
             umma_commit_w(bar(C::B_PVDONE + 1));
             umma_commit_w(empty_bar(lv));  // V_j done (read by both tiles' PVs)
           }
-          base_load += 2 * n_kv;
+          base_load += 2 * (g.j1 - g.j0);
         }
       }
     }
@@ -452,14 +601,18 @@ __global__ void __launch_bounds__(352, 1)
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       w = __shfl_sync(0xffffffffu, w, 0);
       if (!ok || w < 0) break;
-      int b, h, q0, n_kv;
-      item_geometry(w, b, h, q0, n_kv);
+      int q0, j_begin, j_end;  // (the rest of the geometry is recomputed for the epilogue)
+      {
+        const Work g = work_geometry(w);
+        q0 = g.q0;
+        j_begin = g.j0;
+        j_end = t == 0 ? min(g.j1, tile0_kv(q0, g.n_kv)) : g.j1;
+      }
       const int qrow = q0 + t * C::BM + row;
-      const int n_kv_t = t == 0 ? tile0_kv(q0, n_kv) : n_kv;
       float m_run = -INFINITY;  // running max of s * scale * log2(e)
       float l_run = 0.f;
 
-      for (int j = 0; j < n_kv_t; ++j) {
+      for (int j = j_begin; j < j_end; ++j) {
         if (!mbar_wait_all(bar(C::B_SFULL + t), (n_sfull++) & 1u, ctl)) {
           ok = false;
           break;
@@ -484,13 +637,13 @@ __global__ void __launch_bounds__(352, 1)
         // stale max is usable (exact: O, l and P share it).  Otherwise -- and on a row's first
         // tile, where m_run is still -inf -- the warp takes the slow path: exact tile max, new
         // running max, P recomputed, l and O rescaled.  After a slow pass m_run is the true running
-        // max, so later triggers are rare.  (Key 0 is never masked, so m_run is finite after j = 0.)
-        // P_t and O_t are free once PV_t(j-1) has completed: the fast pass waits for that between
-        // computing and storing its first half (no wait at j = 0: the previous item's epilogue
-        // already waited for its last PV).
+        // max, so later triggers are rare.  (The first key of a work item's range is never masked,
+        // so m_run is finite after its first tile.)  P_t and O_t are free once PV_t(j-1) has
+        // completed: the fast pass waits for that between computing and storing its first half (no
+        // wait on a range's first tile: the previous item's epilogue already waited for its last PV).
         float l_tile = 0.f;
         float alpha = 1.f;
-        bool slow = (j == 0);
+        bool slow = (j == j_begin);
         if (!slow) {
           bool pv_ok = true;
           l_tile = exp_pass<BF16, C::EMU>(s, sl2, -m_run, p_tm, [&] {
@@ -511,7 +664,7 @@ __global__ void __launch_bounds__(352, 1)
             m_run = m_tile;
           }
           l_tile = exp_pass<BF16, C::EMU>(s, sl2, -m_run, p_tm, [] {});
-          if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+          if (j > j_begin && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
             for (int c = 0; c < DP / 32; ++c) {
               uint32_t o[32];
@@ -534,11 +687,23 @@ __global__ void __launch_bounds__(352, 1)
       // take turns per 32-row quarter (tile 0 of item k waits for tile 1 of item k-1 and vice versa).
       if (!(ok = mbar_wait_all(bar(C::B_PVDONE + t), (n_pvdone++) & 1u, ctl))) break;
       tc_fence_after_sync();
+      const Work g = work_geometry(w);
+      const int b = g.b, h = g.h;
       const float inv_l = 1.f / l_run;
       const uint32_t turn_bar = bar(C::B_OST + t * 4 + wq);
       if (t == 1 || k > 0) {
         const uint32_t par = t == 1 ? static_cast<uint32_t>(k) & 1u : static_cast<uint32_t>(k - 1) & 1u;
         if (!(ok = mbar_wait_all(turn_bar, par, ctl))) break;
+      }
+      if (SPLIT && g.part >= 0) {
+        // A key range of a split item: park this row's partial result for the merge kernel.  The
+        // staging turn is taken and handed straight on, unused (the turn order of later items
+        // stays as it is).
+        if (lane == 0) mbar_arrive(bar(C::B_OST + (1 - t) * 4 + wq));
+        __syncwarp();
+        fmha_split_epilogue<DP>(p.part_o, p.part_ml, g.part, t, row, m_run, l_run, o_tm,
+                                bar(C::B_OFREE + t));
+        continue;
       }
       const uint32_t stage = base + C::OFF_OST;
 #pragma unroll 1
@@ -612,12 +777,51 @@ namespace {
 
 bool stride_ok(int64_t s, int esize) { return s > 0 && ((s * esize) % 16) == 0 && (s * esize) < (1ll << 40); }
 
-template <int DP, bool BF16>
+template <int DP, bool BF16, bool SPLIT>
 void* fmha_kernel_ptr() {
-  return reinterpret_cast<void*>(&fmha_fwd_sm100_kernel<DP, BF16>);
+  return reinterpret_cast<void*>(&fmha_fwd_sm100_kernel<DP, BF16, SPLIT>);
+}
+
+// Tail split of a non-causal launch on num_sms persistent CTAs.  With n items and G CTAs, the
+// first n - n % G items run whole (full waves); the n % G items of the last, partial wave would
+// leave most CTAs idle while they run, so each is cut into split = G / (n % G) key ranges (at most
+// kMaxSplit, and at least 4 key tiles per range).  Workspace: the 256-byte work counters, then each
+// range's (m, l) per row and its fp32 O rows (scratch: written before they are read).
+struct FmhaSplit {
+  int n_whole = 0, split = 1, n_work = 0;
+  size_t ml_off = 0, o_off = 0, bytes = kAttnWorkspaceMin;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+FmhaSplit fmha_split_plan(const cmpx_attn_desc* d, int num_sms) {
+  FmhaSplit sp;
+  const int64_t n_items = ((d->len_q + 255) / 256) * d->heads * d->batch;
+  sp.n_whole = static_cast<int>(n_items);
+  sp.n_work = static_cast<int>(n_items);
+  if (d->causal || num_sms <= 1 || n_items <= 0) return sp;
+  const int64_t rem = n_items % num_sms;
+  if (rem == 0) return sp;
+  const int64_t n_kv = (d->len_k + 127) / 128;
+  const int64_t split = std::min<int64_t>({num_sms / rem, n_kv / 4, kMaxSplit});
+  if (split < 2) return sp;
+  const int dp = d->head_dim <= 64 ? 64 : 128;
+  sp.split = static_cast<int>(split);
+  sp.n_whole = static_cast<int>(n_items - rem);
+  sp.n_work = static_cast<int>(sp.n_whole + rem * split);
+  const size_t ranges = static_cast<size_t>(rem * split);
+  sp.ml_off = kAttnWorkspaceMin;
+  sp.o_off = sp.ml_off + align256(ranges * 256 * 2 * sizeof(float));
+  sp.bytes = sp.o_off + ranges * 256 * dp * sizeof(float);
+  return sp;
 }
 
 }  // namespace
+
+size_t fmha_workspace_bytes(const cmpx_attn_desc* d, int num_sms) {
+  if (fmha_short_eligible(d)) return kAttnWorkspaceMin;
+  return fmha_split_plan(d, num_sms).bytes;
+}
 
 const char* fmha_sm100_plan(const cmpx_attn_desc* d, int* status) {
   *status = CMPX_OK;
@@ -651,10 +855,16 @@ const char* fmha_sm100_plan(const cmpx_attn_desc* d, int* status) {
     return "none";
   }
   if (fmha_short_eligible(d)) return fmha_short_name(d);
+  // The name shows the schedule a call given cmpx_attn_workspace_size() bytes runs: "+tail-split"
+  // when the last wave's items are split into key ranges (a second, merging kernel follows).
+  const bool split = fmha_split_plan(d, current_num_sms()).split > 1;
   const bool bf = d->dtype == CMPX_BF16;
-  if (d->head_dim <= 64)
-    return bf ? "fmha_sm100<bf16,D64,2x128q,128kv,6st,persistent>" : "fmha_sm100<f16,D64,2x128q,128kv,6st,persistent>";
-  return bf ? "fmha_sm100<bf16,D128,2x128q,128kv,4st,persistent>" : "fmha_sm100<f16,D128,2x128q,128kv,4st,persistent>";
+  static const char* const names[2][2][2] = {
+      {{"fmha_sm100<f16,D64,2x128q,128kv,6st,persistent>", "fmha_sm100<f16,D64,2x128q,128kv,6st,persistent+tail-split>"},
+       {"fmha_sm100<bf16,D64,2x128q,128kv,6st,persistent>", "fmha_sm100<bf16,D64,2x128q,128kv,6st,persistent+tail-split>"}},
+      {{"fmha_sm100<f16,D128,2x128q,128kv,4st,persistent>", "fmha_sm100<f16,D128,2x128q,128kv,4st,persistent+tail-split>"},
+       {"fmha_sm100<bf16,D128,2x128q,128kv,4st,persistent>", "fmha_sm100<bf16,D128,2x128q,128kv,4st,persistent+tail-split>"}}};
+  return names[d->head_dim <= 64 ? 0 : 1][bf ? 1 : 0][split ? 1 : 0];
 }
 
 bool make_bhsd_map(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, int64_t D, int64_t L,
@@ -686,8 +896,11 @@ int launch_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   cudaGetDevice(&dev);
   cudaError_t attr_err = cudaSuccess;
   std::call_once(once[dev & 63], [&] {
-    attr_err = cudaFuncSetAttribute(fmha_kernel_ptr<DP, BF16>(),
+    attr_err = cudaFuncSetAttribute(fmha_kernel_ptr<DP, BF16, false>(),
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (attr_err == cudaSuccess)
+      attr_err = cudaFuncSetAttribute(fmha_kernel_ptr<DP, BF16, true>(),
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   });
   if (attr_err != cudaSuccess) return CMPX_ERR_LAUNCH;
 
@@ -709,8 +922,23 @@ int launch_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   p.work = static_cast<unsigned int*>(d->workspace);
   p.timeout_ns = ctx.timeout_ns;
   p.dev_flags = ctx.dev_flags;
-  const int grid = std::min(p.n_items, std::max(1, ctx.num_sms));
-  fmha_fwd_sm100_kernel<DP, BF16><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, to, p);
+  FmhaSplit sp = fmha_split_plan(d, ctx.num_sms);
+  if (d->workspace_bytes < sp.bytes) sp = FmhaSplit{};  // too small a workspace: no split
+  uint8_t* ws = static_cast<uint8_t*>(d->workspace);
+  p.n_whole = sp.split > 1 ? sp.n_whole : p.n_items;
+  p.split = sp.split;
+  p.n_work = sp.split > 1 ? sp.n_work : p.n_items;
+  p.part_ml = sp.split > 1 ? reinterpret_cast<float*>(ws + sp.ml_off) : nullptr;
+  p.part_o = sp.split > 1 ? reinterpret_cast<float*>(ws + sp.o_off) : nullptr;
+  const int grid = std::min(p.n_work, std::max(1, ctx.num_sms));
+  if (sp.split > 1) {
+    fmha_fwd_sm100_kernel<DP, BF16, true><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, to, p);
+    if (cudaGetLastError() != cudaSuccess) return CMPX_ERR_LAUNCH;
+    const int rows = (p.n_items - p.n_whole) * 256;
+    fmha_split_merge_kernel<DP, BF16><<<(rows + 7) / 8, 128, 0, ctx.stream>>>(p);
+  } else {
+    fmha_fwd_sm100_kernel<DP, BF16, false><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, to, p);
+  }
   return cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
 }
 

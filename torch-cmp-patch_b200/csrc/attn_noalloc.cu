@@ -60,7 +60,8 @@ void* scratch_on_current_device(int* status) {
 
 extern "C" CMPX_API int cmpx_attn_fwd_noalloc(const cmpx_attn_desc* desc, void* stream) {
   if (!desc) return CMPX_ERR_INVALID_ARGUMENT;
-  const size_t need = cmpx_attn_workspace_size(desc);
+  // The 16-bit kernels run with their minimum workspace (the work counters; no tail split).
+  const size_t need = (desc->dtype == CMPX_F16 || desc->dtype == CMPX_BF16) ? cmpx::kAttnWorkspaceMin : 0;
   if (need > kNoAllocScratchBytes) return CMPX_ERR_WORKSPACE;  // beyond the fixed scratch
   cmpx_attn_desc d = *desc;  // the caller's workspace fields are ignored
   d.workspace = nullptr;

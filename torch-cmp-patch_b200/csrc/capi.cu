@@ -26,7 +26,6 @@ __device__ unsigned int g_dev_flags;
 namespace {
 
 constexpr int kMaxDevices = 64;
-constexpr size_t kAttnWorkspaceBytes = 256;
 
 struct DeviceState {
   std::once_flag once;
@@ -187,6 +186,18 @@ int launch_wait_selftest(uint64_t timeout_ns, const LaunchCtx& ctx) {
   return cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
 }
 
+// SM count of the current device (148, a B200's, when no device can be queried: sizes computed
+// from it are upper bounds that a launch on fewer SMs checks again).
+int current_num_sms() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices) {
+    LaunchCtx ctx;
+    if (device_ctx(&ctx, nullptr) == CMPX_OK && ctx.num_sms > 0) return ctx.num_sms;
+  }
+  cudaGetLastError();
+  return 148;
+}
+
 }  // namespace cmpx
 
 using namespace cmpx;
@@ -211,9 +222,10 @@ const char* cmpx_status_str(int status) {
 }
 
 size_t cmpx_attn_workspace_size(const cmpx_attn_desc* desc) {
-  // The persistent 16-bit kernel keeps two work counters (next item, CTAs finished).
+  // The persistent 16-bit kernels keep two work counters (next item, CTAs finished); a non-causal
+  // call whose last wave of items is partial also parks the split items' partial results.
   if (!desc || (desc->dtype != CMPX_F16 && desc->dtype != CMPX_BF16)) return 0;
-  return kAttnWorkspaceBytes;
+  return fmha_workspace_bytes(desc, current_num_sms());
 }
 
 int cmpx_attn_plan(const cmpx_attn_desc* desc, char* buf, size_t buf_len) {
@@ -235,8 +247,8 @@ int cmpx_attn_fwd(const cmpx_attn_desc* desc, void* stream) {
   attn_plan_impl(desc, &st);
   if (st != CMPX_OK) return st;
   if (desc->batch == 0 || desc->heads == 0 || desc->len_q == 0) return CMPX_OK;
-  if (cmpx_attn_workspace_size(desc) > 0 &&
-      (!desc->workspace || desc->workspace_bytes < cmpx_attn_workspace_size(desc) ||
+  if ((desc->dtype == CMPX_F16 || desc->dtype == CMPX_BF16) &&
+      (!desc->workspace || desc->workspace_bytes < kAttnWorkspaceMin ||
        (reinterpret_cast<uintptr_t>(desc->workspace) & 15u) != 0))
     return CMPX_ERR_WORKSPACE;
   LaunchCtx ctx;

@@ -36,8 +36,18 @@ inline int attn_group(const cmpx_attn_desc* d) {
   return hk > 0 ? static_cast<int>(d->heads / hk) : 1;
 }
 
+// SM count of the current device (148, a B200's, when no device can be queried).
+int current_num_sms();
+
+// Smallest workspace the 16-bit attention kernels accept: their two work counters.
+constexpr size_t kAttnWorkspaceMin = 256;
+
 // Tile-table lookups: return a static name and whether the kernel supports the call.
 const char* fmha_sm100_plan(const cmpx_attn_desc* d, int* status);
+// Workspace for the fastest schedule of a 16-bit call on num_sms SMs (>= kAttnWorkspaceMin: the
+// tail split's partial results on top of the counters; a workspace of at least kAttnWorkspaceMin
+// but below this runs unsplit).
+size_t fmha_workspace_bytes(const cmpx_attn_desc* d, int num_sms);
 int launch_fmha_sm100(const cmpx_attn_desc* d, const LaunchCtx& ctx);
 // Short key sequences (non-causal, 1 <= Lk <= 128): one key tile, Q tiles streamed.
 bool fmha_short_eligible(const cmpx_attn_desc* d);

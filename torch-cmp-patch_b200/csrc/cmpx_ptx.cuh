@@ -508,6 +508,20 @@ __device__ __forceinline__ uint64_t exp2_poly3_x2(uint64_t xv) {
                  __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23)));
 }
 
+// Global loads cached in L2 only (data another SM wrote in this launch).  Neither volatile nor a
+// memory clobber: the compiler may move them across unrelated stores, so a caller must only use
+// them on data that no store of the same thread can alias in between.
+__device__ __forceinline__ float2 ld_cg_f2(const float* ptr) {
+  float2 v;
+  asm("ld.global.cg.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "l"(ptr));
+  return v;
+}
+__device__ __forceinline__ float4 ld_cg_f4(const float* ptr) {
+  float4 v;
+  asm("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(ptr));
+  return v;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
