@@ -166,6 +166,15 @@ def test_bmm_plan_for_the_einsum_attention_shapes():
     assert st == 0 and name.startswith("bmm_f32_simt")
 
 
+@pytest.mark.parametrize("shape,width", [((8, 4096, 4096, 4096), "128x256"), ((1, 300, 520, 600), "128x256"),
+                                         ((4, 512, 256, 256), "128x128"), ((64, 2048, 2048, 64), "128x128"),
+                                         ((2, 512, 128, 1024), "128x64")])
+def test_bmm_tile_width(shape, width):
+    nb, m, n, k = shape  # 128x256 only for wide N with K >= 512 (compute-bound); 128x128 / 128x64 else
+    st, name = _bplan(_bmm(nb, m, n, k, bt=True))
+    assert st == 0 and width in name, name
+
+
 def test_bmm_rejects_misaligned_rows():
     d = _bmm(2, 64, 62, 64)  # N*2 bytes = 124, not a 16-byte multiple
     assert _bplan(d)[0] == N.ERR_MISALIGNED

@@ -37,19 +37,24 @@ struct BmmCfg {
   static constexpr int A_BYTES = BM * BK * 2;       // 16 KB
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = BN == 128 ? 4 : 6;
+  static constexpr int STAGES = BN == 64 ? 6 : 4;
   static constexpr int CHUNKS = BN / 64;            // 64-column (128-byte) chunks of a C tile
   static constexpr int SLOT_BYTES = 32 * 128;       // one warp's 32 rows of one chunk
-  static constexpr int STAGING_BYTES = 4 * CHUNKS * SLOT_BYTES;      // [quarter][chunk] slots
-  static constexpr int OFF_STAGING = STAGES * STAGE_BYTES;           // two staging buffers
-  static constexpr int OFF_BAR = OFF_STAGING + 2 * STAGING_BYTES;
+  // Staging of the C tile for the TMA stores.  BN <= 128: a slot per (quarter, chunk), two buffers
+  // alternating by tile.  BN = 256 (4 x 48 KB of stages leave 32 KB): one slot per epilogue warp,
+  // reused chunk after chunk once the previous chunk's store has read it (ONE_SLOT).
+  static constexpr bool ONE_SLOT = BN == 256;
+  static constexpr int STAGING_BYTES = ONE_SLOT ? 8 * SLOT_BYTES : 4 * CHUNKS * SLOT_BYTES;
+  static constexpr int NBUF = ONE_SLOT ? 1 : 2;
+  static constexpr int OFF_STAGING = STAGES * STAGE_BYTES;
+  static constexpr int OFF_BAR = OFF_STAGING + NBUF * STAGING_BYTES;
   static constexpr int B_FULL = 0, B_EMPTY = STAGES;                 // [STAGES] each
   static constexpr int B_ACCF = 2 * STAGES, B_ACCE = 2 * STAGES + 2;  // [2] each
   static constexpr int B_DRAIN = 2 * STAGES + 4;
   static constexpr int NBAR = 2 * STAGES + 5;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
-  static constexpr int TMEM_COLS = 2 * BN;          // two accumulators (128 / 256 columns)
+  static constexpr int TMEM_COLS = 2 * BN;          // two accumulators (128 / 256 / 512 columns)
   static constexpr int THREADS = 320;               // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
   static constexpr int EPI_WARPS = 8;
 };
@@ -191,12 +196,52 @@ __global__ void __launch_bounds__(320, 1)
     const int half = (warp - 2) >> 2;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     bool ok = true;
+    bool stored = false;  // (ONE_SLOT) this warp has a store in flight that may still read its slot
     for (int t = blockIdx.x, i = 0; ok && t < p.n_tiles; t += gridDim.x, ++i) {
       const int b = i & 1;
       int z, m0, n0;
       decode(t, z, m0, n0);
       if (!(ok = mbar_wait_all(bar(C::B_ACCF + b), static_cast<uint32_t>(i >> 1) & 1u, ctl))) break;
       tc_fence_after_sync();
+      if constexpr (C::ONE_SLOT) {
+        const uint32_t slot = base + C::OFF_STAGING + (warp - 2) * C::SLOT_BYTES;
+        const int r0 = m0 + quarter * 32;
+#pragma unroll 1
+        for (int c = half; c < C::CHUNKS; c += 2) {
+          uint32_t acc[2][32];
+          tmem_ld32(t_lane + b * BN + c * 64, acc[0]);
+          tmem_ld32(t_lane + b * BN + c * 64 + 32, acc[1]);
+          if (c + 2 >= C::CHUNKS) {
+            tc_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(C::B_ACCE + b));  // accumulator b read
+          }
+          if (stored) {  // the slot's previous chunk must have been read by its store
+            if (lane == 0) bulk_wait_group_read0();
+            __syncwarp();
+          }
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float lo = __uint_as_float(acc[q >> 2][(q & 3) * 8 + 2 * e]);
+              const float hi = __uint_as_float(acc[q >> 2][(q & 3) * 8 + 2 * e + 1]);
+              w[e] = BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+            }
+            st_shared_v4(slot + lane * 128 + ((q ^ (lane & 7)) << 4), w[0], w[1], w[2], w[3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (r0 < p.m && n0 + 64 * c < p.n) tma_store_3d(&tm_c, slot, n0 + 64 * c, r0, z);
+            bulk_commit_group();
+          }
+          __syncwarp();
+          stored = true;
+        }
+        continue;
+      }
       const uint32_t staging = base + C::OFF_STAGING + b * C::STAGING_BYTES;
       if (i > 1) {  // this buffer's slots: tile i-2's stores (one group per tile) must have read them
         if (lane == 0) bulk_wait_group_read1();
@@ -263,25 +308,30 @@ namespace {
 
 inline bool s16(int64_t s) { return s > 0 && ((s * 2) % 16) == 0 && (s * 2) < (1ll << 40); }
 
-int pick_bn(int64_t n) { return n > 64 ? 128 : 64; }
+// Tile width: 256 for compute-bound shapes (wide N, K >= 512), where the operand traffic through
+// shared memory sets the pace -- per 128-row MMA step a 128x256 tile moves 24 KB (TMA writes +
+// MMA reads) per 128 clk of tensor work against 16 KB per 64 clk for 128x128, so it can run the
+// pipe at ~2/3 instead of ~1/2 of its rate on a ~128 B/clk shared-memory port; 128 or 64 otherwise
+// (short K: an output-write stream, where the 128-wide tile's double staging keeps stores going).
+int pick_bn(int64_t n, int64_t k) { return (n > 128 && k >= 512) ? 256 : n > 64 ? 128 : 64; }
 
 // Name of one tile-table entry (static storage, built once).
 const char* bmm_table_name(bool bf16, int bn, int am, int bm) {
-  static const std::array<std::string, 16> names = [] {
-    std::array<std::string, 16> out;
-    const int bns[2] = {64, 128};
+  static const std::array<std::string, 24> names = [] {
+    std::array<std::string, 24> out;
+    const int bns[3] = {64, 128, 256};
     for (int t = 0; t < 2; ++t)
-      for (int i = 0; i < 2; ++i)
+      for (int i = 0; i < 3; ++i)
         for (int a = 0; a < 2; ++a)
           for (int b = 0; b < 2; ++b)
-            out[((t * 2 + i) * 2 + a) * 2 + b] =
+            out[((t * 3 + i) * 2 + a) * 2 + b] =
                 std::string("bmm_sm100<") + (t ? "bf16" : "f16") + ",128x" + std::to_string(bns[i]) +
                 "x64,A:" + (a ? "mn" : "k") + "-major,B:" + (b ? "mn" : "k") + "-major," +
-                std::to_string(bns[i] == 128 ? 4 : 6) + "st,persistent>";
+                std::to_string(bns[i] == 64 ? 6 : 4) + "st,persistent>";
     return out;
   }();
-  const int i = bn == 128 ? 1 : 0;
-  return names[(((bf16 ? 1 : 0) * 2 + i) * 2 + am) * 2 + bm].c_str();
+  const int i = bn == 256 ? 2 : bn == 128 ? 1 : 0;
+  return names[(((bf16 ? 1 : 0) * 3 + i) * 2 + am) * 2 + bm].c_str();
 }
 
 // Layout of one operand: 0 = K-major (contiguous along K), 1 = MN-major, -1 = unusable.
@@ -322,7 +372,7 @@ const char* bmm_sm100_plan(const cmpx_bmm_desc* d, int* status) {
     *status = CMPX_ERR_MISALIGNED;
     return "none";
   }
-  return bmm_table_name(d->dtype == CMPX_BF16, pick_bn(d->n), am, bmj);
+  return bmm_table_name(d->dtype == CMPX_BF16, pick_bn(d->n, d->k), am, bmj);
 }
 
 namespace {
@@ -392,7 +442,8 @@ int launch_bmm_bn(const cmpx_bmm_desc* d, const LaunchCtx& ctx, int am, int bm) 
 
 template <bool BF16>
 int launch_bmm_dt(const cmpx_bmm_desc* d, const LaunchCtx& ctx, int am, int bm) {
-  const int bn = pick_bn(d->n);
+  const int bn = pick_bn(d->n, d->k);
+  if (bn == 256) return launch_bmm_bn<256, BF16>(d, ctx, am, bm);
   if (bn == 128) return launch_bmm_bn<128, BF16>(d, ctx, am, bm);
   return launch_bmm_bn<64, BF16>(d, ctx, am, bm);
 }
