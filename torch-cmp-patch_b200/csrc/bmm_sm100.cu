@@ -82,13 +82,21 @@ __global__ void __launch_bounds__(320, 1)
   auto bar = [&](int i) -> uint32_t { return base + C::OFF_BAR + 8u * i; };
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
-  // Tile t of the flattened (batch, m tile, n tile) order, n fastest: consecutive tiles share A.
+  // Tile t of a batch item's tiles in bands of kBand m tiles: inside a band m runs fastest, then n.
+  // The CTAs busy at one moment hold consecutive tiles -- kBand row tiles of A and ~G / kBand
+  // column tiles of B -- so both stay in L2 while they are reused (n fastest over whole rows would
+  // stream all of B through L2 once per ~G / tiles_n rows of tiles).
+  constexpr int kBand = 16;
   auto decode = [&](int t, int& z, int& m0, int& n0) {
-    const int nt = t % p.tiles_n;
-    const int r = t / p.tiles_n;
-    m0 = (r % p.tiles_m) * C::BM;
-    z = r / p.tiles_m;
-    n0 = nt * BN;
+    const int per_item = p.tiles_m * p.tiles_n;
+    z = t / per_item;
+    const int r = t - z * per_item;
+    const int band = r / (kBand * p.tiles_n);
+    const int first_m = band * kBand;
+    const int rows = min(kBand, p.tiles_m - first_m);
+    const int w = r - band * kBand * p.tiles_n;
+    m0 = (first_m + w % rows) * C::BM;
+    n0 = (w / rows) * BN;
   };
 
   if (threadIdx.x == 0) {
