@@ -2,9 +2,10 @@
  * cmpx_b200.h -- C ABI of the B200 (sm_100a) attention / batched-matmul library.
  *
  * This is the drop-in boundary for the hot path of cmpext3 (WifiLast/torch-cmp-patch):
- * the two native ops that the Python monkeypatch reaches for
+ * the native ops that the Python monkeypatch reaches for
  *   F.scaled_dot_product_attention  -> cmpext3.ops.attention(query, key, value, scale=None, causal=False)
  *   torch.bmm / matmul / einsum     -> cmpext3.ops.bmm(input, mat2)
+ *   F.linear (nn.Linear)            -> cmpext3.ops.linear(input, weight, bias=None)
  * In the reference those are pybind11 functions over ATen tensors
  * (src/main.cpp:2307-2309 `bmm`, src/main.cpp:2353-2358 `attention`, implemented by
  * custom_bmm_forward src/main.cpp:363-441 and custom_attention_forward src/main.cpp:1603-1774).
@@ -38,7 +39,7 @@
 extern "C" {
 #endif
 
-#define CMPX_ABI_VERSION 2  /* 2: cmpx_attn_desc.heads_kv (grouped-query attention) */
+#define CMPX_ABI_VERSION 3  /* 2: cmpx_attn_desc.heads_kv (grouped-query attention); 3: cmpx_linear */
 
 /* Element type of every operand of one call (inputs and output share it, as in the reference:
  * dtype in == dtype out, src/main.cpp:1623-1627, :366-369). */
@@ -129,8 +130,8 @@ CMPX_API size_t cmpx_attn_workspace_size(const cmpx_attn_desc* desc);
  * allocator callback, stacks that only allocate at start-up -- cudaMalloc may also synchronise the
  * device).  Same descriptor and results as cmpx_attn_fwd, but the workspace fields are ignored: the
  * kernel's scratch (its work counters) lives in a fixed 256-byte array inside the library, which
- * every GPU that loads the library keeps until the process exits.  A call whose scratch need
- * (cmpx_attn_workspace_size) exceeds 256 bytes returns CMPX_ERR_WORKSPACE.  The first call on a
+ * every GPU that loads the library keeps until the process exits; the 16-bit kernels then run the
+ * schedule that needs no more than their 256 bytes of work counters (no tail split).  The first call on a
  * device looks up that array's device address (cudaGetSymbolAddress); make that first call before
  * capturing the stream into a graph.  Each call clears the counters it needs with an enqueued
  * memset.  All calls share the one array, so calls whose work overlaps on the GPU (different
@@ -140,6 +141,28 @@ CMPX_API int cmpx_attn_fwd_noalloc(const cmpx_attn_desc* desc, void* stream);
 
 /* Batched matmul.  Replaces cmpext3.ops.bmm (src/main.cpp:2307-2309). */
 CMPX_API int cmpx_bmm(const cmpx_bmm_desc* desc, void* stream);
+
+/* Linear layer  y = x W^T (+ bias):  x [m, k], W [n, k] (the nn.Linear weight, read in place as the
+ * K-major operand of the same GEMM as cmpx_bmm), bias [n] or NULL, y [m, n]; rows of x, W and y are
+ * *_row_stride elements apart, columns contiguous.  fp16 / bf16 only (fp32 returns
+ * CMPX_ERR_UNSUPPORTED_DTYPE); the bias is added to the fp32 accumulator before the one rounding
+ * to the output type.  Rows must start on 16-byte boundaries (k, n and the strides multiples of 8)
+ * and the bias pointer must be 16-byte aligned.
+ * Replaces: custom_linear_forward (src/main.cpp:195-346: bf16 converted to fp32 copies, W
+ * transposed into a contiguous copy, an fp32 / fp16-accumulating GEMM, then a separate bias-add
+ * kernel in the output type) behind cmpext3.ops.linear (the reference's _C.linear). */
+typedef struct cmpx_linear_desc {
+  const void* x;
+  const void* w;
+  const void* bias;    /* NULL: no bias */
+  void* y;
+  int64_t m, n, k;
+  int64_t x_row_stride, w_row_stride, y_row_stride;
+  int32_t dtype;       /* cmpx_dtype */
+  int32_t reserved;
+} cmpx_linear_desc;
+
+CMPX_API int cmpx_linear(const cmpx_linear_desc* desc, void* stream);
 
 /* Row softmax over the last dimension:  y[r, :] = softmax(x[r, :]) for r < rows, computed in
  * fp32 (max, exp, sum) and rounded once to the output dtype (dtype in == dtype out), which is what
@@ -166,6 +189,7 @@ CMPX_API int cmpx_softmax_rows(const cmpx_softmax_desc* desc, void* stream);
  * which this library does not need: the kernel choice is a fixed function of the shape. */
 CMPX_API int cmpx_attn_plan(const cmpx_attn_desc* desc, char* buf, size_t buf_len);
 CMPX_API int cmpx_bmm_plan(const cmpx_bmm_desc* desc, char* buf, size_t buf_len);
+CMPX_API int cmpx_linear_plan(const cmpx_linear_desc* desc, char* buf, size_t buf_len);
 
 /* Human-readable text for a status code (static storage). */
 CMPX_API const char* cmpx_status_str(int status);

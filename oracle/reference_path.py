@@ -3,7 +3,8 @@
 cmpext3's wrappers route CPU tensors to the stock PyTorch ops they saved at enable() time
 (reference cmpext3/__init__.py:609-633 ``_patched_sdpa``: ``_usable`` fails for a CPU tensor, so
 ``orig(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=..., scale=...)`` runs; :467-479
-``_patched_bmm`` -> ``orig(input, mat2)``; :482-501 ``_patched_einsum`` -> ``orig(*args)``).  The calls
+``_patched_bmm`` -> ``orig(input, mat2)``; :482-501 ``_patched_einsum`` -> ``orig(*args)``; :410-420
+``_patched_linear`` -> ``orig(input, weight, bias)``).  The calls
 below are those calls, made on CPU tensors with the host's threads.
 """
 from __future__ import annotations
@@ -18,6 +19,7 @@ _SDPA = F.scaled_dot_product_attention
 _BMM = torch.bmm
 _EINSUM = torch.einsum
 _SOFTMAX = torch.softmax
+_LINEAR = F.linear
 
 
 def set_threads(n: int | None = None) -> int:
@@ -36,6 +38,13 @@ def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale=None, is_causa
 def bmm(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     assert a.device.type == "cpu"
     return _BMM(a, b)
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None) -> torch.Tensor:
+    """Stock CPU F.linear as the reference's ``_patched_linear`` (cmpext3/__init__.py:410-420) calls it
+    for a CPU tensor: ``orig(input, weight, bias)``."""
+    assert x.device.type == "cpu"
+    return _LINEAR(x, w, b)
 
 
 def einsum(eq: str, *operands: torch.Tensor) -> torch.Tensor:

@@ -56,6 +56,13 @@ def bmm(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     return np.matmul(np.asarray(a, dtype=np.float64), np.asarray(b, dtype=np.float64))
 
 
+def linear(x: np.ndarray, w: np.ndarray, b: np.ndarray | None = None) -> np.ndarray:
+    """y = x W^T + b in float64 (the reference's custom_linear_forward, src/main.cpp:195-346, computes
+    this product and then adds the bias row to every output row)."""
+    y = np.matmul(np.asarray(x, dtype=np.float64), np.asarray(w, dtype=np.float64).T)
+    return y if b is None else y + np.asarray(b, dtype=np.float64)
+
+
 def softmax(x: np.ndarray, axis: int = -1) -> np.ndarray:
     x = np.asarray(x, dtype=np.float64)
     x = np.moveaxis(x, axis, -1)

@@ -43,13 +43,13 @@ import torch.nn.functional as F  # noqa: E402
 
 import cmpext3  # noqa: E402
 
-# Ops this package leaves alone (the reference's other patches -- linear, conv, norms -- are out of
-# this hot path's scope).  softmax is patched, but diverts only the attention chain's softmax.
-STOCK_UNPATCHED = {(F, "linear"): F.linear, (torch, "baddbmm"): torch.baddbmm,
-                   (F, "layer_norm"): F.layer_norm}
+# Ops this package leaves alone (the reference's other patches -- conv, norms, activations -- are out
+# of this hot path's scope).  softmax is patched, but diverts only the attention chain's softmax.
+STOCK_UNPATCHED = {(torch, "baddbmm"): torch.baddbmm, (F, "layer_norm"): F.layer_norm,
+                   (F, "conv2d"): F.conv2d, (F, "gelu"): F.gelu}
 STOCK_SOFTMAX = {"torch": torch.softmax, "F": F.softmax, "Tensor": torch.Tensor.softmax}
 
-NATIVE_OPS = ["attention", "bmm", "attention_plan", "bmm_plan", "softmax"]
+NATIVE_OPS = ["attention", "bmm", "attention_plan", "bmm_plan", "softmax", "linear", "linear_plan"]
 
 
 def pytest_configure(config):
@@ -82,6 +82,7 @@ def native(monkeypatch):
         setattr(fake, name, MagicMock(name=name))
     fake.attention_plan.return_value = "fake-attention-entry"
     fake.bmm_plan.return_value = "fake-bmm-entry"
+    fake.linear_plan.return_value = "fake-linear-entry"
     monkeypatch.setattr(cmpext3, "_C", fake)
     monkeypatch.setattr(cmpext3, "ops", fake)
     return fake

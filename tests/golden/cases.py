@@ -33,6 +33,14 @@ BMM_CASES = [
     ("f32_bmm", "float32", 2, 33, 17, 45),
 ]
 
+# (name, dtype, input shape, out_features, bias)
+LINEAR_CASES = [
+    ("bf16_linear_bias", "bfloat16", (2, 37, 96), 80, True),
+    ("f16_linear", "float16", (130, 72), 64, False),
+    ("f16_linear_bias_3d", "float16", (3, 17, 128), 136, True),
+    ("f32_linear_bias", "float32", (33, 40), 24, True),
+]
+
 EINSUM_ATTN_SHAPE = (1, 2, 128, 64)
 
 
@@ -69,6 +77,19 @@ def bmm_inputs(i: int):
     a = torch.randn(nb, m, k, generator=g).to(dt)
     b = torch.randn(nb, k, n, generator=g).to(dt)
     return a, b
+
+
+def linear_inputs(i: int):
+    """x, weight, bias (or None) for LINEAR_CASES[i]: N(0,1) inputs, N(0, 1/in_features) weights
+    and N(0,1) biases, the scale of an initialised nn.Linear."""
+    import torch
+    name, dtn, shape, n, has_bias = LINEAR_CASES[i]
+    dt = torch_dtype(dtn)
+    g = torch.Generator().manual_seed(4000 + i)
+    x = torch.randn(*shape, generator=g).to(dt)
+    w = (torch.randn(n, shape[-1], generator=g) / shape[-1] ** 0.5).to(dt)
+    b = torch.randn(n, generator=g).to(dt) if has_bias else None
+    return x, w, b
 
 
 def einsum_attn_inputs():

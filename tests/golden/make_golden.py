@@ -9,7 +9,7 @@ What it does:
     (the reference's own test conftest does the same, tests/conftest.py:42-46 there; its CUDA
     extension cannot be built for a CPU), with the monkeypatch ENABLED and NVML changes off
     (CMPEXT3_NVML_BOOST=0);
-  * calls the patched ``F.scaled_dot_product_attention``, ``torch.bmm`` and ``torch.einsum`` on seeded
+  * calls the patched ``F.scaled_dot_product_attention``, ``torch.bmm``, ``F.linear`` and ``torch.einsum`` on seeded
     CPU tensors -- the reference's wrappers route those to stock PyTorch (``_usable`` is False for CPU
     tensors), which is the reference's own CPU implementation of the path;
   * runs the reference planner ``cmpext3.einsum_ops.einsum`` on the equations of its own planner test
@@ -94,6 +94,15 @@ def main() -> None:
         out[f"bmm/{name}/a_sha256"] = np.array(C.digest(a))
         out[f"bmm/{name}/b_sha256"] = np.array(C.digest(b))
         out[f"bmm/{name}/c"] = C.to_numpy(c)
+
+    for i, (name, dtn, shape, n, has_bias) in enumerate(C.LINEAR_CASES):
+        x, w, b = C.linear_inputs(i)
+        with torch.no_grad():
+            y = F.linear(x, w, b)
+        assert F.linear is ref._patched_linear
+        for key, t in (("x", x), ("w", w)) + ((("b", b),) if b is not None else ()):
+            out[f"linear/{name}/{key}_sha256"] = np.array(C.digest(t))
+        out[f"linear/{name}/y"] = C.to_numpy(y)
 
     # einsum-routed attention (the bf16 einsum -> softmax -> einsum workload, small)
     q, k, v = C.einsum_attn_inputs()

@@ -42,7 +42,7 @@ def test_library_exports_nothing_undeclared():
 
 
 def test_abi_version_and_status_strings():
-    assert N.lib.cmpx_abi_version() == 2
+    assert N.lib.cmpx_abi_version() == 3
     header = HEADER.read_text()
     m = re.search(r"#define CMPX_ABI_VERSION (\d+)", header)
     assert m and int(m.group(1)) == N.ABI_VERSION == N.lib.cmpx_abi_version()
@@ -173,6 +173,51 @@ def test_bmm_tile_width(shape, width):
     nb, m, n, k = shape  # 128x256 only for wide N with K >= 512 (compute-bound); 128x128 / 128x64 else
     st, name = _bplan(_bmm(nb, m, n, k, bt=True))
     assert st == 0 and width in name, name
+
+
+def _linear(m=64, n=128, k=256, dtype=2, bias=True, ptr=0x10000, ldx=None, ldw=None, ldy=None):
+    d = N.LinearDesc()
+    d.x = d.w = d.y = ptr
+    d.bias = ptr if bias else None
+    d.m, d.n, d.k = m, n, k
+    d.x_row_stride = ldx if ldx is not None else k
+    d.w_row_stride = ldw if ldw is not None else k
+    d.y_row_stride = ldy if ldy is not None else n
+    d.dtype = dtype
+    return d
+
+
+def _lplan(d):
+    buf = ctypes.create_string_buffer(128)
+    st = N.lib.cmpx_linear_plan(ctypes.byref(d), buf, 128)
+    return st, buf.value.decode()
+
+
+def test_linear_plan_reads_the_weight_as_a_k_major_operand():
+    st, name = _lplan(_linear(m=8192, n=4096, k=4096))
+    assert st == 0 and "128x256" in name and "A:k-major,B:k-major" in name, name
+    st, name = _lplan(_linear(m=100, n=64, k=128, dtype=1, bias=False))
+    assert st == 0 and name.startswith("bmm_sm100<f16,128x64"), name
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(dtype=0), "ERR_UNSUPPORTED_DTYPE"),          # fp32 linear stays stock
+    (dict(k=100), "ERR_MISALIGNED"),                   # 200-byte rows
+    (dict(n=36), "ERR_MISALIGNED"),                    # 72-byte output rows
+    (dict(ldx=100), "ERR_INVALID_ARGUMENT"),           # row stride shorter than a row
+    (dict(m=-1), "ERR_INVALID_ARGUMENT"),
+])
+def test_linear_rejects(kw, status):
+    assert _lplan(_linear(**kw))[0] == getattr(N, status)
+
+
+def test_linear_rejects_misaligned_bias_and_null_pointers():
+    d = _linear()
+    d.bias = 0x10008
+    assert _lplan(d)[0] == N.ERR_MISALIGNED
+    d = _linear()
+    d.w = None
+    assert N.lib.cmpx_linear(ctypes.byref(d), None) == N.ERR_INVALID_ARGUMENT
 
 
 def test_bmm_rejects_misaligned_rows():

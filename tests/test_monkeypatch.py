@@ -70,6 +70,7 @@ class TestEnableDisable:
         assert torch.bmm is cmpext3._patched_bmm
         assert torch.einsum is cmpext3._patched_einsum
         assert F.scaled_dot_product_attention is cmpext3._patched_sdpa
+        assert F.linear is cmpext3._patched_linear
 
     def test_disable_ops_pins_named_ops_to_stock(self, monkeypatch):
         assert not cmpext3.is_enabled()
@@ -237,6 +238,69 @@ class TestBmm:
         b = torch.randn(2, 128, 64)
         torch.bmm(a, b)
         native.bmm.assert_not_called()
+
+
+class TestLinear:
+    """The reference's gates for F.linear (cmpext3/__init__.py:410-420)."""
+
+    def test_calls_native_when_eligible(self, patched, native, monkeypatch):
+        force_eligible(monkeypatch)
+        x, w, b = torch.randn(4, 16, 64), torch.randn(32, 64), torch.randn(32)
+        sentinel = torch.zeros(4, 16, 32)
+        native.linear.return_value = sentinel
+        assert F.linear(x, w, b) is sentinel
+        args = native.linear.call_args[0]
+        assert args[0] is x and args[1] is w and args[2] is b
+
+    def test_nn_linear_module_reaches_native(self, patched, native, monkeypatch):
+        force_eligible(monkeypatch)
+        layer = torch.nn.Linear(64, 32)
+        native.linear.return_value = torch.zeros(8, 32)
+        with torch.no_grad():
+            layer(torch.randn(8, 64))
+        native.linear.assert_called_once()
+
+    def test_falls_back_when_not_cuda(self, patched, native):
+        x, w = torch.randn(3, 8), torch.randn(5, 8)
+        got = F.linear(x, w)
+        native.linear.assert_not_called()
+        assert torch.equal(got, cmpext3._ORIGINALS[(F, "linear")](x, w))
+
+    def test_fp16_odd_out_features_goes_to_stock(self, patched, native, monkeypatch):
+        force_eligible(monkeypatch)
+        x, w = torch.randn(4, 8).half(), torch.randn(5, 8).half()
+        F.linear(x, w)
+        native.linear.assert_not_called()
+
+    def test_1d_input_or_3d_weight_goes_to_stock(self, patched, native, monkeypatch):
+        force_eligible(monkeypatch)
+        F.linear(torch.randn(8), torch.randn(4, 8))
+        with pytest.raises(RuntimeError):
+            F.linear(torch.randn(2, 8), torch.randn(1, 4, 8))
+        native.linear.assert_not_called()
+
+    def test_autograd_live_goes_to_stock(self, patched, native, monkeypatch):
+        monkeypatch.setattr(cmpext3, "_usable", lambda *a, **k: True)
+        layer = torch.nn.Linear(8, 4)  # its weight requires grad
+        layer(torch.randn(2, 8))
+        native.linear.assert_not_called()
+
+    def test_falls_back_on_native_runtime_error(self, patched, native, monkeypatch):
+        force_eligible(monkeypatch)
+        native.linear.side_effect = RuntimeError("linear: input/weight must share one dtype among float16/bfloat16")
+        x, w, b = torch.randn(4, 8), torch.randn(6, 8), torch.randn(6)
+        got = F.linear(x, w, b)
+        native.linear.assert_called_once()
+        assert torch.equal(got, cmpext3._ORIGINALS[(F, "linear")](x, w, b))
+
+    def test_disable_ops_linear_pins_stock(self, monkeypatch):
+        monkeypatch.setattr(cmpext3, "_DISABLED_OPS", frozenset({"linear"}))
+        stock = F.linear
+        cmpext3.enable()
+        try:
+            assert F.linear is stock
+        finally:
+            cmpext3.disable()
 
 
 class TestSoftmax:

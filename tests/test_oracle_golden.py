@@ -1,7 +1,7 @@
 """Pins the oracle against golden vectors made by the reference package itself (CPU, no GPU).
 
 tests/golden/reference_cpu_path.npz holds the outputs of the reference's patched
-F.scaled_dot_product_attention / torch.bmm / torch.einsum on seeded CPU tensors (which the
+F.scaled_dot_product_attention / torch.bmm / F.linear / torch.einsum on seeded CPU tensors (which the
 reference routes to stock PyTorch); tests/golden/make_golden.py made it.  Both oracles must
 reproduce them: ``oracle.reference_path`` (the same stock calls) bit-for-bit, and the float64
 numpy restatement ``oracle.sdpa_np`` within the rounding of the output dtype.
@@ -60,6 +60,19 @@ def test_numpy_restatement_matches_golden_sdpa(i):
     ref = sdpa_np.sdpa(q.float().numpy(), k.float().numpy(), v.float().numpy(), scale=scale, causal=causal)
     gold = _golden(f"sdpa/{name}/o").astype(np.float64)
     assert sdpa_np.rel_err(ref, gold) <= _NP_TOL[dtn], name
+
+
+@pytest.mark.parametrize("i", range(len(C.LINEAR_CASES)), ids=[c[0] for c in C.LINEAR_CASES])
+def test_linear_oracles_match_golden(i):
+    name, dtn, shape, n, has_bias = C.LINEAR_CASES[i]
+    x, w, b = C.linear_inputs(i)
+    for key, t in (("x", x), ("w", w)) + ((("b", b),) if b is not None else ()):
+        assert C.digest(t) == str(G[f"linear/{name}/{key}_sha256"]), f"{name}/{key} generator drifted"
+    gold = G[f"linear/{name}/y"]
+    got = RP.linear(x, w, b)
+    assert np.array_equal(C.to_numpy(got), gold if not isinstance(gold, torch.Tensor) else C.to_numpy(gold))
+    ref = sdpa_np.linear(x.float().numpy(), w.float().numpy(), None if b is None else b.float().numpy())
+    assert sdpa_np.rel_err(ref, _golden(f"linear/{name}/y")) <= _NP_TOL[dtn], name
 
 
 @pytest.mark.parametrize("i", range(len(C.BMM_CASES)), ids=[c[0] for c in C.BMM_CASES])

@@ -8,6 +8,7 @@ auto-run at :822-823 of the reference):
     torch.bmm                       -> cmpext3.ops.bmm(input, mat2)
     torch.matmul (2D / 3D)          -> cmpext3.ops.bmm
     torch.einsum                    -> einsum_ops planner -> torch.bmm (patched)
+    F.linear (so nn.Linear)         -> cmpext3.ops.linear(input, weight, bias)  (fp16 / bf16)
 
 and, beyond the reference, the middle step of an einsum / bmm attention chain
 (``einsum('bhid,bhjd->bhij') -> softmax(-1) -> einsum('bhij,bhjd->bhid')``):
@@ -25,15 +26,15 @@ whenever the native op raises ``RuntimeError``/``TypeError`` for an argument out
 What changed underneath: the kernels are tcgen05/TMA/TMEM kernels for B200 in a C-ABI library
 (include/cmpx_b200.h), bf16 is computed natively (the reference converted it to fp16 for attention
 and to fp32 for bmm), and the runtime native-versus-stock race is replaced by a fixed tile table
-(see cmpext3.autoselect).  The rest of the reference (linear, conv, norms, activations, TensorRT,
-NVML clock/power changes) is not part of this package; in particular nothing here changes GPU
-clocks or power limits.
+(see cmpext3.autoselect).  The rest of the reference (conv, norms, activations, TensorRT, NVML
+clock/power changes) is not part of this package; in particular nothing here changes GPU clocks or
+power limits.  fp32 linear stays stock here (the reference ran it on its own CUDA-core kernel).
 
     import cmpext3            # patches on import
     cmpext3.disable(); cmpext3.enable()
 
 Set CMPEXT3_AUTOPATCH=0 to import without patching; CMPEXT3_DISABLE_OPS=attention,bmm,matmul,einsum,
-softmax pins named ops to stock; CMPEXT3_VERBOSE=1 logs each new signature's tile-table entry;
+softmax,linear pins named ops to stock; CMPEXT3_VERBOSE=1 logs each new signature's tile-table entry;
 cmpext3.autoselect_report() lists them.
 
 SAFETY: the kernels are forward-only (no autograd); every patched call falls back to stock when
@@ -157,6 +158,23 @@ def _dispatch(op: str, ref: torch.Tensor, key: tuple, native_call: Callable,
 # ---------------------------------------------------------------------------------------------
 # Wrappers (signatures and gates as in the reference: __init__.py:423-501, :609-633)
 # ---------------------------------------------------------------------------------------------
+
+def _patched_linear(input, weight, bias=None):
+    """F.linear with the reference's gates (__init__.py:410-420): stock under live autograd, for
+    non-CUDA / unsupported dtypes, for input.dim() < 2 or a non-2-D weight, for fp16 with an odd
+    out_features; the native op raising (fp32, misaligned rows) also serves the call from stock."""
+    orig = _ORIGINALS[(F, "linear")]
+    if not (_grad_safe(input, weight, bias) and _usable(input, weight)):
+        return orig(input, weight, bias)
+    if input.dim() < 2 or weight.dim() != 2:
+        return orig(input, weight, bias)
+    if input.dtype == torch.float16 and weight.size(0) % 2 != 0:
+        return orig(input, weight, bias)
+    return _dispatch("linear", input, (input.shape, input.dtype, weight.shape, bias is not None),
+                     lambda: _C.linear(input, weight, bias),
+                     lambda: orig(input, weight, bias),
+                     lambda: _C.linear_plan(input, weight, bias))
+
 
 def _patched_matmul(input, other, *, out=None):
     orig = _ORIGINALS[(torch, "matmul")]
@@ -315,6 +333,7 @@ def enable() -> None:
     global _ENABLED
     if _ENABLED:
         return
+    _install(F, "linear", _patched_linear)
     _install(torch, "matmul", _patched_matmul)
     _install(torch, "bmm", _patched_bmm)
     _install(torch, "einsum", _patched_einsum)

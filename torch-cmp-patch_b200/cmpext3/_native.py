@@ -74,6 +74,15 @@ class BmmDesc(ctypes.Structure):
     ]
 
 
+class LinearDesc(ctypes.Structure):
+    _fields_ = [
+        ("x", ctypes.c_void_p), ("w", ctypes.c_void_p), ("bias", ctypes.c_void_p), ("y", ctypes.c_void_p),
+        ("m", ctypes.c_int64), ("n", ctypes.c_int64), ("k", ctypes.c_int64),
+        ("x_row_stride", ctypes.c_int64), ("w_row_stride", ctypes.c_int64), ("y_row_stride", ctypes.c_int64),
+        ("dtype", ctypes.c_int32), ("reserved", ctypes.c_int32),
+    ]
+
+
 class SoftmaxDesc(ctypes.Structure):
     _fields_ = [("x", ctypes.c_void_p), ("y", ctypes.c_void_p),
                 ("rows", ctypes.c_int64), ("cols", ctypes.c_int64),
@@ -82,7 +91,7 @@ class SoftmaxDesc(ctypes.Structure):
 
 
 # CMPX_ABI_VERSION of include/cmpx_b200.h that the ctypes structures above mirror.
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 
 def _load() -> ctypes.CDLL:
@@ -103,6 +112,10 @@ def _load() -> ctypes.CDLL:
     L.cmpx_attn_plan.restype = ctypes.c_int
     L.cmpx_bmm_plan.argtypes = [ctypes.POINTER(BmmDesc), ctypes.c_char_p, ctypes.c_size_t]
     L.cmpx_bmm_plan.restype = ctypes.c_int
+    L.cmpx_linear.argtypes = [ctypes.POINTER(LinearDesc), ctypes.c_void_p]
+    L.cmpx_linear.restype = ctypes.c_int
+    L.cmpx_linear_plan.argtypes = [ctypes.POINTER(LinearDesc), ctypes.c_char_p, ctypes.c_size_t]
+    L.cmpx_linear_plan.restype = ctypes.c_int
     L.cmpx_softmax_rows.argtypes = [ctypes.POINTER(SoftmaxDesc), ctypes.c_void_p]
     L.cmpx_softmax_rows.restype = ctypes.c_int
     L.cmpx_status_str.argtypes = [ctypes.c_int]
@@ -347,6 +360,88 @@ def bmm_plan(input, mat2) -> str:
     st = lib.cmpx_bmm_plan(ctypes.byref(desc), buf, 128)
     if st != OK:
         raise CmpxError("bmm plan", st)
+    return buf.value.decode()
+
+
+# ---------------------------------------------------------------------------------------------
+# linear  y = x W^T + b  (the reference's _C.linear, src/main.cpp:195-346)
+# ---------------------------------------------------------------------------------------------
+
+def _rows_ok(t: torch.Tensor) -> bool:
+    """A 2-D operand the 16-bit TMA path reads in place: unit column stride, 16-byte aligned rows."""
+    es = t.element_size()
+    return (t.data_ptr() % 16 == 0 and t.stride(1) == 1
+            and (t.shape[0] == 1 or (t.stride(0) > 0 and (t.stride(0) * es) % 16 == 0)))
+
+
+def _prepare_linear(input, weight, bias):
+    for name, t in (("input", input), ("weight", weight)):
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{name} must be a Tensor")
+        if not t.is_cuda:
+            raise RuntimeError(f"{name} must be a CUDA tensor")
+    if input.dim() < 2:
+        raise RuntimeError("Input dim >= 2")
+    if weight.dim() != 2:
+        raise RuntimeError("Weight dim == 2")
+    if input.device != weight.device:
+        raise RuntimeError("Device mismatch")
+    n, k = weight.shape
+    if input.shape[-1] != k:
+        raise RuntimeError("Input shape mismatch with Weight")
+    if input.dtype not in (torch.float16, torch.bfloat16) or weight.dtype != input.dtype:
+        raise RuntimeError("linear: input/weight must share one dtype among float16/bfloat16")
+    if bias is not None:
+        if not isinstance(bias, torch.Tensor) or bias.dim() != 1 or bias.shape[0] != n:
+            raise RuntimeError("Bias must be 1D of size out_features")
+        if bias.dtype != input.dtype or bias.device != input.device:
+            raise RuntimeError("Bias dtype/device mismatch")
+        bias = bias if (bias.stride(0) == 1 and bias.data_ptr() % 16 == 0) else bias.contiguous()
+        if bias.data_ptr() % 16 != 0:
+            bias = bias.clone()
+    x = input.reshape(-1, k)
+    x = x if _rows_ok(x) else x.contiguous()
+    w = weight if _rows_ok(weight) else weight.contiguous()
+    y = torch.empty((x.shape[0], n), dtype=input.dtype, device=input.device)
+    return x, w, bias, y
+
+
+def _linear_desc(x, w, bias, y) -> LinearDesc:
+    return LinearDesc(x.data_ptr(), w.data_ptr(), None if bias is None else bias.data_ptr(), y.data_ptr(),
+                      x.shape[0], w.shape[0], w.shape[1], x.stride(0), w.stride(0), y.stride(0),
+                      _DTYPE[x.dtype], 0)
+
+
+def linear(input, weight, bias=None):
+    """F.linear on the sm_100a GEMM with the bias added in its epilogue.  Same contract as the
+    reference's ops.linear (input [..., K], weight [N, K], bias [N] -> [..., N])."""
+    x, w, b, y = _prepare_linear(input, weight, bias)
+    out_shape = tuple(input.shape[:-1]) + (w.shape[0],)
+    if y.numel() == 0:
+        return y.view(out_shape)
+    if w.shape[1] == 0:
+        return (y.zero_() if b is None else y.copy_(b.expand_as(y))).view(out_shape)
+    desc = _linear_desc(x, w, b, y)
+    dev = x.device
+    if dev.index == torch.cuda.current_device():
+        st = lib.cmpx_linear(ctypes.byref(desc), _stream_handle(dev))
+    else:
+        with torch.cuda.device(dev):
+            st = lib.cmpx_linear(ctypes.byref(desc), _stream_handle(dev))
+    if st != OK:
+        raise CmpxError("linear", st)
+    _post_check()
+    return y.view(out_shape)
+
+
+def linear_plan(input, weight, bias=None) -> str:
+    """Name of the tile-table entry ``linear`` would run for these arguments."""
+    x, w, b, y = _prepare_linear(input, weight, bias)
+    desc = _linear_desc(x, w, b, y)
+    buf = ctypes.create_string_buffer(128)
+    st = lib.cmpx_linear_plan(ctypes.byref(desc), buf, 128)
+    if st != OK:
+        raise CmpxError("linear plan", st)
     return buf.value.decode()
 
 

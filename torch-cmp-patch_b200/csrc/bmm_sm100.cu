@@ -18,6 +18,7 @@
 //   For the attention-score shape (K = 64: one k-block per tile, 64 KB of output per tile) the
 //   kernel is an HBM write stream; the double accumulator keeps the stores going back to back.
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -65,7 +66,38 @@ struct BmmParams {
   int tiles_m, tiles_n, n_tiles;
   unsigned long long timeout_ns;
   unsigned int* dev_flags;
+  const uint16_t* bias;  // [n], same 16-bit type as C, added to every row in fp32 (linear); or null
 };
+
+// Adds bias[col0 .. col0+31] (16-bit, converted to fp32) to the 32 fp32 accumulator columns of one
+// row; columns at or past n get nothing (their outputs are clipped by the store).  Every lane of
+// the warp reads the same 64 bytes: one broadcast request per 16 bytes.
+template <bool BF16>
+__device__ __forceinline__ void add_bias32(uint32_t (&acc)[32], const uint16_t* bias, int col0, int n) {
+  if (col0 + 32 <= n) {
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(bias + col0) + v);
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float lo = BF16 ? __uint_as_float(w[e] << 16) : __half2float(__ushort_as_half(w[e] & 0xffffu));
+        const float hi = BF16 ? __uint_as_float(w[e] & 0xffff0000u) : __half2float(__ushort_as_half(w[e] >> 16));
+        acc[v * 8 + 2 * e] = __float_as_uint(__uint_as_float(acc[v * 8 + 2 * e]) + lo);
+        acc[v * 8 + 2 * e + 1] = __float_as_uint(__uint_as_float(acc[v * 8 + 2 * e + 1]) + hi);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (col0 + j < n) {
+        const uint16_t h = bias[col0 + j];
+        const float f = BF16 ? __uint_as_float(static_cast<uint32_t>(h) << 16) : __half2float(__ushort_as_half(h));
+        acc[j] = __float_as_uint(__uint_as_float(acc[j]) + f);
+      }
+    }
+  }
+}
 
 template <int BN, bool A_MN, bool B_MN, bool BF16>
 __global__ void __launch_bounds__(320, 1)
@@ -219,6 +251,10 @@ __global__ void __launch_bounds__(320, 1)
           uint32_t acc[2][32];
           tmem_ld32(t_lane + b * BN + c * 64, acc[0]);
           tmem_ld32(t_lane + b * BN + c * 64 + 32, acc[1]);
+          if (p.bias) {
+            add_bias32<BF16>(acc[0], p.bias, n0 + c * 64, p.n);
+            add_bias32<BF16>(acc[1], p.bias, n0 + c * 64 + 32, p.n);
+          }
           if (c + 2 >= C::CHUNKS) {
             tc_fence_before_sync();
             __syncwarp();
@@ -262,6 +298,7 @@ __global__ void __launch_bounds__(320, 1)
         for (int hh = 0; hh < 2; ++hh) {
           uint32_t acc[32];
           tmem_ld32(t_lane + b * BN + c * 64 + hh * 32, acc);
+          if (p.bias) add_bias32<BF16>(acc, p.bias, n0 + c * 64 + hh * 32, p.n);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint32_t w[4];
@@ -386,7 +423,7 @@ const char* bmm_sm100_plan(const cmpx_bmm_desc* d, int* status) {
 namespace {
 
 template <int BN, bool A_MN, bool B_MN, bool BF16>
-int launch_bmm_typed(const cmpx_bmm_desc* d, const LaunchCtx& ctx) {
+int launch_bmm_typed(const cmpx_bmm_desc* d, const LaunchCtx& ctx, const void* bias) {
   using C = BmmCfg<BN>;
   const CUtensorMapDataType dt =
       BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -435,25 +472,50 @@ int launch_bmm_typed(const cmpx_bmm_desc* d, const LaunchCtx& ctx) {
   p.n_tiles = static_cast<int>(n_tiles);
   p.timeout_ns = ctx.timeout_ns;
   p.dev_flags = ctx.dev_flags;
+  p.bias = static_cast<const uint16_t*>(bias);
   const int grid = static_cast<int>(std::min<int64_t>(n_tiles, std::max(1, ctx.num_sms)));
   bmm_sm100_kernel<BN, A_MN, B_MN, BF16><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(ta, tb, tc, p);
   return cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
 }
 
 template <int BN, bool BF16>
-int launch_bmm_bn(const cmpx_bmm_desc* d, const LaunchCtx& ctx, int am, int bm) {
-  if (am == 0 && bm == 0) return launch_bmm_typed<BN, false, false, BF16>(d, ctx);
-  if (am == 0 && bm == 1) return launch_bmm_typed<BN, false, true, BF16>(d, ctx);
-  if (am == 1 && bm == 0) return launch_bmm_typed<BN, true, false, BF16>(d, ctx);
-  return launch_bmm_typed<BN, true, true, BF16>(d, ctx);
+int launch_bmm_bn(const cmpx_bmm_desc* d, const LaunchCtx& ctx, int am, int bm, const void* bias) {
+  if (am == 0 && bm == 0) return launch_bmm_typed<BN, false, false, BF16>(d, ctx, bias);
+  if (am == 0 && bm == 1) return launch_bmm_typed<BN, false, true, BF16>(d, ctx, bias);
+  if (am == 1 && bm == 0) return launch_bmm_typed<BN, true, false, BF16>(d, ctx, bias);
+  return launch_bmm_typed<BN, true, true, BF16>(d, ctx, bias);
 }
 
 template <bool BF16>
-int launch_bmm_dt(const cmpx_bmm_desc* d, const LaunchCtx& ctx, int am, int bm) {
+int launch_bmm_dt(const cmpx_bmm_desc* d, const LaunchCtx& ctx, int am, int bm, const void* bias) {
   const int bn = pick_bn(d->n, d->k);
-  if (bn == 256) return launch_bmm_bn<256, BF16>(d, ctx, am, bm);
-  if (bn == 128) return launch_bmm_bn<128, BF16>(d, ctx, am, bm);
-  return launch_bmm_bn<64, BF16>(d, ctx, am, bm);
+  if (bn == 256) return launch_bmm_bn<256, BF16>(d, ctx, am, bm, bias);
+  if (bn == 128) return launch_bmm_bn<128, BF16>(d, ctx, am, bm, bias);
+  return launch_bmm_bn<64, BF16>(d, ctx, am, bm, bias);
+}
+
+// The GEMM a linear layer is: x [m, k] (rows ld_x apart) times W^T, W [n, k] (rows ld_w apart) --
+// a K-major B operand read in place -- into y [m, n].
+cmpx_bmm_desc linear_as_bmm(const cmpx_linear_desc* d) {
+  cmpx_bmm_desc b{};
+  b.a = d->x;
+  b.b = d->w;
+  b.c = d->y;
+  b.batch = 1;
+  b.m = d->m;
+  b.n = d->n;
+  b.k = d->k;
+  b.a_stride[0] = d->m * d->x_row_stride;
+  b.a_stride[1] = d->x_row_stride;
+  b.a_stride[2] = 1;
+  b.b_stride[0] = d->n * d->w_row_stride;
+  b.b_stride[1] = 1;                // along K
+  b.b_stride[2] = d->w_row_stride;  // along N
+  b.c_stride[0] = d->m * d->y_row_stride;
+  b.c_stride[1] = d->y_row_stride;
+  b.c_stride[2] = 1;
+  b.dtype = d->dtype;
+  return b;
 }
 
 }  // namespace
@@ -464,7 +526,34 @@ int launch_bmm_sm100(const cmpx_bmm_desc* d, const LaunchCtx& ctx) {
   if (st != CMPX_OK) return st;
   if (d->m == 0 || d->n == 0 || d->batch == 0) return CMPX_OK;
   const int am = a_major(d), bm = b_major(d);
-  return d->dtype == CMPX_BF16 ? launch_bmm_dt<true>(d, ctx, am, bm) : launch_bmm_dt<false>(d, ctx, am, bm);
+  return d->dtype == CMPX_BF16 ? launch_bmm_dt<true>(d, ctx, am, bm, nullptr)
+                               : launch_bmm_dt<false>(d, ctx, am, bm, nullptr);
+}
+
+const char* linear_sm100_plan(const cmpx_linear_desc* d, int* status) {
+  *status = CMPX_OK;
+  if (d->m < 0 || d->n < 1 || d->k < 1 || d->x_row_stride < d->k || d->w_row_stride < d->k ||
+      d->y_row_stride < d->n) {
+    *status = CMPX_ERR_INVALID_ARGUMENT;
+    return "none";
+  }
+  if (d->bias && (reinterpret_cast<uintptr_t>(d->bias) & 15u) != 0) {
+    *status = CMPX_ERR_MISALIGNED;
+    return "none";
+  }
+  const cmpx_bmm_desc b = linear_as_bmm(d);
+  return bmm_sm100_plan(&b, status);
+}
+
+int launch_linear_sm100(const cmpx_linear_desc* d, const LaunchCtx& ctx) {
+  int st = CMPX_OK;
+  linear_sm100_plan(d, &st);
+  if (st != CMPX_OK) return st;
+  if (d->m == 0) return CMPX_OK;
+  const cmpx_bmm_desc b = linear_as_bmm(d);
+  const int am = a_major(&b), bm = b_major(&b);
+  return d->dtype == CMPX_BF16 ? launch_bmm_dt<true>(&b, ctx, am, bm, d->bias)
+                               : launch_bmm_dt<false>(&b, ctx, am, bm, d->bias);
 }
 
 // --------------------------------------------------------------------------------------------

@@ -135,6 +135,16 @@ const char* bmm_plan_impl(const cmpx_bmm_desc* d, int* st) {
   return "none";
 }
 
+const char* linear_plan_impl(const cmpx_linear_desc* d, int* st) {
+  if (!d || !d->x || !d->w || !d->y) {
+    *st = CMPX_ERR_INVALID_ARGUMENT;
+    return "none";
+  }
+  if (d->dtype == CMPX_F16 || d->dtype == CMPX_BF16) return linear_sm100_plan(d, st);
+  *st = CMPX_ERR_UNSUPPORTED_DTYPE;
+  return "none";
+}
+
 void copy_name(const char* name, char* buf, size_t len) {
   if (!buf || len == 0) return;
   std::strncpy(buf, name, len - 1);
@@ -240,6 +250,24 @@ int cmpx_bmm_plan(const cmpx_bmm_desc* desc, char* buf, size_t buf_len) {
   const char* name = bmm_plan_impl(desc, &st);
   copy_name(st == CMPX_OK ? name : "none", buf, buf_len);
   return st;
+}
+
+int cmpx_linear_plan(const cmpx_linear_desc* desc, char* buf, size_t buf_len) {
+  int st = CMPX_OK;
+  const char* name = linear_plan_impl(desc, &st);
+  copy_name(st == CMPX_OK ? name : "none", buf, buf_len);
+  return st;
+}
+
+int cmpx_linear(const cmpx_linear_desc* desc, void* stream) {
+  int st = CMPX_OK;
+  linear_plan_impl(desc, &st);
+  if (st != CMPX_OK) return st;
+  if (desc->m == 0) return CMPX_OK;
+  LaunchCtx ctx;
+  st = device_ctx(&ctx, static_cast<cudaStream_t>(stream));
+  if (st != CMPX_OK) return st;
+  return launch_linear_sm100(desc, ctx);
 }
 
 int cmpx_attn_fwd(const cmpx_attn_desc* desc, void* stream) {

@@ -67,6 +67,10 @@ int launch_bmm_sm100(const cmpx_bmm_desc* d, const LaunchCtx& ctx);
 const char* bmm_f32_plan(const cmpx_bmm_desc* d, int* status);
 int launch_bmm_f32(const cmpx_bmm_desc* d, const LaunchCtx& ctx);
 
+// ---- linear (the bmm GEMM with batch 1, W read as a K-major B, bias in the epilogue) ----
+const char* linear_sm100_plan(const cmpx_linear_desc* d, int* status);
+int launch_linear_sm100(const cmpx_linear_desc* d, const LaunchCtx& ctx);
+
 // ---- row softmax (einsum-attention chain) ----
 const char* softmax_rows_plan(const cmpx_softmax_desc* d, int* status);
 int launch_softmax_rows(const cmpx_softmax_desc* d, const LaunchCtx& ctx);
