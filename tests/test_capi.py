@@ -225,6 +225,21 @@ def test_bmm_rejects_misaligned_rows():
     assert _bplan(d)[0] == N.ERR_MISALIGNED
 
 
+@pytest.mark.parametrize("cfg,entry", [
+    (dict(B=2, H=8, Lq=256, Lk=256, D=160, dtype=1), "fmha_sm100<f16,D192,2x128q,64kv"),    # SD1.5 level 4
+    (dict(B=1, H=4, Lq=1000, Lk=1000, D=192, dtype=2, causal=1), "fmha_sm100<bf16,D192,2x128q,64kv"),
+    (dict(B=2, H=8, Lq=4096, Lk=77, D=160, dtype=1), "fmha_sm100<f16,D192"),               # not the short kernel
+])
+def test_plan_for_head_dims_above_128(cfg, entry):
+    st, name = _plan(_attn(**cfg))
+    assert st == 0 and name.startswith(entry), name
+
+
+@pytest.mark.parametrize("D", [200, 256])
+def test_head_dims_above_192_are_outside_the_table(D):
+    assert _plan(_attn(D=D))[0] == N.ERR_UNSUPPORTED_SHAPE
+
+
 def test_workspace_contract():
     assert N.lib.cmpx_attn_workspace_size(ctypes.byref(_attn(dtype=2))) == 256
     assert N.lib.cmpx_attn_workspace_size(ctypes.byref(_attn(dtype=1))) == 256

@@ -54,12 +54,15 @@ constexpr int kMaxSplit = 8;
 template <int DP>
 struct FmhaCfg {
   static constexpr int BM = 128;                    // rows of one Q tile
-  static constexpr int BN = 128;                    // keys per K/V tile
+  // Keys per K/V tile: 128; 64 for head dims above 128, where the two O accumulators take 2 x 192
+  // TMEM columns and S / P0 / P1 have to fit in the 128 left.
+  static constexpr int BN = DP <= 128 ? 128 : 64;
   static constexpr int NCH = DP / 64;               // 128-byte chunks per row
-  static constexpr int CH_BYTES = 128 * 128;        // one chunk of a 128-row tile
+  static constexpr int CH_BYTES = 128 * 128;        // one chunk of a 128-row (Q / O) tile
+  static constexpr int KV_CH_BYTES = BN * 128;      // one chunk of a K / V tile
   static constexpr int QTILE_BYTES = NCH * CH_BYTES;
-  static constexpr int KV_BYTES = NCH * CH_BYTES;
-  static constexpr int NSTAGE = DP == 128 ? 4 : 6;
+  static constexpr int KV_BYTES = NCH * KV_CH_BYTES;
+  static constexpr int NSTAGE = DP > 128 ? 3 : DP == 128 ? 4 : 6;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_KV = 2 * QTILE_BYTES;
   static constexpr int OFF_OST = OFF_KV + NSTAGE * KV_BYTES;   // O staging (one tile) for TMA stores
@@ -82,8 +85,9 @@ struct FmhaCfg {
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // tmem base, abort word, item slots [2]
   static constexpr int SMEM_BYTES = OFF_MISC + 32 + 1024;  // +1024: runtime alignment slack
   // One S buffer shared by the two Q tiles (their QKs alternate), a P buffer per tile, an O
-  // accumulator per tile: S [0,128) P0 [128,192) P1 [192,256) O0 [256,256+DP) O1 [256+DP, 256+2DP).
-  static constexpr int TM_S = 0, TM_P0 = 128, TM_P1 = 192, TM_O0 = 256, TM_O1 = 256 + DP;
+  // accumulator per tile: S [0,BN) P0 [BN,1.5BN) P1 [1.5BN,2BN) O0 [2BN,2BN+DP) O1 [2BN+DP, 2BN+2DP).
+  static constexpr int TM_S = 0, TM_P0 = BN, TM_P1 = BN + BN / 2, TM_O0 = 2 * BN, TM_O1 = 2 * BN + DP;
+  static_assert(TM_O1 + DP <= 512, "TMEM columns");
   static constexpr int TMEM_COLS = 512;
   // Warp roles: 0-3 softmax/epilogue of tile 0, 4-7 of tile 1 (thread = row), 8 TMA producer
   // (and work fetch), 9 QK issuer (and TMEM owner), 10 PV issuer.
@@ -148,11 +152,11 @@ __device__ __forceinline__ void exp_chunk(const float* s, int q, uint64_t sl2x2,
   }
 }
 
-// One pass over a row's 128 scores: the four chunks' P stored to TMEM (16 columns each at p_tm);
+// One pass over a row's BN scores: the BN/32 chunks' P stored to TMEM (16 columns each at p_tm);
 // returns the row sum of p.  before_store() runs after the first chunk is computed and before
 // anything is stored: the wait for the P buffer to be free (the previous PV) overlaps the first
-// quarter of the exponentials instead of preceding them.
-template <bool BF16, int EMU, class BeforeStore>
+// chunk of the exponentials instead of preceding them.
+template <int BN, bool BF16, int EMU, class BeforeStore>
 __device__ __forceinline__ float exp_pass(const float* s, float sl2, float nmb, uint32_t p_tm,
                                           BeforeStore&& before_store) {
   uint64_t la = f2_pack(0.f, 0.f), lb = la;
@@ -161,7 +165,7 @@ __device__ __forceinline__ float exp_pass(const float* s, float sl2, float nmb, 
   exp_chunk<BF16, EMU>(s, 0, sl2x2, nmbx2, la, lb, pk);
   before_store();
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
+  for (int q = 0; q < BN / 32; ++q) {
     if (q > 0) exp_chunk<BF16, EMU>(s, q, sl2x2, nmbx2, la, lb, pk);
     tmem_st16(p_tm + q * 16, pk);
   }
@@ -170,24 +174,26 @@ __device__ __forceinline__ float exp_pass(const float* s, float sl2, float nmb, 
   return a0 + a1;
 }
 
-// Row maximum / minimum of 128 values: 8 independent chains, the first 16 values seed them in pairs,
-// the other 112 follow two at a time with the 3-input form.
-__device__ __forceinline__ float row_max128(const float* s) {
+// Row maximum / minimum of BN values: 8 independent chains, the first 16 values seed them in pairs,
+// the others follow two at a time with the 3-input form.
+template <int BN>
+__device__ __forceinline__ float row_max(const float* s) {
   float a[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) a[i] = fmaxf(s[2 * i], s[2 * i + 1]);
 #pragma unroll
-  for (int c = 16; c < 128; c += 16)
+  for (int c = 16; c < BN; c += 16)
 #pragma unroll
     for (int i = 0; i < 8; ++i) a[i] = fmax3(a[i], s[c + 2 * i], s[c + 2 * i + 1]);
   return fmax3(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
 }
-__device__ __forceinline__ float row_min128(const float* s) {
+template <int BN>
+__device__ __forceinline__ float row_min(const float* s) {
   float a[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) a[i] = fminf(s[2 * i], s[2 * i + 1]);
 #pragma unroll
-  for (int c = 16; c < 128; c += 16)
+  for (int c = 16; c < BN; c += 16)
 #pragma unroll
     for (int i = 0; i < 8; ++i) a[i] = fmin3(a[i], s[c + 2 * i], s[c + 2 * i + 1]);
   return fmin3(fmin3(a[0], a[1], a[2]), fmin3(a[3], a[4], a[5]), fminf(a[6], a[7]));
@@ -227,7 +233,7 @@ __device__ __noinline__ void fmha_split_epilogue(float* part_o, float* part_ml, 
 // CTA it was bound by the loads one SM can keep in flight.
 template <int DP, bool BF16>
 __global__ void __launch_bounds__(128) fmha_split_merge_kernel(const __grid_constant__ FmhaParams p) {
-  constexpr int CPL = DP / 32;  // fp32 columns per lane: 2 or 4
+  constexpr int CPL = DP / 32;  // fp32 columns per lane: 2, 4 or 6
   constexpr int ROWS = 2;       // rows per warp
   const int lane = threadIdx.x & 31;
   const int col = lane * CPL;
@@ -247,16 +253,19 @@ __global__ void __launch_bounds__(128) fmha_split_merge_kernel(const __grid_cons
       const size_t slot = slot0 + static_cast<size_t>(r) * 2 * 128;
       if (r < split) {
         ml[i][r] = __ldcg(reinterpret_cast<const float2*>(p.part_ml) + slot);
-        if constexpr (CPL == 2) {
-          const float2 x = ld_cg_f2(p.part_o + slot * DP + col);
-          o[i][r][0] = x.x;
-          o[i][r][1] = x.y;
-        } else {
+        if constexpr (CPL == 4) {
           const float4 x = ld_cg_f4(p.part_o + slot * DP + col);
           o[i][r][0] = x.x;
           o[i][r][1] = x.y;
           o[i][r][2] = x.z;
           o[i][r][3] = x.w;
+        } else {
+#pragma unroll
+          for (int e = 0; e < CPL; e += 2) {
+            const float2 x = ld_cg_f2(p.part_o + slot * DP + col + e);
+            o[i][r][e] = x.x;
+            o[i][r][e + 1] = x.y;
+          }
         }
       } else {
         ml[i][r] = make_float2(-INFINITY, 0.f);
@@ -275,7 +284,7 @@ __global__ void __launch_bounds__(128) fmha_split_merge_kernel(const __grid_cons
     const int b = bh / p.heads;
     const int h = bh - b * p.heads;
     const int qrow = pair * 256 + gr % 256;
-    if (qrow >= p.len_q || col >= p.head_dim) continue;
+    if (qrow >= p.len_q) continue;
     float mx = -INFINITY;
 #pragma unroll
     for (int r = 0; r < kMaxSplit; ++r) mx = fmaxf(mx, ml[i][r].x);
@@ -293,13 +302,12 @@ __global__ void __launch_bounds__(128) fmha_split_merge_kernel(const __grid_cons
     const float inv = 1.f / lsum;
     uint16_t* dst = static_cast<uint16_t*>(p.o) + b * p.os_b + h * p.os_h +
                     static_cast<long long>(qrow) * p.os_s + col;
-    const uint32_t lo = BF16 ? pack_bf16x2(a[0] * inv, a[1] * inv) : pack_f16x2(a[0] * inv, a[1] * inv);
-    if constexpr (CPL == 2) {
-      *reinterpret_cast<uint32_t*>(dst) = lo;
-    } else {
-      const uint32_t hi = BF16 ? pack_bf16x2(a[2] * inv, a[3] * inv) : pack_f16x2(a[2] * inv, a[3] * inv);
-      *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
-    }
+    // column pairs inside the head dim (a multiple of 8, so a pair is all in or all out)
+#pragma unroll
+    for (int e = 0; e < CPL; e += 2)
+      if (col + e < p.head_dim)
+        *reinterpret_cast<uint32_t*>(dst + e) =
+            BF16 ? pack_bf16x2(a[e] * inv, a[e + 1] * inv) : pack_f16x2(a[e] * inv, a[e + 1] * inv);
   }
 }
 
@@ -414,9 +422,10 @@ __global__ void __launch_bounds__(352, 1)
     return g;
   };
   // Key tiles tile 0 of an item takes part in: under the causal mask its rows (q0 .. q0+127) see no
-  // key of a last tile that starts past q0 + 127, so QK_0, its softmax and PV_0 skip that tile.
+  // key past q0 + 127, so QK_0, its softmax and PV_0 skip the item's last key tiles that start
+  // past it (one tile of 128 keys, two of 64).
   auto tile0_kv = [&](int q0, int n_kv) -> int {
-    return (p.causal && (n_kv - 1) * C::BN > q0 + C::BM - 1) ? n_kv - 1 : n_kv;
+    return p.causal ? min(n_kv, (min(p.len_k, q0 + C::BM) + C::BN - 1) / C::BN) : n_kv;
   };
 
   if (warp >= 8) {
@@ -458,7 +467,7 @@ __global__ void __launch_bounds__(352, 1)
               mbar_arrive_expect_tx(bar(C::B_FULL + st), C::KV_BYTES);
               const CUtensorMap* m = which ? &tm_v : &tm_k;
               for (int c = 0; c < C::NCH; ++c)
-                tma_load_4d(sKV + st * C::KV_BYTES + c * C::CH_BYTES, m, bar(C::B_FULL + st), c * 64,
+                tma_load_4d(sKV + st * C::KV_BYTES + c * C::KV_CH_BYTES, m, bar(C::B_FULL + st), c * 64,
                             j * C::BN, h / p.group, b);
             }
           }
@@ -480,7 +489,7 @@ __global__ void __launch_bounds__(352, 1)
       // warp-uniform control flow (waits are warp-wide and return one verdict) and one elected
       // lane issues its MMAs and commits (the *_w helpers).  The two streams touch disjoint TMEM
       // (QK: S;  PV: P_t, O_t); every cross-dependency goes through an mbarrier.
-      constexpr uint32_t kIdescQK = idesc_f16(128, 128, BF16 ? 1 : 0, 0, 0);
+      constexpr uint32_t kIdescQK = idesc_f16(128, C::BN, BF16 ? 1 : 0, 0, 0);
       constexpr uint32_t kIdescPV = idesc_f16(128, DP, BF16 ? 1 : 0, 0, 1);
       auto stage_of = [&](int load) -> uint32_t { return sKV + (load % C::NSTAGE) * C::KV_BYTES; };
       auto full_bar = [&](int load) -> uint32_t { return bar(C::B_FULL + load % C::NSTAGE); };
@@ -495,9 +504,10 @@ __global__ void __launch_bounds__(352, 1)
           const uint32_t q_addr = sQ + t * C::QTILE_BYTES;
 #pragma unroll
           for (int k = 0; k < DP / 16; ++k) {
-            const uint32_t off = (k >> 2) * C::CH_BYTES + (k & 3) * 32;
-            umma_ss_w(tmem + C::TM_S, smem_desc_sw128(q_addr + off, 16, 1024),
-                      smem_desc_sw128(k_addr + off, 16, 1024), kIdescQK, k > 0 ? 1u : 0u);
+            const uint32_t q_off = (k >> 2) * C::CH_BYTES + (k & 3) * 32;
+            const uint32_t k_off = (k >> 2) * C::KV_CH_BYTES + (k & 3) * 32;
+            umma_ss_w(tmem + C::TM_S, smem_desc_sw128(q_addr + q_off, 16, 1024),
+                      smem_desc_sw128(k_addr + k_off, 16, 1024), kIdescQK, k > 0 ? 1u : 0u);
           }
         };
         uint32_t n_sfree0 = 0, n_sfree1 = 0;  // barrier phase counters carried across items
@@ -545,7 +555,7 @@ __global__ void __launch_bounds__(352, 1)
 #pragma unroll
           for (int k = 0; k < C::BN / 16; ++k) {
             umma_ts_w(d_tmem, p_tmem + k * 8,
-                      smem_desc_sw128(v_addr + k * 2048, C::CH_BYTES, 1024), kIdescPV,
+                      smem_desc_sw128(v_addr + k * 2048, C::KV_CH_BYTES, 1024), kIdescPV,
                       (acc || k > 0) ? 1u : 0u);
           }
         };
@@ -618,8 +628,13 @@ __global__ void __launch_bounds__(352, 1)
           break;
         }
         tc_fence_after_sync();
-        uint32_t sr[128];
-        tmem_ld128(s_tm, sr);
+        uint32_t sr[C::BN];
+        if constexpr (C::BN == 128) {
+          tmem_ld128(s_tm, sr);
+        } else {
+          tmem_ld32(s_tm, *reinterpret_cast<uint32_t(*)[32]>(sr));
+          tmem_ld32(s_tm + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+        }
         float* s = reinterpret_cast<float*>(sr);
         tc_fence_before_sync();
         mbar_arrive(bar(C::B_SFREE + t));  // S is in registers: the other tile's QK may overwrite it
@@ -629,7 +644,7 @@ __global__ void __launch_bounds__(352, 1)
           int lim = p.len_k - kv0;
           if (p.causal) lim = min(lim, qrow - kv0 + 1);
 #pragma unroll
-          for (int c = 0; c < 128; ++c)
+          for (int c = 0; c < C::BN; ++c)
             if (c >= lim) s[c] = masked;
         }
         // Fast pass against the running max m_run.  Any p above 2^8 (a key more than 8 above
@@ -646,7 +661,7 @@ __global__ void __launch_bounds__(352, 1)
         bool slow = (j == j_begin);
         if (!slow) {
           bool pv_ok = true;
-          l_tile = exp_pass<BF16, C::EMU>(s, sl2, -m_run, p_tm, [&] {
+          l_tile = exp_pass<C::BN, BF16, C::EMU>(s, sl2, -m_run, p_tm, [&] {
             pv_ok = mbar_wait_all(bar(C::B_PVDONE + t), (n_pvdone++) & 1u, ctl);
             tc_fence_after_sync();
           });
@@ -658,12 +673,12 @@ __global__ void __launch_bounds__(352, 1)
           if (slow) tmem_st_wait();  // the redo overwrites the fast pass's P columns
         }
         if (slow) {
-          const float m_tile = (p.neg_scale ? row_min128(s) : row_max128(s)) * sl2;
+          const float m_tile = (p.neg_scale ? row_min<C::BN>(s) : row_max<C::BN>(s)) * sl2;
           if (m_tile > m_run) {  // (always on the first tile: m_run = -inf, m_tile finite)
             alpha = ex2_approx(m_run - m_tile);
             m_run = m_tile;
           }
-          l_tile = exp_pass<BF16, C::EMU>(s, sl2, -m_run, p_tm, [] {});
+          l_tile = exp_pass<C::BN, BF16, C::EMU>(s, sl2, -m_run, p_tm, [] {});
           if (j > j_begin && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
             for (int c = 0; c < DP / 32; ++c) {
@@ -802,10 +817,11 @@ FmhaSplit fmha_split_plan(const cmpx_attn_desc* d, int num_sms) {
   if (d->causal || num_sms <= 1 || n_items <= 0) return sp;
   const int64_t rem = n_items % num_sms;
   if (rem == 0) return sp;
-  const int64_t n_kv = (d->len_k + 127) / 128;
+  const int64_t bn = d->head_dim <= 128 ? 128 : 64;
+  const int64_t n_kv = (d->len_k + bn - 1) / bn;
   const int64_t split = std::min<int64_t>({num_sms / rem, n_kv / 4, kMaxSplit});
   if (split < 2) return sp;
-  const int dp = d->head_dim <= 64 ? 64 : 128;
+  const int dp = d->head_dim <= 64 ? 64 : d->head_dim <= 128 ? 128 : 192;
   sp.split = static_cast<int>(split);
   sp.n_whole = static_cast<int>(n_items - rem);
   sp.n_work = static_cast<int>(sp.n_whole + rem * split);
@@ -829,7 +845,7 @@ const char* fmha_sm100_plan(const cmpx_attn_desc* d, int* status) {
     *status = CMPX_ERR_UNSUPPORTED_DTYPE;
     return "none";
   }
-  if (d->head_dim < 8 || d->head_dim > 128 || (d->head_dim % 8) != 0) {
+  if (d->head_dim < 8 || d->head_dim > 192 || (d->head_dim % 8) != 0) {
     *status = CMPX_ERR_UNSUPPORTED_SHAPE;
     return "none";
   }
@@ -859,6 +875,11 @@ const char* fmha_sm100_plan(const cmpx_attn_desc* d, int* status) {
   // when the last wave's items are split into key ranges (a second, merging kernel follows).
   const bool split = fmha_split_plan(d, current_num_sms()).split > 1;
   const bool bf = d->dtype == CMPX_BF16;
+  if (d->head_dim > 128)
+    return bf ? (split ? "fmha_sm100<bf16,D192,2x128q,64kv,3st,persistent+tail-split>"
+                       : "fmha_sm100<bf16,D192,2x128q,64kv,3st,persistent>")
+              : (split ? "fmha_sm100<f16,D192,2x128q,64kv,3st,persistent+tail-split>"
+                       : "fmha_sm100<f16,D192,2x128q,64kv,3st,persistent>");
   static const char* const names[2][2][2] = {
       {{"fmha_sm100<f16,D64,2x128q,128kv,6st,persistent>", "fmha_sm100<f16,D64,2x128q,128kv,6st,persistent+tail-split>"},
        {"fmha_sm100<bf16,D64,2x128q,128kv,6st,persistent>", "fmha_sm100<bf16,D64,2x128q,128kv,6st,persistent+tail-split>"}},
@@ -886,8 +907,8 @@ int launch_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
       BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap tq, tk, tv, to;
   if (!make_bhsd_map(&tq, dt, d->q, d->head_dim, d->len_q, d->heads, d->batch, d->q_stride, 128) ||
-      !make_bhsd_map(&tk, dt, d->k, d->head_dim, d->len_k, attn_heads_kv(d), d->batch, d->k_stride, 128) ||
-      !make_bhsd_map(&tv, dt, d->v, d->head_dim, d->len_k, attn_heads_kv(d), d->batch, d->v_stride, 128) ||
+      !make_bhsd_map(&tk, dt, d->k, d->head_dim, d->len_k, attn_heads_kv(d), d->batch, d->k_stride, C::BN) ||
+      !make_bhsd_map(&tv, dt, d->v, d->head_dim, d->len_k, attn_heads_kv(d), d->batch, d->v_stride, C::BN) ||
       !make_bhsd_map(&to, dt, d->o, d->head_dim, d->len_q, d->heads, d->batch, d->o_stride, 32))
     return CMPX_ERR_LAUNCH;
 
@@ -952,7 +973,8 @@ int launch_fmha_sm100(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   if (fmha_short_eligible(d)) return launch_fmha_short(d, ctx);
   const bool bf = d->dtype == CMPX_BF16;
   if (d->head_dim <= 64) return bf ? launch_typed<64, true>(d, ctx) : launch_typed<64, false>(d, ctx);
-  return bf ? launch_typed<128, true>(d, ctx) : launch_typed<128, false>(d, ctx);
+  if (d->head_dim <= 128) return bf ? launch_typed<128, true>(d, ctx) : launch_typed<128, false>(d, ctx);
+  return bf ? launch_typed<192, true>(d, ctx) : launch_typed<192, false>(d, ctx);
 }
 
 }  // namespace cmpx
