@@ -52,7 +52,7 @@ typedef enum cmpx_dtype {
 typedef enum cmpx_status {
   CMPX_OK = 0,
   CMPX_ERR_INVALID_ARGUMENT = 1,  /* null pointer, negative size, shape mismatch */
-  CMPX_ERR_UNSUPPORTED_SHAPE = 2, /* outside the tile table (e.g. head_dim > 128) */
+  CMPX_ERR_UNSUPPORTED_SHAPE = 2, /* outside the tile table (e.g. head_dim > 192) */
   CMPX_ERR_UNSUPPORTED_DTYPE = 3,
   CMPX_ERR_MISALIGNED = 4,        /* pointer/stride not 16-byte aligned for TMA */
   CMPX_ERR_WORKSPACE = 5,         /* workspace missing or too small */
