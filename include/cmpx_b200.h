@@ -39,7 +39,8 @@
 extern "C" {
 #endif
 
-#define CMPX_ABI_VERSION 3  /* 2: cmpx_attn_desc.heads_kv (grouped-query attention); 3: cmpx_linear */
+#define CMPX_ABI_VERSION 4  /* 2: cmpx_attn_desc.heads_kv (grouped-query attention); 3: cmpx_linear;
+                               4: cmpx_attn_desc.mask (boolean attention mask) */
 
 /* Element type of every operand of one call (inputs and output share it, as in the reference:
  * dtype in == dtype out, src/main.cpp:1623-1627, :366-369). */
@@ -68,6 +69,13 @@ typedef enum cmpx_status {
  * iff j <= i), which is what torch's is_causal does for len_q != len_k.
  * Grouped-query attention: k and v may have heads_kv heads (a divisor of heads); query head h then
  * reads key/value head h / (heads / heads_kv), as torch's enable_gqa=True does.
+ * Boolean mask (16-bit calls): key j takes part in query i's softmax only where mask[b, h, i, j] is
+ * nonzero (and, with causal, j <= i) -- torch's attn_mask of dtype bool, is_causal ANDed in as its
+ * math path does.  A query row with no key left gets an all-zero output (torch's result), not NaN.
+ * The mask is one byte per element, broadcastable: mask_stride holds element strides over batch,
+ * head, query row and key, 0 for a broadcast dimension; the key stride must be 1.  The call packs
+ * it to bits in the workspace (cmpx_attn_workspace_size counts that), so a masked call needs the
+ * full workspace; fp32 calls with a mask return CMPX_ERR_UNSUPPORTED_SHAPE.
  * Replaces: custom_attention_forward (src/main.cpp:1603-1774) and its launchers
  * launch_flash_attention_hfma2 (src/cuda/fp16_flash_attention_hfma2.cu:269-286),
  * launch_attention_fp16 (src/cuda/fp16_attention.cu:328-386),
@@ -88,6 +96,8 @@ typedef struct cmpx_attn_desc {
   void* workspace;     /* device scratch of cmpx_attn_workspace_size() bytes (may be NULL if 0) */
   size_t workspace_bytes;
   int64_t heads_kv;    /* heads of k and v: 0 or heads = one per query head, else a divisor of heads */
+  const void* mask;    /* boolean mask, one byte per element (see above); NULL = none */
+  int64_t mask_stride[4]; /* batch, head, query-row, key strides of mask (elements; 0 = broadcast) */
 } cmpx_attn_desc;
 
 /* Batched matmul  C[b] = A[b] @ B[b],  A: [batch, m, k], B: [batch, k, n], C: [batch, m, n].
@@ -131,7 +141,8 @@ CMPX_API size_t cmpx_attn_workspace_size(const cmpx_attn_desc* desc);
  * device).  Same descriptor and results as cmpx_attn_fwd, but the workspace fields are ignored: the
  * kernel's scratch (its work counters) lives in a fixed 256-byte array inside the library, which
  * every GPU that loads the library keeps until the process exits; the 16-bit kernels then run the
- * schedule that needs no more than their 256 bytes of work counters (no tail split).  The first call on a
+ * schedule that needs no more than their 256 bytes of work counters (no tail split; a call with a
+ * mask returns CMPX_ERR_WORKSPACE: the mask is packed in the workspace).  The first call on a
  * device looks up that array's device address (cudaGetSymbolAddress); make that first call before
  * capturing the stream into a graph.  Each call clears the counters it needs with an enqueued
  * memset.  All calls share the one array, so calls whose work overlaps on the GPU (different

@@ -42,7 +42,7 @@ def test_library_exports_nothing_undeclared():
 
 
 def test_abi_version_and_status_strings():
-    assert N.lib.cmpx_abi_version() == 3
+    assert N.lib.cmpx_abi_version() == 4
     header = HEADER.read_text()
     m = re.search(r"#define CMPX_ABI_VERSION (\d+)", header)
     assert m and int(m.group(1)) == N.ABI_VERSION == N.lib.cmpx_abi_version()
@@ -238,6 +238,40 @@ def test_plan_for_head_dims_above_128(cfg, entry):
 @pytest.mark.parametrize("D", [200, 256])
 def test_head_dims_above_192_are_outside_the_table(D):
     assert _plan(_attn(D=D))[0] == N.ERR_UNSUPPORTED_SHAPE
+
+
+def _with_mask(d, strides):
+    d.mask = 0x20000
+    d.mask_stride[:] = strides
+    return d
+
+
+def test_mask_is_packed_in_the_workspace():
+    # [B, 1, Lq, Lk] key/query mask broadcast over heads: B x Lq rows of ceil(Lk/32) words (a
+    # multiple of 4), 256-byte aligned, after the 256 bytes of work counters
+    d = _with_mask(_attn(B=2, H=8, Lq=300, Lk=77, D=64, dtype=2, causal=1), (300 * 77, 0, 77, 1))
+    rows, words = 2 * 300, 4
+    packed = (rows * words * 4 + 255) // 256 * 256
+    assert N.lib.cmpx_attn_workspace_size(ctypes.byref(d)) == 256 + packed
+    d.workspace, d.workspace_bytes = 0x10000, 256  # too small for the packed mask
+    assert N.lib.cmpx_attn_fwd(ctypes.byref(d), None) == N.ERR_WORKSPACE
+
+
+@pytest.mark.parametrize("strides,status", [
+    ((0, 0, 77, 2), N.ERR_INVALID_ARGUMENT),    # keys not contiguous
+    ((-1, 0, 77, 1), N.ERR_INVALID_ARGUMENT),
+])
+def test_mask_stride_rules(strides, status):
+    d = _with_mask(_attn(Lq=64, Lk=77, dtype=2), strides)
+    assert _plan(d)[0] == status
+
+
+def test_mask_plans_on_the_16bit_kernel_only():
+    d = _with_mask(_attn(Lq=64, Lk=77, dtype=2), (0, 0, 77, 1))
+    st, name = _plan(d)
+    assert st == 0 and name.startswith("fmha_sm100<bf16") and name.endswith("+mask>"), name
+    d = _with_mask(_attn(Lq=64, Lk=77, dtype=0), (0, 0, 77, 1))
+    assert _plan(d)[0] == N.ERR_UNSUPPORTED_SHAPE   # fp32 with a mask: stock
 
 
 def test_workspace_contract():

@@ -1,0 +1,129 @@
+"""Boolean attn_mask on the 16-bit attention kernel (packed to bits in the workspace, applied in the
+softmax) against the reference's CPU path -- stock torch SDPA with the same mask on CPU tensors
+(needs a B200; marked gpu).  The reference itself sent every masked call to stock; these are the
+mask shapes models pass: key padding [B,1,1,Lk], a shared [Lq,Lk] pattern, per-head [B,H,Lq,Lk],
+rows left with no key (output 0, as torch), masks combined with is_causal (ANDed, torch's math
+path), the tail-split schedule, grouped-query heads, head dim 160, and the patched F.sdpa.
+Tolerances as in test_parity_gpu.py."""
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+import cmpext3
+from cmpext3 import _native as N
+from tests.test_parity_gpu import check
+
+pytestmark = pytest.mark.gpu
+
+
+def _qkv(B, H, Lq, Lk, D, dtype, seed, Hkv=None):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, H, Lq, D, generator=g).to(dtype)
+    k = torch.randn(B, Hkv or H, Lk, D, generator=g).to(dtype)
+    v = torch.randn(B, Hkv or H, Lk, D, generator=g).to(dtype)
+    return q, k, v, g
+
+
+def _ref(q, k, v, mask, causal, gqa=False):
+    with torch.no_grad():
+        return F.scaled_dot_product_attention(q.float(), k.float(), v.float(), attn_mask=mask,
+                                              is_causal=causal, enable_gqa=gqa).to(q.dtype)
+
+
+def _run(dev, q, k, v, mask, causal, what, gqa=False):
+    got = cmpext3.ops.attention(q.to(dev), k.to(dev), v.to(dev), None, causal, mask.to(dev))
+    torch.cuda.synchronize()
+    assert torch.isfinite(got.float()).all(), f"{what}: non-finite output"
+    check(got, _ref(q, k, v, mask, causal, gqa), q.dtype, what)
+    assert N.device_status() == 0
+    return got
+
+
+MASK_SHAPES = ["key_padding", "shared", "per_head", "per_batch_query"]
+
+
+def _mask(kind, B, H, Lq, Lk, g):
+    if kind == "key_padding":     # [B, 1, 1, Lk]: the last keys of each batch item are padding
+        lens = torch.randint(1, Lk + 1, (B,), generator=g)
+        return (torch.arange(Lk)[None, :] < lens[:, None]).view(B, 1, 1, Lk)
+    if kind == "shared":          # [Lq, Lk]
+        return torch.rand(Lq, Lk, generator=g) > 0.3
+    if kind == "per_head":        # [B, H, Lq, Lk]
+        return torch.rand(B, H, Lq, Lk, generator=g) > 0.5
+    return torch.rand(B, 1, Lq, Lk, generator=g) > 0.2   # [B, 1, Lq, Lk]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+@pytest.mark.parametrize("kind", MASK_SHAPES)
+@pytest.mark.parametrize("D", [64, 128, 160])
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+@pytest.mark.parametrize("lens", [(77, 77), (300, 1000), (513, 384), (1, 200)], ids=str)
+def test_boolean_mask_sweep(cuda_device, dtype, kind, D, causal, lens):
+    lq, lk = lens
+    q, k, v, g = _qkv(2, 3, lq, lk, D, dtype, seed=lq + 7 * lk + D + causal)
+    m = _mask(kind, 2, 3, lq, lk, g)
+    assert N.attention_plan(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), None, causal,
+                            m.to(cuda_device)).endswith("+mask>")
+    _run(cuda_device, q, k, v, m, causal, f"{kind} D{D} {lens} causal={causal}")
+
+
+def test_rows_with_no_key_output_zero(cuda_device):
+    q, k, v, g = _qkv(1, 2, 300, 400, 128, torch.bfloat16, seed=4)
+    m = torch.rand(300, 400, generator=g) > 0.5
+    m[7] = False      # row 7: nothing in any key tile
+    m[200, :] = False
+    m[200, 399] = True  # row 200: only the very last key
+    m[255, :128] = False  # row 255: nothing in the first key tile, keys later
+    got = _run(cuda_device, q, k, v, m, False, "empty rows")
+    assert torch.equal(got[:, :, 7].float().cpu(), torch.zeros(1, 2, 128))
+
+
+def test_mask_with_tail_split(cuda_device):
+    # 2 items on 148 SMs: split into 8 key ranges; some rows have no key in some ranges, one in none
+    q, k, v, g = _qkv(1, 1, 512, 4096, 64, torch.float16, seed=5)
+    m = torch.rand(512, 4096, generator=g) > 0.97
+    m[10] = False
+    m[11, :4000] = False
+    qd, kd, vd, md = (t.to(cuda_device) for t in (q, k, v, m))
+    assert "+tail-split+mask" in N.attention_plan(qd, kd, vd, None, False, md)
+    _run(cuda_device, q, k, v, m, False, "split + mask")
+
+
+def test_mask_with_grouped_query_heads(cuda_device):
+    q, k, v, g = _qkv(2, 8, 257, 300, 128, torch.bfloat16, seed=6, Hkv=2)
+    m = torch.rand(2, 8, 257, 300, generator=g) > 0.4
+    _run(cuda_device, q, k, v, m, True, "gqa + mask", gqa=True)
+
+
+def test_mask_broadcast_along_keys_is_materialised(cuda_device):
+    # [B, H, Lq, 1]: one verdict per query row for every key
+    q, k, v, g = _qkv(1, 2, 130, 200, 64, torch.bfloat16, seed=9)
+    m = torch.rand(1, 2, 130, 1, generator=g) > 0.3
+    _run(cuda_device, q, k, v, m, False, "mask broadcast along keys")
+
+
+def test_patched_sdpa_boolean_mask_native_float_mask_stock(cuda_device, patched):
+    q, k, v, g = _qkv(1, 4, 256, 256, 128, torch.bfloat16, seed=2)
+    qd, kd, vd = (t.to(cuda_device) for t in (q, k, v))
+    m = torch.rand(256, 256, generator=g) > 0.5
+    with torch.no_grad():
+        got = F.scaled_dot_product_attention(qd, kd, vd, attn_mask=m.to(cuda_device))
+        add = torch.zeros(256, 256, dtype=torch.bfloat16, device=cuda_device)
+        F.scaled_dot_product_attention(qd, kd, vd, attn_mask=add)  # additive: stock
+    torch.cuda.synchronize()
+    check(got, _ref(q, k, v, m, False), torch.bfloat16, "patched sdpa mask")
+    entries = [d.entry for d in cmpext3.autoselect.report() if d.use_native]
+    assert any((e or "").endswith("+mask>") for e in entries), cmpext3.autoselect_report()
+
+
+def test_noalloc_declines_masked_calls(cuda_device):
+    q, k, v, _ = _qkv(1, 1, 64, 64, 64, torch.bfloat16, seed=1)
+    qd, kd, vd = (t.to(cuda_device) for t in (q, k, v))
+    m = torch.ones(64, 64, dtype=torch.bool, device=cuda_device).expand(1, 1, 64, 64)
+    out = torch.empty_like(qd)
+    desc = N._attn_desc(qd, kd, vd, out, 0.125, False, mask=m)
+    assert N.lib.cmpx_attn_fwd_noalloc(ctypes.byref(desc), N._stream_handle(cuda_device)) == N.ERR_WORKSPACE

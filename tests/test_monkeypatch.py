@@ -442,11 +442,30 @@ class TestScaledDotProductAttention:
         F.scaled_dot_product_attention(q, k, v, scale=0.25)
         assert_called_once_with_tensors(native.attention, q, k, v, 0.25, False)
 
-    def test_falls_back_when_attn_mask_given(self, patched, native, monkeypatch):
+    def test_falls_back_when_float_attn_mask_given(self, patched, native, monkeypatch):
+        # additive masks stay stock (the reference sent every masked call to stock)
         force_eligible(monkeypatch)
         q, k, v = self._qkv(1, 2, 3, 4)
-        F.scaled_dot_product_attention(q, k, v, attn_mask=torch.zeros(3, 3, dtype=torch.bool))
+        F.scaled_dot_product_attention(q, k, v, attn_mask=torch.zeros(3, 3))
         native.attention.assert_not_called()
+
+    def test_boolean_attn_mask_runs_native(self, patched, native, monkeypatch):
+        force_eligible(monkeypatch)
+        q, k, v = self._qkv(1, 2, 3, 4)
+        m = torch.ones(3, 3, dtype=torch.bool).tril()
+        native.attention.return_value = torch.zeros(1, 2, 3, 4)
+        F.scaled_dot_product_attention(q, k, v, attn_mask=m)
+        args = native.attention.call_args[0]
+        assert args[5] is m and args[4] is False
+
+    def test_native_mask_error_falls_back_to_stock(self, patched, native, monkeypatch):
+        force_eligible(monkeypatch)
+        native.attention.side_effect = RuntimeError("attn_mask does not broadcast")
+        q, k, v = self._qkv(1, 2, 3, 4)
+        m = torch.rand(3, 3) > 0.5
+        got = F.scaled_dot_product_attention(q, k, v, attn_mask=m)
+        ref = cmpext3._ORIGINALS[(F, "scaled_dot_product_attention")](q, k, v, attn_mask=m)
+        assert torch.equal(got, ref)
 
     def test_falls_back_when_dropout_nonzero(self, patched, native, monkeypatch):
         force_eligible(monkeypatch)

@@ -61,6 +61,7 @@ class AttnDesc(ctypes.Structure):
         ("dtype", ctypes.c_int32), ("causal", ctypes.c_int32), ("scale", ctypes.c_double),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
         ("heads_kv", ctypes.c_int64),
+        ("mask", ctypes.c_void_p), ("mask_stride", ctypes.c_int64 * 4),
     ]
 
 
@@ -91,7 +92,7 @@ class SoftmaxDesc(ctypes.Structure):
 
 
 # CMPX_ABI_VERSION of include/cmpx_b200.h that the ctypes structures above mirror.
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 
 def _load() -> ctypes.CDLL:
@@ -178,7 +179,7 @@ def _tma_ok(t: torch.Tensor) -> bool:
     return s0 > 0 and s1 > 0 and s2 > 0 and (s0 * es) % 16 == 0 and (s1 * es) % 16 == 0 and (s2 * es) % 16 == 0
 
 
-def _attn_desc(q, k, v, o, scale: float, causal: bool, workspace=None) -> AttnDesc:
+def _attn_desc(q, k, v, o, scale: float, causal: bool, workspace=None, mask=None) -> AttnDesc:
     B, H, Lq, D = q.shape
     qs, ks, vs, os_ = q.stride(), k.stride(), v.stride(), o.stride()
     return AttnDesc(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), B, H, Lq, k.shape[2], D,
@@ -186,7 +187,34 @@ def _attn_desc(q, k, v, o, scale: float, causal: bool, workspace=None) -> AttnDe
                     (ctypes.c_int64 * 3)(*vs[:3]), (ctypes.c_int64 * 3)(*os_[:3]),
                     _DTYPE[q.dtype], 1 if causal else 0, float(scale),
                     None if workspace is None else workspace.data_ptr(),
-                    0 if workspace is None else workspace.numel(), k.shape[1])
+                    0 if workspace is None else workspace.numel(), k.shape[1],
+                    None if mask is None else mask.data_ptr(),
+                    (ctypes.c_int64 * 4)(*(mask.stride() if mask is not None else (0, 0, 0, 0))))
+
+
+def _prepare_mask(attn_mask, query, key):
+    """A boolean attn_mask broadcast to [B, H, Lq, Lk] as a strided view (0 along broadcast dims,
+    the key dimension contiguous), or None.  Float (additive) masks are not in the tile table."""
+    if attn_mask is None:
+        return None
+    if not isinstance(attn_mask, torch.Tensor):
+        raise TypeError("attn_mask must be a Tensor")
+    if attn_mask.dtype != torch.bool:
+        raise RuntimeError("attention: only a boolean attn_mask runs on the kernels (additive masks: stock)")
+    if attn_mask.device != query.device:
+        raise RuntimeError("attn_mask must be on the query's device")
+    B, H, Lq, _ = query.shape
+    Lk = key.shape[2]
+    m = attn_mask if attn_mask.stride(-1) == 1 or attn_mask.size(-1) == 1 else attn_mask.contiguous()
+    if m.dim() > 4:
+        raise RuntimeError("attn_mask has more than 4 dimensions")
+    try:
+        m = m.expand(B, H, Lq, Lk)
+    except RuntimeError as exc:
+        raise RuntimeError(f"attn_mask {tuple(attn_mask.shape)} does not broadcast to {(B, H, Lq, Lk)}") from exc
+    if m.stride(3) != 1:  # (a mask broadcast along keys: materialise its rows)
+        m = m.contiguous()
+    return m
 
 
 def _check_attention_args(query, key, value) -> None:
@@ -242,15 +270,18 @@ def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
     return ws
 
 
-def attention(query, key, value, scale=None, causal=False):
-    """SDPA forward on the sm_100a kernels.  Same contract as the reference's ops.attention."""
+def attention(query, key, value, scale=None, causal=False, attn_mask=None):
+    """SDPA forward on the sm_100a kernels.  Same contract as the reference's ops.attention, plus an
+    optional boolean attn_mask (torch's meaning: True = the key takes part; with causal the two
+    are ANDed; a row left with no key outputs 0)."""
     q, k, v, out, scale = _prepare_attention(query, key, value, scale, causal)
+    mask = _prepare_mask(attn_mask, q, k)
     dev = q.device
     stream = _stream_handle(dev)
-    # The 16-bit kernels keep their work counters (and, for a non-causal call whose last wave of
-    # work is partial, the split key ranges' partial results) in a workspace; the fp32 ones need
-    # none.  One zero-filled buffer per (device, stream), grown on demand.
-    desc = _attn_desc(q, k, v, out, scale, bool(causal))
+    # The 16-bit kernels keep their work counters (and the packed mask, and for a non-causal call
+    # whose last wave of work is partial the split key ranges' partial results) in a workspace; the
+    # fp32 ones need none.  One zero-filled buffer per (device, stream), grown on demand.
+    desc = _attn_desc(q, k, v, out, scale, bool(causal), mask=mask)
     nbytes = lib.cmpx_attn_workspace_size(ctypes.byref(desc))
     if nbytes:
         ws = _workspace(dev, stream, nbytes)
@@ -266,10 +297,11 @@ def attention(query, key, value, scale=None, causal=False):
     return out
 
 
-def attention_plan(query, key, value, scale=None, causal=False) -> str:
+def attention_plan(query, key, value, scale=None, causal=False, attn_mask=None) -> str:
     """Name of the tile-table entry ``attention`` would run for these arguments."""
     q, k, v, out, scale = _prepare_attention(query, key, value, scale, causal)
-    desc = _attn_desc(q, k, v, out, scale, bool(causal))
+    mask = _prepare_mask(attn_mask, q, k)
+    desc = _attn_desc(q, k, v, out, scale, bool(causal), mask=mask)
     buf = ctypes.create_string_buffer(128)
     st = lib.cmpx_attn_plan(ctypes.byref(desc), buf, 128)
     if st != OK:

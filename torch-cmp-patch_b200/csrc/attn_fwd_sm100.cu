@@ -30,9 +30,11 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <array>
 #include <cmath>
 #include <cstdio>
 #include <mutex>
+#include <string>
 
 #include "cmpx_internal.h"
 #include "cmpx_ptx.cuh"
@@ -120,9 +122,36 @@ struct FmhaParams {
   int n_work;
   float* part_ml;              // [n_work - n_whole][2][128] (m, l) pairs
   float* part_o;               // [n_work - n_whole][2][128][DP]
+  // Boolean mask packed to bits (MASK instantiations): key j of query row i of (b, h) is bit j%32
+  // of word mask_bits[b*mb_b + h*mb_h + i*mb_q + j/32] (strides in words, 0 = broadcast); rows
+  // hold a multiple of 4 words, so each 128-key tile's bits are one aligned 16-byte load.
+  const uint32_t* mask_bits;
+  long long mb_b, mb_h, mb_q;
   unsigned long long timeout_ns;
   unsigned int* dev_flags;
 };
+
+// Packs a boolean mask (one byte per element, nonzero = the key takes part; element strides sb, sh,
+// sq over the packed extents nb x nh x nq, keys contiguous) to bits: one warp per mask row, one
+// ballot per 32 keys; words past the last key are 0.
+__global__ void __launch_bounds__(256) fmha_pack_mask_kernel(const uint8_t* __restrict__ mask,
+                                                             long long sb, long long sh, long long sq,
+                                                             int nh, int nq, int len_k, int words,
+                                                             long long rows, uint32_t* __restrict__ bits) {
+  const long long row = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const long long q = row % nq;
+  const long long bh = row / nq;
+  const long long src = (bh / nh) * sb + (bh % nh) * sh + q * sq;
+#pragma unroll 4
+  for (int w = 0; w < words; ++w) {
+    const int key = w * 32 + lane;
+    const bool on = key < len_k && mask[src + key] != 0;
+    const uint32_t word = __ballot_sync(0xffffffffu, on);
+    if (lane == 0) bits[row * words + w] = word;
+  }
+}
 
 // One chunk (16 column pairs = 32 keys) of a row's exponentials: p = 2^(s*sl2 + nmb) packed to
 // 16-bit pairs in pk, the row sum accumulated in la/lb.  x = s*sl2 + nmb is formed and the sum
@@ -292,14 +321,15 @@ __global__ void __launch_bounds__(128) fmha_split_merge_kernel(const __grid_cons
 #pragma unroll
     for (int e = 0; e < CPL; ++e) a[e] = 0.f;
     float lsum = 0.f;
+    // (ranges in which a masked row has no key: m = -inf, l = 0, O = 0 -- weight 0)
 #pragma unroll
     for (int r = 0; r < kMaxSplit; ++r) {
-      const float w = r < split ? ex2_approx(ml[i][r].x - mx) : 0.f;
+      const float w = (r < split && ml[i][r].x > -INFINITY) ? ex2_approx(ml[i][r].x - mx) : 0.f;
       lsum += w * ml[i][r].y;
 #pragma unroll
       for (int e = 0; e < CPL; ++e) a[e] += w * o[i][r][e];
     }
-    const float inv = 1.f / lsum;
+    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;  // a row with no key at all: output 0
     uint16_t* dst = static_cast<uint16_t*>(p.o) + b * p.os_b + h * p.os_h +
                     static_cast<long long>(qrow) * p.os_s + col;
     // column pairs inside the head dim (a multiple of 8, so a pair is all in or all out)
@@ -313,9 +343,9 @@ __global__ void __launch_bounds__(128) fmha_split_merge_kernel(const __grid_cons
 
 // Work item w (persistent schedule): bh = w / n_pairs, pair = n_pairs - 1 - w % n_pairs.  The items
 // of one (b, h) are consecutive, so the CTAs busy at any moment share a few heads' K/V in L2, and
-// within a head the heavy (late, causal) row pairs go first.  SPLIT: the launch has a tail split
-// (a separate instantiation, so that launches without one run the unsplit code unchanged).
-template <int DP, bool BF16, bool SPLIT>
+// within a head the heavy (late, causal) row pairs go first.  SPLIT: the launch has a tail split;
+// MASK: a boolean mask (separate instantiations, so that plain launches run their code unchanged).
+template <int DP, bool BF16, bool SPLIT, bool MASK>
 __global__ void __launch_bounds__(352, 1)
     fmha_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
@@ -612,17 +642,38 @@ __global__ void __launch_bounds__(352, 1)
       w = __shfl_sync(0xffffffffu, w, 0);
       if (!ok || w < 0) break;
       int q0, j_begin, j_end;  // (the rest of the geometry is recomputed for the epilogue)
+      const uint32_t* mrow = nullptr;  // (MASK) this row's mask words
       {
         const Work g = work_geometry(w);
         q0 = g.q0;
         j_begin = g.j0;
         j_end = t == 0 ? min(g.j1, tile0_kv(q0, g.n_kv)) : g.j1;
+        if constexpr (MASK) {
+          const int r = q0 + t * C::BM + row;
+          if (r < p.len_q) mrow = p.mask_bits + g.b * p.mb_b + g.h * p.mb_h + r * p.mb_q;
+        }
       }
       const int qrow = q0 + t * C::BM + row;
       float m_run = -INFINITY;  // running max of s * scale * log2(e)
       float l_run = 0.f;
 
       for (int j = j_begin; j < j_end; ++j) {
+        // (MASK) this tile's mask bits, loaded before the wait for S so the load overlaps it
+        uint32_t mw[C::BN / 32];
+        if constexpr (MASK) {
+          if (mrow) {
+            if constexpr (C::BN == 128) {
+              const uint4 v = __ldg(reinterpret_cast<const uint4*>(mrow) + j);
+              mw[0] = v.x; mw[1] = v.y; mw[2] = v.z; mw[3] = v.w;
+            } else {
+              const uint2 v = __ldg(reinterpret_cast<const uint2*>(mrow) + j);
+              mw[0] = v.x; mw[1] = v.y;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < C::BN / 32; ++i) mw[i] = ~0u;  // rows past Lq: not stored
+          }
+        }
         if (!mbar_wait_all(bar(C::B_SFULL + t), (n_sfull++) & 1u, ctl)) {
           ok = false;
           break;
@@ -636,6 +687,11 @@ __global__ void __launch_bounds__(352, 1)
           tmem_ld32(s_tm + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
         }
         float* s = reinterpret_cast<float*>(sr);
+        if constexpr (MASK) {
+#pragma unroll
+          for (int c = 0; c < C::BN; ++c)
+            if (!((mw[c >> 5] >> (c & 31)) & 1u)) s[c] = masked;
+        }
         tc_fence_before_sync();
         mbar_arrive(bar(C::B_SFREE + t));  // S is in registers: the other tile's QK may overwrite it
 
@@ -678,7 +734,9 @@ __global__ void __launch_bounds__(352, 1)
             alpha = ex2_approx(m_run - m_tile);
             m_run = m_tile;
           }
-          l_tile = exp_pass<C::BN, BF16, C::EMU>(s, sl2, -m_run, p_tm, [] {});
+          // (MASK: a row with no key left so far keeps m_run = -inf; its p are 0, not NaN)
+          const float nm = (MASK && m_run == -INFINITY) ? 0.f : -m_run;
+          l_tile = exp_pass<C::BN, BF16, C::EMU>(s, sl2, nm, p_tm, [] {});
           if (j > j_begin && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
             for (int c = 0; c < DP / 32; ++c) {
@@ -704,7 +762,8 @@ __global__ void __launch_bounds__(352, 1)
       tc_fence_after_sync();
       const Work g = work_geometry(w);
       const int b = g.b, h = g.h;
-      const float inv_l = 1.f / l_run;
+      // (a row with no key left -- MASK only -- has l = 0 and O = 0: output 0, as torch)
+      const float inv_l = (MASK && !(l_run > 0.f)) ? 0.f : 1.f / l_run;
       const uint32_t turn_bar = bar(C::B_OST + t * 4 + wq);
       if (t == 1 || k > 0) {
         const uint32_t par = t == 1 ? static_cast<uint32_t>(k) & 1u : static_cast<uint32_t>(k - 1) & 1u;
@@ -792,16 +851,17 @@ namespace {
 
 bool stride_ok(int64_t s, int esize) { return s > 0 && ((s * esize) % 16) == 0 && (s * esize) < (1ll << 40); }
 
-template <int DP, bool BF16, bool SPLIT>
+template <int DP, bool BF16, bool SPLIT, bool MASK>
 void* fmha_kernel_ptr() {
-  return reinterpret_cast<void*>(&fmha_fwd_sm100_kernel<DP, BF16, SPLIT>);
+  return reinterpret_cast<void*>(&fmha_fwd_sm100_kernel<DP, BF16, SPLIT, MASK>);
 }
 
 // Tail split of a non-causal launch on num_sms persistent CTAs.  With n items and G CTAs, the
 // first n - n % G items run whole (full waves); the n % G items of the last, partial wave would
 // leave most CTAs idle while they run, so each is cut into split = G / (n % G) key ranges (at most
-// kMaxSplit, and at least 4 key tiles per range).  Workspace: the 256-byte work counters, then each
-// range's (m, l) per row and its fp32 O rows (scratch: written before they are read).
+// kMaxSplit, and at least 4 key tiles per range).  Workspace: the 256-byte work counters, the
+// packed mask if the call has one, then each range's (m, l) per row and its fp32 O rows (scratch:
+// written before they are read).
 struct FmhaSplit {
   int n_whole = 0, split = 1, n_work = 0;
   size_t ml_off = 0, o_off = 0, bytes = kAttnWorkspaceMin;
@@ -809,8 +869,32 @@ struct FmhaSplit {
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
+// The packed form of a call's boolean mask: extents (1 along a broadcast dimension), words per
+// row (a multiple of 4) and word strides (0 along a broadcast dimension).
+struct MaskPack {
+  long long nb = 0, nh = 0, nq = 0, words = 0, rows = 0;
+  long long wb = 0, wh = 0, wq = 0;
+  size_t bytes = 0;
+};
+
+MaskPack mask_pack_plan(const cmpx_attn_desc* d) {
+  MaskPack m;
+  if (!d->mask) return m;
+  m.nb = d->mask_stride[0] == 0 ? 1 : d->batch;
+  m.nh = d->mask_stride[1] == 0 ? 1 : d->heads;
+  m.nq = d->mask_stride[2] == 0 ? 1 : d->len_q;
+  m.words = ((d->len_k + 31) / 32 + 3) / 4 * 4;
+  m.rows = m.nb * m.nh * m.nq;
+  m.wq = m.nq > 1 ? m.words : 0;
+  m.wh = m.nh > 1 ? m.nq * m.words : 0;
+  m.wb = m.nb > 1 ? m.nh * m.nq * m.words : 0;
+  m.bytes = align256(static_cast<size_t>(m.rows * m.words) * sizeof(uint32_t));
+  return m;
+}
+
 FmhaSplit fmha_split_plan(const cmpx_attn_desc* d, int num_sms) {
   FmhaSplit sp;
+  sp.bytes = kAttnWorkspaceMin + mask_pack_plan(d).bytes;
   const int64_t n_items = ((d->len_q + 255) / 256) * d->heads * d->batch;
   sp.n_whole = static_cast<int>(n_items);
   sp.n_work = static_cast<int>(n_items);
@@ -826,7 +910,7 @@ FmhaSplit fmha_split_plan(const cmpx_attn_desc* d, int num_sms) {
   sp.n_whole = static_cast<int>(n_items - rem);
   sp.n_work = static_cast<int>(sp.n_whole + rem * split);
   const size_t ranges = static_cast<size_t>(rem * split);
-  sp.ml_off = kAttnWorkspaceMin;
+  sp.ml_off = kAttnWorkspaceMin + mask_pack_plan(d).bytes;
   sp.o_off = sp.ml_off + align256(ranges * 256 * 2 * sizeof(float));
   sp.bytes = sp.o_off + ranges * 256 * dp * sizeof(float);
   return sp;
@@ -837,6 +921,10 @@ FmhaSplit fmha_split_plan(const cmpx_attn_desc* d, int num_sms) {
 size_t fmha_workspace_bytes(const cmpx_attn_desc* d, int num_sms) {
   if (fmha_short_eligible(d)) return kAttnWorkspaceMin;
   return fmha_split_plan(d, num_sms).bytes;
+}
+
+size_t fmha_workspace_min(const cmpx_attn_desc* d) {
+  return kAttnWorkspaceMin + (fmha_short_eligible(d) ? 0 : mask_pack_plan(d).bytes);
 }
 
 const char* fmha_sm100_plan(const cmpx_attn_desc* d, int* status) {
@@ -872,20 +960,24 @@ const char* fmha_sm100_plan(const cmpx_attn_desc* d, int* status) {
   }
   if (fmha_short_eligible(d)) return fmha_short_name(d);
   // The name shows the schedule a call given cmpx_attn_workspace_size() bytes runs: "+tail-split"
-  // when the last wave's items are split into key ranges (a second, merging kernel follows).
+  // when the last wave's items are split into key ranges (a second, merging kernel follows),
+  // "+mask" when a boolean mask is packed to bits (a packing kernel runs first).
   const bool split = fmha_split_plan(d, current_num_sms()).split > 1;
   const bool bf = d->dtype == CMPX_BF16;
-  if (d->head_dim > 128)
-    return bf ? (split ? "fmha_sm100<bf16,D192,2x128q,64kv,3st,persistent+tail-split>"
-                       : "fmha_sm100<bf16,D192,2x128q,64kv,3st,persistent>")
-              : (split ? "fmha_sm100<f16,D192,2x128q,64kv,3st,persistent+tail-split>"
-                       : "fmha_sm100<f16,D192,2x128q,64kv,3st,persistent>");
-  static const char* const names[2][2][2] = {
-      {{"fmha_sm100<f16,D64,2x128q,128kv,6st,persistent>", "fmha_sm100<f16,D64,2x128q,128kv,6st,persistent+tail-split>"},
-       {"fmha_sm100<bf16,D64,2x128q,128kv,6st,persistent>", "fmha_sm100<bf16,D64,2x128q,128kv,6st,persistent+tail-split>"}},
-      {{"fmha_sm100<f16,D128,2x128q,128kv,4st,persistent>", "fmha_sm100<f16,D128,2x128q,128kv,4st,persistent+tail-split>"},
-       {"fmha_sm100<bf16,D128,2x128q,128kv,4st,persistent>", "fmha_sm100<bf16,D128,2x128q,128kv,4st,persistent+tail-split>"}}};
-  return names[d->head_dim <= 64 ? 0 : 1][bf ? 1 : 0][split ? 1 : 0];
+  static const std::array<std::string, 24> names = [] {
+    std::array<std::string, 24> out;
+    const char* const dims[3] = {"D64,2x128q,128kv,6st", "D128,2x128q,128kv,4st", "D192,2x128q,64kv,3st"};
+    for (int dd = 0; dd < 3; ++dd)
+      for (int t = 0; t < 2; ++t)
+        for (int sp = 0; sp < 2; ++sp)
+          for (int mk = 0; mk < 2; ++mk)
+            out[((dd * 2 + t) * 2 + sp) * 2 + mk] = std::string("fmha_sm100<") + (t ? "bf16," : "f16,") +
+                                                    dims[dd] + ",persistent" + (sp ? "+tail-split" : "") +
+                                                    (mk ? "+mask" : "") + ">";
+    return out;
+  }();
+  const int dd = d->head_dim <= 64 ? 0 : d->head_dim <= 128 ? 1 : 2;
+  return names[((dd * 2 + (bf ? 1 : 0)) * 2 + (split ? 1 : 0)) * 2 + (d->mask ? 1 : 0)].c_str();
 }
 
 bool make_bhsd_map(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, int64_t D, int64_t L,
@@ -917,11 +1009,11 @@ int launch_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   cudaGetDevice(&dev);
   cudaError_t attr_err = cudaSuccess;
   std::call_once(once[dev & 63], [&] {
-    attr_err = cudaFuncSetAttribute(fmha_kernel_ptr<DP, BF16, false>(),
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    if (attr_err == cudaSuccess)
-      attr_err = cudaFuncSetAttribute(fmha_kernel_ptr<DP, BF16, true>(),
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    void* const ptrs[4] = {fmha_kernel_ptr<DP, BF16, false, false>(), fmha_kernel_ptr<DP, BF16, true, false>(),
+                           fmha_kernel_ptr<DP, BF16, false, true>(), fmha_kernel_ptr<DP, BF16, true, true>()};
+    for (void* k : ptrs)
+      if (attr_err == cudaSuccess)
+        attr_err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   });
   if (attr_err != cudaSuccess) return CMPX_ERR_LAUNCH;
 
@@ -946,19 +1038,42 @@ int launch_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   FmhaSplit sp = fmha_split_plan(d, ctx.num_sms);
   if (d->workspace_bytes < sp.bytes) sp = FmhaSplit{};  // too small a workspace: no split
   uint8_t* ws = static_cast<uint8_t*>(d->workspace);
+  const MaskPack mp = mask_pack_plan(d);
+  p.mask_bits = nullptr;
+  p.mb_b = p.mb_h = p.mb_q = 0;
+  if (d->mask) {  // pack the mask to bits in the workspace, after the work counters
+    uint32_t* bits = reinterpret_cast<uint32_t*>(ws + kAttnWorkspaceMin);
+    const long long blocks = (mp.rows + 7) / 8;
+    if (blocks > 0x7fffffffll) return CMPX_ERR_UNSUPPORTED_SHAPE;
+    fmha_pack_mask_kernel<<<static_cast<unsigned int>(blocks), 256, 0, ctx.stream>>>(
+        static_cast<const uint8_t*>(d->mask), d->mask_stride[0], d->mask_stride[1], d->mask_stride[2],
+        static_cast<int>(mp.nh), static_cast<int>(mp.nq), static_cast<int>(d->len_k),
+        static_cast<int>(mp.words), mp.rows, bits);
+    if (cudaGetLastError() != cudaSuccess) return CMPX_ERR_LAUNCH;
+    p.mask_bits = bits;
+    p.mb_b = mp.wb;
+    p.mb_h = mp.wh;
+    p.mb_q = mp.wq;
+  }
   p.n_whole = sp.split > 1 ? sp.n_whole : p.n_items;
   p.split = sp.split;
   p.n_work = sp.split > 1 ? sp.n_work : p.n_items;
   p.part_ml = sp.split > 1 ? reinterpret_cast<float*>(ws + sp.ml_off) : nullptr;
   p.part_o = sp.split > 1 ? reinterpret_cast<float*>(ws + sp.o_off) : nullptr;
   const int grid = std::min(p.n_work, std::max(1, ctx.num_sms));
+  const bool mask = d->mask != nullptr;
   if (sp.split > 1) {
-    fmha_fwd_sm100_kernel<DP, BF16, true><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, to, p);
+    if (mask)
+      fmha_fwd_sm100_kernel<DP, BF16, true, true><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, to, p);
+    else
+      fmha_fwd_sm100_kernel<DP, BF16, true, false><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, to, p);
     if (cudaGetLastError() != cudaSuccess) return CMPX_ERR_LAUNCH;
     const int rows = (p.n_items - p.n_whole) * 256;
     fmha_split_merge_kernel<DP, BF16><<<(rows + 7) / 8, 128, 0, ctx.stream>>>(p);
+  } else if (mask) {
+    fmha_fwd_sm100_kernel<DP, BF16, false, true><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, to, p);
   } else {
-    fmha_fwd_sm100_kernel<DP, BF16, false><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, to, p);
+    fmha_fwd_sm100_kernel<DP, BF16, false, false><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, to, p);
   }
   return cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
 }

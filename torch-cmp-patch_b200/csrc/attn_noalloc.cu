@@ -60,8 +60,11 @@ void* scratch_on_current_device(int* status) {
 
 extern "C" CMPX_API int cmpx_attn_fwd_noalloc(const cmpx_attn_desc* desc, void* stream) {
   if (!desc) return CMPX_ERR_INVALID_ARGUMENT;
-  // The 16-bit kernels run with their minimum workspace (the work counters; no tail split).
-  const size_t need = (desc->dtype == CMPX_F16 || desc->dtype == CMPX_BF16) ? cmpx::kAttnWorkspaceMin : 0;
+  // The 16-bit kernels run with their minimum workspace (the work counters; no tail split).  A
+  // boolean mask is packed to bits in the workspace, which the fixed scratch has no room for.
+  const bool sixteen = desc->dtype == CMPX_F16 || desc->dtype == CMPX_BF16;
+  if (sixteen && desc->mask) return CMPX_ERR_WORKSPACE;
+  const size_t need = sixteen ? cmpx::kAttnWorkspaceMin : 0;
   if (need > kNoAllocScratchBytes) return CMPX_ERR_WORKSPACE;  // beyond the fixed scratch
   cmpx_attn_desc d = *desc;  // the caller's workspace fields are ignored
   d.workspace = nullptr;

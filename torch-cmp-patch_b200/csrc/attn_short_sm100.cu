@@ -427,7 +427,7 @@ __global__ void __launch_bounds__(320, 1)
 // --------------------------------------------------------------------------------------------
 bool fmha_short_eligible(const cmpx_attn_desc* d) {
   return (d->dtype == CMPX_F16 || d->dtype == CMPX_BF16) && !d->causal && d->len_k >= 1 &&
-         d->len_k <= 128 && d->len_q > 0 && d->head_dim <= 128;
+         d->len_k <= 128 && d->len_q > 0 && d->head_dim <= 128 && !d->mask;
 }
 
 const char* fmha_short_name(const cmpx_attn_desc* d) {

@@ -96,6 +96,11 @@ bool attn_desc_valid(const cmpx_attn_desc* d) {
   // grouped-query attention: heads_kv (0 = heads) must divide heads
   if (d->heads_kv < 0 || (d->heads_kv > 0 && (d->heads_kv > d->heads || d->heads % d->heads_kv != 0)))
     return false;
+  if (d->mask) {  // strides: 0 (broadcast) or positive; the key stride must be 1
+    for (int i = 0; i < 3; ++i)
+      if (d->mask_stride[i] < 0) return false;
+    if (d->mask_stride[3] != 1) return false;
+  }
   return true;
 }
 
@@ -118,7 +123,13 @@ int attn_common_checks(const cmpx_attn_desc* d) {
 const char* attn_plan_impl(const cmpx_attn_desc* d, int* st) {
   *st = attn_common_checks(d);
   if (*st != CMPX_OK) return "none";
-  if (d->dtype == CMPX_F32) return attn_f32_plan(d, st);
+  if (d->dtype == CMPX_F32) {
+    if (d->mask) {  // masks run on the 16-bit kernel only
+      *st = CMPX_ERR_UNSUPPORTED_SHAPE;
+      return "none";
+    }
+    return attn_f32_plan(d, st);
+  }
   if (d->dtype == CMPX_F16 || d->dtype == CMPX_BF16) return fmha_sm100_plan(d, st);
   *st = CMPX_ERR_UNSUPPORTED_DTYPE;
   return "none";
@@ -276,7 +287,7 @@ int cmpx_attn_fwd(const cmpx_attn_desc* desc, void* stream) {
   if (st != CMPX_OK) return st;
   if (desc->batch == 0 || desc->heads == 0 || desc->len_q == 0) return CMPX_OK;
   if ((desc->dtype == CMPX_F16 || desc->dtype == CMPX_BF16) &&
-      (!desc->workspace || desc->workspace_bytes < kAttnWorkspaceMin ||
+      (!desc->workspace || desc->workspace_bytes < fmha_workspace_min(desc) ||
        (reinterpret_cast<uintptr_t>(desc->workspace) & 15u) != 0))
     return CMPX_ERR_WORKSPACE;
   LaunchCtx ctx;

@@ -48,6 +48,8 @@ const char* fmha_sm100_plan(const cmpx_attn_desc* d, int* status);
 // tail split's partial results on top of the counters; a workspace of at least kAttnWorkspaceMin
 // but below this runs unsplit).
 size_t fmha_workspace_bytes(const cmpx_attn_desc* d, int num_sms);
+// Smallest workspace a 16-bit call accepts: the work counters, plus the packed mask if it has one.
+size_t fmha_workspace_min(const cmpx_attn_desc* d);
 int launch_fmha_sm100(const cmpx_attn_desc* d, const LaunchCtx& ctx);
 // Short key sequences (non-causal, 1 <= Lk <= 128): one key tile, Q tiles streamed.
 bool fmha_short_eligible(const cmpx_attn_desc* d);
