@@ -40,7 +40,7 @@ extern "C" {
 #endif
 
 #define CMPX_ABI_VERSION 4  /* 2: cmpx_attn_desc.heads_kv (grouped-query attention); 3: cmpx_linear;
-                               4: cmpx_attn_desc.mask (boolean attention mask) */
+                               4: cmpx_attn_desc.mask / mask_kind (boolean or additive attention mask) */
 
 /* Element type of every operand of one call (inputs and output share it, as in the reference:
  * dtype in == dtype out, src/main.cpp:1623-1627, :366-369). */
@@ -49,6 +49,11 @@ typedef enum cmpx_dtype {
   CMPX_F16 = 1,
   CMPX_BF16 = 2
 } cmpx_dtype;
+
+typedef enum cmpx_mask_kind {
+  CMPX_MASK_BOOL = 0,  /* one byte per element, nonzero = the key takes part */
+  CMPX_MASK_ADD = 1    /* added to the scaled scores, in the call's dtype */
+} cmpx_mask_kind;
 
 typedef enum cmpx_status {
   CMPX_OK = 0,
@@ -69,13 +74,17 @@ typedef enum cmpx_status {
  * iff j <= i), which is what torch's is_causal does for len_q != len_k.
  * Grouped-query attention: k and v may have heads_kv heads (a divisor of heads); query head h then
  * reads key/value head h / (heads / heads_kv), as torch's enable_gqa=True does.
- * Boolean mask (16-bit calls): key j takes part in query i's softmax only where mask[b, h, i, j] is
- * nonzero (and, with causal, j <= i) -- torch's attn_mask of dtype bool, is_causal ANDed in as its
- * math path does.  A query row with no key left gets an all-zero output (torch's result), not NaN.
- * The mask is one byte per element, broadcastable: mask_stride holds element strides over batch,
- * head, query row and key, 0 for a broadcast dimension; the key stride must be 1.  The call packs
- * it to bits in the workspace (cmpx_attn_workspace_size counts that), so a masked call needs the
- * full workspace; fp32 calls with a mask return CMPX_ERR_UNSUPPORTED_SHAPE.
+ * Attention mask (16-bit calls), torch's attn_mask, broadcastable: mask_stride holds element strides
+ * over batch, head, query row and key, 0 for a broadcast dimension; the key stride must be 1.
+ *  - mask_kind CMPX_MASK_BOOL: one byte per element; key j takes part in query i's softmax only where
+ *    mask[b, h, i, j] is nonzero.  The call packs it to bits in the workspace
+ *    (cmpx_attn_workspace_size counts that), so a masked call needs the full workspace.
+ *  - mask_kind CMPX_MASK_ADD: values in the call's 16-bit type added to the scaled scores
+ *    (softmax(q k^T * scale + mask)); -inf removes a key.  Rows must start on 16-byte boundaries
+ *    (the query-row stride a multiple of 8, or 0).
+ * With causal the mask applies on top of it (torch's math path ANDs them).  A query row with no key
+ * left gets an all-zero output (torch's result), not NaN.  fp32 calls with a mask return
+ * CMPX_ERR_UNSUPPORTED_SHAPE.
  * Replaces: custom_attention_forward (src/main.cpp:1603-1774) and its launchers
  * launch_flash_attention_hfma2 (src/cuda/fp16_flash_attention_hfma2.cu:269-286),
  * launch_attention_fp16 (src/cuda/fp16_attention.cu:328-386),
@@ -96,8 +105,10 @@ typedef struct cmpx_attn_desc {
   void* workspace;     /* device scratch of cmpx_attn_workspace_size() bytes (may be NULL if 0) */
   size_t workspace_bytes;
   int64_t heads_kv;    /* heads of k and v: 0 or heads = one per query head, else a divisor of heads */
-  const void* mask;    /* boolean mask, one byte per element (see above); NULL = none */
+  const void* mask;    /* attention mask (see above); NULL = none */
   int64_t mask_stride[4]; /* batch, head, query-row, key strides of mask (elements; 0 = broadcast) */
+  int32_t mask_kind;   /* cmpx_mask_kind */
+  int32_t reserved2;
 } cmpx_attn_desc;
 
 /* Batched matmul  C[b] = A[b] @ B[b],  A: [batch, m, k], B: [batch, k, n], C: [batch, m, n].

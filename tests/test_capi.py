@@ -266,6 +266,19 @@ def test_mask_stride_rules(strides, status):
     assert _plan(d)[0] == status
 
 
+def test_additive_mask_rules():
+    d = _with_mask(_attn(Lq=64, Lk=80, dtype=1), (0, 0, 80, 1))
+    d.mask_kind = 1
+    st, name = _plan(d)
+    assert st == 0 and name.endswith("+addmask>"), name
+    assert N.lib.cmpx_attn_workspace_size(ctypes.byref(d)) == 256  # nothing to pack
+    d.mask_stride[2] = 77   # 154-byte rows: no 16-byte vector loads
+    assert _plan(d)[0] == N.ERR_MISALIGNED
+    d.mask_stride[2] = 80
+    d.mask_kind = 7
+    assert _plan(d)[0] == N.ERR_INVALID_ARGUMENT
+
+
 def test_mask_plans_on_the_16bit_kernel_only():
     d = _with_mask(_attn(Lq=64, Lk=77, dtype=2), (0, 0, 77, 1))
     st, name = _plan(d)

@@ -1,5 +1,5 @@
-"""Boolean attn_mask on the 16-bit attention kernel (packed to bits in the workspace, applied in the
-softmax) against the reference's CPU path -- stock torch SDPA with the same mask on CPU tensors
+"""attn_mask on the 16-bit attention kernel -- boolean (packed to bits in the workspace) and additive
+in the query's dtype (added to the scores in the softmax) -- against the reference's CPU path -- stock torch SDPA with the same mask on CPU tensors
 (needs a B200; marked gpu).  The reference itself sent every masked call to stock; these are the
 mask shapes models pass: key padding [B,1,1,Lk], a shared [Lq,Lk] pattern, per-head [B,H,Lq,Lk],
 rows left with no key (output 0, as torch), masks combined with is_causal (ANDed, torch's math
@@ -106,18 +106,65 @@ def test_mask_broadcast_along_keys_is_materialised(cuda_device):
     _run(cuda_device, q, k, v, m, False, "mask broadcast along keys")
 
 
-def test_patched_sdpa_boolean_mask_native_float_mask_stock(cuda_device, patched):
+def test_patched_sdpa_boolean_and_additive_masks_native(cuda_device, patched):
     q, k, v, g = _qkv(1, 4, 256, 256, 128, torch.bfloat16, seed=2)
     qd, kd, vd = (t.to(cuda_device) for t in (q, k, v))
     m = torch.rand(256, 256, generator=g) > 0.5
+    add = (torch.randn(256, 256, generator=g) * 2).to(torch.bfloat16)
     with torch.no_grad():
         got = F.scaled_dot_product_attention(qd, kd, vd, attn_mask=m.to(cuda_device))
-        add = torch.zeros(256, 256, dtype=torch.bfloat16, device=cuda_device)
-        F.scaled_dot_product_attention(qd, kd, vd, attn_mask=add)  # additive: stock
+        got_add = F.scaled_dot_product_attention(qd, kd, vd, attn_mask=add.to(cuda_device))
+        F.scaled_dot_product_attention(qd, kd, vd, attn_mask=add.float().to(cuda_device))  # fp32 mask: stock
     torch.cuda.synchronize()
     check(got, _ref(q, k, v, m, False), torch.bfloat16, "patched sdpa mask")
+    check(got_add, _ref(q, k, v, add.float(), False), torch.bfloat16, "patched sdpa additive mask")
     entries = [d.entry for d in cmpext3.autoselect.report() if d.use_native]
     assert any((e or "").endswith("+mask>") for e in entries), cmpext3.autoselect_report()
+    assert any((e or "").endswith("+addmask>") for e in entries), cmpext3.autoselect_report()
+
+
+def _additive(kind, B, H, Lq, Lk, dtype, g):
+    if kind == "padding":        # 0 / -inf key padding [B, 1, 1, Lk] (the form older models pass)
+        lens = torch.randint(1, Lk + 1, (B,), generator=g)
+        keep = (torch.arange(Lk)[None, :] < lens[:, None]).view(B, 1, 1, Lk)
+        return torch.zeros(B, 1, 1, Lk).masked_fill(~keep, float("-inf")).to(dtype)
+    if kind == "alibi":          # per-head linear distance bias [1, H, Lq, Lk]
+        slopes = torch.tensor([2.0 ** (-(i + 1)) for i in range(H)]).view(1, H, 1, 1)
+        dist = (torch.arange(Lk)[None, :] - torch.arange(Lq)[:, None]).abs().float()
+        return (-slopes * dist).to(dtype)
+    return (torch.randn(B, H, Lq, Lk, generator=g) * 3).to(dtype)   # arbitrary [B, H, Lq, Lk]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+@pytest.mark.parametrize("kind", ["padding", "alibi", "random"])
+@pytest.mark.parametrize("D", [64, 128, 160])
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+@pytest.mark.parametrize("lens", [(77, 77), (300, 1000), (1, 200)], ids=str)
+def test_additive_mask_sweep(cuda_device, dtype, kind, D, causal, lens):
+    lq, lk = lens
+    q, k, v, g = _qkv(2, 3, lq, lk, D, dtype, seed=lq + 5 * lk + D + causal)
+    m = _additive(kind, 2, 3, lq, lk, dtype, g)
+    qd, kd, vd, md = (t.to(cuda_device) for t in (q, k, v, m))
+    assert N.attention_plan(qd, kd, vd, None, causal, md).endswith("+addmask>")
+    got = cmpext3.ops.attention(qd, kd, vd, None, causal, md)
+    torch.cuda.synchronize()
+    assert torch.isfinite(got.float()).all()
+    check(got, _ref(q, k, v, m.float(), causal), dtype, f"additive {kind} D{D} {lens} causal={causal}")
+    assert N.device_status() == 0
+
+
+def test_additive_mask_all_minus_inf_rows_and_split(cuda_device):
+    q, k, v, g = _qkv(1, 1, 512, 4096, 64, torch.float16, seed=11)
+    m = torch.randn(512, 4096, generator=g).half()
+    m[3] = float("-inf")
+    m[4, :4000] = float("-inf")
+    qd, kd, vd, md = (t.to(cuda_device) for t in (q, k, v, m))
+    assert "+tail-split+addmask" in N.attention_plan(qd, kd, vd, None, False, md)
+    got = cmpext3.ops.attention(qd, kd, vd, None, False, md)
+    torch.cuda.synchronize()
+    assert torch.isfinite(got.float()).all()
+    assert torch.equal(got[0, 0, 3].float().cpu(), torch.zeros(64))
+    check(got, _ref(q, k, v, m.float(), False), torch.float16, "additive split")
 
 
 def test_noalloc_declines_masked_calls(cuda_device):

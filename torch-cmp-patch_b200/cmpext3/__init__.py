@@ -19,9 +19,9 @@ and, beyond the reference, the middle step of an einsum / bmm attention chain
 (every other softmax stays stock, as in the reference, which does not patch softmax at all).
 
 with the reference's wrapper signatures, gates and stock bail-outs: stock PyTorch runs when autograd
-is live for an input, when a tensor is not a CUDA fp16/fp32/bf16 tensor, when SDPA gets a float
-``attn_mask`` or ``dropout_p > 0`` or a non-4D query (a boolean ``attn_mask`` runs natively, beyond
-the reference, which sent every masked call to stock), when bmm/matmul get ``out=`` or mixed dtypes, and
+is live for an input, when a tensor is not a CUDA fp16/fp32/bf16 tensor, when SDPA gets an
+``attn_mask`` that is neither boolean nor in the query's 16-bit dtype, ``dropout_p > 0`` or a non-4D
+query (masks run natively beyond the reference, which sent every masked call to stock), when bmm/matmul get ``out=`` or mixed dtypes, and
 whenever the native op raises ``RuntimeError``/``TypeError`` for an argument outside its tile table.
 
 What changed underneath: the kernels are tcgen05/TMA/TMEM kernels for B200 in a C-ABI library
@@ -312,10 +312,12 @@ def _patched_tensor_softmax(self, dim, dtype=None):
 def _patched_sdpa(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=False,
                   scale=None, **kwargs):
     orig = _ORIGINALS[(F, "scaled_dot_product_attention")]
-    # Gates as in the reference (__init__.py:609-633), except that a boolean attn_mask (on the query's
-    # device) runs natively too; float (additive) masks stay stock.
-    mask_ok = attn_mask is None or (isinstance(attn_mask, torch.Tensor) and attn_mask.dtype == torch.bool
-                                    and attn_mask.device == query.device)
+    # Gates as in the reference (__init__.py:609-633), except that an attn_mask on the query's device
+    # runs natively too -- boolean, or additive in the query's 16-bit dtype; other masks stay stock.
+    mask_ok = attn_mask is None or (
+        isinstance(attn_mask, torch.Tensor) and attn_mask.device == query.device
+        and (attn_mask.dtype == torch.bool
+             or (attn_mask.dtype == query.dtype and query.dtype in (torch.float16, torch.bfloat16))))
     if (not mask_ok or dropout_p != 0.0
             or query.dim() != 4 or not _grad_safe(query, key, value)
             or not _usable(query, key, value)):
@@ -334,7 +336,7 @@ def _patched_sdpa(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=Fa
                          lambda: _C.attention_plan(query, key, value, scale, is_causal))
     return _dispatch("attention", query,
                      (query.shape, query.dtype, key.shape, value.shape, scale, is_causal,
-                      tuple(attn_mask.shape)),
+                      tuple(attn_mask.shape), attn_mask.dtype),
                      lambda: _C.attention(query, key, value, scale, is_causal, attn_mask),
                      lambda: orig(query, key, value, attn_mask=attn_mask, dropout_p=dropout_p,
                                   is_causal=is_causal, scale=scale, **kwargs),

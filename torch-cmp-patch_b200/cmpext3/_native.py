@@ -62,6 +62,7 @@ class AttnDesc(ctypes.Structure):
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
         ("heads_kv", ctypes.c_int64),
         ("mask", ctypes.c_void_p), ("mask_stride", ctypes.c_int64 * 4),
+        ("mask_kind", ctypes.c_int32), ("reserved2", ctypes.c_int32),
     ]
 
 
@@ -189,31 +190,47 @@ def _attn_desc(q, k, v, o, scale: float, causal: bool, workspace=None, mask=None
                     None if workspace is None else workspace.data_ptr(),
                     0 if workspace is None else workspace.numel(), k.shape[1],
                     None if mask is None else mask.data_ptr(),
-                    (ctypes.c_int64 * 4)(*(mask.stride() if mask is not None else (0, 0, 0, 0))))
+                    (ctypes.c_int64 * 4)(*(mask.stride() if mask is not None else (0, 0, 0, 0))),
+                    0 if mask is None or mask.dtype == torch.bool else 1, 0)
 
 
 def _prepare_mask(attn_mask, query, key):
-    """A boolean attn_mask broadcast to [B, H, Lq, Lk] as a strided view (0 along broadcast dims,
-    the key dimension contiguous), or None.  Float (additive) masks are not in the tile table."""
+    """attn_mask broadcast to [B, H, Lq, Lk] as a strided view (0 along broadcast dims, the key
+    dimension contiguous), or None.  Boolean masks (any layout), and additive masks in the query's
+    16-bit dtype (rows padded to 16-byte boundaries when they are not) are in the tile table; an
+    additive mask of another dtype, or with an fp32 call, is not (stock serves it)."""
     if attn_mask is None:
         return None
     if not isinstance(attn_mask, torch.Tensor):
         raise TypeError("attn_mask must be a Tensor")
-    if attn_mask.dtype != torch.bool:
-        raise RuntimeError("attention: only a boolean attn_mask runs on the kernels (additive masks: stock)")
+    additive = attn_mask.dtype != torch.bool
+    if additive and (attn_mask.dtype != query.dtype or query.dtype == torch.float32):
+        raise RuntimeError("attention: an additive attn_mask runs on the kernels only in the 16-bit query dtype")
     if attn_mask.device != query.device:
         raise RuntimeError("attn_mask must be on the query's device")
+    if attn_mask.dim() > 4:
+        raise RuntimeError("attn_mask has more than 4 dimensions")
     B, H, Lq, _ = query.shape
     Lk = key.shape[2]
-    m = attn_mask if attn_mask.stride(-1) == 1 or attn_mask.size(-1) == 1 else attn_mask.contiguous()
-    if m.dim() > 4:
-        raise RuntimeError("attn_mask has more than 4 dimensions")
+    m = attn_mask.reshape((1,) * (4 - attn_mask.dim()) + tuple(attn_mask.shape))
+    if m.stride(3) != 1 and m.size(3) != 1:
+        m = m.contiguous()
+    if m.size(3) == 1 and Lk != 1:  # broadcast along keys: materialise its rows
+        m = m.expand(*m.shape[:3], Lk).contiguous()
+    if additive:
+        # 16-byte vector loads: base and every non-broadcast row / head / batch stride aligned
+        def aligned(t):
+            return t.data_ptr() % 16 == 0 and all(
+                t.size(i) == 1 or t.stride(i) % 8 == 0 for i in range(3))
+        if not aligned(m):
+            lk_pad = (m.size(3) + 7) // 8 * 8
+            padded = torch.zeros(*m.shape[:3], lk_pad, dtype=m.dtype, device=m.device)
+            padded[..., :m.size(3)] = m
+            m = padded[..., :m.size(3)]
     try:
         m = m.expand(B, H, Lq, Lk)
     except RuntimeError as exc:
         raise RuntimeError(f"attn_mask {tuple(attn_mask.shape)} does not broadcast to {(B, H, Lq, Lk)}") from exc
-    if m.stride(3) != 1:  # (a mask broadcast along keys: materialise its rows)
-        m = m.contiguous()
     return m
 
 

@@ -27,6 +27,7 @@
 // Every wait is bounded (see cmpx_ptx.cuh); a CTA that gives up drains its in-flight copies
 // and MMAs, frees TMEM, sets the device status word and returns.
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -35,6 +36,7 @@
 #include <cstdio>
 #include <mutex>
 #include <string>
+#include <type_traits>
 
 #include "cmpx_internal.h"
 #include "cmpx_ptx.cuh"
@@ -53,12 +55,17 @@ namespace cmpx {
 // Most key ranges one item of the tail split is cut into.
 constexpr int kMaxSplit = 8;
 
-template <int DP>
+// Keys per K/V tile of an instantiation: 128; 64 for head dims above 128, where the two O
+// accumulators take 2 x 192 TMEM columns and S / P0 / P1 have to fit in the 128 left, and for
+// additive masks (MK = 2), whose values in flight would not fit the softmax's registers next to a
+// 128-key row of scores.
+template <int DP, int MK>
+constexpr int fmha_bn() { return (DP > 128 || MK == 2) ? 64 : 128; }
+
+template <int DP, int BN_ = fmha_bn<DP, 0>()>
 struct FmhaCfg {
   static constexpr int BM = 128;                    // rows of one Q tile
-  // Keys per K/V tile: 128; 64 for head dims above 128, where the two O accumulators take 2 x 192
-  // TMEM columns and S / P0 / P1 have to fit in the 128 left.
-  static constexpr int BN = DP <= 128 ? 128 : 64;
+  static constexpr int BN = BN_;                    // keys per K/V tile
   static constexpr int NCH = DP / 64;               // 128-byte chunks per row
   static constexpr int CH_BYTES = 128 * 128;        // one chunk of a 128-row (Q / O) tile
   static constexpr int KV_CH_BYTES = BN * 128;      // one chunk of a K / V tile
@@ -122,11 +129,16 @@ struct FmhaParams {
   int n_work;
   float* part_ml;              // [n_work - n_whole][2][128] (m, l) pairs
   float* part_o;               // [n_work - n_whole][2][128][DP]
-  // Boolean mask packed to bits (MASK instantiations): key j of query row i of (b, h) is bit j%32
+  // Boolean mask packed to bits (MK = 1): key j of query row i of (b, h) is bit j%32
   // of word mask_bits[b*mb_b + h*mb_h + i*mb_q + j/32] (strides in words, 0 = broadcast); rows
   // hold a multiple of 4 words, so each 128-key tile's bits are one aligned 16-byte load.
   const uint32_t* mask_bits;
   long long mb_b, mb_h, mb_q;
+  // Additive mask (MK = 2): 16-bit values in the call's type at mask_add[b*ma_b + h*ma_h + i*ma_q + j]
+  // (element strides, 0 = broadcast; rows 16-byte aligned), added to the scores as value / scale.
+  const uint16_t* mask_add;
+  long long ma_b, ma_h, ma_q;
+  float mask_inv_scale;
   unsigned long long timeout_ns;
   unsigned int* dev_flags;
 };
@@ -344,15 +356,16 @@ __global__ void __launch_bounds__(128) fmha_split_merge_kernel(const __grid_cons
 // Work item w (persistent schedule): bh = w / n_pairs, pair = n_pairs - 1 - w % n_pairs.  The items
 // of one (b, h) are consecutive, so the CTAs busy at any moment share a few heads' K/V in L2, and
 // within a head the heavy (late, causal) row pairs go first.  SPLIT: the launch has a tail split;
-// MASK: a boolean mask (separate instantiations, so that plain launches run their code unchanged).
-template <int DP, bool BF16, bool SPLIT, bool MASK>
+// MK: no mask (0), a boolean mask packed to bits (1), an additive 16-bit mask (2) -- separate
+// instantiations, so that plain launches run their code unchanged.
+template <int DP, bool BF16, bool SPLIT, int MK>
 __global__ void __launch_bounds__(352, 1)
     fmha_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v,
                           const __grid_constant__ CUtensorMap tm_o,
                           const __grid_constant__ FmhaParams p) {
-  using C = FmhaCfg<DP>;
+  using C = FmhaCfg<DP, fmha_bn<DP, MK>()>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
   const uint32_t base = (raw_base + 1023u) & ~1023u;
@@ -642,15 +655,18 @@ __global__ void __launch_bounds__(352, 1)
       w = __shfl_sync(0xffffffffu, w, 0);
       if (!ok || w < 0) break;
       int q0, j_begin, j_end;  // (the rest of the geometry is recomputed for the epilogue)
-      const uint32_t* mrow = nullptr;  // (MASK) this row's mask words
+      const uint32_t* mrow = nullptr;  // (MK 1) this row's mask words
+      const uint16_t* arow = nullptr;  // (MK 2) this row's additive mask values
       {
         const Work g = work_geometry(w);
         q0 = g.q0;
         j_begin = g.j0;
         j_end = t == 0 ? min(g.j1, tile0_kv(q0, g.n_kv)) : g.j1;
-        if constexpr (MASK) {
-          const int r = q0 + t * C::BM + row;
+        const int r = q0 + t * C::BM + row;
+        if constexpr (MK == 1) {
           if (r < p.len_q) mrow = p.mask_bits + g.b * p.mb_b + g.h * p.mb_h + r * p.mb_q;
+        } else if constexpr (MK == 2) {
+          if (r < p.len_q) arow = p.mask_add + g.b * p.ma_b + g.h * p.ma_h + r * p.ma_q;
         }
       }
       const int qrow = q0 + t * C::BM + row;
@@ -658,9 +674,21 @@ __global__ void __launch_bounds__(352, 1)
       float l_run = 0.f;
 
       for (int j = j_begin; j < j_end; ++j) {
-        // (MASK) this tile's mask bits, loaded before the wait for S so the load overlaps it
+        // (MK 1) this tile's mask bits, (MK 2) its first 32 additive values: loaded before the
+        // wait for S so the load overlaps it
+        const int kv_first = j * C::BN;
         uint32_t mw[C::BN / 32];
-        if constexpr (MASK) {
+        uint4 acur[4];
+        auto load_add = [&](int c, uint4 (&v)[4]) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int key = kv_first + c * 32 + e * 8;
+            v[e] = (arow && key < p.len_k) ? __ldg(reinterpret_cast<const uint4*>(arow + key))
+                                           : make_uint4(0u, 0u, 0u, 0u);
+          }
+        };
+        if constexpr (MK == 2) load_add(0, acur);
+        if constexpr (MK == 1) {
           if (mrow) {
             if constexpr (C::BN == 128) {
               const uint4 v = __ldg(reinterpret_cast<const uint4*>(mrow) + j);
@@ -687,10 +715,34 @@ __global__ void __launch_bounds__(352, 1)
           tmem_ld32(s_tm + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
         }
         float* s = reinterpret_cast<float*>(sr);
-        if constexpr (MASK) {
+        if constexpr (MK == 1) {
 #pragma unroll
           for (int c = 0; c < C::BN; ++c)
             if (!((mw[c >> 5] >> (c & 31)) & 1u)) s[c] = masked;
+        } else if constexpr (MK == 2) {
+          // s += mask / scale (so that s * scale = q.k * scale + mask), chunk by chunk with the
+          // next chunk's values in flight
+#pragma unroll
+          for (int c = 0; c < C::BN / 32; ++c) {
+            uint4 anext[4];
+            if (c + 1 < C::BN / 32) load_add(c + 1, anext);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const uint32_t wds[4] = {acur[e].x, acur[e].y, acur[e].z, acur[e].w};
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int idx = c * 32 + e * 8 + 2 * i;
+                const float lo = BF16 ? __uint_as_float(wds[i] << 16) : __half2float(__ushort_as_half(wds[i] & 0xffffu));
+                const float hi = BF16 ? __uint_as_float(wds[i] & 0xffff0000u) : __half2float(__ushort_as_half(wds[i] >> 16));
+                s[idx] = fmaf(lo, p.mask_inv_scale, s[idx]);
+                s[idx + 1] = fmaf(hi, p.mask_inv_scale, s[idx + 1]);
+              }
+            }
+            if (c + 1 < C::BN / 32) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) acur[e] = anext[e];
+            }
+          }
         }
         tc_fence_before_sync();
         mbar_arrive(bar(C::B_SFREE + t));  // S is in registers: the other tile's QK may overwrite it
@@ -734,8 +786,8 @@ __global__ void __launch_bounds__(352, 1)
             alpha = ex2_approx(m_run - m_tile);
             m_run = m_tile;
           }
-          // (MASK: a row with no key left so far keeps m_run = -inf; its p are 0, not NaN)
-          const float nm = (MASK && m_run == -INFINITY) ? 0.f : -m_run;
+          // (a masked row with no key left so far keeps m_run = -inf; its p are 0, not NaN)
+          const float nm = (MK != 0 && m_run == -INFINITY) ? 0.f : -m_run;
           l_tile = exp_pass<C::BN, BF16, C::EMU>(s, sl2, nm, p_tm, [] {});
           if (j > j_begin && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
@@ -762,8 +814,8 @@ __global__ void __launch_bounds__(352, 1)
       tc_fence_after_sync();
       const Work g = work_geometry(w);
       const int b = g.b, h = g.h;
-      // (a row with no key left -- MASK only -- has l = 0 and O = 0: output 0, as torch)
-      const float inv_l = (MASK && !(l_run > 0.f)) ? 0.f : 1.f / l_run;
+      // (a masked row with no key left has l = 0 and O = 0: output 0, as torch)
+      const float inv_l = (MK != 0 && !(l_run > 0.f)) ? 0.f : 1.f / l_run;
       const uint32_t turn_bar = bar(C::B_OST + t * 4 + wq);
       if (t == 1 || k > 0) {
         const uint32_t par = t == 1 ? static_cast<uint32_t>(k) & 1u : static_cast<uint32_t>(k - 1) & 1u;
@@ -851,9 +903,9 @@ namespace {
 
 bool stride_ok(int64_t s, int esize) { return s > 0 && ((s * esize) % 16) == 0 && (s * esize) < (1ll << 40); }
 
-template <int DP, bool BF16, bool SPLIT, bool MASK>
+template <int DP, bool BF16, bool SPLIT, int MK>
 void* fmha_kernel_ptr() {
-  return reinterpret_cast<void*>(&fmha_fwd_sm100_kernel<DP, BF16, SPLIT, MASK>);
+  return reinterpret_cast<void*>(&fmha_fwd_sm100_kernel<DP, BF16, SPLIT, MK>);
 }
 
 // Tail split of a non-causal launch on num_sms persistent CTAs.  With n items and G CTAs, the
@@ -879,7 +931,7 @@ struct MaskPack {
 
 MaskPack mask_pack_plan(const cmpx_attn_desc* d) {
   MaskPack m;
-  if (!d->mask) return m;
+  if (!d->mask || d->mask_kind != CMPX_MASK_BOOL) return m;
   m.nb = d->mask_stride[0] == 0 ? 1 : d->batch;
   m.nh = d->mask_stride[1] == 0 ? 1 : d->heads;
   m.nq = d->mask_stride[2] == 0 ? 1 : d->len_q;
@@ -901,7 +953,8 @@ FmhaSplit fmha_split_plan(const cmpx_attn_desc* d, int num_sms) {
   if (d->causal || num_sms <= 1 || n_items <= 0) return sp;
   const int64_t rem = n_items % num_sms;
   if (rem == 0) return sp;
-  const int64_t bn = d->head_dim <= 128 ? 128 : 64;
+  const bool add_mask = d->mask && d->mask_kind == CMPX_MASK_ADD;
+  const int64_t bn = (d->head_dim <= 128 && !add_mask) ? 128 : 64;
   const int64_t n_kv = (d->len_k + bn - 1) / bn;
   const int64_t split = std::min<int64_t>({num_sms / rem, n_kv / 4, kMaxSplit});
   if (split < 2) return sp;
@@ -958,26 +1011,40 @@ const char* fmha_sm100_plan(const cmpx_attn_desc* d, int* status) {
     *status = CMPX_ERR_UNSUPPORTED_SHAPE;
     return "none";
   }
+  if (d->mask && d->mask_kind == CMPX_MASK_ADD) {  // 16-byte vector loads of each row's values
+    if ((reinterpret_cast<uintptr_t>(d->mask) & 15u) != 0) {
+      *status = CMPX_ERR_MISALIGNED;
+      return "none";
+    }
+    for (int i = 0; i < 3; ++i)
+      if (d->mask_stride[i] % 8 != 0) {
+        *status = CMPX_ERR_MISALIGNED;
+        return "none";
+      }
+  }
   if (fmha_short_eligible(d)) return fmha_short_name(d);
   // The name shows the schedule a call given cmpx_attn_workspace_size() bytes runs: "+tail-split"
   // when the last wave's items are split into key ranges (a second, merging kernel follows),
-  // "+mask" when a boolean mask is packed to bits (a packing kernel runs first).
+  // "+mask" when a boolean mask is packed to bits (a packing kernel runs first), "+addmask" for an
+  // additive mask.
   const bool split = fmha_split_plan(d, current_num_sms()).split > 1;
   const bool bf = d->dtype == CMPX_BF16;
-  static const std::array<std::string, 24> names = [] {
-    std::array<std::string, 24> out;
+  static const std::array<std::string, 36> names = [] {
+    std::array<std::string, 36> out;
     const char* const dims[3] = {"D64,2x128q,128kv,6st", "D128,2x128q,128kv,4st", "D192,2x128q,64kv,3st"};
+    const char* const masks[3] = {"", "+mask", "+addmask"};
     for (int dd = 0; dd < 3; ++dd)
       for (int t = 0; t < 2; ++t)
         for (int sp = 0; sp < 2; ++sp)
-          for (int mk = 0; mk < 2; ++mk)
-            out[((dd * 2 + t) * 2 + sp) * 2 + mk] = std::string("fmha_sm100<") + (t ? "bf16," : "f16,") +
+          for (int mk = 0; mk < 3; ++mk)
+            out[((dd * 2 + t) * 2 + sp) * 3 + mk] = std::string("fmha_sm100<") + (t ? "bf16," : "f16,") +
                                                     dims[dd] + ",persistent" + (sp ? "+tail-split" : "") +
-                                                    (mk ? "+mask" : "") + ">";
+                                                    masks[mk] + ">";
     return out;
   }();
   const int dd = d->head_dim <= 64 ? 0 : d->head_dim <= 128 ? 1 : 2;
-  return names[((dd * 2 + (bf ? 1 : 0)) * 2 + (split ? 1 : 0)) * 2 + (d->mask ? 1 : 0)].c_str();
+  const int mk = !d->mask ? 0 : d->mask_kind == CMPX_MASK_BOOL ? 1 : 2;
+  return names[((dd * 2 + (bf ? 1 : 0)) * 2 + (split ? 1 : 0)) * 3 + mk].c_str();
 }
 
 bool make_bhsd_map(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, int64_t D, int64_t L,
@@ -994,13 +1061,17 @@ namespace {
 
 template <int DP, bool BF16>
 int launch_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
-  using C = FmhaCfg<DP>;
+  using C = FmhaCfg<DP, fmha_bn<DP, 0>()>;        // plain and boolean-mask instantiations
+  using C2 = FmhaCfg<DP, fmha_bn<DP, 2>()>;       // additive-mask instantiations
+  const int mk = !d->mask ? 0 : d->mask_kind == CMPX_MASK_BOOL ? 1 : 2;
+  const int bn = mk == 2 ? C2::BN : C::BN;
+  const int smem_bytes = mk == 2 ? C2::SMEM_BYTES : C::SMEM_BYTES;
   const CUtensorMapDataType dt =
       BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap tq, tk, tv, to;
   if (!make_bhsd_map(&tq, dt, d->q, d->head_dim, d->len_q, d->heads, d->batch, d->q_stride, 128) ||
-      !make_bhsd_map(&tk, dt, d->k, d->head_dim, d->len_k, attn_heads_kv(d), d->batch, d->k_stride, C::BN) ||
-      !make_bhsd_map(&tv, dt, d->v, d->head_dim, d->len_k, attn_heads_kv(d), d->batch, d->v_stride, C::BN) ||
+      !make_bhsd_map(&tk, dt, d->k, d->head_dim, d->len_k, attn_heads_kv(d), d->batch, d->k_stride, bn) ||
+      !make_bhsd_map(&tv, dt, d->v, d->head_dim, d->len_k, attn_heads_kv(d), d->batch, d->v_stride, bn) ||
       !make_bhsd_map(&to, dt, d->o, d->head_dim, d->len_q, d->heads, d->batch, d->o_stride, 32))
     return CMPX_ERR_LAUNCH;
 
@@ -1009,11 +1080,13 @@ int launch_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   cudaGetDevice(&dev);
   cudaError_t attr_err = cudaSuccess;
   std::call_once(once[dev & 63], [&] {
-    void* const ptrs[4] = {fmha_kernel_ptr<DP, BF16, false, false>(), fmha_kernel_ptr<DP, BF16, true, false>(),
-                           fmha_kernel_ptr<DP, BF16, false, true>(), fmha_kernel_ptr<DP, BF16, true, true>()};
-    for (void* k : ptrs)
+    void* const ptrs[6] = {fmha_kernel_ptr<DP, BF16, false, 0>(), fmha_kernel_ptr<DP, BF16, true, 0>(),
+                           fmha_kernel_ptr<DP, BF16, false, 1>(), fmha_kernel_ptr<DP, BF16, true, 1>(),
+                           fmha_kernel_ptr<DP, BF16, false, 2>(), fmha_kernel_ptr<DP, BF16, true, 2>()};
+    const int bytes[6] = {C::SMEM_BYTES, C::SMEM_BYTES, C::SMEM_BYTES, C::SMEM_BYTES, C2::SMEM_BYTES, C2::SMEM_BYTES};
+    for (int i = 0; i < 6; ++i)
       if (attr_err == cudaSuccess)
-        attr_err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+        attr_err = cudaFuncSetAttribute(ptrs[i], cudaFuncAttributeMaxDynamicSharedMemorySize, bytes[i]);
   });
   if (attr_err != cudaSuccess) return CMPX_ERR_LAUNCH;
 
@@ -1041,7 +1114,16 @@ int launch_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   const MaskPack mp = mask_pack_plan(d);
   p.mask_bits = nullptr;
   p.mb_b = p.mb_h = p.mb_q = 0;
-  if (d->mask) {  // pack the mask to bits in the workspace, after the work counters
+  p.mask_add = nullptr;
+  p.ma_b = p.ma_h = p.ma_q = 0;
+  p.mask_inv_scale = static_cast<float>(1.0 / d->scale);
+  if (mk == 2) {
+    p.mask_add = static_cast<const uint16_t*>(d->mask);
+    p.ma_b = d->mask_stride[0];
+    p.ma_h = d->mask_stride[1];
+    p.ma_q = d->mask_stride[2];
+  }
+  if (mk == 1) {  // pack the mask to bits in the workspace, after the work counters
     uint32_t* bits = reinterpret_cast<uint32_t*>(ws + kAttnWorkspaceMin);
     const long long blocks = (mp.rows + 7) / 8;
     if (blocks > 0x7fffffffll) return CMPX_ERR_UNSUPPORTED_SHAPE;
@@ -1061,19 +1143,26 @@ int launch_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   p.part_ml = sp.split > 1 ? reinterpret_cast<float*>(ws + sp.ml_off) : nullptr;
   p.part_o = sp.split > 1 ? reinterpret_cast<float*>(ws + sp.o_off) : nullptr;
   const int grid = std::min(p.n_work, std::max(1, ctx.num_sms));
-  const bool mask = d->mask != nullptr;
+  auto launch = [&](auto split_tag, auto mk_tag) {
+    fmha_fwd_sm100_kernel<DP, BF16, decltype(split_tag)::value, decltype(mk_tag)::value>
+        <<<grid, C::THREADS, smem_bytes, ctx.stream>>>(tq, tk, tv, to, p);
+  };
+  using Split = std::true_type;
+  using NoSplit = std::false_type;
+  using M0 = std::integral_constant<int, 0>;
+  using M1 = std::integral_constant<int, 1>;
+  using M2 = std::integral_constant<int, 2>;
   if (sp.split > 1) {
-    if (mask)
-      fmha_fwd_sm100_kernel<DP, BF16, true, true><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, to, p);
-    else
-      fmha_fwd_sm100_kernel<DP, BF16, true, false><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, to, p);
+    if (mk == 1) launch(Split{}, M1{});
+    else if (mk == 2) launch(Split{}, M2{});
+    else launch(Split{}, M0{});
     if (cudaGetLastError() != cudaSuccess) return CMPX_ERR_LAUNCH;
     const int rows = (p.n_items - p.n_whole) * 256;
     fmha_split_merge_kernel<DP, BF16><<<(rows + 7) / 8, 128, 0, ctx.stream>>>(p);
-  } else if (mask) {
-    fmha_fwd_sm100_kernel<DP, BF16, false, true><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, to, p);
   } else {
-    fmha_fwd_sm100_kernel<DP, BF16, false, false><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, to, p);
+    if (mk == 1) launch(NoSplit{}, M1{});
+    else if (mk == 2) launch(NoSplit{}, M2{});
+    else launch(NoSplit{}, M0{});
   }
   return cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
 }

@@ -100,6 +100,7 @@ bool attn_desc_valid(const cmpx_attn_desc* d) {
     for (int i = 0; i < 3; ++i)
       if (d->mask_stride[i] < 0) return false;
     if (d->mask_stride[3] != 1) return false;
+    if (d->mask_kind != CMPX_MASK_BOOL && d->mask_kind != CMPX_MASK_ADD) return false;
   }
   return true;
 }
