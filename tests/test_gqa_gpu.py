@@ -22,7 +22,6 @@ CASES = [
     (torch.bfloat16, 1, 8, 1, 257, 257, 64, True, "fmha_sm100<"),       # multi-query
     (torch.float16, 2, 10, 5, 500, 77, 64, False, "fmha_sm100_short"),  # short key sequences
     (torch.float32, 1, 8, 2, 300, 300, 40, False, "attn_tf32x3"),        # fp32 tensor cores
-    (torch.float32, 1, 4, 2, 130, 200, 100, True, "attn_f32_simt"),     # fp32 CUDA cores
 ]
 
 

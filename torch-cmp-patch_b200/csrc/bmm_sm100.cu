@@ -556,110 +556,4 @@ int launch_linear_sm100(const cmpx_linear_desc* d, const LaunchCtx& ctx) {
                                : launch_bmm_dt<false>(&b, ctx, am, bm, d->bias);
 }
 
-// --------------------------------------------------------------------------------------------
-// fp32 batched matmul on the CUDA cores (fp32 FMA, any strides).  128 x 128 output tile per CTA,
-// 256 threads each owning an 8 x 8 block, K staged through shared memory 16 at a time.
-// --------------------------------------------------------------------------------------------
-struct F32BmmParams {
-  const float* a;
-  const float* b;
-  float* c;
-  long long as[3], bs[3], cs[3];
-  int m, n, k;
-};
-
-__global__ void __launch_bounds__(256) bmm_f32_kernel(const F32BmmParams p) {
-  constexpr int BM = 128, BN = 128, BK = 16;
-  __shared__ float sA[BK][BM + 4];
-  __shared__ float sB[BK][BN + 4];
-  const int tid = threadIdx.x;
-  const int tx = tid & 15, ty = tid >> 4;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, z = blockIdx.z;
-  const float* A = p.a + z * p.as[0];
-  const float* B = p.b + z * p.bs[0];
-  float* Cp = p.c + z * p.cs[0];
-  float acc[8][8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
-  for (int k0 = 0; k0 < p.k; k0 += BK) {
-    for (int idx = tid; idx < BM * BK; idx += 256) {
-      // A: choose the thread->element map so consecutive threads walk the contiguous dim
-      int r, kk;
-      if (p.as[2] == 1) { r = idx / BK; kk = idx % BK; } else { kk = idx / BM; r = idx % BM; }
-      const int gm = m0 + r, gk = k0 + kk;
-      sA[kk][r] = (gm < p.m && gk < p.k) ? A[gm * p.as[1] + gk * p.as[2]] : 0.f;
-      int cc;
-      if (p.bs[2] == 1) { kk = idx / BN; cc = idx % BN; } else { cc = idx / BK; kk = idx % BK; }
-      const int gn = n0 + cc;
-      const int gk2 = k0 + kk;
-      sB[kk][cc] = (gn < p.n && gk2 < p.k) ? B[gk2 * p.bs[1] + gn * p.bs[2]] : 0.f;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int kk = 0; kk < BK; ++kk) {
-      float a[8], bb[8];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        a[i] = sA[kk][ty * 4 + i];
-        a[4 + i] = sA[kk][64 + ty * 4 + i];
-        bb[i] = sB[kk][tx * 4 + i];
-        bb[4 + i] = sB[kk][64 + tx * 4 + i];
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], bb[j], acc[i][j]);
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int gm = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
-    if (gm >= p.m) continue;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int gn = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4);
-      if (gn < p.n) Cp[gm * p.cs[1] + gn * p.cs[2]] = acc[i][j];
-    }
-  }
-}
-
-const char* bmm_f32_plan(const cmpx_bmm_desc* d, int* status) {
-  *status = CMPX_OK;
-  if (d->dtype != CMPX_F32) {
-    *status = CMPX_ERR_UNSUPPORTED_DTYPE;
-    return "none";
-  }
-  if (d->m > (int64_t)128 * 65535 || d->batch > 65535 || d->n > (1ll << 31) - 256) {
-    *status = CMPX_ERR_UNSUPPORTED_SHAPE;
-    return "none";
-  }
-  return "bmm_f32_simt<128x128x16>";
-}
-
-int launch_bmm_f32(const cmpx_bmm_desc* d, const LaunchCtx& ctx) {
-  int st = CMPX_OK;
-  bmm_f32_plan(d, &st);
-  if (st != CMPX_OK) return st;
-  if (d->m == 0 || d->n == 0 || d->batch == 0) return CMPX_OK;
-  F32BmmParams p;
-  p.a = static_cast<const float*>(d->a);
-  p.b = static_cast<const float*>(d->b);
-  p.c = static_cast<float*>(d->c);
-  for (int i = 0; i < 3; ++i) {
-    p.as[i] = d->a_stride[i];
-    p.bs[i] = d->b_stride[i];
-    p.cs[i] = d->c_stride[i];
-  }
-  p.m = static_cast<int>(d->m);
-  p.n = static_cast<int>(d->n);
-  p.k = static_cast<int>(d->k);
-  dim3 grid(static_cast<unsigned>((d->n + 127) / 128), static_cast<unsigned>((d->m + 127) / 128),
-            static_cast<unsigned>(d->batch));
-  bmm_f32_kernel<<<grid, 256, 0, ctx.stream>>>(p);
-  return cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
-}
-
 }  // namespace cmpx

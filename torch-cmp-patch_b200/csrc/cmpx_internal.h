@@ -66,8 +66,6 @@ int launch_attn_tf32x3(const cmpx_attn_desc* d, const LaunchCtx& ctx);
 const char* bmm_sm100_plan(const cmpx_bmm_desc* d, int* status);
 int launch_bmm_sm100(const cmpx_bmm_desc* d, const LaunchCtx& ctx);
 
-const char* bmm_f32_plan(const cmpx_bmm_desc* d, int* status);
-int launch_bmm_f32(const cmpx_bmm_desc* d, const LaunchCtx& ctx);
 
 // ---- linear (the bmm GEMM with batch 1, W read as a K-major B, bias in the epilogue) ----
 const char* linear_sm100_plan(const cmpx_linear_desc* d, int* status);
