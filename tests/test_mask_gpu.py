@@ -174,3 +174,47 @@ def test_noalloc_declines_masked_calls(cuda_device):
     out = torch.empty_like(qd)
     desc = N._attn_desc(qd, kd, vd, out, 0.125, False, mask=m)
     assert N.lib.cmpx_attn_fwd_noalloc(ctypes.byref(desc), N._stream_handle(cuda_device)) == N.ERR_WORKSPACE
+
+
+@pytest.mark.parametrize("kind", ["bool", "additive"])
+@pytest.mark.parametrize("scale", [-0.2, 0.05, 1.7])
+def test_masks_with_any_scale(cuda_device, kind, scale):
+    # a negative scale flips the order of the scores: masked scores become +inf before scaling
+    q, k, v, g = _qkv(1, 2, 200, 300, 64, torch.bfloat16, seed=int(abs(scale) * 100) + len(kind))
+    if kind == "bool":
+        m = torch.rand(200, 300, generator=g) > 0.3
+    else:
+        m = (torch.randn(200, 300, generator=g) * 2).to(torch.bfloat16)
+        m[:, 250:] = float("-inf")
+    got = cmpext3.ops.attention(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), scale, False,
+                                m.to(cuda_device))
+    torch.cuda.synchronize()
+    with torch.no_grad():
+        ref = F.scaled_dot_product_attention(q.float(), k.float(), v.float(), scale=scale,
+                                             attn_mask=m if kind == "bool" else m.float()).to(q.dtype)
+    check(got, ref, q.dtype, f"{kind} mask scale {scale}")
+
+
+@pytest.mark.parametrize("kind", ["bool", "additive"])
+def test_masks_with_gqa_wide_heads_and_ragged_rows(cuda_device, kind):
+    q, k, v, g = _qkv(2, 6, 333, 517, 192, torch.float16, seed=21, Hkv=3)
+    if kind == "bool":
+        m = torch.rand(2, 1, 333, 517, generator=g) > 0.25
+    else:
+        m = (torch.rand(2, 6, 333, 517, generator=g) * -4).half()
+    got = cmpext3.ops.attention(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), None, True,
+                                m.to(cuda_device))
+    torch.cuda.synchronize()
+    check(got, _ref(q, k, v, m if kind == "bool" else m.float(), True, gqa=True), torch.float16,
+          f"{kind} mask gqa D192")
+
+
+def test_single_query_row_with_masks(cuda_device):
+    q, k, v, g = _qkv(3, 4, 1, 777, 128, torch.bfloat16, seed=31)
+    mb = torch.rand(3, 1, 1, 777, generator=g) > 0.5
+    ma = torch.where(mb, 0.0, float("-inf")).to(torch.bfloat16)
+    for m in (mb, ma):
+        got = cmpext3.ops.attention(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), None, False,
+                                    m.to(cuda_device))
+        torch.cuda.synchronize()
+        check(got, _ref(q, k, v, m if m.dtype == torch.bool else m.float(), False), torch.bfloat16, "Lq=1")
