@@ -46,6 +46,10 @@
 #ifndef CMPX_FMHA_EMU64
 #define CMPX_FMHA_EMU64 0
 #endif
+// Causal launches: work items per CTA in the longest-first tail (0: no such tail).
+#ifndef CMPX_FMHA_LPT
+#define CMPX_FMHA_LPT 2
+#endif
 #ifndef CMPX_FMHA_EMU
 #define CMPX_FMHA_EMU 0
 #endif
@@ -112,6 +116,10 @@ struct FmhaParams {
   int len_k;
   int n_pairs;        // ceil(len_q / 256)
   int n_items;        // n_pairs * heads * batch
+  // Causal launches: items from lpt_first on (the last lpt_heads (b, h) slices) are dealt heaviest
+  // row pair first across those slices, not slice by slice (n_items: no such tail).
+  int lpt_first;
+  int lpt_heads;
   int causal;
   int neg_scale;      // scale < 0: masked scores are +inf so that masked * scale = -inf
   float scale_log2;   // scale * log2(e)
@@ -142,6 +150,23 @@ struct FmhaParams {
   unsigned long long timeout_ns;
   unsigned int* dev_flags;
 };
+
+// Work item -> (b*heads + h, row pair).  Items of one (b, h) slice are consecutive and within a slice
+// the heavy (late, causal) row pairs go first, so the CTAs busy at any moment share a few slices' K/V
+// in L2.  The last lpt_heads slices are dealt heaviest row pair first across all of them instead
+// (longest-processing-time order): dealt slice by slice, the last slice's heaviest pair would start
+// shortly before the work runs out and finish long after every other CTA.
+__device__ __forceinline__ void item_slice_pair(const FmhaParams& p, int item, int& bh, int& pair) {
+  if (item < p.lpt_first) {
+    bh = item / p.n_pairs;
+    pair = p.n_pairs - 1 - (item - bh * p.n_pairs);
+  } else {
+    const int t = item - p.lpt_first;
+    const int r = t / p.lpt_heads;
+    bh = p.lpt_first / p.n_pairs + (t - r * p.lpt_heads);
+    pair = p.n_pairs - 1 - r;
+  }
+}
 
 // Packs a boolean mask (one byte per element, nonzero = the key takes part; element strides sb, sh,
 // sq over the packed extents nb x nh x nq, keys contiguous) to bits: one warp per mask row, one
@@ -320,8 +345,8 @@ __global__ void __launch_bounds__(128) fmha_split_merge_kernel(const __grid_cons
     const int gr = r0 + i;
     if (gr >= n_rows) break;
     const int item = p.n_whole + gr / 256;
-    const int bh = item / p.n_pairs;
-    const int pair = p.n_pairs - 1 - (item - bh * p.n_pairs);
+    int bh, pair;
+    item_slice_pair(p, item, bh, pair);
     const int b = bh / p.heads;
     const int h = bh - b * p.heads;
     const int qrow = pair * 256 + gr % 256;
@@ -353,9 +378,8 @@ __global__ void __launch_bounds__(128) fmha_split_merge_kernel(const __grid_cons
   }
 }
 
-// Work item w (persistent schedule): bh = w / n_pairs, pair = n_pairs - 1 - w % n_pairs.  The items
-// of one (b, h) are consecutive, so the CTAs busy at any moment share a few heads' K/V in L2, and
-// within a head the heavy (late, causal) row pairs go first.  SPLIT: the launch has a tail split;
+// Persistent schedule: CTAs take work items from a counter; item_slice_pair gives each item's (b, h)
+// slice and row pair.  SPLIT: the launch has a tail split;
 // MK: no mask (0), a boolean mask packed to bits (1), an additive 16-bit mask (2) -- separate
 // instantiations, so that plain launches run their code unchanged.
 template <int DP, bool BF16, bool SPLIT, int MK>
@@ -448,8 +472,8 @@ __global__ void __launch_bounds__(352, 1)
       g.part = w - p.n_whole;
       g.item = p.n_whole + g.part / p.split;
     }
-    const int bh = g.item / p.n_pairs;
-    const int pair = p.n_pairs - 1 - (g.item - bh * p.n_pairs);
+    int bh, pair;
+    item_slice_pair(p, g.item, bh, pair);
     g.b = bh / p.heads;
     g.h = bh - g.b * p.heads;
     g.q0 = pair * 256;
@@ -1096,6 +1120,16 @@ int launch_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   p.len_k = static_cast<int>(d->len_k);
   p.n_pairs = static_cast<int>((d->len_q + 255) / 256);
   p.n_items = static_cast<int>(p.n_pairs * d->heads * d->batch);
+  p.lpt_first = p.n_items;
+  p.lpt_heads = 1;
+  if (d->causal && p.n_pairs > 1) {
+    // enough slices that the sorted tail holds CMPX_FMHA_LPT items per CTA
+    const long long slices = d->heads * d->batch;
+    const long long ctas = std::min<long long>(p.n_items, std::max(1, ctx.num_sms));
+    p.lpt_heads = static_cast<int>(std::min<long long>(slices, (CMPX_FMHA_LPT * ctas + p.n_pairs - 1) / p.n_pairs));
+    if (p.lpt_heads > 0) p.lpt_first = static_cast<int>((slices - p.lpt_heads) * p.n_pairs);
+    else p.lpt_heads = 1;
+  }
   p.causal = d->causal ? 1 : 0;
   p.neg_scale = d->scale < 0 ? 1 : 0;
   p.scale_log2 = static_cast<float>(d->scale * 1.4426950408889634);
