@@ -115,6 +115,13 @@ typedef struct cmpx_attn_desc {
  * Each operand has a batch stride and two matrix strides (row, col).  One of the two matrix
  * strides of A and of B must be 1 (row-major or column-major view: a transposed operand is
  * passed as a view, never copied); C must be row-major (col stride 1).
+ * fp32 runs on the tensor cores as 3xTF32 (each operand split into a TF32 hi part and an fp32
+ * remainder; a*b ~ a_hi*b_hi + a_hi*b_lo + a_lo*b_hi with fp32 accumulation), and needs K-major
+ * operands: A contiguous along k (a_stride[2] == 1), B contiguous along k (b_stride[1] == 1), every
+ * stride that is stepped a multiple of 4 elements and every pointer 16-byte aligned; other fp32
+ * layouts return CMPX_ERR_MISALIGNED (copy B to a column-major view first).  fp32 takes k <= 8192
+ * (CMPX_ERR_UNSUPPORTED_SHAPE beyond): the tensor core's fp32 accumulation error grows with k
+ * (2e-5 of the output's peak at k = 8192, 9e-5 at 32768).
  * Replaces: custom_bmm_forward (src/main.cpp:363-441) and its per-batch host loop over
  * launch_matmul_fp32 (src/cuda/fp32_matmul.cu:236-265) / launch_matmul_fp16
  * (src/cuda/fp16_matmul.cu:373-427). */
@@ -166,10 +173,11 @@ CMPX_API int cmpx_bmm(const cmpx_bmm_desc* desc, void* stream);
 
 /* Linear layer  y = x W^T (+ bias):  x [m, k], W [n, k] (the nn.Linear weight, read in place as the
  * K-major operand of the same GEMM as cmpx_bmm), bias [n] or NULL, y [m, n]; rows of x, W and y are
- * *_row_stride elements apart, columns contiguous.  fp16 / bf16 only (fp32 returns
- * CMPX_ERR_UNSUPPORTED_DTYPE); the bias is added to the fp32 accumulator before the one rounding
- * to the output type.  Rows must start on 16-byte boundaries (k, n and the strides multiples of 8)
- * and the bias pointer must be 16-byte aligned.
+ * *_row_stride elements apart, columns contiguous.  fp16 / bf16: the bias is added to the fp32
+ * accumulator before the one rounding to the output type; rows must start on 16-byte boundaries
+ * (k, n and the strides multiples of 8) and the bias pointer must be 16-byte aligned.  fp32: the
+ * 3xTF32 GEMM of cmpx_bmm, fp32 bias (4-byte aligned) added to the accumulator; k, n and the
+ * strides multiples of 4.
  * Replaces: custom_linear_forward (src/main.cpp:195-346: bf16 converted to fp32 copies, W
  * transposed into a contiguous copy, an fp32 / fp16-accumulating GEMM, then a separate bias-add
  * kernel in the output type) behind cmpext3.ops.linear (the reference's _C.linear). */

@@ -165,8 +165,32 @@ def test_bmm_plan_for_the_einsum_attention_shapes():
     assert st == 0 and "128x128" in name and "B:k-major" in name
     st, name = _bplan(_bmm(64, 2048, 64, 2048, bt=False))    # values: B = V (N-major)
     assert st == 0 and "128x64" in name and "B:mn-major" in name
-    # fp32 bmm: not in the tile table (cuBLAS's fp32 GEMM is faster than a CUDA-core kernel on B200)
-    assert _bplan(_bmm(2, 33, 45, 17, dtype=0))[0] == N.ERR_UNSUPPORTED_DTYPE
+
+    # fp32: the 3xTF32 GEMM, which reads K-major operands only
+    st, name = _bplan(_bmm(64, 2048, 2048, 64, dtype=0, bt=True))
+    assert st == 0 and name.startswith("bmm_x3tf32_sm100<f32,128x128x32"), name
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(bt=False), "ERR_MISALIGNED"),        # B contiguous along n (MN-major): the binding copies it
+    (dict(k=30), "ERR_MISALIGNED"),            # 120-byte A rows
+    (dict(n=30), "ERR_MISALIGNED"),            # 120-byte C rows
+    (dict(ptr=0x10004), "ERR_MISALIGNED"),     # 4-byte aligned pointers
+    (dict(k=0), "ERR_UNSUPPORTED_SHAPE"),
+    (dict(k=8196), "ERR_UNSUPPORTED_SHAPE"),   # past K = 8192 the fp32 accumulation drifts: stock
+])
+def test_fp32_bmm_plan_rejects(kw, status):
+    args = dict(nb=2, m=256, n=256, k=64, dtype=0, bt=True)
+    args.update(kw)
+    assert _bplan(_bmm(**args))[0] == getattr(N, status)
+
+
+def test_fp32_bmm_plan_single_rows_need_no_aligned_row_stride():
+    # one batch item, m = 1 and n = 1: no stride is ever stepped
+    st, name = _bplan(_bmm(1, 1, 1, 64, dtype=0, bt=True))
+    assert st == 0 and name.startswith("bmm_x3tf32"), name
+    # four items of a 1 x 1 output are 4 bytes apart: not a TMA stride
+    assert _bplan(_bmm(4, 1, 1, 64, dtype=0, bt=True))[0] == N.ERR_MISALIGNED
 
 
 @pytest.mark.parametrize("shape,width", [((8, 4096, 4096, 4096), "128x256"), ((1, 300, 520, 600), "128x256"),
@@ -201,10 +225,11 @@ def test_linear_plan_reads_the_weight_as_a_k_major_operand():
     assert st == 0 and "128x256" in name and "A:k-major,B:k-major" in name, name
     st, name = _lplan(_linear(m=100, n=64, k=128, dtype=1, bias=False))
     assert st == 0 and name.startswith("bmm_sm100<f16,128x64"), name
+    st, name = _lplan(_linear(m=300, n=100, k=36, dtype=0))  # fp32: 16-byte rows at k, n % 4 == 0
+    assert st == 0 and name.startswith("bmm_x3tf32_sm100"), name
 
 
 @pytest.mark.parametrize("kw,status", [
-    (dict(dtype=0), "ERR_UNSUPPORTED_DTYPE"),          # fp32 linear stays stock
     (dict(k=100), "ERR_MISALIGNED"),                   # 200-byte rows
     (dict(n=36), "ERR_MISALIGNED"),                    # 72-byte output rows
     (dict(ldx=100), "ERR_INVALID_ARGUMENT"),           # row stride shorter than a row

@@ -24,11 +24,6 @@ def test_linear_matches_reference_golden(cuda_device, i):
     name, dtn, shape, n, has_bias = C.LINEAR_CASES[i]
     x, w, b = C.linear_inputs(i)
     gold = load()[f"linear/{name}/y"]
-    if x.dtype == torch.float32:
-        # fp32 linear is not in the tile table: the op declines, the patched F.linear serves it stock
-        with pytest.raises(RuntimeError):
-            cmpext3.ops.linear(x.to(cuda_device), w.to(cuda_device), b.to(cuda_device))
-        return
     got = cmpext3.ops.linear(x.to(cuda_device), w.to(cuda_device), None if b is None else b.to(cuda_device))
     torch.cuda.synchronize()
     assert got.shape == x.shape[:-1] + (n,) and got.dtype == x.dtype
@@ -46,7 +41,7 @@ SHAPES = [
 ]
 
 
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32], ids=["bf16", "f16", "f32"])
 @pytest.mark.parametrize("bias", [False, True], ids=["nobias", "bias"])
 @pytest.mark.parametrize("shape", SHAPES, ids=[f"{'x'.join(map(str, s[0]))}->{s[1]}" for s in SHAPES])
 def test_linear_sweep(cuda_device, dtype, bias, shape):

@@ -56,11 +56,11 @@ def _golden_tensor(key) -> torch.Tensor:
     return x if isinstance(x, torch.Tensor) else torch.from_numpy(x)
 
 
-# fp32 calls outside the 3xTF32 kernel's table (head dim above 64) and fp32 bmm are declined: on
-# B200 stock torch serves them faster than a CUDA-core fp32 kernel would.  The op raises; the
-# patched torch op returns stock's (the golden) answer.
-def _declined(dtn, D=None):
-    return dtn == "float32" and (D is None or D > 64)
+# fp32 attention outside the 3xTF32 kernel's table (head dim above 64) is declined: on B200 stock
+# torch serves it faster than a CUDA-core fp32 kernel would.  The op raises; the patched torch op
+# returns stock's (the golden) answer.  (fp32 bmm runs on the 3xTF32 GEMM.)
+def _declined(dtn, D):
+    return dtn == "float32" and D > 64
 
 
 @pytest.mark.parametrize("i", range(len(C.SDPA_CASES)), ids=[c[0] for c in C.SDPA_CASES])
@@ -87,13 +87,7 @@ def test_attention_matches_reference_golden(cuda_device, patched, i):
 def test_bmm_matches_reference_golden(cuda_device, patched, i):
     name, dtn = C.BMM_CASES[i][:2]
     a, b = C.bmm_inputs(i)
-    if _declined(dtn):
-        with pytest.raises(RuntimeError):
-            cmpext3.ops.bmm(a.to(cuda_device), b.to(cuda_device))
-        with torch.no_grad():
-            got = torch.bmm(a.to(cuda_device), b.to(cuda_device))
-    else:
-        got = cmpext3.ops.bmm(a.to(cuda_device), b.to(cuda_device))
+    got = cmpext3.ops.bmm(a.to(cuda_device), b.to(cuda_device))
     torch.cuda.synchronize()
     assert got.dtype == a.dtype
     check(got, _golden_tensor(f"bmm/{name}/c"), a.dtype, name, attention=False)
@@ -268,9 +262,9 @@ def test_bmm_sweep(cuda_device, dtype, shape, bt):
     a = torch.randn(nb, m, k, generator=g).to(dtype)
     b = (torch.randn(nb, n, k, generator=g).to(dtype).transpose(1, 2) if bt
          else torch.randn(nb, k, n, generator=g).to(dtype))
-    # 16-bit operands are read by TMA: rows of A, B and C must be 16-byte multiples (k, n % 8);
-    # fp32 bmm is declined (cuBLAS serves it)
-    native_ok = dtype != torch.float32 and k % 8 == 0 and n % 8 == 0
+    # 16-bit operands are read by TMA in place: rows of A, B and C must be 16-byte multiples
+    # (k, n % 8); fp32 operands are copied to padded K-major buffers where they are not
+    native_ok = dtype == torch.float32 or (k % 8 == 0 and n % 8 == 0)
     if not native_ok:
         with pytest.raises(RuntimeError):
             cmpext3.ops.bmm(a.to(cuda_device), b.to(cuda_device))

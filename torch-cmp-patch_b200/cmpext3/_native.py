@@ -361,14 +361,39 @@ def _check_bmm_args(a, b) -> None:
         raise RuntimeError("Contracting dimension (K) mismatch")
 
 
+def _kmajor_f32(t: torch.Tensor) -> torch.Tensor:
+    """A [batch, r, k] fp32 operand as the 3xTF32 GEMM reads it: contiguous along k, rows and batch
+    items on 16-byte boundaries.  Returned as is when it already is; otherwise copied into a buffer
+    whose rows are padded to a multiple of 4 elements (the padding is never read)."""
+    nb, r, k = t.shape
+    s0, s1, s2 = t.stride()
+    if (t.data_ptr() % 16 == 0 and s2 == 1 and (r == 1 or (s1 > 0 and s1 % 4 == 0))
+            and (nb == 1 or (s0 > 0 and s0 % 4 == 0))):
+        return t
+    buf = torch.empty((nb, r, (k + 3) // 4 * 4), dtype=t.dtype, device=t.device)
+    buf[..., :k].copy_(t)
+    return buf[..., :k]
+
+
+def _out_rows(nb: int, m: int, n: int, dtype, device) -> torch.Tensor:
+    """The [nb, m, n] output; for fp32, rows padded to 16 bytes when n is not a multiple of 4 and a
+    row or batch stride is stepped (the caller returns a contiguous copy of the view)."""
+    if dtype != torch.float32 or n % 4 == 0 or (m <= 1 and nb <= 1):
+        return torch.empty((nb, m, n), dtype=dtype, device=device)
+    return torch.empty((nb, m, (n + 3) // 4 * 4), dtype=dtype, device=device)[..., :n]
+
+
 def _prepare_bmm(a, b):
     _check_bmm_args(a, b)
     if a.dtype != torch.float32:
         a = a if _mat_ok(a) else a.contiguous()
         b = b if _mat_ok(b) else b.contiguous()
+    else:  # K-major A and B (B as the transpose of a k-contiguous [batch, n, k] buffer)
+        a = _kmajor_f32(a)
+        b = _kmajor_f32(b.transpose(1, 2)).transpose(1, 2)
     nb, m, _ = a.shape
     n = b.shape[2]
-    c = torch.empty((nb, m, n), dtype=a.dtype, device=a.device)
+    c = _out_rows(nb, m, n, a.dtype, a.device)
     return a, b, c
 
 
@@ -398,7 +423,7 @@ def bmm(input, mat2):
     if st != OK:
         raise CmpxError("bmm", st)
     _post_check()
-    return c
+    return c if c.is_contiguous() else c.contiguous()
 
 
 def bmm_plan(input, mat2) -> str:
@@ -438,8 +463,8 @@ def _prepare_linear(input, weight, bias):
     n, k = weight.shape
     if input.shape[-1] != k:
         raise RuntimeError("Input shape mismatch with Weight")
-    if input.dtype not in (torch.float16, torch.bfloat16) or weight.dtype != input.dtype:
-        raise RuntimeError("linear: input/weight must share one dtype among float16/bfloat16")
+    if input.dtype not in _DTYPE or weight.dtype != input.dtype:
+        raise RuntimeError("linear: input/weight must share one dtype among float32/float16/bfloat16")
     if bias is not None:
         if not isinstance(bias, torch.Tensor) or bias.dim() != 1 or bias.shape[0] != n:
             raise RuntimeError("Bias must be 1D of size out_features")
@@ -449,6 +474,11 @@ def _prepare_linear(input, weight, bias):
         if bias.data_ptr() % 16 != 0:
             bias = bias.clone()
     x = input.reshape(-1, k)
+    if input.dtype == torch.float32:  # rows padded to 16 bytes where needed (3xTF32 GEMM)
+        x = _kmajor_f32(x.unsqueeze(0))[0]
+        w = _kmajor_f32(weight.unsqueeze(0))[0]
+        y = _out_rows(1, x.shape[0], n, input.dtype, input.device)[0]
+        return x, w, bias, y
     x = x if _rows_ok(x) else x.contiguous()
     w = weight if _rows_ok(weight) else weight.contiguous()
     y = torch.empty((x.shape[0], n), dtype=input.dtype, device=input.device)
@@ -467,9 +497,9 @@ def linear(input, weight, bias=None):
     x, w, b, y = _prepare_linear(input, weight, bias)
     out_shape = tuple(input.shape[:-1]) + (w.shape[0],)
     if y.numel() == 0:
-        return y.view(out_shape)
+        return y.contiguous().view(out_shape)
     if w.shape[1] == 0:
-        return (y.zero_() if b is None else y.copy_(b.expand_as(y))).view(out_shape)
+        return (y.zero_() if b is None else y.copy_(b.expand_as(y))).contiguous().view(out_shape)
     desc = _linear_desc(x, w, b, y)
     dev = x.device
     if dev.index == torch.cuda.current_device():
@@ -480,7 +510,7 @@ def linear(input, weight, bias=None):
     if st != OK:
         raise CmpxError("linear", st)
     _post_check()
-    return y.view(out_shape)
+    return (y if y.is_contiguous() else y.contiguous()).view(out_shape)
 
 
 def linear_plan(input, weight, bias=None) -> str:

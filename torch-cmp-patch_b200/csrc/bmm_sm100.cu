@@ -494,6 +494,8 @@ int launch_bmm_dt(const cmpx_bmm_desc* d, const LaunchCtx& ctx, int am, int bm, 
   return launch_bmm_bn<64, BF16>(d, ctx, am, bm, bias);
 }
 
+}  // namespace
+
 // The GEMM a linear layer is: x [m, k] (rows ld_x apart) times W^T, W [n, k] (rows ld_w apart) --
 // a K-major B operand read in place -- into y [m, n].
 cmpx_bmm_desc linear_as_bmm(const cmpx_linear_desc* d) {
@@ -517,8 +519,6 @@ cmpx_bmm_desc linear_as_bmm(const cmpx_linear_desc* d) {
   b.dtype = d->dtype;
   return b;
 }
-
-}  // namespace
 
 int launch_bmm_sm100(const cmpx_bmm_desc* d, const LaunchCtx& ctx) {
   int st = CMPX_OK;

@@ -141,9 +141,8 @@ const char* bmm_plan_impl(const cmpx_bmm_desc* d, int* st) {
     *st = CMPX_ERR_INVALID_ARGUMENT;
     return "none";
   }
-  // fp32 bmm is not in the tile table: cuBLAS's fp32 GEMM is 2.5-3.5x a CUDA-core fp32 kernel on
-  // B200, so the binding's callers serve it from stock (the reference's runtime selection would).
   if (d->dtype == CMPX_F16 || d->dtype == CMPX_BF16) return bmm_sm100_plan(d, st);
+  if (d->dtype == CMPX_F32) return bmm_x3_plan(d, st);
   *st = CMPX_ERR_UNSUPPORTED_DTYPE;
   return "none";
 }
@@ -154,6 +153,7 @@ const char* linear_plan_impl(const cmpx_linear_desc* d, int* st) {
     return "none";
   }
   if (d->dtype == CMPX_F16 || d->dtype == CMPX_BF16) return linear_sm100_plan(d, st);
+  if (d->dtype == CMPX_F32) return linear_x3_plan(d, st);
   *st = CMPX_ERR_UNSUPPORTED_DTYPE;
   return "none";
 }
@@ -280,6 +280,7 @@ int cmpx_linear(const cmpx_linear_desc* desc, void* stream) {
   LaunchCtx ctx;
   st = device_ctx(&ctx, static_cast<cudaStream_t>(stream));
   if (st != CMPX_OK) return st;
+  if (desc->dtype == CMPX_F32) return launch_linear_x3(desc, ctx);
   return launch_linear_sm100(desc, ctx);
 }
 
@@ -307,6 +308,7 @@ int cmpx_bmm(const cmpx_bmm_desc* desc, void* stream) {
   LaunchCtx ctx;
   st = device_ctx(&ctx, static_cast<cudaStream_t>(stream));
   if (st != CMPX_OK) return st;
+  if (desc->dtype == CMPX_F32) return launch_bmm_x3(desc, ctx);
   return launch_bmm_sm100(desc, ctx);
 }
 

@@ -65,11 +65,18 @@ int launch_attn_tf32x3(const cmpx_attn_desc* d, const LaunchCtx& ctx);
 // ---- batched matmul ----
 const char* bmm_sm100_plan(const cmpx_bmm_desc* d, int* status);
 int launch_bmm_sm100(const cmpx_bmm_desc* d, const LaunchCtx& ctx);
+// fp32 on the tensor cores (3xTF32), K-major operands.
+const char* bmm_x3_plan(const cmpx_bmm_desc* d, int* status);
+int launch_bmm_x3(const cmpx_bmm_desc* d, const LaunchCtx& ctx);
+// The GEMM of a linear layer: x [m, k] times W^T with W [n, k] read in place as a K-major B.
+cmpx_bmm_desc linear_as_bmm(const cmpx_linear_desc* d);
 
 
 // ---- linear (the bmm GEMM with batch 1, W read as a K-major B, bias in the epilogue) ----
 const char* linear_sm100_plan(const cmpx_linear_desc* d, int* status);
 int launch_linear_sm100(const cmpx_linear_desc* d, const LaunchCtx& ctx);
+const char* linear_x3_plan(const cmpx_linear_desc* d, int* status);
+int launch_linear_x3(const cmpx_linear_desc* d, const LaunchCtx& ctx);
 
 // ---- row softmax (einsum-attention chain) ----
 const char* softmax_rows_plan(const cmpx_softmax_desc* d, int* status);
