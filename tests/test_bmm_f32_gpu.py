@@ -117,6 +117,7 @@ def test_fp32_einsum_attention_chain_runs_native(cuda_device, patched):
     g = torch.Generator().manual_seed(6)
     q, k, v = (torch.randn(2, 4, 256, 64, generator=g) for _ in range(3))
     qd, kd, vd = q.to(cuda_device), k.to(cuda_device), v.to(cuda_device)
+    cmpext3.autoselect.reset()
     with torch.no_grad():
         s = torch.einsum("bhid,bhjd->bhij", qd, kd)
         p = torch.softmax(s, dim=-1)
@@ -133,6 +134,7 @@ def test_fp32_einsum_attention_chain_runs_native(cuda_device, patched):
 def test_fp32_matmul_2d_runs_native(cuda_device, patched):
     g = torch.Generator().manual_seed(7)
     a, b = torch.randn(300, 520, generator=g), torch.randn(520, 260, generator=g)
+    cmpext3.autoselect.reset()
     with torch.no_grad():
         got = torch.matmul(a.to(cuda_device), b.to(cuda_device))
     torch.cuda.synchronize()
@@ -163,6 +165,7 @@ def test_fp32_nn_linear_through_the_patched_f_linear(cuda_device, patched):
     torch.manual_seed(0)
     layer = torch.nn.Linear(640, 1280).to(cuda_device)
     x = torch.randn(2, 1024, 640, device=cuda_device)
+    cmpext3.autoselect.reset()
     with torch.no_grad():
         got = layer(x)
     torch.cuda.synchronize()
