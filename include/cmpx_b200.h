@@ -74,17 +74,19 @@ typedef enum cmpx_status {
  * iff j <= i), which is what torch's is_causal does for len_q != len_k.
  * Grouped-query attention: k and v may have heads_kv heads (a divisor of heads); query head h then
  * reads key/value head h / (heads / heads_kv), as torch's enable_gqa=True does.
- * Attention mask (16-bit calls), torch's attn_mask, broadcastable: mask_stride holds element strides
+ * Attention mask, torch's attn_mask, broadcastable: mask_stride holds element strides
  * over batch, head, query row and key, 0 for a broadcast dimension; the key stride must be 1.
  *  - mask_kind CMPX_MASK_BOOL: one byte per element; key j takes part in query i's softmax only where
- *    mask[b, h, i, j] is nonzero.  The call packs it to bits in the workspace
- *    (cmpx_attn_workspace_size counts that), so a masked call needs the full workspace.
- *  - mask_kind CMPX_MASK_ADD: values in the call's 16-bit type added to the scaled scores
+ *    mask[b, h, i, j] is nonzero.  A 16-bit call packs it to bits in the workspace
+ *    (cmpx_attn_workspace_size counts that), so a masked 16-bit call needs the full workspace.
+ *  - mask_kind CMPX_MASK_ADD: values in the call's dtype added to the scaled scores
  *    (softmax(q k^T * scale + mask)); -inf removes a key.  Rows must start on 16-byte boundaries
- *    (the query-row stride a multiple of 8, or 0).
+ *    (the query-row stride a multiple of 8 elements for 16-bit calls, 4 for fp32, or 0).
+ *  - fp32 calls read the mask in place (no workspace): its pointer 16-byte aligned and every
+ *    stride a multiple of 16 bytes (boolean: 16 elements; additive: 4), else
+ *    CMPX_ERR_UNSUPPORTED_SHAPE.
  * With causal the mask applies on top of it (torch's math path ANDs them).  A query row with no key
- * left gets an all-zero output (torch's result), not NaN.  fp32 calls with a mask return
- * CMPX_ERR_UNSUPPORTED_SHAPE.
+ * left gets an all-zero output (torch's result), not NaN.
  * Replaces: custom_attention_forward (src/main.cpp:1603-1774) and its launchers
  * launch_flash_attention_hfma2 (src/cuda/fp16_flash_attention_hfma2.cu:269-286),
  * launch_attention_fp16 (src/cuda/fp16_attention.cu:328-386),

@@ -311,8 +311,17 @@ def test_mask_plans_on_the_16bit_kernel_only():
     d = _with_mask(_attn(Lq=64, Lk=77, dtype=2), (0, 0, 77, 1))
     st, name = _plan(d)
     assert st == 0 and name.startswith("fmha_sm100<bf16") and name.endswith("+mask>"), name
-    d = _with_mask(_attn(Lq=64, Lk=77, dtype=0), (0, 0, 77, 1))
-    assert _plan(d)[0] == N.ERR_UNSUPPORTED_SHAPE   # fp32 with a mask: stock
+    # fp32 reads the mask in place with 16-byte loads: rows 16-byte aligned, else stock
+    d = _with_mask(_attn(Lq=64, Lk=77, D=40, dtype=0), (0, 0, 80, 1))
+    st, name = _plan(d)
+    assert st == 0 and name.startswith("attn_tf32x3_sm100") and name.endswith("+mask>"), name
+    d = _with_mask(_attn(Lq=64, Lk=77, D=40, dtype=0), (0, 0, 77, 1))
+    assert _plan(d)[0] == N.ERR_UNSUPPORTED_SHAPE
+    d = _with_mask(_attn(Lq=64, Lk=77, D=40, dtype=0), (0, 0, 80, 1))
+    d.mask_kind = 1
+    st, name = _plan(d)
+    assert st == 0 and name.endswith("+addmask>"), name
+    assert N.lib.cmpx_attn_workspace_size(ctypes.byref(d)) == 0   # no packing for fp32
 
 
 def test_workspace_contract():

@@ -1,4 +1,4 @@
-"""attn_mask on the 16-bit attention kernel -- boolean (packed to bits in the workspace) and additive
+"""attn_mask on the attention kernels -- boolean (packed to bits in the workspace for 16-bit calls) and additive
 in the query's dtype (added to the scores in the softmax) -- against the reference's CPU path -- stock torch SDPA with the same mask on CPU tensors
 (needs a B200; marked gpu).  The reference itself sent every masked call to stock; these are the
 mask shapes models pass: key padding [B,1,1,Lk], a shared [Lq,Lk] pattern, per-head [B,H,Lq,Lk],
@@ -218,3 +218,87 @@ def test_single_query_row_with_masks(cuda_device):
                                     m.to(cuda_device))
         torch.cuda.synchronize()
         check(got, _ref(q, k, v, m if m.dtype == torch.bool else m.float(), False), torch.bfloat16, "Lq=1")
+
+
+# ------------------------------------------------------------------ fp32 calls (3xTF32 kernel)
+# The fp32 kernel reads the mask in place (bytes or fp32 values, 16-byte aligned rows -- the
+# binding pads rows that are not) instead of packing it; the contract is fp32's 1e-4.
+
+@pytest.mark.parametrize("kind", MASK_SHAPES)
+@pytest.mark.parametrize("D", [40, 64])
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+@pytest.mark.parametrize("lens", [(77, 77), (300, 1000), (513, 384), (1, 200)], ids=str)
+def test_fp32_boolean_mask_sweep(cuda_device, kind, D, causal, lens):
+    lq, lk = lens
+    q, k, v, g = _qkv(2, 3, lq, lk, D, torch.float32, seed=lq + 7 * lk + D + causal)
+    m = _mask(kind, 2, 3, lq, lk, g)
+    plan = N.attention_plan(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), None, causal,
+                            m.to(cuda_device))
+    assert plan.startswith("attn_tf32x3_sm100") and plan.endswith("+mask>"), plan
+    _run(cuda_device, q, k, v, m, causal, f"fp32 {kind} D{D} {lens} causal={causal}")
+
+
+@pytest.mark.parametrize("kind", ["padding", "alibi", "random"])
+@pytest.mark.parametrize("D", [40, 64])
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+@pytest.mark.parametrize("lens", [(77, 77), (300, 1000), (1, 200)], ids=str)
+def test_fp32_additive_mask_sweep(cuda_device, kind, D, causal, lens):
+    lq, lk = lens
+    q, k, v, g = _qkv(2, 3, lq, lk, D, torch.float32, seed=lq + 5 * lk + D + causal)
+    m = _additive(kind, 2, 3, lq, lk, torch.float32, g)
+    qd, kd, vd, md = (t.to(cuda_device) for t in (q, k, v, m))
+    assert N.attention_plan(qd, kd, vd, None, causal, md).endswith("+addmask>")
+    got = cmpext3.ops.attention(qd, kd, vd, None, causal, md)
+    torch.cuda.synchronize()
+    assert torch.isfinite(got).all()
+    check(got, _ref(q, k, v, m, causal), torch.float32, f"fp32 additive {kind} D{D} {lens} causal={causal}")
+    assert N.device_status() == 0
+
+
+def test_fp32_rows_with_no_key_output_zero(cuda_device):
+    q, k, v, g = _qkv(1, 2, 300, 400, 64, torch.float32, seed=4)
+    m = torch.rand(300, 400, generator=g) > 0.5
+    m[7] = False          # row 7: nothing in any key tile
+    m[200, :] = False
+    m[200, 399] = True    # row 200: only the very last key
+    m[255, :128] = False  # row 255: nothing in the first two key tiles, keys later
+    got = _run(cuda_device, q, k, v, m, False, "fp32 empty rows")
+    assert torch.equal(got[:, :, 7].cpu(), torch.zeros(1, 2, 64))
+    add = torch.randn(300, 400, generator=g)
+    add[9] = float("-inf")
+    add[10, :300] = float("-inf")
+    qd, kd, vd = (t.to(cuda_device) for t in (q, k, v))
+    got = cmpext3.ops.attention(qd, kd, vd, None, False, add.to(cuda_device))
+    torch.cuda.synchronize()
+    assert torch.equal(got[:, :, 9].cpu(), torch.zeros(1, 2, 64))
+    check(got, _ref(q, k, v, add, False), torch.float32, "fp32 additive -inf rows")
+
+
+@pytest.mark.parametrize("kind", ["bool", "additive"])
+@pytest.mark.parametrize("scale", [-0.2, 0.05, 1.7])
+def test_fp32_masks_with_any_scale_and_gqa(cuda_device, kind, scale):
+    q, k, v, g = _qkv(2, 4, 150, 170, 40, torch.float32, seed=int(scale * 100) + 3, Hkv=2)
+    m = (torch.rand(2, 4, 150, 170, generator=g) > 0.4) if kind == "bool" else torch.randn(1, 4, 150, 170, generator=g)
+    got = cmpext3.ops.attention(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), scale, False,
+                                m.to(cuda_device))
+    torch.cuda.synchronize()
+    with torch.no_grad():
+        ref = F.scaled_dot_product_attention(q, k, v, attn_mask=m, scale=scale, enable_gqa=True)
+    check(got, ref, torch.float32, f"fp32 {kind} scale {scale}")
+
+
+def test_fp32_patched_sdpa_masks_native(cuda_device, patched):
+    q, k, v, g = _qkv(1, 4, 256, 300, 40, torch.float32, seed=12)
+    qd, kd, vd = (t.to(cuda_device) for t in (q, k, v))
+    m = torch.rand(256, 300, generator=g) > 0.5
+    add = torch.randn(1, 1, 256, 300, generator=g)
+    cmpext3.autoselect.reset()
+    with torch.no_grad():
+        got = F.scaled_dot_product_attention(qd, kd, vd, attn_mask=m.to(cuda_device))
+        got_add = F.scaled_dot_product_attention(qd, kd, vd, attn_mask=add.to(cuda_device))
+    torch.cuda.synchronize()
+    check(got, _ref(q, k, v, m, False), torch.float32, "fp32 patched sdpa mask")
+    check(got_add, _ref(q, k, v, add, False), torch.float32, "fp32 patched sdpa additive mask")
+    entries = [d.entry for d in cmpext3.autoselect.report() if d.use_native]
+    assert any("attn_tf32x3" in (e or "") and (e or "").endswith("+mask>") for e in entries), cmpext3.autoselect_report()
+    assert any("attn_tf32x3" in (e or "") and (e or "").endswith("+addmask>") for e in entries), cmpext3.autoselect_report()

@@ -442,12 +442,21 @@ class TestScaledDotProductAttention:
         F.scaled_dot_product_attention(q, k, v, scale=0.25)
         assert_called_once_with_tensors(native.attention, q, k, v, 0.25, False)
 
-    def test_falls_back_when_float_attn_mask_given(self, patched, native, monkeypatch):
-        # additive masks stay stock (the reference sent every masked call to stock)
+    def test_falls_back_when_float_attn_mask_of_another_dtype_given(self, patched, native, monkeypatch):
+        # an additive mask runs natively only in the query's dtype; others stay stock (the
+        # reference sent every masked call to stock)
+        force_eligible(monkeypatch)
+        q, k, v = (t.to(torch.bfloat16) for t in self._qkv(1, 2, 3, 4))
+        F.scaled_dot_product_attention(q, k, v, attn_mask=torch.zeros(3, 3))  # fp32 mask, bf16 query
+        native.attention.assert_not_called()
+
+    def test_additive_attn_mask_in_the_query_dtype_runs_native(self, patched, native, monkeypatch):
         force_eligible(monkeypatch)
         q, k, v = self._qkv(1, 2, 3, 4)
-        F.scaled_dot_product_attention(q, k, v, attn_mask=torch.zeros(3, 3))
-        native.attention.assert_not_called()
+        m = torch.zeros(3, 3)
+        native.attention.return_value = torch.zeros(1, 2, 3, 4)
+        F.scaled_dot_product_attention(q, k, v, attn_mask=m)
+        assert native.attention.call_args[0][5] is m
 
     def test_boolean_attn_mask_runs_native(self, patched, native, monkeypatch):
         force_eligible(monkeypatch)

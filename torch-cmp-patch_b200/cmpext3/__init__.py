@@ -8,7 +8,7 @@ auto-run at :822-823 of the reference):
     torch.bmm                       -> cmpext3.ops.bmm(input, mat2)
     torch.matmul (2D / 3D)          -> cmpext3.ops.bmm
     torch.einsum                    -> einsum_ops planner -> torch.bmm (patched)
-    F.linear (so nn.Linear)         -> cmpext3.ops.linear(input, weight, bias)  (fp16 / bf16)
+    F.linear (so nn.Linear)         -> cmpext3.ops.linear(input, weight, bias)
 
 and, beyond the reference, the middle step of an einsum / bmm attention chain
 (``einsum('bhid,bhjd->bhij') -> softmax(-1) -> einsum('bhij,bhjd->bhid')``):
@@ -20,7 +20,7 @@ and, beyond the reference, the middle step of an einsum / bmm attention chain
 
 with the reference's wrapper signatures, gates and stock bail-outs: stock PyTorch runs when autograd
 is live for an input, when a tensor is not a CUDA fp16/fp32/bf16 tensor, when SDPA gets an
-``attn_mask`` that is neither boolean nor in the query's 16-bit dtype, ``dropout_p > 0`` or a non-4D
+``attn_mask`` that is neither boolean nor in the query's dtype, ``dropout_p > 0`` or a non-4D
 query (masks run natively beyond the reference, which sent every masked call to stock), when bmm/matmul get ``out=`` or mixed dtypes, and
 whenever the native op raises ``RuntimeError``/``TypeError`` for an argument outside its tile table.
 
@@ -29,7 +29,7 @@ What changed underneath: the kernels are tcgen05/TMA/TMEM kernels for B200 in a 
 and to fp32 for bmm), and the runtime native-versus-stock race is replaced by a fixed tile table
 (see cmpext3.autoselect).  The rest of the reference (conv, norms, activations, TensorRT, NVML
 clock/power changes) is not part of this package; in particular nothing here changes GPU clocks or
-power limits.  fp32 linear stays stock here (the reference ran it on its own CUDA-core kernel).
+power limits.  fp32 bmm / matmul / einsum / linear run on a 3xTF32 tensor-core GEMM (k <= 8192).
 
     import cmpext3            # patches on import
     cmpext3.disable(); cmpext3.enable()
@@ -163,7 +163,8 @@ def _dispatch(op: str, ref: torch.Tensor, key: tuple, native_call: Callable,
 def _patched_linear(input, weight, bias=None):
     """F.linear with the reference's gates (__init__.py:410-420): stock under live autograd, for
     non-CUDA / unsupported dtypes, for input.dim() < 2 or a non-2-D weight, for fp16 with an odd
-    out_features; the native op raising (fp32, misaligned rows) also serves the call from stock."""
+    out_features; the native op raising (misaligned 16-bit rows, fp32 k > 8192) also serves the call
+    from stock."""
     orig = _ORIGINALS[(F, "linear")]
     if not (_grad_safe(input, weight, bias) and _usable(input, weight)):
         return orig(input, weight, bias)
@@ -313,11 +314,10 @@ def _patched_sdpa(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=Fa
                   scale=None, **kwargs):
     orig = _ORIGINALS[(F, "scaled_dot_product_attention")]
     # Gates as in the reference (__init__.py:609-633), except that an attn_mask on the query's device
-    # runs natively too -- boolean, or additive in the query's 16-bit dtype; other masks stay stock.
+    # runs natively too -- boolean, or additive in the query's dtype; other masks stay stock.
     mask_ok = attn_mask is None or (
         isinstance(attn_mask, torch.Tensor) and attn_mask.device == query.device
-        and (attn_mask.dtype == torch.bool
-             or (attn_mask.dtype == query.dtype and query.dtype in (torch.float16, torch.bfloat16))))
+        and attn_mask.dtype in (torch.bool, query.dtype))
     if (not mask_ok or dropout_p != 0.0
             or query.dim() != 4 or not _grad_safe(query, key, value)
             or not _usable(query, key, value)):

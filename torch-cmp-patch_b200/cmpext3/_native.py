@@ -196,16 +196,17 @@ def _attn_desc(q, k, v, o, scale: float, causal: bool, workspace=None, mask=None
 
 def _prepare_mask(attn_mask, query, key):
     """attn_mask broadcast to [B, H, Lq, Lk] as a strided view (0 along broadcast dims, the key
-    dimension contiguous), or None.  Boolean masks (any layout), and additive masks in the query's
-    16-bit dtype (rows padded to 16-byte boundaries when they are not) are in the tile table; an
-    additive mask of another dtype, or with an fp32 call, is not (stock serves it)."""
+    dimension contiguous), or None.  Boolean masks and additive masks in the query's dtype are in
+    the tile table; an additive mask of another dtype is not (stock serves it).  Rows are padded to
+    16-byte boundaries where the kernel reads them with vector loads: additive masks, and every
+    mask of an fp32 call (which reads the mask in place instead of packing it)."""
     if attn_mask is None:
         return None
     if not isinstance(attn_mask, torch.Tensor):
         raise TypeError("attn_mask must be a Tensor")
     additive = attn_mask.dtype != torch.bool
-    if additive and (attn_mask.dtype != query.dtype or query.dtype == torch.float32):
-        raise RuntimeError("attention: an additive attn_mask runs on the kernels only in the 16-bit query dtype")
+    if additive and attn_mask.dtype != query.dtype:
+        raise RuntimeError("attention: an additive attn_mask runs on the kernels only in the query's dtype")
     if attn_mask.device != query.device:
         raise RuntimeError("attn_mask must be on the query's device")
     if attn_mask.dim() > 4:
@@ -217,13 +218,15 @@ def _prepare_mask(attn_mask, query, key):
         m = m.contiguous()
     if m.size(3) == 1 and Lk != 1:  # broadcast along keys: materialise its rows
         m = m.expand(*m.shape[:3], Lk).contiguous()
-    if additive:
+    if additive or query.dtype == torch.float32:
         # 16-byte vector loads: base and every non-broadcast row / head / batch stride aligned
+        unit = 16 // m.element_size()
+
         def aligned(t):
             return t.data_ptr() % 16 == 0 and all(
-                t.size(i) == 1 or t.stride(i) % 8 == 0 for i in range(3))
+                t.size(i) == 1 or t.stride(i) % unit == 0 for i in range(3))
         if not aligned(m):
-            lk_pad = (m.size(3) + 7) // 8 * 8
+            lk_pad = (m.size(3) + unit - 1) // unit * unit
             padded = torch.zeros(*m.shape[:3], lk_pad, dtype=m.dtype, device=m.device)
             padded[..., :m.size(3)] = m
             m = padded[..., :m.size(3)]

@@ -26,7 +26,11 @@ const char* attn_f32_plan(const cmpx_attn_desc* d, int* status) {
     *status = CMPX_ERR_UNSUPPORTED_SHAPE;
     return "none";
   }
-  if (attn_tf32x3_eligible(d)) return "attn_tf32x3_sm100<D64,128q,64kv,persistent>";
+  if (attn_tf32x3_eligible(d)) {
+    if (!d->mask) return "attn_tf32x3_sm100<D64,128q,64kv,persistent>";
+    return d->mask_kind == CMPX_MASK_BOOL ? "attn_tf32x3_sm100<D64,128q,64kv,persistent+mask>"
+                                          : "attn_tf32x3_sm100<D64,128q,64kv,persistent+addmask>";
+  }
   // Head dims above 64, or operands the 3xTF32 kernel cannot read with TMA: stock torch is faster
   // than a CUDA-core fp32 kernel on B200 (measured: 20 vs 47 TFLOP/s at D = 128), so these calls
   // are left to it -- what the reference's own runtime selection did for fp32 attention.

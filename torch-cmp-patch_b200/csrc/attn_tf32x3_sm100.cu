@@ -86,6 +86,12 @@ struct X3Params {
   float scale_log2;
   float* o;
   long long os_b, os_h, os_s;
+  // Mask (MK = 1: one byte per element, nonzero = the key takes part; MK = 2: fp32 values added to
+  // the scores as value / scale): element (b, h, i, j) at mask[b*mk_b + h*mk_h + i*mk_q + j]
+  // (strides in elements, 0 = broadcast); rows start on 16-byte boundaries.
+  const void* mask;
+  long long mk_b, mk_h, mk_q;
+  float mask_inv_scale;
   unsigned long long timeout_ns;
   unsigned int* dev_flags;
 };
@@ -103,6 +109,8 @@ __device__ __forceinline__ void split_v4(uint32_t addr_in, uint32_t addr_hi, uin
                __float_as_uint(__uint_as_float(d) - __uint_as_float(hd)));
 }
 
+// MK: no mask (0), a boolean mask (1), an additive fp32 mask (2) -- separate instantiations.
+template <int MK>
 __global__ void __launch_bounds__(320, 1)
     attn_tf32x3_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                              const __grid_constant__ CUtensorMap tm_k,
@@ -402,6 +410,47 @@ __global__ void __launch_bounds__(320, 1)
         float* s = reinterpret_cast<float*>(sr);
         tc_fence_before_sync();
         const int kv0 = j * C::BN;
+        if constexpr (MK != 0) {
+          if (qrow < p.len_q) {
+            const long long roff = b * p.mk_b + h * p.mk_h + static_cast<long long>(qrow) * p.mk_q + kv0;
+            const int nvalid = min(C::BN, p.len_k - kv0);  // keys past len_k are masked below
+            if constexpr (MK == 1) {
+              const uint8_t* mp = static_cast<const uint8_t*>(p.mask) + roff;
+              if (nvalid == C::BN) {
+#pragma unroll
+                for (int v = 0; v < C::BN / 16; ++v) {
+                  const uint4 w = __ldg(reinterpret_cast<const uint4*>(mp) + v);
+                  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                  for (int e = 0; e < 16; ++e)
+                    if (((ws[e >> 2] >> ((e & 3) * 8)) & 0xffu) == 0u) s[v * 16 + e] = masked;
+                }
+              } else {
+#pragma unroll
+                for (int c = 0; c < C::BN; ++c)
+                  if (c < nvalid && mp[c] == 0) s[c] = masked;
+              }
+            } else {
+              // s += mask / scale, so that s * scale = q.k * scale + mask
+              const float* mp = static_cast<const float*>(p.mask) + roff;
+              const float is = p.mask_inv_scale;
+              if (nvalid == C::BN) {
+#pragma unroll
+                for (int v = 0; v < C::BN / 4; ++v) {
+                  const float4 w = __ldg(reinterpret_cast<const float4*>(mp) + v);
+                  s[4 * v] = fmaf(w.x, is, s[4 * v]);
+                  s[4 * v + 1] = fmaf(w.y, is, s[4 * v + 1]);
+                  s[4 * v + 2] = fmaf(w.z, is, s[4 * v + 2]);
+                  s[4 * v + 3] = fmaf(w.w, is, s[4 * v + 3]);
+                }
+              } else {
+#pragma unroll
+                for (int c = 0; c < C::BN; ++c)
+                  if (c < nvalid) s[c] = fmaf(mp[c], is, s[c]);
+              }
+            }
+          }
+        }
         if (kv0 + C::BN > p.len_k || (p.causal && kv0 + C::BN - 1 > q0)) {
           int lim = p.len_k - kv0;
           if (p.causal) lim = min(lim, qrow - kv0 + 1);
@@ -432,7 +481,8 @@ __global__ void __launch_bounds__(320, 1)
         float alpha = 1.f;
         if (m_run == -INFINITY || m_tile > m_run + 64.f) {
           const float m_new = fmaxf(m_run, m_tile);
-          alpha = ex2_approx(m_run - m_new);
+          // (a masked row with no key so far keeps m = -inf and its l and O at 0)
+          alpha = m_new == -INFINITY ? 1.f : ex2_approx(m_run - m_new);
           m_run = m_new;
         }
         const float nm = (m_run == -INFINITY) ? 0.f : -m_run;
@@ -496,7 +546,7 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_before_sync();
       mbar_arrive(bar(C::B_OFREE));
       if (qrow < p.len_q) {
-        const float inv_l = 1.f / l_run;
+        const float inv_l = (MK != 0 && !(l_run > 0.f)) ? 0.f : 1.f / l_run;  // no key: output 0
         float* dst = p.o + b * p.os_b + h * p.os_h + static_cast<long long>(qrow) * p.os_s;
         if ((p.head_dim & 3) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
 #pragma unroll
@@ -551,6 +601,12 @@ bool make_map_f32(CUtensorMap* map, const void* ptr, int64_t D, int64_t L, int64
 
 bool attn_tf32x3_eligible(const cmpx_attn_desc* d) {
   if (d->dtype != CMPX_F32 || d->head_dim < 1 || d->head_dim > 64) return false;
+  if (d->mask) {  // rows read with 16-byte loads: base and stepped strides 16-byte aligned
+    const int64_t unit = d->mask_kind == CMPX_MASK_BOOL ? 16 : 4;  // elements per 16 bytes
+    if ((reinterpret_cast<uintptr_t>(d->mask) & 15u) != 0 || d->mask_stride[3] != 1) return false;
+    for (int i = 0; i < 3; ++i)
+      if (d->mask_stride[i] % unit != 0) return false;
+  }
   const void* ptrs[3] = {d->q, d->k, d->v};
   for (const void* ptr : ptrs)
     if ((reinterpret_cast<uintptr_t>(ptr) & 15u) != 0) return false;
@@ -574,8 +630,12 @@ int launch_attn_tf32x3(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   cudaGetDevice(&dev);
   cudaError_t attr_err = cudaSuccess;
   std::call_once(once[dev & 63], [&] {
-    attr_err = cudaFuncSetAttribute(reinterpret_cast<const void*>(&attn_tf32x3_sm100_kernel),
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    const void* ptrs[3] = {reinterpret_cast<const void*>(&attn_tf32x3_sm100_kernel<0>),
+                           reinterpret_cast<const void*>(&attn_tf32x3_sm100_kernel<1>),
+                           reinterpret_cast<const void*>(&attn_tf32x3_sm100_kernel<2>)};
+    for (const void* f : ptrs)
+      if (attr_err == cudaSuccess)
+        attr_err = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   });
   if (attr_err != cudaSuccess) return CMPX_ERR_LAUNCH;
   X3Params p;
@@ -594,10 +654,20 @@ int launch_attn_tf32x3(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   p.os_b = d->o_stride[0];
   p.os_h = d->o_stride[1];
   p.os_s = d->o_stride[2];
+  p.mask = d->mask;
+  p.mk_b = d->mask_stride[0];
+  p.mk_h = d->mask_stride[1];
+  p.mk_q = d->mask_stride[2];
+  p.mask_inv_scale = static_cast<float>(1.0 / d->scale);
   p.timeout_ns = ctx.timeout_ns;
   p.dev_flags = ctx.dev_flags;
   const int grid = std::min(p.n_items, std::max(1, ctx.num_sms));
-  attn_tf32x3_sm100_kernel<<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, p);
+  if (!d->mask)
+    attn_tf32x3_sm100_kernel<0><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, p);
+  else if (d->mask_kind == CMPX_MASK_BOOL)
+    attn_tf32x3_sm100_kernel<1><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, p);
+  else
+    attn_tf32x3_sm100_kernel<2><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, p);
   return cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
 }
 

@@ -124,13 +124,7 @@ int attn_common_checks(const cmpx_attn_desc* d) {
 const char* attn_plan_impl(const cmpx_attn_desc* d, int* st) {
   *st = attn_common_checks(d);
   if (*st != CMPX_OK) return "none";
-  if (d->dtype == CMPX_F32) {
-    if (d->mask) {  // masks run on the 16-bit kernel only
-      *st = CMPX_ERR_UNSUPPORTED_SHAPE;
-      return "none";
-    }
-    return attn_f32_plan(d, st);
-  }
+  if (d->dtype == CMPX_F32) return attn_f32_plan(d, st);
   if (d->dtype == CMPX_F16 || d->dtype == CMPX_BF16) return fmha_sm100_plan(d, st);
   *st = CMPX_ERR_UNSUPPORTED_DTYPE;
   return "none";
