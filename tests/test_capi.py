@@ -322,6 +322,9 @@ def test_mask_plans_on_the_16bit_kernel_only():
     st, name = _plan(d)
     assert st == 0 and name.endswith("+addmask>"), name
     assert N.lib.cmpx_attn_workspace_size(ctypes.byref(d)) == 0   # no packing for fp32
+    # one query row: its row stride is never stepped and need not be aligned
+    d = _with_mask(_attn(B=1, H=1, Lq=1, Lk=200, D=40, dtype=0), (200, 200, 200, 1))
+    assert _plan(d)[0] == 0
 
 
 def test_workspace_contract():

@@ -604,8 +604,9 @@ bool attn_tf32x3_eligible(const cmpx_attn_desc* d) {
   if (d->mask) {  // rows read with 16-byte loads: base and stepped strides 16-byte aligned
     const int64_t unit = d->mask_kind == CMPX_MASK_BOOL ? 16 : 4;  // elements per 16 bytes
     if ((reinterpret_cast<uintptr_t>(d->mask) & 15u) != 0 || d->mask_stride[3] != 1) return false;
+    const int64_t extent[3] = {d->batch, d->heads, d->len_q};
     for (int i = 0; i < 3; ++i)
-      if (d->mask_stride[i] % unit != 0) return false;
+      if (extent[i] > 1 && d->mask_stride[i] % unit != 0) return false;  // (a single index: never stepped)
   }
   const void* ptrs[3] = {d->q, d->k, d->v};
   for (const void* ptr : ptrs)
