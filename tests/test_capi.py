@@ -307,7 +307,7 @@ def test_additive_mask_rules():
     assert _plan(d)[0] == N.ERR_INVALID_ARGUMENT
 
 
-def test_mask_plans_on_the_16bit_kernel_only():
+def test_mask_plans_on_the_16bit_and_fp32_kernels():
     d = _with_mask(_attn(Lq=64, Lk=77, dtype=2), (0, 0, 77, 1))
     st, name = _plan(d)
     assert st == 0 and name.startswith("fmha_sm100<bf16") and name.endswith("+mask>"), name
