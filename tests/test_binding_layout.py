@@ -83,3 +83,34 @@ def test_additive_mask_of_another_dtype_is_refused():
     q, k = torch.randn(1, 2, 7, 64), torch.randn(1, 2, 9, 64)
     with pytest.raises(RuntimeError):
         N._prepare_mask(torch.zeros(7, 9, dtype=torch.float16), q, k)
+
+
+def test_nvtx_ranges_wrap_the_ops_when_enabled():
+    # CMPEXT3_NVTX is read at import: check in a fresh interpreter that the public ops are wrapped
+    # and that a call pushes and pops a range (the op itself then refuses the CPU tensors)
+    import os
+    import subprocess
+    import sys
+    code = (
+        "import sys; sys.path[:0] = ['torch-cmp-patch_b200', '.']\n"
+        "import torch\n"
+        "pushed = []\n"
+        "torch.cuda.nvtx.range_push = lambda name: pushed.append(name) or 0\n"
+        "torch.cuda.nvtx.range_pop = lambda: pushed.append('pop') or 0\n"
+        "from cmpext3 import _native as N\n"
+        "assert all(hasattr(f, '__wrapped__') for f in (N.attention, N.bmm, N.linear, N.softmax))\n"
+        "try:\n"
+        "    N.bmm(torch.randn(1, 2, 2), torch.randn(1, 2, 2))\n"
+        "except RuntimeError:\n"
+        "    pass\n"
+        "assert pushed == ['cmpx.bmm', 'pop'], pushed\n"
+        "print('ok')\n")
+    env = dict(os.environ, CMPEXT3_NVTX="1", CMPEXT3_AUTOPATCH="0")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True,
+                         timeout=300)
+    assert out.returncode == 0 and out.stdout.strip().endswith("ok"), out.stderr[-2000:]
+
+
+def test_ops_are_unwrapped_by_default():
+    assert not hasattr(N.attention, "__wrapped__") and not hasattr(N.bmm, "__wrapped__")

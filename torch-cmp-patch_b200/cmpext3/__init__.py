@@ -36,7 +36,7 @@ power limits.  fp32 bmm / matmul / einsum / linear run on a 3xTF32 tensor-core G
 
 Set CMPEXT3_AUTOPATCH=0 to import without patching; CMPEXT3_DISABLE_OPS=attention,bmm,matmul,einsum,
 softmax,linear pins named ops to stock; CMPEXT3_VERBOSE=1 logs each new signature's tile-table entry;
-cmpext3.autoselect_report() lists them.
+cmpext3.autoselect_report() lists them; CMPEXT3_NVTX=1 puts an NVTX range around every native call.
 
 SAFETY: the kernels are forward-only (no autograd); every patched call falls back to stock when
 autograd is live, as in the reference.

@@ -15,6 +15,7 @@ table, it raises ``RuntimeError``.
 from __future__ import annotations
 
 import ctypes
+import functools
 import math
 import os
 from pathlib import Path
@@ -139,6 +140,26 @@ lib = _load()
 
 # Debug switch: synchronise after every call and raise if a device-side wait timed out.
 _CHECK = os.environ.get("CMPEXT3_CHECK", "0") not in ("0", "", "false", "False")
+_NVTX = os.environ.get("CMPEXT3_NVTX", "0") not in ("0", "", "false", "False")
+
+
+def _traced(name: str):
+    """With CMPEXT3_NVTX=1 (read at import), an NVTX range ``cmpx.<name>`` around every call of the
+    op -- the binding's host work and the kernels it enqueues -- so that profiler timelines (nsys,
+    ncu --nvtx) name the native calls.  Otherwise the op is returned unchanged (no cost)."""
+    def wrap(fn):
+        if not _NVTX:
+            return fn
+
+        @functools.wraps(fn)
+        def inner(*args, **kwargs):
+            torch.cuda.nvtx.range_push(f"cmpx.{name}")
+            try:
+                return fn(*args, **kwargs)
+            finally:
+                torch.cuda.nvtx.range_pop()
+        return inner
+    return wrap
 
 
 def _status_str(status: int) -> str:
@@ -290,6 +311,7 @@ def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
     return ws
 
 
+@_traced("attention")
 def attention(query, key, value, scale=None, causal=False, attn_mask=None):
     """SDPA forward on the sm_100a kernels.  Same contract as the reference's ops.attention, plus an
     optional boolean attn_mask (torch's meaning: True = the key takes part; with causal the two
@@ -413,6 +435,7 @@ def _bmm_desc(a, b, c) -> BmmDesc:
     return d
 
 
+@_traced("bmm")
 def bmm(input, mat2):
     """Batched matmul on the sm_100a kernels.  Same contract as the reference's ops.bmm."""
     a, b, c = _prepare_bmm(input, mat2)
@@ -494,6 +517,7 @@ def _linear_desc(x, w, bias, y) -> LinearDesc:
                       _DTYPE[x.dtype], 0)
 
 
+@_traced("linear")
 def linear(input, weight, bias=None):
     """F.linear on the sm_100a GEMM with the bias added in its epilogue.  Same contract as the
     reference's ops.linear (input [..., K], weight [N, K], bias [N] -> [..., N])."""
@@ -531,6 +555,7 @@ def linear_plan(input, weight, bias=None) -> str:
 # softmax over the last dimension (the einsum-attention chain's middle step)
 # ---------------------------------------------------------------------------------------------
 
+@_traced("softmax")
 def softmax(input, dim=-1):
     """torch.softmax(input, dim=-1) on the sm_100a row-softmax kernel (fp32 arithmetic, output in
     the input's dtype).  Only the last dimension; the rows must be contiguous."""
