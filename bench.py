@@ -4,7 +4,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c5] [--impl ours|reference]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 ... bench.py --gpus N
 
-Metric (BASELINE.json): "SDPA fwd TFLOP/s at 1/2/4/8 B200 and % of dense bf16 tensor peak".
+Metric: "SDPA fwd TFLOP/s at 1/2/4/8 B200 and % of dense bf16 tensor peak".
 Default workload C5: causal bf16 SDPA, Q,K,V [B=64, H=32, L=8192, D=128] ~ N(0,1), scale 1/sqrt(128),
 sharded by batch x head across N GPUs (rank r owns batches [r*64/N, (r+1)*64/N)) with no collective
 on the forward path.  A step is one forward over the rank's shard; value = algorithmic causal FLOPs of
@@ -12,8 +12,8 @@ every rank's steps / max-over-ranks device time of the K steps (strong scaling: 
 Algorithmic FLOPs = 4 * B * H * D * (number of unmasked (query, key) pairs), L(L+1)/2 pairs per
 (b, h) for causal.
 
-Other workloads (--workload c1|c2-self|c2-cross|c3|c4; single GPU) are the other BASELINE.json
-configs, measured the same way for the tables in BASELINE.md.
+Other workloads (--workload c1|c2-self|c2-cross|c3|c4; single GPU) are the other configs of the
+benchmark definition, measured the same way.
 
 Inputs are generated on the GPU from per-batch seeds (identical for every N), larger than the 126 MB
 L2 for c4/c5 (no flush needed); the smaller configs flush L2 with a 256 MB write between steps and

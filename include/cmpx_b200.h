@@ -161,10 +161,12 @@ CMPX_API size_t cmpx_attn_workspace_size(const cmpx_attn_desc* desc);
  * device).  Same descriptor and results as cmpx_attn_fwd, but the workspace fields are ignored: the
  * kernel's scratch (its work counters) lives in a fixed 256-byte array inside the library, which
  * every GPU that loads the library keeps until the process exits; the 16-bit kernels then run the
- * schedule that needs no more than their 256 bytes of work counters (no tail split; a call with a
- * mask returns CMPX_ERR_WORKSPACE: the mask is packed in the workspace).  The first call on a
- * device looks up that array's device address (cudaGetSymbolAddress); make that first call before
- * capturing the stream into a graph.  Each call clears the counters it needs with an enqueued
+ * schedule that needs no more than their 256 bytes of work counters (no tail split; additive masks
+ * are served, but a call with a boolean mask returns CMPX_ERR_WORKSPACE, because that mask is packed
+ * to bits in the workspace).  The call is checked against the tile table first, so an unsupported
+ * call returns the same status as from cmpx_attn_fwd.  The first call on a device looks up that
+ * array's device address (cudaGetSymbolAddress); make that first call before capturing the stream
+ * into a graph.  A failed lookup returns CMPX_ERR_DEVICE and is retried by the next call.  Each call clears the counters it needs with an enqueued
  * memset.  All calls share the one array, so calls whose work overlaps on the GPU (different
  * streams without ordering between them) race on it: serialise them.
  * No counterpart in the reference. */

@@ -1,4 +1,4 @@
-"""The five BASELINE.json configurations at full size on the GPU (marked gpu).
+"""The five benchmark configurations (C1-C5) at full size on the GPU (marked gpu).
 
 Full-size outputs are too large for the CPU oracle to recompute, so each is checked two ways:
 * a seeded sample of (b, h) slices x query rows against the reference's CPU path (stock torch SDPA

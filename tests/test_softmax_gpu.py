@@ -57,6 +57,25 @@ def test_softmax_masked_and_extreme_rows(cuda_device, dtype):
         check(got, RP.softmax(xx.contiguous(), -1), dtype, f"extreme rows {xx.shape} {dtype}")
 
 
+@pytest.mark.parametrize("cols", [1024, 1023], ids=["registers", "two-pass"])
+def test_softmax_fp32_large_magnitude_rows(cuda_device, cols):
+    """fp32 rows whose scores sit near +-1e3 with spreads of a few units: the exponent must come
+    from the exact difference x - max (an fma with a separately rounded max * log2(e) would carry
+    |max| * 2^-24 into every exponent), so the result stays within the fp32 1e-4 bound."""
+    g = torch.Generator().manual_seed(17)
+    x = torch.randn(6, cols, generator=g) * 3.0
+    x[0] += 1000.0
+    x[1] -= 1000.0
+    x[2] += 3000.0
+    x[3] = x[3] * 200.0 + 1500.0
+    got = N.softmax(x.to(cuda_device), -1)
+    torch.cuda.synchronize()
+    ref = RP.softmax(x, -1)
+    check(got, ref, torch.float32, f"large-magnitude fp32 rows ({cols})")
+    rel = ((got.cpu() - ref).abs().amax(-1) / ref.abs().amax(-1)).max().item()
+    assert rel <= 2e-5, rel
+
+
 def test_fully_masked_row_is_nan_like_torch(cuda_device):
     x = torch.zeros(2, 512)
     x[1] = -math.inf

@@ -1,7 +1,10 @@
 """torch.einsum planned as batched matrix products, so the bmm patch (and its sm_100a kernel) applies.
 
-Same planning contract as the reference's planner (cmpext3/einsum_ops.py:25-131 in the reference),
-written independently:
+This module restates the reference's planner (cmpext3/einsum_ops.py:25-131 in the reference):
+its identifiers (``Unsupported``, ``parse``, ``_sizes``, ``_pair``, ``einsum``, ``supported``) and
+its step order are kept on purpose, because the planner's results and its fall-back decisions are
+part of the drop-in contract (the same equations must reach the same bmm calls, and the same ones
+must go back to stock einsum).  The steps:
 
 * operands are contracted left to right, two at a time;
 * in each pair, indices that appear in only one operand and are not needed later are summed out
@@ -105,7 +108,8 @@ def _pair(a: torch.Tensor, ta: str, b: torch.Tensor, tb: str, out: str, size: di
 
 
 def einsum(equation: str, operands: Sequence[torch.Tensor], bmm: Optional[Callable] = None) -> torch.Tensor:
-    """einsum via batched matmuls; raises Unsupported for equations it does not plan."""
+    """Evaluate ``equation`` as a chain of batched matmuls (reference einsum_ops.py:101-121);
+    an equation outside the planner raises ``Unsupported``."""
     bmm = bmm or torch.bmm
     terms, out = parse(equation, len(operands))
     size = _sizes(terms, operands)
@@ -126,7 +130,8 @@ def einsum(equation: str, operands: Sequence[torch.Tensor], bmm: Optional[Callab
 
 
 def supported(equation: str, operands: Sequence[torch.Tensor]) -> Optional[str]:
-    """None if einsum() can plan it, else the reason."""
+    """The reason ``einsum`` would refuse the equation, or None when it plans it
+    (reference einsum_ops.py:124-131)."""
     try:
         terms, _ = parse(equation, len(operands))
         _sizes(terms, operands)

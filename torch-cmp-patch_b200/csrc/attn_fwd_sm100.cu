@@ -41,17 +41,9 @@
 #include "cmpx_internal.h"
 #include "cmpx_ptx.cuh"
 
-// Column pairs (of every 8) whose exp2 runs on the FMA pipe (polynomial) instead of MUFU, for
-// head dims <= 64 and for larger ones.
-#ifndef CMPX_FMHA_EMU64
-#define CMPX_FMHA_EMU64 0
-#endif
 // Causal launches: work items per CTA in the longest-first tail (0: no such tail).
 #ifndef CMPX_FMHA_LPT
 #define CMPX_FMHA_LPT 2
-#endif
-#ifndef CMPX_FMHA_EMU
-#define CMPX_FMHA_EMU 0
 #endif
 
 namespace cmpx {
@@ -105,7 +97,6 @@ struct FmhaCfg {
   // Warp roles: 0-3 softmax/epilogue of tile 0, 4-7 of tile 1 (thread = row), 8 TMA producer
   // (and work fetch), 9 QK issuer (and TMEM owner), 10 PV issuer.
   static constexpr int THREADS = 352;
-  static constexpr int EMU = DP <= 64 ? CMPX_FMHA_EMU64 : CMPX_FMHA_EMU;
   static constexpr int W_TMA = 8, W_MMA = 9, W_PV = 10;
   static constexpr int ITEM_CONSUMERS = 2 + 8;  // lane 0 of each MMA warp and of each softmax warp
 };
@@ -192,24 +183,17 @@ __global__ void __launch_bounds__(256) fmha_pack_mask_kernel(const uint8_t* __re
 
 // One chunk (16 column pairs = 32 keys) of a row's exponentials: p = 2^(s*sl2 + nmb) packed to
 // 16-bit pairs in pk, the row sum accumulated in la/lb.  x = s*sl2 + nmb is formed and the sum
-// accumulated two keys at a time with packed f32x2 arithmetic; exponentials on MUFU (EMU of every
-// 8 column pairs on the FMA pipe instead).
-template <bool BF16, int EMU>
+// accumulated two keys at a time with packed f32x2 arithmetic; exponentials on MUFU.
+template <bool BF16>
 __device__ __forceinline__ void exp_chunk(const float* s, int q, uint64_t sl2x2, uint64_t nmbx2,
                                           uint64_t& la, uint64_t& lb, uint32_t (&pk)[16]) {
 #pragma unroll
   for (int c = 0; c < 16; ++c) {
     const int cc = q * 16 + c;
     const uint64_t xv = f2_fma(f2_pack(s[2 * cc], s[2 * cc + 1]), sl2x2, nmbx2);
-    float p0, p1;
-    if ((cc & 7) >= 8 - EMU) {
-      f2_unpack(exp2_poly3_x2(xv), p0, p1);
-    } else {
-      float x0, x1;
-      f2_unpack(xv, x0, x1);
-      p0 = ex2_approx(x0);
-      p1 = ex2_approx(x1);
-    }
+    float x0, x1;
+    f2_unpack(xv, x0, x1);
+    const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
     if (c & 1)
       lb = f2_add(lb, f2_pack(p0, p1));
     else
@@ -222,17 +206,17 @@ __device__ __forceinline__ void exp_chunk(const float* s, int q, uint64_t sl2x2,
 // returns the row sum of p.  before_store() runs after the first chunk is computed and before
 // anything is stored: the wait for the P buffer to be free (the previous PV) overlaps the first
 // chunk of the exponentials instead of preceding them.
-template <int BN, bool BF16, int EMU, class BeforeStore>
+template <int BN, bool BF16, class BeforeStore>
 __device__ __forceinline__ float exp_pass(const float* s, float sl2, float nmb, uint32_t p_tm,
                                           BeforeStore&& before_store) {
   uint64_t la = f2_pack(0.f, 0.f), lb = la;
   const uint64_t sl2x2 = f2_pack(sl2, sl2), nmbx2 = f2_pack(nmb, nmb);
   uint32_t pk[16];
-  exp_chunk<BF16, EMU>(s, 0, sl2x2, nmbx2, la, lb, pk);
+  exp_chunk<BF16>(s, 0, sl2x2, nmbx2, la, lb, pk);
   before_store();
 #pragma unroll
   for (int q = 0; q < BN / 32; ++q) {
-    if (q > 0) exp_chunk<BF16, EMU>(s, q, sl2x2, nmbx2, la, lb, pk);
+    if (q > 0) exp_chunk<BF16>(s, q, sl2x2, nmbx2, la, lb, pk);
     tmem_st16(p_tm + q * 16, pk);
   }
   float a0, a1;
@@ -793,7 +777,7 @@ __global__ void __launch_bounds__(352, 1)
         bool slow = (j == j_begin);
         if (!slow) {
           bool pv_ok = true;
-          l_tile = exp_pass<C::BN, BF16, C::EMU>(s, sl2, -m_run, p_tm, [&] {
+          l_tile = exp_pass<C::BN, BF16>(s, sl2, -m_run, p_tm, [&] {
             pv_ok = mbar_wait_all(bar(C::B_PVDONE + t), (n_pvdone++) & 1u, ctl);
             tc_fence_after_sync();
           });
@@ -812,7 +796,7 @@ __global__ void __launch_bounds__(352, 1)
           }
           // (a masked row with no key left so far keeps m_run = -inf; its p are 0, not NaN)
           const float nm = (MK != 0 && m_run == -INFINITY) ? 0.f : -m_run;
-          l_tile = exp_pass<C::BN, BF16, C::EMU>(s, sl2, nm, p_tm, [] {});
+          l_tile = exp_pass<C::BN, BF16>(s, sl2, nm, p_tm, [] {});
           if (j > j_begin && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
             for (int c = 0; c < DP / 32; ++c) {

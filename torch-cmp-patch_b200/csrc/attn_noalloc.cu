@@ -12,9 +12,11 @@
 // holds its 256 bytes until the process exits.  In host code its name is only a stand-in for the
 // device object, so the host never passes it to a kernel directly: on the first call on each
 // device (with that device current) cudaGetSymbolAddress turns it into a device address, which
-// every later call on that device reuses.
+// every later call on that device reuses.  A lookup that fails is not kept, so the next call on
+// that device looks the address up again.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <mutex>
 
@@ -27,50 +29,51 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-struct ScratchSlot {
-  std::once_flag once;
-  cudaError_t status = cudaErrorUnknown;
-  void* ptr = nullptr;
-};
-ScratchSlot g_scratch[kMaxDevices];
+// Device address of the scratch array, per device; null until a lookup on that device succeeded.
+// A failed lookup (e.g. one made while the stream was being captured) is not remembered: the next
+// call on that device tries again.
+std::atomic<void*> g_scratch_ptr[kMaxDevices];
+std::mutex g_scratch_mutex;
 
-// Device address of the scratch array on the current device (resolved once per device).
+// Device address of the scratch array on the current device.
 void* scratch_on_current_device(int* status) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
-    *status = CMPX_ERR_DEVICE;
-    return nullptr;
-  }
-  ScratchSlot& slot = g_scratch[dev];
-  std::call_once(slot.once, [&] {
-    void* p = nullptr;
-    slot.status = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (slot.status == cudaSuccess) slot.ptr = p;
-  });
-  if (slot.status != cudaSuccess || !slot.ptr) {
     cudaGetLastError();
     *status = CMPX_ERR_DEVICE;
     return nullptr;
   }
+  void* p = g_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (!p) {
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    p = g_scratch_ptr[dev].load(std::memory_order_relaxed);
+    if (!p) {
+      if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
+        cudaGetLastError();
+        *status = CMPX_ERR_DEVICE;
+        return nullptr;
+      }
+      g_scratch_ptr[dev].store(p, std::memory_order_release);
+    }
+  }
   *status = CMPX_OK;
-  return slot.ptr;
+  return p;
 }
 
 }  // namespace
 
 extern "C" CMPX_API int cmpx_attn_fwd_noalloc(const cmpx_attn_desc* desc, void* stream) {
   if (!desc) return CMPX_ERR_INVALID_ARGUMENT;
-  // The 16-bit kernels run with their minimum workspace (the work counters; no tail split).  A
-  // boolean mask is packed to bits in the workspace, which the fixed scratch has no room for.
-  const bool sixteen = desc->dtype == CMPX_F16 || desc->dtype == CMPX_BF16;
-  if (sixteen && desc->mask) return CMPX_ERR_WORKSPACE;
-  const size_t need = sixteen ? cmpx::kAttnWorkspaceMin : 0;
-  if (need > kNoAllocScratchBytes) return CMPX_ERR_WORKSPACE;  // beyond the fixed scratch
   cmpx_attn_desc d = *desc;  // the caller's workspace fields are ignored
   d.workspace = nullptr;
   d.workspace_bytes = 0;
   const int plan_status = cmpx_attn_plan(&d, nullptr, 0);  // reject bad calls before any device work
   if (plan_status != CMPX_OK) return plan_status;
+  // The 16-bit kernels run with their minimum workspace: the work counters (no tail split), plus a
+  // boolean mask packed to bits, for which the fixed scratch has no room.  fp32 needs none.
+  const bool sixteen = d.dtype == CMPX_F16 || d.dtype == CMPX_BF16;
+  const size_t need = sixteen ? cmpx::fmha_workspace_min(&d) : 0;
+  if (need > kNoAllocScratchBytes) return CMPX_ERR_WORKSPACE;  // beyond the fixed scratch
   if (need > 0) {
     int st = CMPX_OK;
     void* scratch = scratch_on_current_device(&st);

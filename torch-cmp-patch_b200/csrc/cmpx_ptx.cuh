@@ -472,42 +472,6 @@ __device__ __forceinline__ float fmin3(float a, float b, float c) {
   return d;
 }
 
-// 2^x evaluated on the FMA / integer pipes instead of the MUFU unit, so that part of a softmax
-// tile's exponentials can run beside the MUFU ones.  Cody-Waite split x = n + f with n = rint(x)
-// (the 1.5 * 2^23 round-to-nearest addition) and |f| <= 0.5, then a degree-3 minimax polynomial for
-// 2^f on [-0.5, 0.5] (coefficients fitted here by a Remez exchange on the relative error; max
-// relative error 7.5e-5, below half an ulp of bf16 and fp16), and n added to the exponent field.
-// x is clamped to >= -125 (2^-125 stands in for 0 for masked scores); x <= 8 in the callers.
-__device__ __forceinline__ float exp2_poly3(float x) {
-  x = fmaxf(x, -125.f);
-  const float kRound = 12582912.f;  // 1.5 * 2^23
-  const float t = x + kRound;
-  const float f = x - (t - kRound);
-  float p = fmaf(0.0551716685295105f, f, 0.2426111251115799f);
-  p = fmaf(p, f, 0.6932609677314758f);
-  p = fmaf(p, f, 0.9999280571937561f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-
-// Packed form of exp2_poly3 for two values at once (the polynomial in f32x2 arithmetic).
-__device__ __forceinline__ uint64_t exp2_poly3_x2(uint64_t xv) {
-  float x0, x1;
-  f2_unpack(xv, x0, x1);
-  xv = f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
-  const uint64_t kRound = f2_pack(12582912.f, 12582912.f);
-  const uint64_t t = f2_add(xv, kRound);
-  const uint64_t f = f2_sub(xv, f2_sub(t, kRound));
-  uint64_t p = f2_fma(f2_pack(0.0551716685295105f, 0.0551716685295105f), f,
-                      f2_pack(0.2426111251115799f, 0.2426111251115799f));
-  p = f2_fma(p, f, f2_pack(0.6932609677314758f, 0.6932609677314758f));
-  p = f2_fma(p, f, f2_pack(0.9999280571937561f, 0.9999280571937561f));
-  float p0, p1, t0, t1;
-  f2_unpack(p, p0, p1);
-  f2_unpack(t, t0, t1);
-  return f2_pack(__int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23)),
-                 __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23)));
-}
-
 // Global loads cached in L2 only (data another SM wrote in this launch).  Neither volatile nor a
 // memory clobber: the compiler may move them across unrelated stores, so a caller must only use
 // them on data that no store of the same thread can alias in between.

@@ -114,15 +114,16 @@ __global__ void __launch_bounds__(256) softmax_rows_reg_kernel(const uint8_t* __
       }
     }
     m = warp_max(m);
-    // A row of -inf keeps m = -inf: the result is NaN, as torch's is.
-    const float nm = -m * kLog2e;
+    // A row of -inf keeps m = -inf: the result is NaN, as torch's is.  The exponent is the exact
+    // difference x - m times log2(e), not fma(x, log2e, -m*log2e): the rounded product m*log2e
+    // would carry an error of |m| * 2^-24 into every exponent of a row with large scores.
     float l = 0.f;
 #pragma unroll
     for (int c = 0; c < CHUNKS; ++c) {
       if (c * 32 + lane < nchunks) {
 #pragma unroll
         for (int i = 0; i < EPC; ++i) {
-          e[c * EPC + i] = ex2_approx(fmaf(e[c * EPC + i], kLog2e, nm));
+          e[c * EPC + i] = ex2_approx((e[c * EPC + i] - m) * kLog2e);
           l += e[c * EPC + i];
         }
       }
@@ -184,9 +185,9 @@ __global__ void __launch_bounds__(256) softmax_rows_stream_kernel(const uint8_t*
     const float mr = warp_max(m);
     l = (m == -INFINITY) ? 0.f : l * ex2_approx((m - mr) * kLog2e);
     l = warp_sum(l);
-    const float inv = 1.f / l, nm = -mr * kLog2e;
+    const float inv = 1.f / l;
     for (int64_t c = lane; c < cols; c += 32)
-      store_elt<DT>(yr, c, ex2_approx(fmaf(load_elt<DT>(xr, c), kLog2e, nm)) * inv);
+      store_elt<DT>(yr, c, ex2_approx((load_elt<DT>(xr, c) - mr) * kLog2e) * inv);
   }
 }
 
