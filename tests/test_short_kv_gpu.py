@@ -1,11 +1,13 @@
 """The streamed short-key kernel (fmha_sm100_short: non-causal, 1 <= Lk <= 128) against the
 reference's CPU path (needs a B200; marked gpu).
 
-The kernel splits the flattened (batch, head, 128-row Q tile) range evenly over the CTAs and
-reloads K/V whenever the head changes inside a CTA's range, so these cases vary how many tiles and
-heads land on one CTA: fewer tiles than SMs, ranges that straddle head boundaries, many tiles per
-CTA, ragged Lq, every Lk edge (1, one K=16 step, 16/17, 77, 127, 128), padded and full head dims,
-a negative scale and strided [B, L, H, D] views.  Tolerances as in test_parity_gpu.py.
+The kernel splits the flattened (batch, head, 128-row Q tile) range evenly over the CTAs, loads
+K/V of every head it meets into one of two buffers (one for D = 128), and keeps 2-4 tiles in
+flight depending on Lk and D, so these cases vary how many tiles and heads land on one CTA: fewer
+tiles than SMs, ranges that straddle head boundaries, one tile per head with several heads per CTA
+(buffer reuse), many tiles per CTA, ragged Lq, every Lk edge (1, one K=16 step, 16/17, 64/65, 77,
+96/97, 127, 128), padded and full head dims, a negative scale and strided [B, L, H, D] views.
+Tolerances as in test_parity_gpu.py.
 """
 from __future__ import annotations
 
@@ -31,6 +33,12 @@ CASES = [
     (1, 2, 700, 127, 128),     # D = 128: three Q stages
     (4, 9, 257, 128, 128),     # full key tile, head changes inside ranges
     (2, 3, 640, 50, 40),       # padded head dim
+    (8, 100, 100, 65, 64),     # one tile per head, 5-6 heads per CTA: both K/V buffers reused
+    (6, 100, 64, 128, 128),    # D = 128, one K/V buffer, reloaded for every tile of a CTA
+    (2, 6, 1000, 64, 64),      # Lk = 64: four tiles in flight per CTA
+    (2, 6, 1000, 96, 64),      # Lk = 96: three in flight, no masked key
+    (2, 6, 1000, 97, 64),      # Lk = 97: two in flight (128-wide S)
+    (1, 1, 2000, 33, 64),      # fewer tiles than SMs, 1-2 tiles per CTA
 ]
 
 

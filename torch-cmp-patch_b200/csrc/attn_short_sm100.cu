@@ -3,24 +3,32 @@
 // Cross-attention to a text encoder's tokens (SD1.5 / SDXL: Lk = 77) has one key tile: the
 // work per query row is tiny and the call is bound by reading Q and writing O.  The reference
 // runs these calls through its non-causal fp16 kernel (flash_attn_hfma2_kernel,
-// src/cuda/fp16_flash_attention_hfma2.cu:72-243; any Sq / Sk); the general kernel of this library
-// (attn_fwd_sm100.cu) handles them correctly too, but its work item (two Q tiles, then the next
-// item's Q) exposes a DRAM latency per item.  This kernel streams instead:
+// src/cuda/fp16_flash_attention_hfma2.cu:72-243, launched for any Sq / Sk at :269-286); the general
+// kernel of this library (attn_fwd_sm100.cu) handles them correctly too, but a whole SM then works
+// on one pair of Q tiles at a time.  At C2-cross sizes every SM owns only 4-5 Q tiles, so the
+// kernel's duration is the latency chain of those few tiles (load Q, S = Q K^T, softmax, O = P V,
+// store O), and the design goal here is to run as many of them side by side as the SM holds:
 //
 //   * each CTA takes a contiguous range of 128-row Q tiles (flattened over batch, head, row
-//     tiles) and loads K and V of the current (batch, head) once -- again only when the head
-//     changes inside its range;
-//   * warp 8 keeps a ring of Q tiles in flight (6 stages for D <= 64, 3 for D = 128) with TMA;
-//   * warp 9 issues S = Q K^T (tcgen05, fp32 in TMEM) for tile i+1 while tile i's softmax and PV
-//     run, and O = P V with P read from TMEM, over only the key steps that hold keys;
-//   * warps 0-3 / 4-7 take even / odd tiles: thread = row; one exact softmax pass (row max,
-//     exp2, row sum -- no running max is needed with a single key tile), P (16-bit) to TMEM; then
-//     the epilogue O / l through a per-warpgroup staging tile and TMA stores (clipped at Lq, D),
-//     which overlaps the other warpgroup's softmax and the next QK.
+//     tiles) and loads K and V of each (batch, head) it meets once, into one of two K/V buffers
+//     (D <= 64), so a range that crosses a head boundary finds the next head's K/V already loaded;
+//   * TMEM is cut into NSLOT tile slots, one per softmax warpgroup: S (fp32, SN columns, SN = Lk
+//     rounded up to 64 / 96 / 128), with P (16-bit pairs) written over S, then O (DP columns).
+//     D = 64 with Lk <= 64 / 96 / 128 gives 4 / 3 / 2 tiles in flight; D = 128 gives 2;
+//   * the producer warp keeps a ring of Q tiles in flight (8 stages for D <= 64, 4 for D = 128);
+//     it sets up the barriers and issues its first loads before the CTA-wide barrier, so they
+//     overlap the TMEM allocation and the other warps' start;
+//   * the MMA warp polls its inputs and issues whichever product is ready: O = P V of the oldest
+//     tile whose P is written (over only the K=16 key steps that hold keys), or S = Q K^T of the
+//     next tile once its slot's previous P V has finished reading P;
+//   * softmax warpgroup g takes tiles i with i % NSLOT == g, thread = row: one exact pass (row max
+//     and the exponentials only over the 16-key groups that hold keys; no running max is needed
+//     with a single key tile); then the epilogue O / l, which stages the 16-bit O tile in the Q
+//     ring slot the tile was loaded into (its Q is dead once S is computed) and stores it with TMA
+//     (clipped at Lq and D), then hands the slot back to the producer.
 //
-// TMEM columns: S [0,128) (shared, the two warpgroups take it in turns), P0 [128,192),
-// P1 [192,256), O0, O1.  Every wait is bounded (cmpx_ptx.cuh); on a timeout the CTA drains its
-// copies and MMAs, frees TMEM, raises the device status word and returns.
+// Every wait is bounded (cmpx_ptx.cuh); on a timeout the CTA drains its copies and MMAs, frees
+// TMEM, raises the device status word and returns.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -33,35 +41,36 @@
 
 namespace cmpx {
 
-template <int DP>
+template <int DP, int SN>
 struct ShortCfg {
   static constexpr int BM = 128;                     // query rows per tile
   static constexpr int NCH = DP / 64;                // 64-element (128-byte) chunks of the head dim
   static constexpr int CH_BYTES = 128 * 128;         // one chunk of 128 rows
   static constexpr int TILE_BYTES = NCH * CH_BYTES;  // one Q, K, V or O tile
-  static constexpr int NQ = DP <= 64 ? 6 : 3;        // Q ring stages
-  static constexpr int OFF_K = 0;
-  static constexpr int OFF_V = OFF_K + TILE_BYTES;
-  static constexpr int OFF_Q = OFF_V + TILE_BYTES;
-  static constexpr int OFF_OST = OFF_Q + NQ * TILE_BYTES;  // [2] staging tiles, one per warpgroup
-  static constexpr int OFF_BAR = OFF_OST + 2 * TILE_BYTES;
-  static constexpr int B_KVFULL = 0;             // K and V of the current head landed
-  static constexpr int B_KVEMPTY = 1;            // every MMA reading the previous head's K/V done
-  static constexpr int B_QFULL = 2;              // [NQ]
-  static constexpr int B_QEMPTY = B_QFULL + NQ;  // [NQ]
-  static constexpr int B_SFULL = B_QEMPTY + NQ;  // [2] S holds the tile of warpgroup g
-  static constexpr int B_SFREE = B_SFULL + 2;    // S read (count 128; the warpgroups alternate)
-  static constexpr int B_PREADY = B_SFREE + 1;   // [2] P_g written (count 128)
-  static constexpr int B_PVDONE = B_PREADY + 2;  // [2] O_g = P_g V complete
-  static constexpr int B_OFREE = B_PVDONE + 2;   // [2] epilogue has read O_g (count 128)
-  static constexpr int B_DRAIN = B_OFREE + 2;
+  static constexpr int SLOT_COLS = SN + DP;          // TMEM columns of one tile: S (and P), then O
+  static constexpr int NSLOT = 512 / SLOT_COLS < 4 ? 512 / SLOT_COLS : 4;
+  static constexpr int NKV = DP <= 64 ? 2 : 1;       // K/V buffers
+  static constexpr int NQ = DP <= 64 ? 8 : 4;        // Q ring stages (each also stages its tile's O)
+  static constexpr int OFF_KV = 0;                   // [NKV] x {K, V}
+  static constexpr int OFF_Q = OFF_KV + NKV * 2 * TILE_BYTES;
+  static constexpr int OFF_BAR = OFF_Q + NQ * TILE_BYTES;
+  static constexpr int B_KVFULL = 0;                   // [NKV] K and V of a head landed
+  static constexpr int B_KVEMPTY = B_KVFULL + NKV;     // [NKV] every MMA reading that head's K/V done
+  static constexpr int B_QFULL = B_KVEMPTY + NKV;      // [NQ] Q tile landed
+  static constexpr int B_QEMPTY = B_QFULL + NQ;        // [NQ] O stored from the stage (count 4)
+  static constexpr int B_SFULL = B_QEMPTY + NQ;        // [NSLOT] S = Q K^T complete
+  static constexpr int B_PREADY = B_SFULL + NSLOT;     // [NSLOT] P written (count 128)
+  static constexpr int B_PVDONE = B_PREADY + NSLOT;    // [NSLOT] O = P V complete
+  static constexpr int B_DRAIN = B_PVDONE + NSLOT;
   static constexpr int NBAR = B_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // tmem base, abort word
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // +1024: runtime alignment slack
-  static constexpr int TM_S = 0, TM_P0 = 128, TM_P1 = 192, TM_O0 = 256, TM_O1 = 256 + DP;
   static constexpr int TMEM_COLS = 512;
-  static constexpr int THREADS = 320;
-  static constexpr int W_TMA = 8, W_MMA = 9;
+  static constexpr int W_TMA = 4 * NSLOT, W_MMA = 4 * NSLOT + 1;
+  static constexpr int THREADS = 128 * NSLOT + 64;
+  static_assert(NSLOT >= 2 && NSLOT * SLOT_COLS <= TMEM_COLS, "TMEM slots");
+  static_assert(SLOT_COLS % 32 == 0, "slot bases on 32-column boundaries");
+  static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
 
 struct ShortParams {
@@ -70,7 +79,7 @@ struct ShortParams {
   int len_k;
   int n_qt;       // ceil(len_q / 128)
   int n_tiles;    // n_qt * heads * batch
-  int pv_steps;   // ceil(len_k / 16): K=16 steps of P V that hold keys
+  int pv_steps;   // ceil(len_k / 16): K=16 steps of P V that hold keys (= 16-key groups of P)
   int neg_scale;  // scale < 0: masked scores are +inf so that masked * scale = -inf
   int group;      // query heads per key/value head (grouped-query attention)
   float scale_log2;
@@ -101,13 +110,44 @@ struct TileCursor {
   __device__ bool last_of_head(const ShortParams& p) const { return qt + 1 == p.n_qt; }
 };
 
-template <int DP, bool BF16>
-__global__ void __launch_bounds__(320, 1)
+// A row's scores: SN fp32 columns of TMEM starting at taddr, loaded with as few waits as possible.
+template <int SN>
+__device__ __forceinline__ void load_scores(uint32_t taddr, uint32_t (&s)[SN]) {
+  static_assert(SN == 64 || SN == 96 || SN == 128, "score widths");
+  if constexpr (SN == 128) {
+    tmem_ld128(taddr, s);
+  } else {
+    tmem_ld64(taddr, *reinterpret_cast<uint32_t(*)[64]>(&s[0]));
+    if constexpr (SN == 96) tmem_ld32(taddr + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
+  }
+}
+
+// Row maximum (NEG: minimum) over the first `groups` 16-key groups of s: 8 chains of 3-input max.
+template <int SN, bool NEG>
+__device__ __forceinline__ float group_max(const uint32_t (&s)[SN], int groups) {
+  auto f = [](uint32_t v) { return __uint_as_float(v); };
+  float a[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) a[e] = NEG ? fminf(f(s[2 * e]), f(s[2 * e + 1])) : fmaxf(f(s[2 * e]), f(s[2 * e + 1]));
+#pragma unroll
+  for (int gg = 1; gg < SN / 16; ++gg)
+    if (gg < groups) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        a[e] = NEG ? fmin3(a[e], f(s[16 * gg + 2 * e]), f(s[16 * gg + 2 * e + 1]))
+                   : fmax3(a[e], f(s[16 * gg + 2 * e]), f(s[16 * gg + 2 * e + 1]));
+    }
+  return NEG ? fmin3(fmin3(a[0], a[1], a[2]), fmin3(a[3], a[4], a[5]), fminf(a[6], a[7]))
+             : fmax3(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
+}
+
+template <int DP, int SN, bool BF16>
+__global__ void __launch_bounds__(ShortCfg<DP, SN>::THREADS, 1)
     fmha_short_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                             const __grid_constant__ CUtensorMap tm_k,
                             const __grid_constant__ CUtensorMap tm_v,
                             const __grid_constant__ CUtensorMap tm_o, const ShortParams p) {
-  using C = ShortCfg<DP>;
+  using C = ShortCfg<DP, SN>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
   const uint32_t base = (raw_base + 1023u) & ~1023u;
@@ -118,232 +158,232 @@ __global__ void __launch_bounds__(320, 1)
   auto bar = [&](int i) -> uint32_t { return base + C::OFF_BAR + 8u * i; };
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+  const WaitCtl ctl{abort_flag, p.dev_flags, p.timeout_ns};
 
   // This CTA's tiles: [t_begin, t_end) of the flattened (batch, head, row tile) order.
   const int t_begin = static_cast<int>(static_cast<long long>(blockIdx.x) * p.n_tiles / gridDim.x);
   const int t_end = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * p.n_tiles / gridDim.x);
   const int n = t_end - t_begin;
 
-  if (threadIdx.x == 0) {
-    mbar_init(bar(C::B_KVFULL), 1);
-    mbar_init(bar(C::B_KVEMPTY), 1);
+  // ---- producer state (lane 0 of the TMA warp) ----
+  int pi = 0;         // next tile to load
+  int phead = -1;     // index (within this CTA's range) of the last head whose K/V was loaded
+  int pq_issued = 0;  // Q tiles loaded so far
+  bool pok = true;
+  TileCursor pcur;
+  // Loads tiles from pi on.  With prologue set it stops before the first wait (a Q stage or a K/V
+  // buffer still in use), so that it can run before the CTA-wide barrier.
+  auto produce = [&](bool prologue) {
+    for (; pok && pi < n; ++pi, pcur.step(1, p)) {
+      const bool new_head = pi == 0 || pcur.qt == 0;
+      if (prologue && (pi >= C::NQ || (new_head && phead + 1 >= C::NKV))) return;
+      if (new_head) {
+        const int hx = phead + 1, kb = hx % C::NKV;
+        // The buffer's previous head (hx - NKV) must be released by every MMA reading it.
+        if (hx >= C::NKV &&
+            !(pok = mbar_wait(bar(C::B_KVEMPTY + kb), static_cast<uint32_t>(hx / C::NKV - 1) & 1u, ctl)))
+          return;
+        phead = hx;
+        const uint32_t kv = base + C::OFF_KV + kb * 2 * C::TILE_BYTES;
+        mbar_arrive_expect_tx(bar(C::B_KVFULL + kb), 2 * C::TILE_BYTES);
+        for (int c = 0; c < C::NCH; ++c) {
+          tma_load_4d(kv + c * C::CH_BYTES, &tm_k, bar(C::B_KVFULL + kb), c * 64, 0, pcur.h / p.group, pcur.b);
+          tma_load_4d(kv + C::TILE_BYTES + c * C::CH_BYTES, &tm_v, bar(C::B_KVFULL + kb), c * 64, 0,
+                      pcur.h / p.group, pcur.b);
+        }
+      }
+      const int st = pi % C::NQ;
+      const int rnd = pi / C::NQ;
+      // The stage's previous tile (pi - NQ) must have stored its O from it.
+      if (rnd > 0 && !(pok = mbar_wait(bar(C::B_QEMPTY + st), static_cast<uint32_t>(rnd - 1) & 1u, ctl)))
+        return;
+      mbar_arrive_expect_tx(bar(C::B_QFULL + st), C::TILE_BYTES);
+      for (int c = 0; c < C::NCH; ++c)
+        tma_load_4d(base + C::OFF_Q + st * C::TILE_BYTES + c * C::CH_BYTES, &tm_q, bar(C::B_QFULL + st),
+                    c * 64, pcur.qt * C::BM, pcur.h, pcur.b);
+      pq_issued = pi + 1;
+    }
+  };
+
+  if (warp == C::W_TMA && lane == 0) {
+    for (int i = 0; i < C::NKV; ++i) {
+      mbar_init(bar(C::B_KVFULL + i), 1);
+      mbar_init(bar(C::B_KVEMPTY + i), 1);
+    }
     for (int s = 0; s < C::NQ; ++s) {
       mbar_init(bar(C::B_QFULL + s), 1);
-      mbar_init(bar(C::B_QEMPTY + s), 1);
+      mbar_init(bar(C::B_QEMPTY + s), 4);  // one arrival per warp of the storing warpgroup
     }
-    mbar_init(bar(C::B_SFREE), 128);
-    for (int g = 0; g < 2; ++g) {
+    for (int g = 0; g < C::NSLOT; ++g) {
       mbar_init(bar(C::B_SFULL + g), 1);
       mbar_init(bar(C::B_PREADY + g), 128);
       mbar_init(bar(C::B_PVDONE + g), 1);
-      mbar_init(bar(C::B_OFREE + g), 128);
     }
     mbar_init(bar(C::B_DRAIN), 1);
     *abort_flag = 0;
     fence_mbarrier_init();
+    fence_proxy_async_smem();  // the initialised barriers are visible to this thread's copies
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+    tma_prefetch_desc(&tm_o);
+    pcur.init(t_begin, p);
+    produce(true);
   }
   if (warp == C::W_MMA) {
     tmem_alloc(smem_u32(tmem_holder), C::TMEM_COLS);
     tmem_relinquish();
   }
-  if (warp == C::W_TMA && lane == 0) {
-    tma_prefetch_desc(&tm_q);
-    tma_prefetch_desc(&tm_k);
-    tma_prefetch_desc(&tm_v);
-    tma_prefetch_desc(&tm_o);
-  }
   tc_fence_before_sync();
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem = *tmem_holder;
-  const WaitCtl ctl{abort_flag, p.dev_flags, p.timeout_ns};
 
   if (warp == C::W_TMA) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      int kv_round = 0, issued = 0;
-      bool ok = true;
-      TileCursor cur;
-      cur.init(t_begin, p);
-      for (int i = 0; ok && i < n; ++i, cur.step(1, p)) {
-        const int b = cur.b, h = cur.h;
-        if (i == 0 || cur.qt == 0) {  // first tile, or the first tile of a new head
-          // K/V of a new head: wait until every MMA reading the previous head's K/V is done.
-          if (kv_round > 0 &&
-              !(ok = mbar_wait(bar(C::B_KVEMPTY), static_cast<uint32_t>(kv_round - 1) & 1u, ctl)))
-            break;
-          mbar_arrive_expect_tx(bar(C::B_KVFULL), 2 * C::TILE_BYTES);
-          for (int c = 0; c < C::NCH; ++c) {
-            tma_load_4d(base + C::OFF_K + c * C::CH_BYTES, &tm_k, bar(C::B_KVFULL), c * 64, 0, h / p.group, b);
-            tma_load_4d(base + C::OFF_V + c * C::CH_BYTES, &tm_v, bar(C::B_KVFULL), c * 64, 0, h / p.group, b);
-          }
-          ++kv_round;
-        }
-        const int st = i % C::NQ;
-        const uint32_t rnd = static_cast<uint32_t>(i / C::NQ);
-        if (!(ok = mbar_wait(bar(C::B_QEMPTY + st), (rnd & 1u) ^ 1u, ctl))) break;
-        mbar_arrive_expect_tx(bar(C::B_QFULL + st), C::TILE_BYTES);
-        for (int c = 0; c < C::NCH; ++c)
-          tma_load_4d(base + C::OFF_Q + st * C::TILE_BYTES + c * C::CH_BYTES, &tm_q,
-                      bar(C::B_QFULL + st), c * 64, cur.qt * C::BM, h, b);
-        issued = i + 1;
-      }
+      produce(false);
       if (*abort_flag) {
-        // Let every copy still in flight land before shared memory goes away.
-        for (int i = max(0, issued - C::NQ); i < issued; ++i)
-          mbar_wait_drain(bar(C::B_QFULL + i % C::NQ), static_cast<uint32_t>(i / C::NQ) & 1u,
+        // Let every copy still in flight land before shared memory goes away: the last load
+        // issued into each Q stage and each K/V buffer.
+        for (int i = max(0, pq_issued - C::NQ); i < pq_issued; ++i)
+          mbar_wait_drain(bar(C::B_QFULL + i % C::NQ), static_cast<uint32_t>(i / C::NQ) & 1u, p.timeout_ns);
+        for (int hx = max(0, phead - C::NKV + 1); hx <= phead; ++hx)
+          mbar_wait_drain(bar(C::B_KVFULL + hx % C::NKV), static_cast<uint32_t>(hx / C::NKV) & 1u,
                           p.timeout_ns);
-        if (kv_round > 0)
-          mbar_wait_drain(bar(C::B_KVFULL), static_cast<uint32_t>(kv_round - 1) & 1u, p.timeout_ns);
       }
     }
   } else if (warp == C::W_MMA) {
     // ------------------------------------------------------------------ MMA issuer
     // Warp-uniform control flow; one elected lane issues the MMAs and commits (the *_w helpers).
-    constexpr uint32_t kIdescQK = idesc_f16(128, 128, BF16 ? 1 : 0, 0, 0);
+    // The warp polls the inputs of the next P V and of the next Q K^T and issues whichever is
+    // ready first.
+    constexpr uint32_t kIdescQK = idesc_f16(128, SN, BF16 ? 1 : 0, 0, 0);
     constexpr uint32_t kIdescPV = idesc_f16(128, DP, BF16 ? 1 : 0, 0, 1);
-    auto issue_qk = [&](int st) {
-      const uint32_t q_addr = base + C::OFF_Q + st * C::TILE_BYTES;
-      const uint32_t k_addr = base + C::OFF_K;
+    auto ready = [&](uint32_t b, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, mbar_test_wait(b, parity));
+    };
+    TileCursor cq, cv;  // tiles of the next QK and of the next PV
+    cq.init(t_begin, p);
+    cv.init(t_begin, p);
+    int j = 0, ip = 0;     // next QK, next PV
+    int hq = -1, hv = -1;  // head index (within the range) of the last QK / PV issued
+    int released = 0;      // heads whose K/V buffer has been released
+    bool ok = true;
+    uint64_t t_idle = global_timer_ns();
+    while (ok && ip < n) {
+      bool progress = false;
+      // O = P V of the oldest tile whose P is written.
+      if (ip < j && ready(bar(C::B_PREADY + ip % C::NSLOT), static_cast<uint32_t>(ip / C::NSLOT) & 1u)) {
+        const int slot = ip % C::NSLOT;
+        if (ip == 0 || cv.qt == 0) ++hv;
+        tc_fence_after_sync();
+        const uint32_t p_tmem = tmem + slot * C::SLOT_COLS;  // P, over the slot's S
+        const uint32_t v_addr = base + C::OFF_KV + (hv % C::NKV) * 2 * C::TILE_BYTES + C::TILE_BYTES;
 #pragma unroll
-      for (int k = 0; k < DP / 16; ++k) {
-        const uint32_t off = (k >> 2) * C::CH_BYTES + (k & 3) * 32;
-        umma_ss_w(tmem + C::TM_S, smem_desc_sw128(q_addr + off, 16, 1024),
-                  smem_desc_sw128(k_addr + off, 16, 1024), kIdescQK, k > 0 ? 1u : 0u);
+        for (int k = 0; k < SN / 16; ++k) {
+          if (k < p.pv_steps)
+            umma_ts_w(p_tmem + SN, p_tmem + k * 8, smem_desc_sw128(v_addr + k * 2048, C::CH_BYTES, 1024),
+                      kIdescPV, k > 0 ? 1u : 0u);
+        }
+        umma_commit_w(bar(C::B_PVDONE + slot));
+        if (ip + 1 == n || cv.last_of_head(p)) {
+          umma_commit_w(bar(C::B_KVEMPTY + hv % C::NKV));  // the last MMA reading this head's K/V
+          ++released;
+        }
+        ++ip;
+        cv.step(1, p);
+        progress = true;
       }
-    };
-    auto issue_pv = [&](int g) {
-      const uint32_t p_tmem = tmem + (g ? C::TM_P1 : C::TM_P0);
-      const uint32_t d_tmem = tmem + (g ? C::TM_O1 : C::TM_O0);
-      const uint32_t v_addr = base + C::OFF_V;
+      // S = Q K^T of the next tile, into its slot.  Its head's K/V buffer must hold that head (a
+      // buffer is reloaded only after the head before it was released), the slot's previous P V
+      // must have finished reading P (which S overwrites), and the Q tile must have landed.
+      if (j < n && j < ip + C::NSLOT) {
+        const int slot = j % C::NSLOT;
+        const int h_next = (j == 0 || cq.qt == 0) ? hq + 1 : hq;
+        if (h_next < released + C::NKV &&
+            ready(bar(C::B_KVFULL + h_next % C::NKV), static_cast<uint32_t>(h_next / C::NKV) & 1u) &&
+            (j < C::NSLOT ||
+             ready(bar(C::B_PVDONE + slot), static_cast<uint32_t>((j - C::NSLOT) / C::NSLOT) & 1u)) &&
+            ready(bar(C::B_QFULL + j % C::NQ), static_cast<uint32_t>(j / C::NQ) & 1u)) {
+          hq = h_next;
+          tc_fence_after_sync();
+          const uint32_t q_addr = base + C::OFF_Q + (j % C::NQ) * C::TILE_BYTES;
+          const uint32_t k_addr = base + C::OFF_KV + (hq % C::NKV) * 2 * C::TILE_BYTES;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        if (k < p.pv_steps)
-          umma_ts_w(d_tmem, p_tmem + k * 8, smem_desc_sw128(v_addr + k * 2048, C::CH_BYTES, 1024),
-                    kIdescPV, k > 0 ? 1u : 0u);
+          for (int k = 0; k < DP / 16; ++k) {
+            const uint32_t off = (k >> 2) * C::CH_BYTES + (k & 3) * 32;
+            umma_ss_w(tmem + slot * C::SLOT_COLS, smem_desc_sw128(q_addr + off, 16, 1024),
+                      smem_desc_sw128(k_addr + off, 16, 1024), kIdescQK, k > 0 ? 1u : 0u);
+          }
+          umma_commit_w(bar(C::B_SFULL + slot));
+          ++j;
+          cq.step(1, p);
+          progress = true;
+        }
       }
-    };
-    // QK of tile i (the S buffer must have been read by tile i-1's softmax).
-    auto start_qk = [&](int i, uint32_t& n_sfree) -> bool {
-      if (i > 0 && !mbar_wait_all(bar(C::B_SFREE), (n_sfree++) & 1u, ctl)) return false;
-      const int st = i % C::NQ;
-      if (!mbar_wait_all(bar(C::B_QFULL + st), static_cast<uint32_t>(i / C::NQ) & 1u, ctl)) return false;
-      tc_fence_after_sync();
-      issue_qk(st);
-      umma_commit_w(bar(C::B_SFULL + (i & 1)));
-      umma_commit_w(bar(C::B_QEMPTY + st));
-      return true;
-    };
-    bool ok = n > 0;
-    int kv_round = 0;
-    uint32_t n_sfree = 0;
-    if (ok) {
-      ok = mbar_wait_all(bar(C::B_KVFULL), 0u, ctl);
-      kv_round = 1;
-      ok = ok && start_qk(0, n_sfree);
-    }
-    TileCursor cur;
-    cur.init(t_begin, p);
-    for (int i = 0; ok && i < n; ++i, cur.step(1, p)) {
-      const int g = i & 1;
-      const bool next = i + 1 < n;
-      const bool same_head = next && !cur.last_of_head(p);
-      if (same_head && !(ok = start_qk(i + 1, n_sfree))) break;
-      if (!(ok = mbar_wait_all(bar(C::B_PREADY + g), static_cast<uint32_t>(i >> 1) & 1u, ctl))) break;
-      // O_g is overwritten: the epilogue of tile i-2 must have read it.
-      if (i >= 2 &&
-          !(ok = mbar_wait_all(bar(C::B_OFREE + g), static_cast<uint32_t>((i - 2) >> 1) & 1u, ctl)))
-        break;
-      tc_fence_after_sync();
-      issue_pv(g);
-      umma_commit_w(bar(C::B_PVDONE + g));
-      if (next && !same_head) {
-        // Tile i+1 belongs to another head: release K/V once every MMA so far is done, then
-        // wait for the new head's K/V.
-        umma_commit_w(bar(C::B_KVEMPTY));
-        if (!(ok = mbar_wait_all(bar(C::B_KVFULL), static_cast<uint32_t>(kv_round) & 1u, ctl))) break;
-        ++kv_round;
-        if (!(ok = start_qk(i + 1, n_sfree))) break;
+      if (progress) {
+        t_idle = global_timer_ns();
+      } else {
+        if (*abort_flag) {
+          ok = false;
+          break;
+        }
+        if (global_timer_ns() - t_idle > p.timeout_ns) {
+          if (lane == 0) {
+            *abort_flag = 1;
+            atomicOr(p.dev_flags, 1u /* CMPX_DEVFLAG_WAIT_TIMEOUT */);
+          }
+          ok = false;
+          break;
+        }
+        __nanosleep(32);
       }
     }
   } else {
     // ------------------------------------------------------------------ softmax / epilogue
-    const int g = warp >> 2;            // warpgroup: tiles i with i % 2 == g
-    const int wq = warp & 3;            // TMEM lane quarter of this warp
-    const int row = wq * 32 + lane;     // row inside the tile
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16);
-    const uint32_t s_tm = lane_base + C::TM_S;
-    const uint32_t p_tm = lane_base + (g ? C::TM_P1 : C::TM_P0);
-    const uint32_t o_tm = lane_base + (g ? C::TM_O1 : C::TM_O0);
+    const int g = warp >> 2;         // warpgroup = TMEM slot: tiles i with i % NSLOT == g
+    const int wq = warp & 3;         // TMEM lane quarter of this warp
+    const int row = wq * 32 + lane;  // row inside the tile
+    const uint32_t s_tm = tmem + (static_cast<uint32_t>(wq * 32) << 16) + g * C::SLOT_COLS;  // S, P
+    const uint32_t o_tm = s_tm + SN;
     const float sl2 = p.scale_log2;
     const float masked = p.neg_scale ? INFINITY : -INFINITY;  // masked * sl2 == -inf
-    const int p_chunks = (p.pv_steps + 1) >> 1;  // 32-key chunks of P that the PV reads
-    const uint32_t stage = base + C::OFF_OST + g * C::TILE_BYTES;
+    const int groups = p.pv_steps;  // 16-key groups of P that the PV reads
     bool ok = true;
     TileCursor cur;
     cur.init(t_begin + g, p);
-    for (int i = g; ok && i < n; i += 2, cur.step(2, p)) {
-      const uint32_t par = static_cast<uint32_t>(i >> 1) & 1u;
+    for (int i = g; ok && i < n; i += C::NSLOT, cur.step(C::NSLOT, p)) {
+      const uint32_t par = static_cast<uint32_t>(i / C::NSLOT) & 1u;
       if (!(ok = mbar_wait_all(bar(C::B_SFULL + g), par, ctl))) break;
       tc_fence_after_sync();
-      uint32_t sr[128];
-      tmem_ld128(s_tm, sr);
-      float* s = reinterpret_cast<float*>(sr);
-      tc_fence_before_sync();
-      mbar_arrive(bar(C::B_SFREE));  // S is in registers: the next tile's QK may overwrite it
-      // Only the first p_chunks 32-key chunks are used; mask keys >= Lk inside the partial one.
+      uint32_t s[SN];
+      load_scores<SN>(s_tm, s);
+      // Keys >= Lk inside the last group that holds keys are masked (written as a range test over
+      // the groups from the last used one on: an equality test lets the compiler fold the loop into
+      // one runtime-indexed access, which moves the whole row to local memory).
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        if (q < p_chunks && (q + 1) * 32 > p.len_k) {
+      for (int gg = 0; gg < SN / 16; ++gg) {
+        if (gg + 1 >= groups) {
 #pragma unroll
-          for (int c = 0; c < 32; ++c)
-            if (q * 32 + c >= p.len_k) s[q * 32 + c] = masked;
+          for (int c = 0; c < 16; ++c)
+            if (gg * 16 + c >= p.len_k) s[gg * 16 + c] = __float_as_uint(masked);
         }
       }
-      // Exact row max (min for a negative scale) over the used chunks, 8 chains of 3-input max.
-      float a[8];
-      if (p.neg_scale) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) a[e] = fmin3(s[2 * e], s[2 * e + 1], s[16 + 2 * e]);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) a[e] = fminf(a[e], s[16 + 2 * e + 1]);
-#pragma unroll
-        for (int q = 1; q < 4; ++q)
-          if (q < p_chunks) {
-#pragma unroll
-            for (int c = 0; c < 32; c += 16)
-#pragma unroll
-              for (int e = 0; e < 8; ++e) a[e] = fmin3(a[e], s[q * 32 + c + 2 * e], s[q * 32 + c + 2 * e + 1]);
-          }
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) a[e] = fmax3(s[2 * e], s[2 * e + 1], s[16 + 2 * e]);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) a[e] = fmaxf(a[e], s[16 + 2 * e + 1]);
-#pragma unroll
-        for (int q = 1; q < 4; ++q)
-          if (q < p_chunks) {
-#pragma unroll
-            for (int c = 0; c < 32; c += 16)
-#pragma unroll
-              for (int e = 0; e < 8; ++e) a[e] = fmax3(a[e], s[q * 32 + c + 2 * e], s[q * 32 + c + 2 * e + 1]);
-          }
-      }
-      const float mx = p.neg_scale ? fmin3(fmin3(a[0], a[1], a[2]), fmin3(a[3], a[4], a[5]), fminf(a[6], a[7]))
-                                   : fmax3(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
-      const float m = mx * sl2;
-      // p = 2^(s*sl2 - m), 16-bit pairs to TMEM, chunk by chunk (only the chunks the PV reads).
-      const uint64_t sl2x2 = f2_pack(sl2, sl2), nmx2 = f2_pack(-m, -m);
+      // Exact row max (min for a negative scale), then p = 2^(s*sl2 - m) group by group: 16-bit
+      // pairs written over the group's S columns, the row sum in fp32.
+      const float mx = p.neg_scale ? group_max<SN, true>(s, groups) : group_max<SN, false>(s, groups);
+      const uint64_t sl2x2 = f2_pack(sl2, sl2), nmx2 = f2_pack(-mx * sl2, -mx * sl2);
       uint64_t la = f2_pack(0.f, 0.f), lb = la;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        if (q < p_chunks) {
-          uint32_t pk[16];
+      for (int gg = 0; gg < SN / 16; ++gg) {
+        if (gg < groups) {
+          uint32_t pk[8];
 #pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const int cc = q * 16 + c;
+          for (int c = 0; c < 8; ++c) {
+            const int k = gg * 16 + 2 * c;
             float x0, x1;
-            f2_unpack(f2_fma(f2_pack(s[2 * cc], s[2 * cc + 1]), sl2x2, nmx2), x0, x1);
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(s[k]), __uint_as_float(s[k + 1])), sl2x2, nmx2), x0, x1);
             const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
             if (c & 1)
               lb = f2_add(lb, f2_pack(p0, p1));
@@ -351,7 +391,7 @@ __global__ void __launch_bounds__(320, 1)
               la = f2_add(la, f2_pack(p0, p1));
             pk[c] = BF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
           }
-          tmem_st16(p_tm + q * 16, pk);
+          tmem_st8(s_tm + gg * 8, pk);
         }
       }
       float l0, l1;
@@ -361,13 +401,13 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_before_sync();
       mbar_arrive(bar(C::B_PREADY + g));
 
-      // Epilogue: O / l, 16-bit, through this warpgroup's staging tile, TMA stores per warp.
+      // Epilogue: O / l, 16-bit, staged in the tile's own Q stage (its Q was read by the QK, which
+      // completed before S was handed over), TMA stores per warp, then the stage goes back to the
+      // producer.
       if (!(ok = mbar_wait_all(bar(C::B_PVDONE + g), par, ctl))) break;
       tc_fence_after_sync();
-      if (i >= 2) {  // this warp's staging rows: the store of tile i-2 must have read them
-        if (lane == 0) bulk_wait_group_read0();
-        __syncwarp();
-      }
+      const int st = i % C::NQ;
+      const uint32_t stage = base + C::OFF_Q + st * C::TILE_BYTES;
 #pragma unroll 1
       for (int c = 0; c < C::NCH; ++c) {
         const uint32_t row_addr = stage + c * C::CH_BYTES + row * 128;
@@ -375,10 +415,6 @@ __global__ void __launch_bounds__(320, 1)
         for (int hh = 0; hh < 2; ++hh) {
           uint32_t o[32];
           tmem_ld32(o_tm + c * 64 + hh * 32, o);
-          if (c == C::NCH - 1 && hh == 1) {
-            tc_fence_before_sync();
-            mbar_arrive(bar(C::B_OFREE + g));  // O_g is read: tile i+2's PV may overwrite it
-          }
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint32_t wv[4];
@@ -393,6 +429,7 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
       }
+      tc_fence_before_sync();  // O is read: the slot's next P V (after this warpgroup's next P) may write it
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
@@ -402,6 +439,8 @@ __global__ void __launch_bounds__(320, 1)
             tma_store_4d(&tm_o, stage + c * C::CH_BYTES + wq * 32 * 128, c * 64, row0, cur.h, cur.b);
         }
         bulk_commit_group();
+        bulk_wait_group_read0();  // the store has read the stage: it may take the next Q tile
+        mbar_arrive(bar(C::B_QEMPTY + st));
       }
       __syncwarp();
     }
@@ -430,20 +469,17 @@ bool fmha_short_eligible(const cmpx_attn_desc* d) {
          d->len_k <= 128 && d->len_q > 0 && d->head_dim <= 128 && !d->mask;
 }
 
-const char* fmha_short_name(const cmpx_attn_desc* d) {
-  const bool bf = d->dtype == CMPX_BF16;
-  if (d->head_dim <= 64)
-    return bf ? "fmha_sm100_short<bf16,D64,128q,kv<=128,6st,streamed>"
-              : "fmha_sm100_short<f16,D64,128q,kv<=128,6st,streamed>";
-  return bf ? "fmha_sm100_short<bf16,D128,128q,kv<=128,3st,streamed>"
-            : "fmha_sm100_short<f16,D128,128q,kv<=128,3st,streamed>";
-}
-
 namespace {
 
-template <int DP, bool BF16>
+// S columns of a tile slot: the key count rounded up to 64 / 96 / 128 (D <= 64); 128 for D = 128.
+int short_sn(const cmpx_attn_desc* d) {
+  if (d->head_dim > 64) return 128;
+  return d->len_k <= 64 ? 64 : d->len_k <= 96 ? 96 : 128;
+}
+
+template <int DP, int SN, bool BF16>
 int launch_short_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
-  using C = ShortCfg<DP>;
+  using C = ShortCfg<DP, SN>;
   const CUtensorMapDataType dt =
       BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap tq, tk, tv, to;
@@ -454,14 +490,15 @@ int launch_short_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
     return CMPX_ERR_LAUNCH;
 
   static std::once_flag once[64];
+  static cudaError_t attr_err[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  cudaError_t attr_err = cudaSuccess;
   std::call_once(once[dev & 63], [&] {
-    attr_err = cudaFuncSetAttribute(reinterpret_cast<const void*>(&fmha_short_sm100_kernel<DP, BF16>),
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    attr_err[dev & 63] = cudaFuncSetAttribute(
+        reinterpret_cast<const void*>(&fmha_short_sm100_kernel<DP, SN, BF16>),
+        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   });
-  if (attr_err != cudaSuccess) return CMPX_ERR_LAUNCH;
+  if (attr_err[dev & 63] != cudaSuccess) return CMPX_ERR_LAUNCH;
 
   ShortParams p;
   p.heads = static_cast<int>(d->heads);
@@ -476,16 +513,35 @@ int launch_short_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   p.timeout_ns = ctx.timeout_ns;
   p.dev_flags = ctx.dev_flags;
   const int grid = std::min(p.n_tiles, std::max(1, ctx.num_sms));
-  fmha_short_sm100_kernel<DP, BF16><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, to, p);
+  fmha_short_sm100_kernel<DP, SN, BF16><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, to, p);
   return cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
 }
 
 }  // namespace
 
+const char* fmha_short_name(const cmpx_attn_desc* d) {
+  static const char* const names[2][4] = {
+      {"fmha_sm100_short<f16,D64,S64,4slot,8st,streamed>", "fmha_sm100_short<f16,D64,S96,3slot,8st,streamed>",
+       "fmha_sm100_short<f16,D64,S128,2slot,8st,streamed>", "fmha_sm100_short<f16,D128,S128,2slot,4st,streamed>"},
+      {"fmha_sm100_short<bf16,D64,S64,4slot,8st,streamed>", "fmha_sm100_short<bf16,D64,S96,3slot,8st,streamed>",
+       "fmha_sm100_short<bf16,D64,S128,2slot,8st,streamed>",
+       "fmha_sm100_short<bf16,D128,S128,2slot,4st,streamed>"}};
+  const int sn = short_sn(d);
+  const int e = d->head_dim > 64 ? 3 : sn == 64 ? 0 : sn == 96 ? 1 : 2;
+  return names[d->dtype == CMPX_BF16 ? 1 : 0][e];
+}
+
 int launch_fmha_short(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   const bool bf = d->dtype == CMPX_BF16;
-  if (d->head_dim <= 64) return bf ? launch_short_typed<64, true>(d, ctx) : launch_short_typed<64, false>(d, ctx);
-  return bf ? launch_short_typed<128, true>(d, ctx) : launch_short_typed<128, false>(d, ctx);
+  if (d->head_dim > 64) return bf ? launch_short_typed<128, 128, true>(d, ctx) : launch_short_typed<128, 128, false>(d, ctx);
+  switch (short_sn(d)) {
+    case 64:
+      return bf ? launch_short_typed<64, 64, true>(d, ctx) : launch_short_typed<64, 64, false>(d, ctx);
+    case 96:
+      return bf ? launch_short_typed<64, 96, true>(d, ctx) : launch_short_typed<64, 96, false>(d, ctx);
+    default:
+      return bf ? launch_short_typed<64, 128, true>(d, ctx) : launch_short_typed<64, 128, false>(d, ctx);
+  }
 }
 
 }  // namespace cmpx

@@ -416,6 +416,11 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       CMPX_W8(0), CMPX_W8(8)
       : "memory");
 }
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+               CMPX_W8(0)
+               : "memory");
+}
 #undef CMPX_W8
 
 __device__ __forceinline__ void tmem_st_wait() {
