@@ -16,16 +16,21 @@
 //     rounded up to 64 / 96 / 128), with P (16-bit pairs) written over S, then O (DP columns).
 //     D = 64 with Lk <= 64 / 96 / 128 gives 4 / 3 / 2 tiles in flight; D = 128 gives 2;
 //   * the producer warp keeps a ring of Q tiles in flight (8 stages for D <= 64, 4 for D = 128);
-//     it sets up the barriers and issues its first loads before the CTA-wide barrier, so they
-//     overlap the TMEM allocation and the other warps' start;
-//   * the MMA warp polls its inputs and issues whichever product is ready: O = P V of the oldest
-//     tile whose P is written (over only the K=16 key steps that hold keys), or S = Q K^T of the
-//     next tile once its slot's previous P V has finished reading P;
+//     it sets up the barriers those loads need, issues its first loads, and only then sets up the
+//     other barriers, all before the CTA-wide barrier, so the first loads leave as early as possible
+//     and overlap the TMEM allocation and the other warps' start;
+//   * the MMA warp issues S = Q K^T of each tile into its slot, as soon as the Q tile has landed and
+//     the slot's previous tile is retired (its O = P V, which reads P from the S columns, is done),
+//     and retires tiles in order: once the last tile of a head is retired, that head's K/V buffer
+//     goes back to the producer;
 //   * softmax warpgroup g takes tiles i with i % NSLOT == g, thread = row: one exact pass (row max
 //     and the exponentials only over the 16-key groups that hold keys; no running max is needed
-//     with a single key tile); then the epilogue O / l, which stages the 16-bit O tile in the Q
-//     ring slot the tile was loaded into (its Q is dead once S is computed) and stores it with TMA
-//     (clipped at Lq and D), then hands the slot back to the producer.
+//     with a single key tile); then the warpgroup meets at an mbarrier and one of its threads
+//     issues O = P V itself (over only the K=16 key steps that hold keys), so no other warp has to
+//     notice that P is ready; then the epilogue O / l, which stages the 16-bit O tile in the same Q
+//     stage and stores it with TMA (clipped at Lq and D).  The stage goes back to the producer one
+//     tile later, once the store has surely read it, so the wait for that read is off the path.
+//     Meanwhile the MMA warp already computes the slot's next S.
 //
 // Every wait is bounded (cmpx_ptx.cuh); on a timeout the CTA drains its copies and MMAs, frees
 // TMEM, raises the device status word and returns.
@@ -50,9 +55,10 @@ struct ShortCfg {
   static constexpr int SLOT_COLS = SN + DP;          // TMEM columns of one tile: S (and P), then O
   static constexpr int NSLOT = 512 / SLOT_COLS < 4 ? 512 / SLOT_COLS : 4;
   static constexpr int NKV = DP <= 64 ? 2 : 1;       // K/V buffers
+  static constexpr int KV_BYTES = NKV * 2 * TILE_BYTES;
   static constexpr int NQ = DP <= 64 ? 8 : 4;        // Q ring stages (each also stages its tile's O)
   static constexpr int OFF_KV = 0;                   // [NKV] x {K, V}
-  static constexpr int OFF_Q = OFF_KV + NKV * 2 * TILE_BYTES;
+  static constexpr int OFF_Q = OFF_KV + KV_BYTES;
   static constexpr int OFF_BAR = OFF_Q + NQ * TILE_BYTES;
   static constexpr int B_KVFULL = 0;                   // [NKV] K and V of a head landed
   static constexpr int B_KVEMPTY = B_KVFULL + NKV;     // [NKV] every MMA reading that head's K/V done
@@ -61,8 +67,8 @@ struct ShortCfg {
   static constexpr int B_SFULL = B_QEMPTY + NQ;        // [NSLOT] S = Q K^T complete
   static constexpr int B_PREADY = B_SFULL + NSLOT;     // [NSLOT] P written (count 128)
   static constexpr int B_PVDONE = B_PREADY + NSLOT;    // [NSLOT] O = P V complete
-  static constexpr int B_DRAIN = B_PVDONE + NSLOT;
-  static constexpr int NBAR = B_DRAIN + 1;
+  static constexpr int B_DRAIN = B_PVDONE + NSLOT;     // [1 + NSLOT] clean-up after an abort
+  static constexpr int NBAR = B_DRAIN + 1 + NSLOT;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // tmem base, abort word
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // +1024: runtime alignment slack
   static constexpr int TMEM_COLS = 512;
@@ -70,7 +76,7 @@ struct ShortCfg {
   static constexpr int THREADS = 128 * NSLOT + 64;
   static_assert(NSLOT >= 2 && NSLOT * SLOT_COLS <= TMEM_COLS, "TMEM slots");
   static_assert(SLOT_COLS % 32 == 0, "slot bases on 32-column boundaries");
-  static_assert(SMEM_BYTES <= 232448, "shared memory");
+  static_assert(SMEM_BYTES <= 232448 && NQ >= NSLOT + 1, "shared memory");
 };
 
 struct ShortParams {
@@ -91,16 +97,19 @@ struct ShortParams {
 // without integer division (one division per role at start).
 struct TileCursor {
   int qt, h, b;  // row tile, head, batch
+  int hidx;      // heads entered since the cursor was initialised (K/V buffer = hidx % NKV)
   __device__ void init(int t, const ShortParams& p) {
     const int bh = t / p.n_qt;
     qt = t - bh * p.n_qt;
     b = bh / p.heads;
     h = bh - b * p.heads;
+    hidx = 0;
   }
   __device__ void step(int k, const ShortParams& p) {
     qt += k;
     while (qt >= p.n_qt) {
       qt -= p.n_qt;
+      ++hidx;
       if (++h == p.heads) {
         h = 0;
         ++b;
@@ -139,6 +148,23 @@ __device__ __forceinline__ float group_max(const uint32_t (&s)[SN], int groups) 
     }
   return NEG ? fmin3(fmin3(a[0], a[1], a[2]), fmin3(a[3], a[4], a[5]), fminf(a[6], a[7]))
              : fmax3(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
+}
+
+// O = P V over the first `groups` K=16 key steps: P from TMEM (16-bit pairs, 8 columns per step), V
+// MN-major in shared memory.  The step count is dispatched once to a straight-line sequence of
+// exactly that many MMAs: measured on B200, a runtime guard around each MMA raised the issue cost
+// from ~28 to ~90 clk per 128x64x16 MMA.
+template <int G, int DP, bool BF16>
+__device__ __forceinline__ void issue_pv(int groups, uint32_t o_tmem, uint32_t p_tmem, uint32_t v_addr) {
+  constexpr uint32_t kIdescPV = idesc_f16(128, DP, BF16 ? 1 : 0, 0, 1);  // P K-major, V MN-major
+  if (groups == G) {
+#pragma unroll
+    for (int k = 0; k < G; ++k)
+      umma_ts_w(o_tmem, p_tmem + k * 8, smem_desc_sw128(v_addr + k * 2048, 128 * 128, 1024),
+                kIdescPV, k > 0 ? 1u : 0u);
+  } else if constexpr (G > 1) {
+    issue_pv<G - 1, DP, BF16>(groups, o_tmem, p_tmem, v_addr);
+  }
 }
 
 template <int DP, int SN, bool BF16>
@@ -206,29 +232,24 @@ __global__ void __launch_bounds__(ShortCfg<DP, SN>::THREADS, 1)
   };
 
   if (warp == C::W_TMA && lane == 0) {
-    for (int i = 0; i < C::NKV; ++i) {
-      mbar_init(bar(C::B_KVFULL + i), 1);
-      mbar_init(bar(C::B_KVEMPTY + i), 1);
-    }
-    for (int s = 0; s < C::NQ; ++s) {
-      mbar_init(bar(C::B_QFULL + s), 1);
-      mbar_init(bar(C::B_QEMPTY + s), 4);  // one arrival per warp of the storing warpgroup
-    }
+    // The barriers the first loads complete on, then the loads, then every other barrier.
+    for (int i = 0; i < C::NKV; ++i) mbar_init(bar(C::B_KVFULL + i), 1);
+    for (int s = 0; s < C::NQ; ++s) mbar_init(bar(C::B_QFULL + s), 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    fence_proxy_async_smem();  // the initialised barriers are visible to this thread's copies
+    pcur.init(t_begin, p);
+    produce(true);
+    for (int i = 0; i < C::NKV; ++i) mbar_init(bar(C::B_KVEMPTY + i), 1);
+    for (int s = 0; s < C::NQ; ++s) mbar_init(bar(C::B_QEMPTY + s), 4);  // one per storing warp
     for (int g = 0; g < C::NSLOT; ++g) {
       mbar_init(bar(C::B_SFULL + g), 1);
       mbar_init(bar(C::B_PREADY + g), 128);
       mbar_init(bar(C::B_PVDONE + g), 1);
     }
-    mbar_init(bar(C::B_DRAIN), 1);
-    *abort_flag = 0;
+    for (int g = 0; g <= C::NSLOT; ++g) mbar_init(bar(C::B_DRAIN + g), 1);
     fence_mbarrier_init();
-    fence_proxy_async_smem();  // the initialised barriers are visible to this thread's copies
-    tma_prefetch_desc(&tm_q);
-    tma_prefetch_desc(&tm_k);
-    tma_prefetch_desc(&tm_v);
     tma_prefetch_desc(&tm_o);
-    pcur.init(t_begin, p);
-    produce(true);
   }
   if (warp == C::W_MMA) {
     tmem_alloc(smem_u32(tmem_holder), C::TMEM_COLS);
@@ -254,73 +275,56 @@ __global__ void __launch_bounds__(ShortCfg<DP, SN>::THREADS, 1)
       }
     }
   } else if (warp == C::W_MMA) {
-    // ------------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------------------------ QK issuer / retirer
     // Warp-uniform control flow; one elected lane issues the MMAs and commits (the *_w helpers).
-    // The warp polls the inputs of the next P V and of the next Q K^T and issues whichever is
-    // ready first.
+    // The warp polls for the next tile it can retire (its P V done) and for the inputs of the next
+    // Q K^T, and acts on whichever is ready first.
     constexpr uint32_t kIdescQK = idesc_f16(128, SN, BF16 ? 1 : 0, 0, 0);
-    constexpr uint32_t kIdescPV = idesc_f16(128, DP, BF16 ? 1 : 0, 0, 1);
     auto ready = [&](uint32_t b, uint32_t parity) -> bool {
       return __all_sync(0xffffffffu, mbar_test_wait(b, parity));
     };
-    TileCursor cq, cv;  // tiles of the next QK and of the next PV
+    TileCursor cq, cr;  // tiles of the next QK and of the next retirement
     cq.init(t_begin, p);
-    cv.init(t_begin, p);
-    int j = 0, ip = 0;     // next QK, next PV
-    int hq = -1, hv = -1;  // head index (within the range) of the last QK / PV issued
-    int released = 0;      // heads whose K/V buffer has been released
+    cr.init(t_begin, p);
+    int j = 0, ir = 0;  // next QK, next tile to retire
+    int released = 0;   // heads whose K/V buffer has been handed back
     bool ok = true;
     uint64_t t_idle = global_timer_ns();
-    while (ok && ip < n) {
+    while (ok && ir < n) {
       bool progress = false;
-      // O = P V of the oldest tile whose P is written.
-      if (ip < j && ready(bar(C::B_PREADY + ip % C::NSLOT), static_cast<uint32_t>(ip / C::NSLOT) & 1u)) {
-        const int slot = ip % C::NSLOT;
-        if (ip == 0 || cv.qt == 0) ++hv;
-        tc_fence_after_sync();
-        const uint32_t p_tmem = tmem + slot * C::SLOT_COLS;  // P, over the slot's S
-        const uint32_t v_addr = base + C::OFF_KV + (hv % C::NKV) * 2 * C::TILE_BYTES + C::TILE_BYTES;
-#pragma unroll
-        for (int k = 0; k < SN / 16; ++k) {
-          if (k < p.pv_steps)
-            umma_ts_w(p_tmem + SN, p_tmem + k * 8, smem_desc_sw128(v_addr + k * 2048, C::CH_BYTES, 1024),
-                      kIdescPV, k > 0 ? 1u : 0u);
-        }
-        umma_commit_w(bar(C::B_PVDONE + slot));
-        if (ip + 1 == n || cv.last_of_head(p)) {
-          umma_commit_w(bar(C::B_KVEMPTY + hv % C::NKV));  // the last MMA reading this head's K/V
+      // Retire the oldest tile whose P V is complete; after the last tile of a head (tiles retire
+      // in order, and each tile's QK completed before its P V was issued) no MMA reads that head's
+      // K/V any more.
+      if (ir < j && ready(bar(C::B_PVDONE + ir % C::NSLOT), static_cast<uint32_t>(ir / C::NSLOT) & 1u)) {
+        if (ir + 1 == n || cr.last_of_head(p)) {
+          if (lane == 0) mbar_arrive(bar(C::B_KVEMPTY + cr.hidx % C::NKV));
           ++released;
         }
-        ++ip;
-        cv.step(1, p);
+        ++ir;
+        cr.step(1, p);
         progress = true;
       }
-      // S = Q K^T of the next tile, into its slot.  Its head's K/V buffer must hold that head (a
-      // buffer is reloaded only after the head before it was released), the slot's previous P V
-      // must have finished reading P (which S overwrites), and the Q tile must have landed.
-      if (j < n && j < ip + C::NSLOT) {
+      // S = Q K^T of the next tile, into its slot.  The slot's previous tile must be retired (its
+      // softmax has read S and its P V is done), its head's K/V buffer must hold that head (a
+      // buffer is reloaded only after the head before it was released), and the Q tile must have
+      // landed.
+      if (j < n && j < ir + C::NSLOT && cq.hidx < released + C::NKV &&
+          ready(bar(C::B_KVFULL + cq.hidx % C::NKV), static_cast<uint32_t>(cq.hidx / C::NKV) & 1u) &&
+          ready(bar(C::B_QFULL + j % C::NQ), static_cast<uint32_t>(j / C::NQ) & 1u)) {
         const int slot = j % C::NSLOT;
-        const int h_next = (j == 0 || cq.qt == 0) ? hq + 1 : hq;
-        if (h_next < released + C::NKV &&
-            ready(bar(C::B_KVFULL + h_next % C::NKV), static_cast<uint32_t>(h_next / C::NKV) & 1u) &&
-            (j < C::NSLOT ||
-             ready(bar(C::B_PVDONE + slot), static_cast<uint32_t>((j - C::NSLOT) / C::NSLOT) & 1u)) &&
-            ready(bar(C::B_QFULL + j % C::NQ), static_cast<uint32_t>(j / C::NQ) & 1u)) {
-          hq = h_next;
-          tc_fence_after_sync();
-          const uint32_t q_addr = base + C::OFF_Q + (j % C::NQ) * C::TILE_BYTES;
-          const uint32_t k_addr = base + C::OFF_KV + (hq % C::NKV) * 2 * C::TILE_BYTES;
+        tc_fence_after_sync();
+        const uint32_t q_addr = base + C::OFF_Q + (j % C::NQ) * C::TILE_BYTES;
+        const uint32_t k_addr = base + C::OFF_KV + (cq.hidx % C::NKV) * 2 * C::TILE_BYTES;
 #pragma unroll
-          for (int k = 0; k < DP / 16; ++k) {
-            const uint32_t off = (k >> 2) * C::CH_BYTES + (k & 3) * 32;
-            umma_ss_w(tmem + slot * C::SLOT_COLS, smem_desc_sw128(q_addr + off, 16, 1024),
-                      smem_desc_sw128(k_addr + off, 16, 1024), kIdescQK, k > 0 ? 1u : 0u);
-          }
-          umma_commit_w(bar(C::B_SFULL + slot));
-          ++j;
-          cq.step(1, p);
-          progress = true;
+        for (int k = 0; k < DP / 16; ++k) {
+          const uint32_t off = (k >> 2) * C::CH_BYTES + (k & 3) * 32;
+          umma_ss_w(tmem + slot * C::SLOT_COLS, smem_desc_sw128(q_addr + off, 16, 1024),
+                    smem_desc_sw128(k_addr + off, 16, 1024), kIdescQK, k > 0 ? 1u : 0u);
         }
+        umma_commit_w(bar(C::B_SFULL + slot));
+        ++j;
+        cq.step(1, p);
+        progress = true;
       }
       if (progress) {
         t_idle = global_timer_ns();
@@ -341,7 +345,7 @@ __global__ void __launch_bounds__(ShortCfg<DP, SN>::THREADS, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------------ softmax / epilogue
+    // ------------------------------------------------------------------ softmax / P V / epilogue
     const int g = warp >> 2;         // warpgroup = TMEM slot: tiles i with i % NSLOT == g
     const int wq = warp & 3;         // TMEM lane quarter of this warp
     const int row = wq * 32 + lane;  // row inside the tile
@@ -351,8 +355,10 @@ __global__ void __launch_bounds__(ShortCfg<DP, SN>::THREADS, 1)
     const float masked = p.neg_scale ? INFINITY : -INFINITY;  // masked * sl2 == -inf
     const int groups = p.pv_steps;  // 16-key groups of P that the PV reads
     bool ok = true;
+    int pending_stage = -1;  // Q stage whose O store may still be reading it
     TileCursor cur;
-    cur.init(t_begin + g, p);
+    cur.init(t_begin, p);
+    cur.step(g, p);
     for (int i = g; ok && i < n; i += C::NSLOT, cur.step(C::NSLOT, p)) {
       const uint32_t par = static_cast<uint32_t>(i / C::NSLOT) & 1u;
       if (!(ok = mbar_wait_all(bar(C::B_SFULL + g), par, ctl))) break;
@@ -397,13 +403,30 @@ __global__ void __launch_bounds__(ShortCfg<DP, SN>::THREADS, 1)
       float l0, l1;
       f2_unpack(f2_add(la, lb), l0, l1);
       const float inv_l = 1.f / (l0 + l1);
+      // Every row's P is written (and this warpgroup's loads of the slot's previous O are done):
+      // one thread of the warpgroup issues O = P V.  (An mbarrier rather than a named barrier, so
+      // that the wait stays bounded if the launch is aborted.)
       tmem_st_wait();
       tc_fence_before_sync();
       mbar_arrive(bar(C::B_PREADY + g));
+      if (wq == 0) {
+        if (!(ok = mbar_wait_all(bar(C::B_PREADY + g), par, ctl))) break;
+        tc_fence_after_sync();
+        const uint32_t p_tmem = tmem + g * C::SLOT_COLS;
+        const uint32_t v_addr = base + C::OFF_KV + (cur.hidx % C::NKV) * 2 * C::TILE_BYTES + C::TILE_BYTES;
+        issue_pv<SN / 16, DP, BF16>(groups, p_tmem + SN, p_tmem, v_addr);
+        umma_commit_w(bar(C::B_PVDONE + g));
+      }
 
       // Epilogue: O / l, 16-bit, staged in the tile's own Q stage (its Q was read by the QK, which
       // completed before S was handed over), TMA stores per warp, then the stage goes back to the
       // producer.
+      // The previous tile's O store has long read its stage by now: hand that stage back.
+      if (lane == 0 && pending_stage >= 0) {
+        bulk_wait_group_read0();
+        mbar_arrive(bar(C::B_QEMPTY + pending_stage));
+      }
+      pending_stage = -1;
       if (!(ok = mbar_wait_all(bar(C::B_PVDONE + g), par, ctl))) break;
       tc_fence_after_sync();
       const int st = i % C::NQ;
@@ -429,7 +452,7 @@ __global__ void __launch_bounds__(ShortCfg<DP, SN>::THREADS, 1)
           }
         }
       }
-      tc_fence_before_sync();  // O is read: the slot's next P V (after this warpgroup's next P) may write it
+      tc_fence_before_sync();  // O is read: the slot's next P V (after the next P-ready) may write it
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
@@ -439,12 +462,24 @@ __global__ void __launch_bounds__(ShortCfg<DP, SN>::THREADS, 1)
             tma_store_4d(&tm_o, stage + c * C::CH_BYTES + wq * 32 * 128, c * 64, row0, cur.h, cur.b);
         }
         bulk_commit_group();
-        bulk_wait_group_read0();  // the store has read the stage: it may take the next Q tile
-        mbar_arrive(bar(C::B_QEMPTY + st));
       }
+      pending_stage = st;  // handed back once the store has read it (next tile, or below)
       __syncwarp();
     }
-    if (lane == 0) bulk_wait_group0();  // every store of this warp complete before exit
+    if (lane == 0) {
+      if (pending_stage >= 0) {
+        bulk_wait_group_read0();
+        mbar_arrive(bar(C::B_QEMPTY + pending_stage));
+      }
+      bulk_wait_group0();  // every store of this warp complete before exit
+    }
+    if (wq == 0 && *abort_flag) {
+      // Let this warpgroup's P V (if one is in flight) finish before TMEM is given back.
+      __syncwarp();
+      umma_commit_w(bar(C::B_DRAIN + 1 + g));  // same election as the P V MMAs
+      if (lane == 0) mbar_wait_drain(bar(C::B_DRAIN + 1 + g), 0, p.timeout_ns);
+      __syncwarp();
+    }
   }
 
   tc_fence_before_sync();
