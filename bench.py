@@ -17,7 +17,12 @@ benchmark definition, measured the same way.
 
 Inputs are generated on the GPU from per-batch seeds (identical for every N), larger than the 126 MB
 L2 for c4/c5 (no flush needed); the smaller configs flush L2 with a 256 MB write between steps and
-time each step with its own CUDA events.
+time each step with its own CUDA events.  The C5 warm-up runs at least --warmup steps and at least
+1.5 s of device work, so that every N is timed at the kernel's sustained (power-capped) clock and a
+short per-GPU step at large N does not run at a boost clock that N=1 never sees.  Under torchrun,
+every rank's device time and median SM clock are gathered to rank 0 (clocks.per_rank).  The
+default run (C5, one GPU) also times C4 afterwards in the same process (extra.c4: value, roofline,
+clocks).
 
 Printed (rank 0, one JSON line): value/ms_per_step, e2e (the same metric through the public API with
 host-resident inputs: pinned H2D of the step's Q/K/V and D2H of its O inside the timed region),
@@ -344,6 +349,108 @@ def cpu_reference_einsum_sample(w: dict, seconds: float, threads: int | None = N
 
 
 # ------------------------------------------------------------------------------------------------
+# timing
+# ------------------------------------------------------------------------------------------------
+def gpu_uuid(dev) -> str | None:
+    import torch
+    try:
+        return "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:  # noqa: BLE001
+        return None
+
+
+def time_steps(step, steps: int, warmup: int, warm_s: float, dev, stream, flush=None, barrier=None):
+    """Warm up (at least ``warmup`` steps and, when ``warm_s`` > 0, until that many seconds of
+    device work have run, so that a power-capped kernel is timed at its sustained clock whatever
+    the step length), then time exactly ``steps`` steps with CUDA events on ``stream`` (one pair
+    per step, an L2 flush between steps when ``flush`` is given), bracketed by barrier +
+    synchronize, while NVML samples the clocks.  Returns (out, per-step ms, region ms, clocks,
+    warm-up steps run, warm-up seconds)."""
+    import torch
+    out = None
+    t0 = time.perf_counter()
+    n_warm = 0
+    while n_warm < max(3, warmup) or (warm_s > 0 and time.perf_counter() - t0 < warm_s):
+        out = step()
+        n_warm += 1
+        if n_warm % 8 == 0:
+            torch.cuda.synchronize(dev)
+    torch.cuda.synchronize(dev)
+    warm_elapsed = time.perf_counter() - t0
+    clocks = ClockSampler(gpu_uuid(dev))
+    clocks.start()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if barrier:
+        barrier()
+    torch.cuda.synchronize(dev)
+    clocks.mark(True)
+    t_start.record(stream)
+    for i in range(steps):
+        if flush is not None:
+            flush.fill_(float(i))
+        ev[i][0].record(stream)
+        out = step()
+        ev[i][1].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks.mark(False)
+    if barrier:
+        barrier()
+    clock_info = clocks.stop()
+    return (out, [a.elapsed_time(b) for a, b in ev], t_start.elapsed_time(t_end), clock_info, n_warm,
+            warm_elapsed)
+
+
+def tensor_roofline(flops_per_launch: float, mean_ms: float, region_ms: float, clock_info, peaks, peak_src,
+                    kernel_name: str) -> dict:
+    """Roofline record of a tensor-bound attention launch against the measured bf16 peak: the
+    sustained (power-capped) cuBLAS figure for a timed region over a second or one that ran
+    power-capped, else the burst figure."""
+    achieved = flops_per_launch / (mean_ms * 1e-3) / 1e12
+    capped = bool(clock_info and "sw_power_cap" in (clock_info.get("reasons") or []))
+    sustained = region_ms > 1000.0 or capped
+    peak = float(peaks.get("bf16_tflops_sustained" if sustained else "bf16_tflops"))
+    return {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4), "kernel": kernel_name,
+            "peak_kind": f"{peak_src} {'sustained' if sustained else 'burst'} cuBLAS bf16"
+                         + (" (sw_power_cap active in the timed region)" if capped else ""),
+            "frac_of_burst": round(achieved / float(peaks.get("bf16_tflops")), 4),
+            "frac_of_2250_spec": round(achieved / 2250.0, 4),
+            "algorithmic_flops_per_launch": flops_per_launch}
+
+
+def extra_sdpa_record(key: str, steps: int, warmup: int, warm_s: float, dev, stream, peaks, peak_src) -> dict:
+    """One more single-GPU SDPA workload timed in the same process (after the main one, with its
+    own warm-up, CUDA events and clock samples): the C4 prefill config beside the C5 headline."""
+    import torch
+    import cmpext3
+    from cmpext3 import _native as N
+    w = WORKLOADS[key]
+    q, k, v = make_inputs(w, 0, w["B"], dev)
+    scale = 1.0 / math.sqrt(w["D"])
+    flops = attn_flops(w["B"], w["H"], w["Lq"], w["Lk"], w["D"], w["causal"])
+
+    def step():
+        return cmpext3.ops.attention(q, k, v, scale, w["causal"])
+    with torch.no_grad():
+        out, per_step, region_ms, clock_info, n_warm, warm_el = time_steps(step, steps, warmup, warm_s, dev, stream)
+    mean_ms = statistics.mean(per_step)
+    kernel = N.attention_plan(q, k, v, scale, w["causal"])
+    rec = {"workload": w["name"], "value": round(flops * steps / (region_ms * 1e-3) / 1e12, 3),
+           "unit": "TFLOP/s", "steps": steps, "ms_per_step": round(region_ms / steps, 4),
+           "warmup_steps_run": n_warm, "warmup_s": round(warm_el, 2),
+           "roofline": tensor_roofline(flops, mean_ms, region_ms, clock_info, peaks, peak_src, kernel),
+           "clocks": clock_info, "gpu_launches": steps, "kernel": kernel}
+    tr = load_traffic("fmha", key)
+    if tr and tr.get("bytes_per_unit"):
+        rec["roofline"]["traffic"] = round(tr["bytes_per_unit"] * flops / tr.get("flops_per_unit", flops))
+    del q, k, v, out
+    torch.cuda.empty_cache()
+    return rec
+
+
+# ------------------------------------------------------------------------------------------------
 # main
 # ------------------------------------------------------------------------------------------------
 def parse_args():
@@ -358,6 +465,11 @@ def parse_args():
     ap.add_argument("--no-verify", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the extra C4 record of the default (C5, one GPU) run")
+    ap.add_argument("--warmup-seconds", type=float, default=None,
+                    help="extend the warm-up to this much device work (default 1.5 s for the "
+                         "tensor-bound c4/c5, 0 for the others)")
     return ap.parse_args()
 
 
@@ -473,45 +585,29 @@ def main() -> int:
         kernel_name = N.bmm_plan(q.reshape(-1, w["Lq"], w["D"]),
                                  k.reshape(-1, w["Lk"], w["D"]).transpose(1, 2))
 
+    # C5 (the scaling workload) is timed at its sustained, power-capped clock at every N: the
+    # warm-up runs at least 1.5 s of device work, whatever the per-GPU step length.
+    warm_s = args.warmup_seconds if args.warmup_seconds is not None else (1.5 if args.workload == "c5" else 0.0)
     with torch.no_grad():
-        for _ in range(max(3, args.warmup)):
-            out = step()
-        torch.cuda.synchronize(dev)
-
-        uuid = None
-        try:
-            uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
-        except Exception:  # noqa: BLE001
-            pass
-        clocks = ClockSampler(uuid)
-        clocks.start()
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in range(args.steps)]
-        t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier()
-        torch.cuda.synchronize(dev)
-        clocks.mark(True)
-        t_start.record(stream)
-        for i in range(args.steps):
-            if flush is not None:
-                flush.fill_(float(i))
-            ev[i][0].record(stream)
-            out = step()
-            ev[i][1].record(stream)
-        t_end.record(stream)
-        torch.cuda.synchronize(dev)
-        clocks.mark(False)
-        barrier()
-        clock_info = clocks.stop()
-
-        per_step_ms = [a.elapsed_time(b) for a, b in ev]
-        region_ms = t_start.elapsed_time(t_end)
+        out, per_step_ms, region_ms, clock_info, n_warm, warm_elapsed = time_steps(
+            step, args.steps, args.warmup, warm_s, dev, stream, flush=flush, barrier=barrier)
         busy_ms = sum(per_step_ms)
         local_ms = region_ms if big else busy_ms
         total_ms = max_ranks(local_ms)
         total_flops = step_flops_rank * world * args.steps
         value = total_flops / (total_ms * 1e-3) / 1e12
         mean_launch_ms = max_ranks(statistics.mean(per_step_ms))
+        if distributed:
+            # every rank's device time and median SM clock over its own timed region
+            mine = [local_ms, (clock_info or {}).get("sm_mhz") or -1.0,
+                    1.0 if "sw_power_cap" in ((clock_info or {}).get("reasons") or []) else 0.0,
+                    (clock_info or {}).get("power_w_max") or -1.0]
+            per_rank = sharding.gather_floats(mine, dev)
+            if rank == 0 and clock_info is not None:
+                clock_info["per_rank"] = [
+                    {"rank": r, "ms": round(ms, 3), "sm_mhz": mhz if mhz > 0 else None,
+                     "sw_power_cap": bool(cap), "power_w_max": pw if pw > 0 else None}
+                    for r, (ms, mhz, cap, pw) in enumerate(per_rank)]
 
         # roofline of the dominant kernel
         if w["kind"] == "sdpa" and w["cross"]:
@@ -524,20 +620,8 @@ def main() -> int:
                     "algorithmic_bytes_per_launch": algo_bytes,
                     "tflops": round(step_flops_rank / (statistics.mean(per_step_ms) * 1e-3) / 1e12, 2)}
         elif w["kind"] == "sdpa":
-            achieved = step_flops_rank / (statistics.mean(per_step_ms) * 1e-3) / 1e12
-            # The sustained (power-capped) cuBLAS figure is the like-for-like denominator for a
-            # kernel that runs in the power-capped regime: a timed region over a second, or one
-            # during which the clock sampler saw sw_power_cap active.  Otherwise the burst figure.
-            capped = bool(clock_info and "sw_power_cap" in (clock_info.get("reasons") or []))
-            sustained = region_ms > 1000.0 or capped
-            peak = float(peaks.get("bf16_tflops_sustained" if sustained else "bf16_tflops"))
-            roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
-                    "frac": round(achieved / peak, 4), "kernel": kernel_name,
-                    "peak_kind": f"{peak_src} {'sustained' if sustained else 'burst'} cuBLAS bf16"
-                                 + (" (sw_power_cap active in the timed region)" if capped else ""),
-                    "frac_of_burst": round(achieved / float(peaks.get("bf16_tflops")), 4),
-                    "frac_of_2250_spec": round(achieved / 2250.0, 4),
-                    "algorithmic_flops_per_launch": step_flops_rank}
+            roof = tensor_roofline(step_flops_rank, statistics.mean(per_step_ms), region_ms, clock_info, peaks,
+                                   peak_src, kernel_name)
         else:
             # C3 is HBM-bound on the scores tensor: bytes of both bmms + softmax over the step
             es = 2
@@ -578,10 +662,19 @@ def main() -> int:
                           f"stock torch CPU einsum->softmax->einsum on {c.get('slices')} (b,h) slices in "
                           f"{c['seconds']:.1f} s")}
 
+    # The default run (C5 on one GPU) also times C4, the causal prefill config the kernel's
+    # tensor-peak target is stated on, in the same process after everything above.
+    extra = None
+    if world == 1 and args.workload == "c5" and not args.no_extra:
+        del q, k, v, out
+        torch.cuda.empty_cache()
+        extra = {"c4": extra_sdpa_record("c4", args.steps, args.warmup, 0.0, dev, stream, peaks, peak_src)}
+
     flags = N.device_status()
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup,
+                "steps": args.steps, "warmup": args.warmup, "warmup_steps_run": n_warm,
+                "warmup_s": round(warm_elapsed, 2),
                 "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic",
                 "config": config_block(w, args.workload, world, nb),
@@ -589,6 +682,8 @@ def main() -> int:
                 "gpu_launches": launches_per_step * args.steps,
                 "mean_launch_ms": round(mean_launch_ms, 4), "kernel": kernel_name,
                 "parity": parity, "device_flags": flags}
+        if extra:
+            line["extra"] = extra
         print(json.dumps(line), flush=True)
     if distributed:
         dist.destroy_process_group()

@@ -50,6 +50,9 @@ def _worker(rank: int, world: int, port: int, outdir: str, mode: str) -> None:
         samples = torch.stack([local[0, 0], local[-1, -1]])
         got = S.gather_samples(samples)
         t = S.max_over_ranks(float(rank + 1))
+        per_rank = S.gather_floats([rank, 10.0 * rank + 0.5])
+        if rank == 0:
+            result["per_rank"] = per_rank
         if rank == 0:
             full = RP.sdpa(q, k, v, is_causal=True)
             per = B // world
@@ -110,6 +113,7 @@ def test_two_ranks_shard_and_gather(tmp_path):
     assert all("error" not in res[r] for r in res), res
     assert res[0]["gather_ok"] is True
     assert res[0]["max"] == 2.0 and res[1]["max"] == 2.0
+    assert res[0]["per_rank"] == [[0.0, 0.5], [1.0, 10.5]]
 
 
 def test_rank_failure_is_seen_by_the_survivor(tmp_path):

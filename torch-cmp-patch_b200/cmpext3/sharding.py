@@ -72,3 +72,16 @@ def max_over_ranks(value: float, device: torch.device | None = None) -> float:
     t = torch.tensor([float(value)], dtype=torch.float64, device=device or "cpu")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def gather_floats(values, device: torch.device | None = None) -> list[list[float]] | None:
+    """All-gather a short per-rank vector of floats (the same length on every rank); rank 0 gets
+    one list per rank, in rank order, the others None.  Used after the timed region, to bring
+    per-rank records (device time, median SM clock) to the rank that prints the result."""
+    world = dist.get_world_size()
+    local = torch.tensor([float(x) for x in values], dtype=torch.float64, device=device or "cpu")
+    out = torch.empty(world * local.numel(), dtype=torch.float64, device=local.device)
+    dist.all_gather_into_tensor(out, local)
+    if dist.get_rank() != 0:
+        return None
+    return out.view(world, -1).cpu().tolist()
