@@ -39,8 +39,9 @@
 extern "C" {
 #endif
 
-#define CMPX_ABI_VERSION 4  /* 2: cmpx_attn_desc.heads_kv (grouped-query attention); 3: cmpx_linear;
-                               4: cmpx_attn_desc.mask / mask_kind (boolean or additive attention mask) */
+#define CMPX_ABI_VERSION 5  /* 2: cmpx_attn_desc.heads_kv (grouped-query attention); 3: cmpx_linear;
+                               4: cmpx_attn_desc.mask / mask_kind (boolean or additive attention mask);
+                               5: cmpx_bmm_small / cmpx_bmm_small_plan */
 
 /* Element type of every operand of one call (inputs and output share it, as in the reference:
  * dtype in == dtype out, src/main.cpp:1623-1627, :366-369). */
@@ -121,9 +122,11 @@ typedef struct cmpx_attn_desc {
  * remainder; a*b ~ a_hi*b_hi + a_hi*b_lo + a_lo*b_hi with fp32 accumulation), and needs K-major
  * operands: A contiguous along k (a_stride[2] == 1), B contiguous along k (b_stride[1] == 1), every
  * stride that is stepped a multiple of 4 elements and every pointer 16-byte aligned; other fp32
- * layouts return CMPX_ERR_MISALIGNED (copy B to a column-major view first).  fp32 takes k <= 8192
- * (CMPX_ERR_UNSUPPORTED_SHAPE beyond): the tensor core's fp32 accumulation error grows with k
- * (2e-5 of the output's peak at k = 8192, 9e-5 at 32768).
+ * layouts return CMPX_ERR_MISALIGNED (copy B to a column-major view first).  The tensor core's fp32
+ * accumulation error grows with k (2e-5 of the output's peak at k = 8192, 9e-5 at 32768), so an fp32
+ * call with k > 8192 runs as several launches over k chunks of at most 8192 on the same stream: the
+ * first stores C, the others add their partial products into it (the plan name ends in
+ * "+k-chunks"); C must not alias A or B.
  * Replaces: custom_bmm_forward (src/main.cpp:363-441) and its per-batch host loop over
  * launch_matmul_fp32 (src/cuda/fp32_matmul.cu:236-265) / launch_matmul_fp16
  * (src/cuda/fp16_matmul.cu:373-427). */
@@ -174,6 +177,16 @@ CMPX_API int cmpx_attn_fwd_noalloc(const cmpx_attn_desc* desc, void* stream);
 
 /* Batched matmul.  Replaces cmpext3.ops.bmm (src/main.cpp:2307-2309). */
 CMPX_API int cmpx_bmm(const cmpx_bmm_desc* desc, void* stream);
+
+/* Batched product of many tiny matrices, same descriptor as cmpx_bmm: any dtype of the three, any
+ * non-negative element strides for A, B and C (views are read and written in place), any m, n, k.
+ * Each output element is a length-k dot product accumulated in fp32 and rounded once; there is no
+ * intermediate tensor.  Meant for the per-item sizes the patched bmm / matmul route here
+ * (m * k * n <= 32768 by default, CMPEXT3_SMALL_BMM_MAX_MKN), where a tiled GEMM wastes its tile.
+ * Replaces: the eager broadcast multiply + sum of _small_bmm (cmpext3/__init__.py:440-464), which
+ * materialises a [batch, m, k, n] intermediate. */
+CMPX_API int cmpx_bmm_small(const cmpx_bmm_desc* desc, void* stream);
+CMPX_API int cmpx_bmm_small_plan(const cmpx_bmm_desc* desc, char* buf, size_t buf_len);
 
 /* Linear layer  y = x W^T (+ bias):  x [m, k], W [n, k] (the nn.Linear weight, read in place as the
  * K-major operand of the same GEMM as cmpx_bmm), bias [n] or NULL, y [m, n]; rows of x, W and y are

@@ -49,7 +49,8 @@ STOCK_UNPATCHED = {(torch, "baddbmm"): torch.baddbmm, (F, "layer_norm"): F.layer
                    (F, "conv2d"): F.conv2d, (F, "gelu"): F.gelu}
 STOCK_SOFTMAX = {"torch": torch.softmax, "F": F.softmax, "Tensor": torch.Tensor.softmax}
 
-NATIVE_OPS = ["attention", "bmm", "attention_plan", "bmm_plan", "softmax", "linear", "linear_plan"]
+NATIVE_OPS = ["attention", "bmm", "attention_plan", "bmm_plan", "softmax", "linear", "linear_plan",
+              "bmm_small", "bmm_small_plan"]
 
 
 def pytest_configure(config):
@@ -83,6 +84,7 @@ def native(monkeypatch):
     fake.attention_plan.return_value = "fake-attention-entry"
     fake.bmm_plan.return_value = "fake-bmm-entry"
     fake.linear_plan.return_value = "fake-linear-entry"
+    fake.bmm_small_plan.return_value = "fake-bmm-small-entry"
     monkeypatch.setattr(cmpext3, "_C", fake)
     monkeypatch.setattr(cmpext3, "ops", fake)
     return fake

@@ -63,18 +63,23 @@ def test_fp32_bmm_large_k_accuracy(cuda_device):
     assert _rel64(got, a, b) <= 5e-5
 
 
-def test_fp32_bmm_past_the_k_limit_is_served_stock(cuda_device, patched):
-    # K > 8192: the op declines (the accumulation error would grow past the contract), the patched
-    # torch.bmm answers with stock's result
+@pytest.mark.parametrize("k", [8200, 16384, 40000])
+def test_fp32_bmm_long_k_runs_in_chunks(cuda_device, patched, k):
+    # K > 8192: the product runs over K chunks of at most 8192, each accumulated in the tensor
+    # core's fp32 and added into C in fp32, so the error stays that of one chunk (the fp32 contract
+    # 1e-4, measured against float64); the patched torch.bmm takes the same kernel
     g = torch.Generator().manual_seed(9)
-    a, b = torch.randn(1, 64, 8200, generator=g), torch.randn(1, 8200, 64, generator=g)
+    a, b = torch.randn(2, 96, k, generator=g), torch.randn(2, k, 80, generator=g)
     ad, bd = a.to(cuda_device), b.to(cuda_device)
-    with pytest.raises(RuntimeError):
-        cmpext3.ops.bmm(ad, bd)
-    with torch.no_grad():
-        got = torch.bmm(ad, bd)
+    assert cmpext3.ops.bmm_plan(ad, bd).endswith("+k-chunks>")
+    got = cmpext3.ops.bmm(ad, bd)
     torch.cuda.synchronize()
-    check(got, RP.bmm(a, b), torch.float32, "K 8200", attention=False)
+    assert _rel64(got, a, b) <= 5e-5
+    with torch.no_grad():
+        got2 = torch.bmm(ad, bd)
+    torch.cuda.synchronize()
+    check(got2, RP.bmm(a, b), torch.float32, f"K {k}", attention=False)
+    assert "k-chunks" in cmpext3.autoselect_report()
 
 
 def test_fp32_bmm_inf_operand(cuda_device):

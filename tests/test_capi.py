@@ -42,7 +42,7 @@ def test_library_exports_nothing_undeclared():
 
 
 def test_abi_version_and_status_strings():
-    assert N.lib.cmpx_abi_version() == 4
+    assert N.lib.cmpx_abi_version() == 5
     header = HEADER.read_text()
     m = re.search(r"#define CMPX_ABI_VERSION (\d+)", header)
     assert m and int(m.group(1)) == N.ABI_VERSION == N.lib.cmpx_abi_version()
@@ -177,12 +177,19 @@ def test_bmm_plan_for_the_einsum_attention_shapes():
     (dict(n=30), "ERR_MISALIGNED"),            # 120-byte C rows
     (dict(ptr=0x10004), "ERR_MISALIGNED"),     # 4-byte aligned pointers
     (dict(k=0), "ERR_UNSUPPORTED_SHAPE"),
-    (dict(k=8196), "ERR_UNSUPPORTED_SHAPE"),   # past K = 8192 the fp32 accumulation drifts: stock
 ])
 def test_fp32_bmm_plan_rejects(kw, status):
     args = dict(nb=2, m=256, n=256, k=64, dtype=0, bt=True)
     args.update(kw)
     assert _bplan(_bmm(**args))[0] == getattr(N, status)
+
+
+@pytest.mark.parametrize("k,chunked", [(8192, False), (8196, True), (40000, True)])
+def test_fp32_bmm_plan_chunks_long_k(k, chunked):
+    # past K = 8192 the product runs over K chunks (each accumulated in the tensor core's fp32,
+    # then summed into C in fp32)
+    st, name = _bplan(_bmm(2, 256, 256, k, dtype=0, bt=True))
+    assert st == 0 and name.startswith("bmm_x3tf32_sm100<f32") and name.endswith("+k-chunks>") == chunked, name
 
 
 def test_fp32_bmm_plan_single_rows_need_no_aligned_row_stride():

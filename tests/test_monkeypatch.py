@@ -141,12 +141,25 @@ class TestMatmul:
         assert torch.matmul(a, b) is sentinel
         assert_called_once_with_tensors(native.bmm, a, b)
 
-    def test_small_3d_takes_broadcast_path(self, patched, native, monkeypatch):
+    def test_small_3d_takes_the_small_matrix_kernel(self, patched, native, monkeypatch):
+        # M*K*N <= 32768 per item: the reference's small-matrix route (its __init__.py:440-464),
+        # here the native small-matrix kernel rather than the tiled GEMM
         force_eligible(monkeypatch)
         a, b = torch.randn(2, 3, 4), torch.randn(2, 4, 5)
-        got = torch.matmul(a, b)
+        sentinel = torch.zeros(2, 3, 5)
+        native.bmm_small.return_value = sentinel
+        assert torch.matmul(a, b) is sentinel
         native.bmm.assert_not_called()
-        assert torch.allclose(got, cmpext3._ORIGINALS[(torch, "matmul")](a, b), atol=1e-6)
+        assert_called_once_with_tensors(native.bmm_small, a, b)
+
+    def test_small_route_threshold(self, patched, native, monkeypatch):
+        force_eligible(monkeypatch)
+        monkeypatch.setattr(cmpext3, "_SMALL_BMM_MAX_MKN", 59)
+        a, b = torch.randn(2, 3, 4), torch.randn(2, 4, 5)  # M*K*N = 60 > 59: the tiled GEMM
+        native.bmm.return_value = torch.zeros(2, 3, 5)
+        torch.bmm(a, b)
+        native.bmm_small.assert_not_called()
+        assert native.bmm.call_count == 1
 
     def test_falls_back_when_not_cuda(self, patched, native):
         a, b = torch.randn(2, 3), torch.randn(3, 4)
@@ -335,8 +348,8 @@ class TestSoftmax:
 
     def test_other_dim_or_dtype_is_stock(self, patched, native, monkeypatch):
         force_eligible(monkeypatch)
-        native.bmm.return_value = torch.randn(2, 8, 6)
-        s = torch.bmm(torch.randn(2, 8, 4), torch.randn(2, 4, 6))
+        native.bmm.return_value = torch.randn(2, 64, 64)  # M*K*N above the small-matrix route
+        s = torch.bmm(torch.randn(2, 64, 32), torch.randn(2, 32, 64))
         torch.softmax(s, 1)
         torch.softmax(s, -1, dtype=torch.float64)
         F.softmax(s)  # implicit dim: stock (with torch's warning)
@@ -344,8 +357,8 @@ class TestSoftmax:
 
     def test_declined_native_softmax_falls_back_to_stock(self, patched, native, monkeypatch):
         force_eligible(monkeypatch)
-        native.bmm.return_value = torch.randn(2, 8, 6)
-        s = torch.bmm(torch.randn(2, 8, 4), torch.randn(2, 4, 6))
+        native.bmm.return_value = torch.randn(2, 64, 64)  # M*K*N above the small-matrix route
+        s = torch.bmm(torch.randn(2, 64, 32), torch.randn(2, 32, 64))
         native.softmax.side_effect = RuntimeError("outside the tile table")
         got = torch.softmax(s, -1)
         assert torch.allclose(got, STOCK_SOFTMAX["torch"](s, -1))

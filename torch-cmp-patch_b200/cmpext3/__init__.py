@@ -29,7 +29,8 @@ What changed underneath: the kernels are tcgen05/TMA/TMEM kernels for B200 in a 
 and to fp32 for bmm), and the runtime native-versus-stock race is replaced by a fixed tile table
 (see cmpext3.autoselect).  The rest of the reference (conv, norms, activations, TensorRT, NVML
 clock/power changes) is not part of this package; in particular nothing here changes GPU clocks or
-power limits.  fp32 bmm / matmul / einsum / linear run on a 3xTF32 tensor-core GEMM (k <= 8192).
+power limits.  fp32 bmm / matmul / einsum / linear run on a 3xTF32 tensor-core GEMM (k > 8192 in
+chunks of at most 8192, summed in fp32).
 
     import cmpext3            # patches on import
     cmpext3.disable(); cmpext3.enable()
@@ -163,8 +164,7 @@ def _dispatch(op: str, ref: torch.Tensor, key: tuple, native_call: Callable,
 def _patched_linear(input, weight, bias=None):
     """F.linear with the reference's gates (__init__.py:410-420): stock under live autograd, for
     non-CUDA / unsupported dtypes, for input.dim() < 2 or a non-2-D weight, for fp16 with an odd
-    out_features; the native op raising (misaligned 16-bit rows, fp32 k > 8192) also serves the call
-    from stock."""
+    out_features; the native op raising (misaligned 16-bit rows) also serves the call from stock."""
     orig = _ORIGINALS[(F, "linear")]
     if not (_grad_safe(input, weight, bias) and _usable(input, weight)):
         return orig(input, weight, bias)
@@ -190,7 +190,8 @@ def _patched_matmul(input, other, *, out=None):
     elif input.dim() == 3 and other.dim() == 3:
         if _small_bmm_eligible(input, other):
             return _dispatch("bmm_small", input, (input.shape, input.dtype, other.shape),
-                             lambda: _small_bmm(input, other), lambda: orig(input, other))
+                             lambda: _small_bmm(input, other), lambda: orig(input, other),
+                             lambda: _C.bmm_small_plan(input, other))
         native = lambda: _C.bmm(input, other)  # noqa: E731
         plan = lambda: _C.bmm_plan(input, other)  # noqa: E731
     else:
@@ -199,8 +200,11 @@ def _patched_matmul(input, other, *, out=None):
                                    native, lambda: orig(input, other), plan))
 
 
-# Many tiny matrices (M*K*N <= 32768): a broadcast multiply + sum, chunked over the batch, as in
-# the reference (__init__.py:446-464).  Thresholds from the same environment variables.
+# Many tiny matrices (M*K*N <= 32768 per item): routed as in the reference (__init__.py:440-464),
+# with the same threshold variable, but computed by the native small-matrix kernel (one fp32 dot
+# product per output element, no [batch, M, K, N] intermediate) instead of an eager broadcast
+# multiply + sum.  CMPEXT3_SMALL_BMM_CHUNK, which bounded that intermediate, is still read for
+# compatibility and has nothing left to bound.
 _SMALL_BMM_MAX_MKN = int(os.environ.get("CMPEXT3_SMALL_BMM_MAX_MKN", "32768"))
 _SMALL_BMM_CHUNK = int(os.environ.get("CMPEXT3_SMALL_BMM_CHUNK", str(1 << 25)))
 
@@ -211,15 +215,7 @@ def _small_bmm_eligible(a: torch.Tensor, b: torch.Tensor) -> bool:
 
 
 def _small_bmm(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    n, m, k = a.shape
-    p = b.size(2)
-    step = max(1, _SMALL_BMM_CHUNK // max(m * k * p, 1))
-    if step >= n:
-        return (a.unsqueeze(-1) * b.unsqueeze(1)).sum(2)
-    out = torch.empty((n, m, p), dtype=a.dtype, device=a.device)
-    for s in range(0, n, step):
-        out[s:s + step] = (a[s:s + step].unsqueeze(-1) * b[s:s + step].unsqueeze(1)).sum(2)
-    return out
+    return _C.bmm_small(a, b)
 
 
 def _patched_bmm(input, mat2, *, out=None):
@@ -231,7 +227,8 @@ def _patched_bmm(input, mat2, *, out=None):
     if _small_bmm_eligible(input, mat2):
         return _dispatch("bmm_small", input, (input.shape, input.dtype, mat2.shape),
                          lambda: _small_bmm(input, mat2),
-                         lambda: orig(input, mat2))
+                         lambda: orig(input, mat2),
+                         lambda: _C.bmm_small_plan(input, mat2))
     return _note_product(_dispatch("bmm", input, (input.shape, input.dtype, mat2.shape),
                                    lambda: _C.bmm(input, mat2),
                                    lambda: orig(input, mat2),

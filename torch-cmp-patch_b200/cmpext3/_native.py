@@ -94,7 +94,7 @@ class SoftmaxDesc(ctypes.Structure):
 
 
 # CMPX_ABI_VERSION of include/cmpx_b200.h that the ctypes structures above mirror.
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 
 def _load() -> ctypes.CDLL:
@@ -115,6 +115,10 @@ def _load() -> ctypes.CDLL:
     L.cmpx_attn_plan.restype = ctypes.c_int
     L.cmpx_bmm_plan.argtypes = [ctypes.POINTER(BmmDesc), ctypes.c_char_p, ctypes.c_size_t]
     L.cmpx_bmm_plan.restype = ctypes.c_int
+    L.cmpx_bmm_small.argtypes = [ctypes.POINTER(BmmDesc), ctypes.c_void_p]
+    L.cmpx_bmm_small.restype = ctypes.c_int
+    L.cmpx_bmm_small_plan.argtypes = [ctypes.POINTER(BmmDesc), ctypes.c_char_p, ctypes.c_size_t]
+    L.cmpx_bmm_small_plan.restype = ctypes.c_int
     L.cmpx_linear.argtypes = [ctypes.POINTER(LinearDesc), ctypes.c_void_p]
     L.cmpx_linear.restype = ctypes.c_int
     L.cmpx_linear_plan.argtypes = [ctypes.POINTER(LinearDesc), ctypes.c_char_p, ctypes.c_size_t]
@@ -460,6 +464,37 @@ def bmm_plan(input, mat2) -> str:
     st = lib.cmpx_bmm_plan(ctypes.byref(desc), buf, 128)
     if st != OK:
         raise CmpxError("bmm plan", st)
+    return buf.value.decode()
+
+
+def _prepare_small(input, mat2):
+    _check_bmm_args(input, mat2)
+    c = torch.empty((input.shape[0], input.shape[1], mat2.shape[2]), dtype=input.dtype, device=input.device)
+    return _bmm_desc(input, mat2, c), c
+
+
+@_traced("bmm_small")
+def bmm_small(input, mat2):
+    """Batched product of many tiny matrices (the reference's _small_bmm route): one fp32 dot
+    product per output element on the GPU, operands read in place through their strides."""
+    desc, c = _prepare_small(input, mat2)
+    if c.numel() == 0:
+        return c
+    with torch.cuda.device(input.device):
+        st = lib.cmpx_bmm_small(ctypes.byref(desc), _stream_handle(input.device))
+    if st != OK:
+        raise CmpxError("bmm_small", st)
+    _post_check()
+    return c
+
+
+def bmm_small_plan(input, mat2) -> str:
+    """Name of the kernel ``bmm_small`` runs for these arguments."""
+    desc, _ = _prepare_small(input, mat2)
+    buf = ctypes.create_string_buffer(128)
+    st = lib.cmpx_bmm_small_plan(ctypes.byref(desc), buf, 128)
+    if st != OK:
+        raise CmpxError("bmm_small plan", st)
     return buf.value.decode()
 
 

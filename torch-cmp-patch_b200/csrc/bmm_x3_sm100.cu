@@ -59,8 +59,11 @@ struct X3GemmCfg {
   static constexpr int THREADS = 576;  // warp 0 TMA, 1 MMA, 2-9 converter, 10-17 epilogue
   static constexpr int CONV_THREADS = 256;
   static constexpr int W_EPI = 10;
-  // Longest K served: the accumulation error grows with K (measured rel-to-peak vs float64: 1e-5
-  // at K = 4096, 2e-5 at 8192, 9e-5 at 32768); longer products are left to stock.
+  // Longest K one launch accumulates: the tensor core's fp32 accumulation error grows with K
+  // (measured rel-to-peak vs float64: 1e-5 at K = 4096, 2e-5 at 8192, 9e-5 at 32768).  Longer
+  // products run as several launches over K chunks of at most this length: the first stores C,
+  // the others add their fp32 partial products into it (TMA reduce-add), so the error stays that
+  // of one chunk.
   static constexpr int MAX_K = 8192;
 };
 static_assert(X3GemmCfg::SMEM_BYTES <= 232448, "shared memory");
@@ -70,6 +73,7 @@ struct X3GemmParams {
   int n_kblocks;
   int tiles_m, tiles_n, n_tiles;
   const float* bias;  // [n] added to every row (linear), or null
+  int accumulate;     // 1: add the product into C (a later K chunk), 0: store it
   unsigned long long timeout_ns;
   unsigned int* dev_flags;
 };
@@ -272,7 +276,12 @@ __global__ void __launch_bounds__(576, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          if (r0 < p.m && col0 < p.n) tma_store_3d(&tm_c, slot, col0, r0, z);
+          if (r0 < p.m && col0 < p.n) {
+            if (p.accumulate)
+              tma_reduce_add_3d(&tm_c, slot, col0, r0, z);
+            else
+              tma_store_3d(&tm_c, slot, col0, r0, z);
+          }
           bulk_commit_group();
         }
         __syncwarp();
@@ -311,6 +320,7 @@ inline uint64_t unit_stride(int64_t s, int64_t extent, int64_t fallback_elems) {
 }
 
 constexpr const char* kX3Name = "bmm_x3tf32_sm100<f32,128x128x32,3st,persistent>";
+constexpr const char* kX3ChunkName = "bmm_x3tf32_sm100<f32,128x128x32,3st,persistent+k-chunks>";
 
 }  // namespace
 
@@ -320,7 +330,7 @@ const char* bmm_x3_plan(const cmpx_bmm_desc* d, int* status) {
     *status = CMPX_ERR_UNSUPPORTED_DTYPE;
     return "none";
   }
-  if (d->k < 1 || d->k > X3GemmCfg::MAX_K || d->m > (int64_t)128 * 65535 || d->n > (1ll << 31) - 256 || d->batch > 65535 ||
+  if (d->k < 1 || d->m > (int64_t)128 * 65535 || d->n > (1ll << 31) - 256 || d->batch > 65535 ||
       d->k > (1ll << 31) - 64) {
     *status = CMPX_ERR_UNSUPPORTED_SHAPE;
     return "none";
@@ -341,12 +351,12 @@ const char* bmm_x3_plan(const cmpx_bmm_desc* d, int* status) {
     *status = CMPX_ERR_MISALIGNED;
     return "none";
   }
-  return kX3Name;
+  return d->k > X3GemmCfg::MAX_K ? kX3ChunkName : kX3Name;
 }
 
 namespace {
 
-int launch_x3(const cmpx_bmm_desc* d, const LaunchCtx& ctx, const float* bias) {
+int launch_x3_once(const cmpx_bmm_desc* d, const LaunchCtx& ctx, const float* bias, int accumulate) {
   using C = X3GemmCfg;
   const uint64_t M = d->m, N = d->n, K = d->k, Z = d->batch;
   CUtensorMap ta, tb, tc;
@@ -394,11 +404,32 @@ int launch_x3(const cmpx_bmm_desc* d, const LaunchCtx& ctx, const float* bias) {
   if (n_tiles > (1ll << 31) - 1) return CMPX_ERR_UNSUPPORTED_SHAPE;
   p.n_tiles = static_cast<int>(n_tiles);
   p.bias = bias;
+  p.accumulate = accumulate;
   p.timeout_ns = ctx.timeout_ns;
   p.dev_flags = ctx.dev_flags;
   const int grid = static_cast<int>(std::min<int64_t>(n_tiles, std::max(1, ctx.num_sms)));
   bmm_x3_sm100_kernel<<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(ta, tb, tc, p);
   return cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
+}
+
+// The product over K in chunks of at most MAX_K (equal lengths, multiples of 32): one launch per
+// chunk on the caller's stream, the first storing C (and adding the bias), the others adding into
+// it.  A and B are K-major, so a chunk is the same operand from element k0 on: its pointers move
+// by k0 elements (16-byte aligned, k0 being a multiple of 32).
+int launch_x3(const cmpx_bmm_desc* d, const LaunchCtx& ctx, const float* bias) {
+  using C = X3GemmCfg;
+  if (d->k <= C::MAX_K) return launch_x3_once(d, ctx, bias, 0);
+  const int64_t chunks = (d->k + C::MAX_K - 1) / C::MAX_K;
+  const int64_t kc = ((d->k + chunks - 1) / chunks + C::BK - 1) / C::BK * C::BK;
+  for (int64_t k0 = 0; k0 < d->k; k0 += kc) {
+    cmpx_bmm_desc c = *d;
+    c.a = static_cast<const float*>(d->a) + k0;
+    c.b = static_cast<const float*>(d->b) + k0;
+    c.k = std::min<int64_t>(kc, d->k - k0);
+    const int st = launch_x3_once(&c, ctx, k0 == 0 ? bias : nullptr, k0 == 0 ? 0 : 1);
+    if (st != CMPX_OK) return st;
+  }
+  return CMPX_OK;
 }
 
 }  // namespace

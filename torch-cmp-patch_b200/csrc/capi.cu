@@ -306,6 +306,24 @@ int cmpx_bmm(const cmpx_bmm_desc* desc, void* stream) {
   return launch_bmm_sm100(desc, ctx);
 }
 
+int cmpx_bmm_small(const cmpx_bmm_desc* desc, void* stream) {
+  int st = CMPX_OK;
+  bmm_small_plan(desc, &st);
+  if (st != CMPX_OK) return st;
+  if (desc->batch == 0 || desc->m == 0 || desc->n == 0) return CMPX_OK;
+  LaunchCtx ctx;
+  st = device_ctx(&ctx, static_cast<cudaStream_t>(stream));
+  if (st != CMPX_OK) return st;
+  return launch_bmm_small(desc, ctx);
+}
+
+int cmpx_bmm_small_plan(const cmpx_bmm_desc* desc, char* buf, size_t buf_len) {
+  int st = CMPX_OK;
+  const char* name = bmm_small_plan(desc, &st);
+  copy_name(st == CMPX_OK ? name : "none", buf, buf_len);
+  return st;
+}
+
 int cmpx_softmax_rows(const cmpx_softmax_desc* desc, void* stream) {
   int st = CMPX_OK;
   softmax_rows_plan(desc, &st);

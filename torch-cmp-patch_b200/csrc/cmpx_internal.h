@@ -68,6 +68,9 @@ int launch_bmm_sm100(const cmpx_bmm_desc* d, const LaunchCtx& ctx);
 // fp32 on the tensor cores (3xTF32), K-major operands.
 const char* bmm_x3_plan(const cmpx_bmm_desc* d, int* status);
 int launch_bmm_x3(const cmpx_bmm_desc* d, const LaunchCtx& ctx);
+// Many tiny products (the reference's M*K*N <= 32768 route): one thread or warp per output element.
+const char* bmm_small_plan(const cmpx_bmm_desc* d, int* status);
+int launch_bmm_small(const cmpx_bmm_desc* d, const LaunchCtx& ctx);
 // The GEMM of a linear layer: x [m, k] times W^T with W [n, k] read in place as a K-major B.
 cmpx_bmm_desc linear_as_bmm(const cmpx_linear_desc* d);
 

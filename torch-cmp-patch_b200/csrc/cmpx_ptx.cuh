@@ -182,6 +182,17 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t sr
       : "memory");
 }
 
+// Element-wise add of a shared-memory tile into global memory (the tensor map's element type), in
+// the same bulk group bookkeeping as a store.
+__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, uint32_t src, int c0, int c1,
+                                                  int c2) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
