@@ -109,6 +109,28 @@ __device__ __forceinline__ void split_v4(uint32_t addr_in, uint32_t addr_hi, uin
                __float_as_uint(__uint_as_float(d) - __uint_as_float(hd)));
 }
 
+// S = Qh Kh^T + Qh Kl^T + Ql Kh^T over the first `steps` K=8 steps of the head dim (Q hi / lo from
+// TMEM, K hi / lo in shared memory, KCH bytes per 32-column chunk).  The step count is dispatched
+// once to a straight-line sequence of exactly that many MMAs per part: measured on B200, a runtime
+// guard around each MMA raised the issue cost from ~30-40 to ~70-90 clk per MMA.
+template <int S, int KCH>
+__device__ __forceinline__ void x3_issue_qk(int steps, uint32_t s_tmem, uint32_t qh, uint32_t ql, uint64_t dkh,
+                                            uint64_t dkl, uint32_t idesc) {
+  if (steps == S) {
+#pragma unroll
+    for (int part = 0; part < 3; ++part) {
+#pragma unroll
+      for (int s = 0; s < S; ++s) {
+        const uint64_t koff = static_cast<uint64_t>(((s >> 2) * KCH + (s & 3) * 32) >> 4);
+        umma_ts_tf32_w(s_tmem, (part == 2 ? ql : qh) + s * 8, (part == 1 ? dkl : dkh) + koff, idesc,
+                       (part > 0 || s > 0) ? 1u : 0u);
+      }
+    }
+  } else if constexpr (S > 1) {
+    x3_issue_qk<S - 1, KCH>(steps, s_tmem, qh, ql, dkh, dkl, idesc);
+  }
+}
+
 // MK: no mask (0), a boolean mask (1), an additive fp32 mask (2) -- separate instantiations.
 template <int MK>
 __global__ void __launch_bounds__(320, 1)
@@ -216,18 +238,7 @@ __global__ void __launch_bounds__(320, 1)
     auto issue_qk = [&](uint32_t sb, uint32_t s_tmem) {
       const uint64_t dkh = smem_desc_sw128(sb + C::ST_K, 16, 1024);
       const uint64_t dkl = smem_desc_sw128(sb + C::ST_B, 16, 1024);
-      const int steps = p.qk_steps;
-#pragma unroll
-      for (int part = 0; part < 3; ++part) {
-#pragma unroll
-        for (int s = 0; s < 8; ++s) {
-          if (s < steps) {
-            const uint64_t koff = static_cast<uint64_t>(((s >> 2) * C::KCH + (s & 3) * 32) >> 4);
-            umma_ts_tf32_w(s_tmem, tmem + (part == 2 ? C::TM_QL : C::TM_QH) + s * 8,
-                           (part == 1 ? dkl : dkh) + koff, kIdesc, (part > 0 || s > 0) ? 1u : 0u);
-          }
-        }
-      }
+      x3_issue_qk<8, C::KCH>(p.qk_steps, s_tmem, tmem + C::TM_QH, tmem + C::TM_QL, dkh, dkl, kIdesc);
     };
     // O (+)= Ph Vh + Ph Vl + Pl Vh over the tile's 64 keys (8 K-steps of 8); P of buffer pb.
     auto issue_pv = [&](uint32_t sb, int pb, bool acc) {
