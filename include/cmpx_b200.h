@@ -85,7 +85,7 @@ typedef enum cmpx_status {
  *    (the query-row stride a multiple of 8 elements for 16-bit calls, 4 for fp32, or 0).
  *  - fp32 calls read the mask in place (no workspace): its pointer 16-byte aligned and every
  *    stride a multiple of 16 bytes (boolean: 16 elements; additive: 4), else
- *    CMPX_ERR_UNSUPPORTED_SHAPE.
+ *    CMPX_ERR_MISALIGNED.
  * With causal the mask applies on top of it (torch's math path ANDs them).  A query row with no key
  * left gets an all-zero output (torch's result), not NaN.
  * Replaces: custom_attention_forward (src/main.cpp:1603-1774) and its launchers

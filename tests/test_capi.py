@@ -102,15 +102,20 @@ def test_grouped_query_heads_are_accepted(heads_kv):
 
 
 @pytest.mark.parametrize("cfg,entry", [
-    (dict(D=40, dtype=0), "attn_tf32x3_sm100"),
-    (dict(D=64, dtype=0, causal=1), "attn_tf32x3_sm100"),
-    (dict(D=100, dtype=0), None),                       # head dim above 64: stock is faster
-    (dict(D=37, dtype=0), None),                        # rows not 16-byte aligned: stock
+    (dict(D=40, dtype=0), "attn_tf32x3_sm100<D64"),
+    (dict(D=64, dtype=0, causal=1), "attn_tf32x3_sm100<D64"),
+    (dict(D=68, dtype=0), "attn_tf32x3_sm100<D128,128q,32kv"),   # 32-key tiles above 64
+    (dict(D=100, dtype=0), "attn_tf32x3_sm100<D128"),
+    (dict(D=128, dtype=0, causal=1), "attn_tf32x3_sm100<D128"),
+    (dict(D=37, dtype=0), "misaligned"),                # 148-byte rows: the binding pads them
+    (dict(D=160, dtype=0), None),                       # above the reference kernel's D <= 128
 ])
 def test_fp32_tile_table(cfg, entry):
     st, name = _plan(_attn(**cfg))
     if entry is None:
         assert st == N.ERR_UNSUPPORTED_SHAPE, (st, name)
+    elif entry == "misaligned":
+        assert st == N.ERR_MISALIGNED, (st, name)
     else:
         assert st == N.OK and name.startswith(entry), (st, name)
 
@@ -318,12 +323,12 @@ def test_mask_plans_on_the_16bit_and_fp32_kernels():
     d = _with_mask(_attn(Lq=64, Lk=77, dtype=2), (0, 0, 77, 1))
     st, name = _plan(d)
     assert st == 0 and name.startswith("fmha_sm100<bf16") and name.endswith("+mask>"), name
-    # fp32 reads the mask in place with 16-byte loads: rows 16-byte aligned, else stock
+    # fp32 reads the mask in place with 16-byte loads: rows 16-byte aligned (the binding pads them)
     d = _with_mask(_attn(Lq=64, Lk=77, D=40, dtype=0), (0, 0, 80, 1))
     st, name = _plan(d)
     assert st == 0 and name.startswith("attn_tf32x3_sm100") and name.endswith("+mask>"), name
     d = _with_mask(_attn(Lq=64, Lk=77, D=40, dtype=0), (0, 0, 77, 1))
-    assert _plan(d)[0] == N.ERR_UNSUPPORTED_SHAPE
+    assert _plan(d)[0] == N.ERR_MISALIGNED
     d = _with_mask(_attn(Lq=64, Lk=77, D=40, dtype=0), (0, 0, 80, 1))
     d.mask_kind = 1
     st, name = _plan(d)

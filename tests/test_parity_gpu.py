@@ -56,11 +56,10 @@ def _golden_tensor(key) -> torch.Tensor:
     return x if isinstance(x, torch.Tensor) else torch.from_numpy(x)
 
 
-# fp32 attention outside the 3xTF32 kernel's table (head dim above 64) is declined: on B200 stock
-# torch serves it faster than a CUDA-core fp32 kernel would.  The op raises; the patched torch op
-# returns stock's (the golden) answer.  (fp32 bmm runs on the 3xTF32 GEMM.)
+# fp32 attention outside the 3xTF32 kernel's table (head dim above 128, beyond the reference
+# kernel's own MAX_DIM) is declined: the op raises and the patched torch op returns stock's answer.
 def _declined(dtn, D):
-    return dtn == "float32" and D > 64
+    return dtn == "float32" and D > 128
 
 
 @pytest.mark.parametrize("i", range(len(C.SDPA_CASES)), ids=[c[0] for c in C.SDPA_CASES])
@@ -153,15 +152,28 @@ def test_attention_16bit_padded_head_dims(cuda_device, D):
     _run_and_check(cuda_device, q, k, v, None, True, f"bf16 D{D} causal")
 
 
-@pytest.mark.parametrize("D", [8, 40, 64, 100, 128])
+@pytest.mark.parametrize("D", [8, 40, 42, 64, 65, 80, 100, 128])
 @pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
 def test_attention_fp32(cuda_device, D, causal):
+    # D <= 64: 64-key tiles; 64 < D <= 128: 32-key tiles (the reference kernel's range, D <= 128);
+    # D = 42 rows are not 16-byte multiples: the binding copies them into padded buffers
     q, k, v = _rand_qkv(2, 2, 150, 170, D, torch.float32, seed=100 + D)
-    if D > 64:  # declined: stock serves it (faster on B200)
-        with pytest.raises(RuntimeError):
-            cmpext3.ops.attention(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), None, causal)
-        return
+    plan = N.attention_plan(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), None, causal)
+    assert plan.startswith("attn_tf32x3_sm100<D64" if D <= 64 else "attn_tf32x3_sm100<D128"), plan
     _run_and_check(cuda_device, q, k, v, None, causal, f"f32 D{D} causal={causal}")
+
+
+@pytest.mark.parametrize("D,causal", [(80, False), (128, True), (96, False)])
+def test_attention_fp32_wide_head_long_sequences(cuda_device, D, causal):
+    # several 128-row items per CTA and many 32-key tiles (both ring stages reused), GQA-free
+    q, k, v = _rand_qkv(2, 3, 1100, 1300, D, torch.float32, seed=7 * D)
+    _run_and_check(cuda_device, q, k, v, None, causal, f"f32 D{D} long causal={causal}")
+
+
+def test_attention_fp32_d160_is_declined(cuda_device):
+    q, k, v = (t.to(cuda_device) for t in _rand_qkv(1, 2, 64, 64, 160, torch.float32, seed=1))
+    with pytest.raises(RuntimeError):
+        cmpext3.ops.attention(q, k, v, None, False)
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32], ids=["bf16", "f16", "f32"])

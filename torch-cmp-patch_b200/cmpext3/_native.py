@@ -284,6 +284,18 @@ def _check_attention_args(query, key, value) -> None:
         raise RuntimeError(f"value shape {tuple(value.shape)} does not match key {tuple(key.shape)}")
 
 
+def _f32_attn_ok(t: torch.Tensor) -> bool:
+    return (t.stride(3) == 1 and t.data_ptr() % 16 == 0
+            and all(st > 0 and st % 4 == 0 for st in t.stride()[:3]))
+
+
+def _padded_f32(t: torch.Tensor) -> torch.Tensor:
+    B, H, L, D = t.shape
+    buf = torch.empty((B, H, L, (D + 3) // 4 * 4), dtype=t.dtype, device=t.device)
+    buf[..., :D].copy_(t)
+    return buf[..., :D]
+
+
 def _prepare_attention(query, key, value, scale, causal):
     _check_attention_args(query, key, value)
     B, H, Lq, D = query.shape
@@ -294,7 +306,10 @@ def _prepare_attention(query, key, value, scale, causal):
         # such inputs contiguous too, src/main.cpp:1693-1698).
         query, key, value = (t if _tma_ok(t) else t.contiguous() for t in (query, key, value))
     else:
-        query, key, value = (t if t.stride(3) == 1 else t.contiguous() for t in (query, key, value))
+        # The 3xTF32 kernel reads with TMA too: pointer and batch / head / row strides 16-byte
+        # aligned, head dim contiguous; other views are copied into buffers whose rows are padded
+        # to a multiple of 4 elements (the padding is never read).
+        query, key, value = (t if _f32_attn_ok(t) else _padded_f32(t) for t in (query, key, value))
     # Output in [B, Lq, H, D] memory viewed as [B, H, Lq, D] -- the layout torch's own CUDA SDPA
     # returns and the one a model's transpose(1, 2).reshape(B, Lq, H*D) wants.
     out = torch.empty((B, Lq, H, D), dtype=query.dtype, device=query.device).transpose(1, 2)

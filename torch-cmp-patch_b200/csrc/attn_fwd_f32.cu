@@ -1,10 +1,12 @@
 // attn_fwd_f32.cu -- routing of fp32 scaled-dot-product attention (fp32 inputs, fp32 accumulation).
 //
 // The accuracy contract for fp32 inputs is 1e-4 relative to stock fp32 SDPA, which rules out
-// single-pass TF32 tensor-core products (10-bit mantissa).  Calls with head_dim <= 64 and 16-byte
-// aligned operands run the tensor-core 3xTF32 kernel (attn_tf32x3_sm100.cu), which replaces
-// attention_fp32_strict_kernel (src/cuda/fp32_attention.cu:35-198).  The other fp32 calls are not
-// in the tile table: on B200 stock torch beats a CUDA-core fp32 kernel for them.
+// single-pass TF32 tensor-core products (10-bit mantissa).  Every fp32 call with head_dim <= 128
+// (the reference kernel's own range, src/cuda/fp32_attention.cu:8 MAX_DIM) and 16-byte aligned
+// operands runs the tensor-core 3xTF32 kernel (attn_tf32x3_sm100.cu; 64-key tiles for D <= 64,
+// 32-key tiles for D <= 128), which replaces attention_fp32_strict_kernel
+// (src/cuda/fp32_attention.cu:35-198).  The binding copies operands that are not 16-byte aligned
+// into padded buffers, so the remaining declines are head_dim > 128.
 #include <cuda_runtime.h>
 
 
@@ -27,14 +29,17 @@ const char* attn_f32_plan(const cmpx_attn_desc* d, int* status) {
     return "none";
   }
   if (attn_tf32x3_eligible(d)) {
-    if (!d->mask) return "attn_tf32x3_sm100<D64,128q,64kv,persistent>";
-    return d->mask_kind == CMPX_MASK_BOOL ? "attn_tf32x3_sm100<D64,128q,64kv,persistent+mask>"
-                                          : "attn_tf32x3_sm100<D64,128q,64kv,persistent+addmask>";
+    static const char* const names[2][3] = {
+        {"attn_tf32x3_sm100<D64,128q,64kv,persistent>", "attn_tf32x3_sm100<D64,128q,64kv,persistent+mask>",
+         "attn_tf32x3_sm100<D64,128q,64kv,persistent+addmask>"},
+        {"attn_tf32x3_sm100<D128,128q,32kv,persistent>", "attn_tf32x3_sm100<D128,128q,32kv,persistent+mask>",
+         "attn_tf32x3_sm100<D128,128q,32kv,persistent+addmask>"}};
+    const int mk = !d->mask ? 0 : d->mask_kind == CMPX_MASK_BOOL ? 1 : 2;
+    return names[d->head_dim <= 64 ? 0 : 1][mk];
   }
-  // Head dims above 64, or operands the 3xTF32 kernel cannot read with TMA: stock torch is faster
-  // than a CUDA-core fp32 kernel on B200 (measured: 20 vs 47 TFLOP/s at D = 128), so these calls
-  // are left to it -- what the reference's own runtime selection did for fp32 attention.
-  *status = CMPX_ERR_UNSUPPORTED_SHAPE;
+  // Operands the 3xTF32 kernel cannot read with TMA (strides or pointers not 16-byte aligned; the
+  // ctypes binding copies such inputs to padded buffers before it gets here).
+  *status = CMPX_ERR_MISALIGNED;
   return "none";
 }
 

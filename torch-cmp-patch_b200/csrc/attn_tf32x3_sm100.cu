@@ -42,13 +42,19 @@
 
 namespace cmpx {
 
+// DP_ = padded head dim (64 or 128).  D = 128 halves the key tile to 32 keys so that Q hi / lo, O
+// and the S / P buffers still fit TMEM's 512 columns, and runs a 2-stage ring (Q staging doubles).
+template <int DP_>
 struct X3Cfg {
-  static constexpr int BM = 128, BN = 64, DP = 64;  // query rows, keys per tile, padded head dim
-  static constexpr int QCH = BM * 128;              // one 32-column (128-byte) chunk of a Q tile
-  static constexpr int Q_BYTES = 2 * QCH;           // 32 KB staging tile
-  static constexpr int KCH = BN * 128;              // one chunk of a K / V / V^T tile (64 rows)
-  static constexpr int T_BYTES = 2 * KCH;           // 16 KB
-  static constexpr int NS = 3;                      // K/V ring stages
+  static constexpr int BM = 128, DP = DP_;          // query rows, padded head dim
+  static constexpr int BN = DP == 64 ? 64 : 32;     // keys per tile
+  static constexpr int NQC = DP / 32;               // 32-column (128-byte) chunks of the head dim
+  static constexpr int QCH = BM * 128;              // one chunk of a Q tile
+  static constexpr int Q_BYTES = NQC * QCH;         // staging tile: 32 KB (D 64) / 64 KB (D 128)
+  static constexpr int KCH = BN * 128;              // one head-dim chunk of a K / V tile (BN rows)
+  static constexpr int T_BYTES = NQC * KCH;         // 16 KB: a K, V, V^T hi or V^T lo tile
+  static constexpr int VCH = DP * 128;              // one 32-key chunk of V^T (DP rows)
+  static constexpr int NS = DP == 64 ? 3 : 2;       // K/V ring stages
   // stage slots: K (hi in place) | raw V, then K lo | V^T hi | V^T lo
   static constexpr int ST_K = 0, ST_B = T_BYTES, ST_VTH = 2 * T_BYTES, ST_VTL = 3 * T_BYTES;
   static constexpr int STAGE_BYTES = 4 * T_BYTES;   // 64 KB
@@ -70,9 +76,11 @@ struct X3Cfg {
   static constexpr int NBAR = B_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
-  static constexpr int TM_S0 = 0, TM_S1 = 64, TM_PL0 = 128, TM_PL1 = 192, TM_O = 256, TM_QH = 320,
-                       TM_QL = 384;
+  static_assert(SMEM_BYTES <= 232448, "shared memory");
+  static constexpr int TM_S0 = 0, TM_S1 = BN, TM_PL0 = 2 * BN, TM_PL1 = 3 * BN, TM_O = 4 * BN,
+                       TM_QH = 4 * BN + DP, TM_QL = 4 * BN + 2 * DP;
   static constexpr int TMEM_COLS = 512;
+  static_assert(TM_QL + DP <= TMEM_COLS, "TMEM columns");
   static constexpr int THREADS = 320;
   static constexpr int W_TMA = 0, W_MMA = 1;
 };
@@ -131,13 +139,29 @@ __device__ __forceinline__ void x3_issue_qk(int steps, uint32_t s_tmem, uint32_t
   }
 }
 
+// O (+)= Ph Vh + Ph Vl + Pl Vh over a tile's BN keys (BN / 8 K-steps of 8; V^T in 32-key chunks of
+// VCH bytes), P hi / lo from TMEM.
+template <int BN, int VCH>
+__device__ __forceinline__ void x3_issue_pv(uint32_t o_tmem, uint32_t ph, uint32_t pl, uint64_t dvh, uint64_t dvl,
+                                            uint32_t idesc, uint32_t acc0) {
+#pragma unroll
+  for (int part = 0; part < 3; ++part) {
+#pragma unroll
+    for (int s = 0; s < BN / 8; ++s) {
+      const uint64_t voff = static_cast<uint64_t>(((s >> 2) * VCH + (s & 3) * 32) >> 4);
+      umma_ts_tf32_w(o_tmem, (part == 2 ? pl : ph) + s * 8, (part == 1 ? dvl : dvh) + voff, idesc,
+                     (part > 0 || s > 0) ? 1u : acc0);
+    }
+  }
+}
+
 // MK: no mask (0), a boolean mask (1), an additive fp32 mask (2) -- separate instantiations.
-template <int MK>
+template <int DP, int MK>
 __global__ void __launch_bounds__(320, 1)
     attn_tf32x3_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                              const __grid_constant__ CUtensorMap tm_k,
                              const __grid_constant__ CUtensorMap tm_v, const X3Params p) {
-  using C = X3Cfg;
+  using C = X3Cfg<DP>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
   const uint32_t base = (raw_base + 1023u) & ~1023u;
@@ -208,13 +232,13 @@ __global__ void __launch_bounds__(320, 1)
         // the staging tile is free once the converter has read the previous item's Q
         if (k > 0 && !(ok = mbar_wait(bar(C::B_QFREE), static_cast<uint32_t>(k - 1) & 1u, ctl))) break;
         mbar_arrive_expect_tx(bar(C::B_QFULL), C::Q_BYTES);
-        for (int c = 0; c < 2; ++c) tma_load_4d(sQ + c * C::QCH, &tm_q, bar(C::B_QFULL), c * 32, q0, h, b);
+        for (int c = 0; c < C::NQC; ++c) tma_load_4d(sQ + c * C::QCH, &tm_q, bar(C::B_QFULL), c * 32, q0, h, b);
         for (int j = 0; ok && j < n_kv; ++j, ++load) {
           const int st = load % C::NS;
           if (!(ok = mbar_wait(bar(C::B_EMPTY + st), (static_cast<uint32_t>(load / C::NS) & 1u) ^ 1u, ctl))) break;
           const uint32_t sb = stage(load);
           mbar_arrive_expect_tx(bar(C::B_FULL + st), 2 * C::T_BYTES);
-          for (int c = 0; c < 2; ++c) {
+          for (int c = 0; c < C::NQC; ++c) {
             tma_load_4d(sb + C::ST_K + c * C::KCH, &tm_k, bar(C::B_FULL + st), c * 32, j * C::BN, h / p.group, b);
             tma_load_4d(sb + C::ST_B + c * C::KCH, &tm_v, bar(C::B_FULL + st), c * 32, j * C::BN, h / p.group, b);
           }
@@ -227,7 +251,8 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else if (warp == C::W_MMA) {
     // ------------------------------------------------------------------ MMA issuer (warp-uniform)
-    constexpr uint32_t kIdesc = idesc_tf32(128, 64, 0, 0);  // K-major A (TMEM) and B
+    constexpr uint32_t kIdesc = idesc_tf32(128, C::BN, 0, 0);    // S: K-major A (TMEM) and B
+    constexpr uint32_t kIdescPV = idesc_tf32(128, DP, 0, 0);     // O: K-major A (TMEM) and B (V^T)
     int load_base = 0;  // ring position of the item's first K/V tile
     int g = 0;          // tiles of all earlier items (S buffer and barrier phase bookkeeping)
     bool ok = true;
@@ -238,23 +263,14 @@ __global__ void __launch_bounds__(320, 1)
     auto issue_qk = [&](uint32_t sb, uint32_t s_tmem) {
       const uint64_t dkh = smem_desc_sw128(sb + C::ST_K, 16, 1024);
       const uint64_t dkl = smem_desc_sw128(sb + C::ST_B, 16, 1024);
-      x3_issue_qk<8, C::KCH>(p.qk_steps, s_tmem, tmem + C::TM_QH, tmem + C::TM_QL, dkh, dkl, kIdesc);
+      x3_issue_qk<DP / 8, C::KCH>(p.qk_steps, s_tmem, tmem + C::TM_QH, tmem + C::TM_QL, dkh, dkl, kIdesc);
     };
     // O (+)= Ph Vh + Ph Vl + Pl Vh over the tile's 64 keys (8 K-steps of 8); P of buffer pb.
     auto issue_pv = [&](uint32_t sb, int pb, bool acc) {
       const uint64_t dvh = smem_desc_sw128(sb + C::ST_VTH, 16, 1024);
       const uint64_t dvl = smem_desc_sw128(sb + C::ST_VTL, 16, 1024);
       const uint32_t ph = tmem + (pb ? C::TM_S1 : C::TM_S0), pl = tmem + (pb ? C::TM_PL1 : C::TM_PL0);
-      const uint32_t acc0 = acc ? 1u : 0u;
-#pragma unroll
-      for (int part = 0; part < 3; ++part) {
-#pragma unroll
-        for (int s = 0; s < 8; ++s) {
-          const uint64_t voff = static_cast<uint64_t>(((s >> 2) * C::KCH + (s & 3) * 32) >> 4);
-          umma_ts_tf32_w(tmem + C::TM_O, (part == 2 ? pl : ph) + s * 8, (part == 1 ? dvl : dvh) + voff,
-                         kIdesc, (part > 0 || s > 0) ? 1u : acc0);
-        }
-      }
+      x3_issue_pv<C::BN, C::VCH>(tmem + C::TM_O, ph, pl, dvh, dvl, kIdescPV, acc ? 1u : 0u);
     };
     // Warp-uniform non-blocking test of one barrier phase.
     auto ready = [&](uint32_t b, uint32_t parity) -> bool {
@@ -328,34 +344,31 @@ __global__ void __launch_bounds__(320, 1)
     for (int k = 0, w = blockIdx.x; ok && w < p.n_items; ++k, w += gridDim.x) {
       int b, h, q0, n_kv;
       geometry(w, b, h, q0, n_kv);
-      // Q: this thread's row from the staging tile -> hi / lo -> TMEM.
+      // Q: this thread's row from the staging tile -> hi / lo -> TMEM, one 32-column chunk at a
+      // time.  TMEM Q is free once the previous item's last S product is done.
       if (!(ok = mbar_wait_all(bar(C::B_QFULL), static_cast<uint32_t>(k) & 1u, ctl))) break;
-      uint32_t q[64];
+      if (k > 0 && !(ok = mbar_wait_all(bar(C::B_QEMPTY), static_cast<uint32_t>(k - 1) & 1u, ctl))) break;
+      tc_fence_after_sync();
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
+      for (int c = 0; c < C::NQC; ++c) {
+        uint32_t q[32];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           const uint32_t addr = sQ + c * C::QCH + row * 128 + ((u ^ (row & 7)) << 4);
           asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                       : "=r"(q[c * 32 + u * 4]), "=r"(q[c * 32 + u * 4 + 1]), "=r"(q[c * 32 + u * 4 + 2]),
-                         "=r"(q[c * 32 + u * 4 + 3])
+                       : "=r"(q[u * 4]), "=r"(q[u * 4 + 1]), "=r"(q[u * 4 + 2]), "=r"(q[u * 4 + 3])
                        : "r"(addr));
         }
-      mbar_arrive(bar(C::B_QFREE));  // the staging tile may take the next item's Q
-      // TMEM Q is free once the previous item's last S product is done.
-      if (k > 0 && !(ok = mbar_wait_all(bar(C::B_QEMPTY), static_cast<uint32_t>(k - 1) & 1u, ctl))) break;
-      tc_fence_after_sync();
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
         uint32_t hi[32], lo[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          hi[e] = tf32_trunc(q[hh * 32 + e]);
-          lo[e] = __float_as_uint(__uint_as_float(q[hh * 32 + e]) - __uint_as_float(hi[e]));
+          hi[e] = tf32_trunc(q[e]);
+          lo[e] = __float_as_uint(__uint_as_float(q[e]) - __uint_as_float(hi[e]));
         }
-        tmem_st32(lane_base + C::TM_QH + hh * 32, hi);
-        tmem_st32(lane_base + C::TM_QL + hh * 32, lo);
+        tmem_st32(lane_base + C::TM_QH + c * 32, hi);
+        tmem_st32(lane_base + C::TM_QL + c * 32, lo);
       }
+      mbar_arrive(bar(C::B_QFREE));  // the staging tile may take the next item's Q
       tmem_st_wait();
       tc_fence_before_sync();
       mbar_arrive(bar(C::B_QCONV));
@@ -363,13 +376,14 @@ __global__ void __launch_bounds__(320, 1)
         const int st = load % C::NS;
         if (!(ok = mbar_wait_all(bar(C::B_FULL + st), static_cast<uint32_t>(load / C::NS) & 1u, ctl))) break;
         const uint32_t sb = stage(load);
-        // V [key][d] (slot B) -> V^T [d][key] hi / lo (K-major B operand: rows d, 64 keys in two
-        // 128-byte chunks).  Thread -> (d = tid % 64, keys half*32 .. half*32+31).
+        // V [key][d] (slot B) -> V^T [d][key] hi / lo (K-major B operand: rows d, BN keys in 32-key
+        // 128-byte chunks of VCH bytes).  Thread -> (d = tid % DP, keys half*32 .. half*32+31):
+        // two threads per row d for D = 64 (64 keys), one for D = 128 (32 keys).
         {
-          const int d = tid & 63, half = tid >> 6;
+          const int d = tid % DP, half = tid / DP;
           const uint32_t vsrc = sb + C::ST_B + (d >> 5) * C::KCH + (d & 3) * 4;
           const int du = (d & 31) >> 2;  // 16-byte unit of column d inside its 128-byte row
-          const uint32_t dst_row = half * C::KCH + d * 128;
+          const uint32_t dst_row = half * C::VCH + d * 128;
 #pragma unroll
           for (int u = 0; u < 8; ++u) {  // four keys per 16-byte unit of the V^T row
             uint32_t x[4];
@@ -416,8 +430,11 @@ __global__ void __launch_bounds__(320, 1)
         const int gj = g + j, bs = gj & 1;
         if (!(ok = mbar_wait_all(bar(C::B_SFULL + bs), static_cast<uint32_t>(gj >> 1) & 1u, ctl))) break;
         tc_fence_after_sync();
-        uint32_t sr[64];
-        tmem_ld64(lane_base + (bs ? C::TM_S1 : C::TM_S0), sr);
+        uint32_t sr[C::BN];
+        if constexpr (C::BN == 64)
+          tmem_ld64(lane_base + (bs ? C::TM_S1 : C::TM_S0), sr);
+        else
+          tmem_ld32(lane_base + (bs ? C::TM_S1 : C::TM_S0), sr);
         float* s = reinterpret_cast<float*>(sr);
         tc_fence_before_sync();
         const int kv0 = j * C::BN;
@@ -466,7 +483,7 @@ __global__ void __launch_bounds__(320, 1)
           int lim = p.len_k - kv0;
           if (p.causal) lim = min(lim, qrow - kv0 + 1);
 #pragma unroll
-          for (int c = 0; c < 64; ++c)
+          for (int c = 0; c < C::BN; ++c)
             if (c >= lim) s[c] = masked;
         }
         float a8[8];
@@ -474,14 +491,14 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
           for (int e = 0; e < 8; ++e) a8[e] = fminf(s[e], s[8 + e]);
 #pragma unroll
-          for (int c = 16; c < 64; c += 16)
+          for (int c = 16; c < C::BN; c += 16)
 #pragma unroll
             for (int e = 0; e < 8; ++e) a8[e] = fmin3(a8[e], s[c + e], s[c + 8 + e]);
         } else {
 #pragma unroll
           for (int e = 0; e < 8; ++e) a8[e] = fmaxf(s[e], s[8 + e]);
 #pragma unroll
-          for (int c = 16; c < 64; c += 16)
+          for (int c = 16; c < C::BN; c += 16)
 #pragma unroll
             for (int e = 0; e < 8; ++e) a8[e] = fmax3(a8[e], s[c + e], s[c + 8 + e]);
         }
@@ -500,7 +517,7 @@ __global__ void __launch_bounds__(320, 1)
         const uint64_t sl2x2 = f2_pack(sl2, sl2), nmx2 = f2_pack(nm, nm);
         uint64_t la = f2_pack(0.f, 0.f), lb = la;
 #pragma unroll
-        for (int c = 0; c < 64; c += 2) {
+        for (int c = 0; c < C::BN; c += 2) {
           float x0, x1;
           f2_unpack(f2_fma(f2_pack(s[c], s[c + 1]), sl2x2, nmx2), x0, x1);
           s[c] = ex2_approx(x0);
@@ -519,20 +536,17 @@ __global__ void __launch_bounds__(320, 1)
           const int gprev = gj - 1;
           if (!(ok = mbar_wait_all(bar(C::B_PVD + (gprev & 1)), static_cast<uint32_t>(gprev >> 1) & 1u, ctl))) break;
           tc_fence_after_sync();
-          uint32_t o[64];
-          tmem_ld64(lane_base + C::TM_O, o);
 #pragma unroll
-          for (int e = 0; e < 64; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          for (int hh = 0; hh < C::NQC; ++hh) {
+            uint32_t o[32];
+            tmem_ld32(lane_base + C::TM_O + hh * 32, o);
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            uint32_t part[32];
-#pragma unroll
-            for (int e = 0; e < 32; ++e) part[e] = o[hh * 32 + e];
-            tmem_st32(lane_base + C::TM_O + hh * 32, part);
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(lane_base + C::TM_O + hh * 32, o);
           }
         }
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
+        for (int hh = 0; hh < C::BN / 32; ++hh) {
           uint32_t ph[32], pl[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
@@ -552,24 +566,30 @@ __global__ void __launch_bounds__(320, 1)
       const int glast = g + n_kv - 1;
       if (!(ok = mbar_wait_all(bar(C::B_PVD + (glast & 1)), static_cast<uint32_t>(glast >> 1) & 1u, ctl))) break;
       tc_fence_after_sync();
-      uint32_t o[64];
-      tmem_ld64(lane_base + C::TM_O, o);
-      tc_fence_before_sync();
-      mbar_arrive(bar(C::B_OFREE));
-      if (qrow < p.len_q) {
-        const float inv_l = (MK != 0 && !(l_run > 0.f)) ? 0.f : 1.f / l_run;  // no key: output 0
-        float* dst = p.o + b * p.os_b + h * p.os_h + static_cast<long long>(qrow) * p.os_s;
-        if ((p.head_dim & 3) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+      const float inv_l = (MK != 0 && !(l_run > 0.f)) ? 0.f : 1.f / l_run;  // no key: output 0
+      float* dst = p.o + b * p.os_b + h * p.os_h + static_cast<long long>(qrow) * p.os_s;
+      const bool vec = (p.head_dim & 3) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
 #pragma unroll
-          for (int c = 0; c < 64; c += 4)
-            if (c < p.head_dim)
-              *reinterpret_cast<float4*>(dst + c) =
-                  make_float4(__uint_as_float(o[c]) * inv_l, __uint_as_float(o[c + 1]) * inv_l,
-                              __uint_as_float(o[c + 2]) * inv_l, __uint_as_float(o[c + 3]) * inv_l);
-        } else {
+      for (int hh = 0; hh < C::NQC; ++hh) {  // O / l, 32 columns at a time
+        uint32_t o[32];
+        tmem_ld32(lane_base + C::TM_O + hh * 32, o);
+        if (hh + 1 == C::NQC) {
+          tc_fence_before_sync();
+          mbar_arrive(bar(C::B_OFREE));
+        }
+        if (qrow < p.len_q && hh * 32 < p.head_dim) {
+          if (vec) {
 #pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if (c < p.head_dim) dst[c] = __uint_as_float(o[c]) * inv_l;
+            for (int c = 0; c < 32; c += 4)
+              if (hh * 32 + c < p.head_dim)
+                *reinterpret_cast<float4*>(dst + hh * 32 + c) =
+                    make_float4(__uint_as_float(o[c]) * inv_l, __uint_as_float(o[c + 1]) * inv_l,
+                                __uint_as_float(o[c + 2]) * inv_l, __uint_as_float(o[c + 3]) * inv_l);
+          } else {
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+              if (hh * 32 + c < p.head_dim) dst[hh * 32 + c] = __uint_as_float(o[c]) * inv_l;
+          }
         }
       }
       g += n_kv;
@@ -611,7 +631,7 @@ bool make_map_f32(CUtensorMap* map, const void* ptr, int64_t D, int64_t L, int64
 }  // namespace
 
 bool attn_tf32x3_eligible(const cmpx_attn_desc* d) {
-  if (d->dtype != CMPX_F32 || d->head_dim < 1 || d->head_dim > 64) return false;
+  if (d->dtype != CMPX_F32 || d->head_dim < 1 || d->head_dim > 128) return false;
   if (d->mask) {  // rows read with 16-byte loads: base and stepped strides 16-byte aligned
     const int64_t unit = d->mask_kind == CMPX_MASK_BOOL ? 16 : 4;  // elements per 16 bytes
     if ((reinterpret_cast<uintptr_t>(d->mask) & 15u) != 0 || d->mask_stride[3] != 1) return false;
@@ -630,8 +650,11 @@ bool attn_tf32x3_eligible(const cmpx_attn_desc* d) {
   return true;
 }
 
-int launch_attn_tf32x3(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
-  using C = X3Cfg;
+namespace {
+
+template <int DP>
+int launch_tf32x3_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
+  using C = X3Cfg<DP>;
   CUtensorMap tq, tk, tv;
   if (!make_map_f32(&tq, d->q, d->head_dim, d->len_q, d->heads, d->batch, d->q_stride, C::BM) ||
       !make_map_f32(&tk, d->k, d->head_dim, d->len_k, attn_heads_kv(d), d->batch, d->k_stride, C::BN) ||
@@ -642,9 +665,9 @@ int launch_attn_tf32x3(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   cudaGetDevice(&dev);
   cudaError_t attr_err = cudaSuccess;
   std::call_once(once[dev & 63], [&] {
-    const void* ptrs[3] = {reinterpret_cast<const void*>(&attn_tf32x3_sm100_kernel<0>),
-                           reinterpret_cast<const void*>(&attn_tf32x3_sm100_kernel<1>),
-                           reinterpret_cast<const void*>(&attn_tf32x3_sm100_kernel<2>)};
+    const void* ptrs[3] = {reinterpret_cast<const void*>(&attn_tf32x3_sm100_kernel<DP, 0>),
+                           reinterpret_cast<const void*>(&attn_tf32x3_sm100_kernel<DP, 1>),
+                           reinterpret_cast<const void*>(&attn_tf32x3_sm100_kernel<DP, 2>)};
     for (const void* f : ptrs)
       if (attr_err == cudaSuccess)
         attr_err = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
@@ -675,12 +698,18 @@ int launch_attn_tf32x3(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   p.dev_flags = ctx.dev_flags;
   const int grid = std::min(p.n_items, std::max(1, ctx.num_sms));
   if (!d->mask)
-    attn_tf32x3_sm100_kernel<0><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, p);
+    attn_tf32x3_sm100_kernel<DP, 0><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, p);
   else if (d->mask_kind == CMPX_MASK_BOOL)
-    attn_tf32x3_sm100_kernel<1><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, p);
+    attn_tf32x3_sm100_kernel<DP, 1><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, p);
   else
-    attn_tf32x3_sm100_kernel<2><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, p);
+    attn_tf32x3_sm100_kernel<DP, 2><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, p);
   return cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
+}
+
+}  // namespace
+
+int launch_attn_tf32x3(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
+  return d->head_dim <= 64 ? launch_tf32x3_typed<64>(d, ctx) : launch_tf32x3_typed<128>(d, ctx);
 }
 
 }  // namespace cmpx
