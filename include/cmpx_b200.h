@@ -39,9 +39,10 @@
 extern "C" {
 #endif
 
-#define CMPX_ABI_VERSION 5  /* 2: cmpx_attn_desc.heads_kv (grouped-query attention); 3: cmpx_linear;
+#define CMPX_ABI_VERSION 6  /* 2: cmpx_attn_desc.heads_kv (grouped-query attention); 3: cmpx_linear;
                                4: cmpx_attn_desc.mask / mask_kind (boolean or additive attention mask);
-                               5: cmpx_bmm_small / cmpx_bmm_small_plan */
+                               5: cmpx_bmm_small / cmpx_bmm_small_plan;
+                               6: cmpx_bmm_rowstats(_plan), cmpx_softmax_product(_plan) */
 
 /* Element type of every operand of one call (inputs and output share it, as in the reference:
  * dtype in == dtype out, src/main.cpp:1623-1627, :366-369). */
@@ -229,6 +230,33 @@ typedef struct cmpx_softmax_desc {
 } cmpx_softmax_desc;
 
 CMPX_API int cmpx_softmax_rows(const cmpx_softmax_desc* desc, void* stream);
+
+/* The einsum-attention chain einsum('bhid,bhjd->bhij') -> softmax(-1) -> einsum('bhij,bhjd->bhid')
+ * (cmpext3/einsum_ops.py:69-121 in the reference, softmax left stock there,
+ * cmpext3/__init__.py:133-138) with the score tensor written once and never read back: the scores
+ * product also emits row statistics, and the softmax recomputes the scores from the product's
+ * operands instead of reading them.  No counterpart among the reference's native ops.
+ *
+ * Row statistics of a 16-bit product C = A @ B: for every row r and every run of 64 columns
+ * j*64 .. j*64+63 (the last one clipped at n), (max, sum) with max = the largest C[r, c] of the run
+ * as stored (rounded to the 16-bit type) and sum = sum over the run of exp(C[r, c] - max), in fp32:
+ * float stats[batch][ceil(n / 64)][m][2] (a run's rows contiguous), 8-byte aligned.
+ *
+ * cmpx_bmm_rowstats: cmpx_bmm (same descriptor, same result, bit for bit) for 16-bit A and B that
+ * are both K-major (a_stride[2] == 1, b_stride[1] == 1), writing the statistics as well. */
+CMPX_API int cmpx_bmm_rowstats(const cmpx_bmm_desc* desc, float* stats, void* stream);
+CMPX_API int cmpx_bmm_rowstats_plan(const cmpx_bmm_desc* desc, const float* stats, char* buf, size_t buf_len);
+
+/* cmpx_softmax_product: y = softmax(A @ B, dim=-1), A [batch, m, k] and B [batch, k, n] as in
+ * cmpx_bmm_desc (16-bit, both K-major; 1 <= k <= 128), y [batch, m, n] with the strides in c_stride
+ * (columns contiguous, rows 16-byte aligned; desc->c is not used), stats the product's row
+ * statistics as cmpx_bmm_rowstats wrote them.  The scores are recomputed on the tensor cores with
+ * the same instruction shape and k order as cmpx_bmm and rounded to the 16-bit type as cmpx_bmm
+ * rounds them, so y is the softmax of exactly the tensor cmpx_bmm returns for (A, B); the
+ * [batch, m, n] score tensor is never read.  Each y is exp(s - max) / sum in fp32, rounded once. */
+CMPX_API int cmpx_softmax_product(const cmpx_bmm_desc* desc, const float* stats, void* y, void* stream);
+CMPX_API int cmpx_softmax_product_plan(const cmpx_bmm_desc* desc, const float* stats, const void* y, char* buf,
+                                       size_t buf_len);
 
 /* Name of the tile-table entry a call would use, written into buf (NUL-terminated).
  * Returns CMPX_OK or the status the call itself would return.  Replaces the per-signature

@@ -50,7 +50,8 @@ STOCK_UNPATCHED = {(torch, "baddbmm"): torch.baddbmm, (F, "layer_norm"): F.layer
 STOCK_SOFTMAX = {"torch": torch.softmax, "F": F.softmax, "Tensor": torch.Tensor.softmax}
 
 NATIVE_OPS = ["attention", "bmm", "attention_plan", "bmm_plan", "softmax", "linear", "linear_plan",
-              "bmm_small", "bmm_small_plan"]
+              "bmm_small", "bmm_small_plan", "bmm_rowstats", "bmm_rowstats_plan", "softmax_product",
+              "softmax_product_plan"]
 
 
 def pytest_configure(config):
@@ -85,6 +86,8 @@ def native(monkeypatch):
     fake.bmm_plan.return_value = "fake-bmm-entry"
     fake.linear_plan.return_value = "fake-linear-entry"
     fake.bmm_small_plan.return_value = "fake-bmm-small-entry"
+    fake.bmm_rowstats_plan.return_value = "fake-bmm-rowstats-entry"
+    fake.softmax_product_plan.return_value = "fake-softmax-product-entry"
     monkeypatch.setattr(cmpext3, "_C", fake)
     monkeypatch.setattr(cmpext3, "ops", fake)
     return fake

@@ -42,7 +42,7 @@ def test_library_exports_nothing_undeclared():
 
 
 def test_abi_version_and_status_strings():
-    assert N.lib.cmpx_abi_version() == 5
+    assert N.lib.cmpx_abi_version() == 6
     header = HEADER.read_text()
     m = re.search(r"#define CMPX_ABI_VERSION (\d+)", header)
     assert m and int(m.group(1)) == N.ABI_VERSION == N.lib.cmpx_abi_version()
@@ -174,6 +174,55 @@ def test_bmm_plan_for_the_einsum_attention_shapes():
     # fp32: the 3xTF32 GEMM, which reads K-major operands only
     st, name = _bplan(_bmm(64, 2048, 2048, 64, dtype=0, bt=True))
     assert st == 0 and name.startswith("bmm_x3tf32_sm100<f32,128x128x32"), name
+
+
+def _rsplan(d, stats=0x20000):
+    buf = ctypes.create_string_buffer(128)
+    st = N.lib.cmpx_bmm_rowstats_plan(ctypes.byref(d), stats, buf, 128)
+    return st, buf.value.decode()
+
+
+def _spplan(d, stats=0x20000, y=0x30000):
+    buf = ctypes.create_string_buffer(128)
+    st = N.lib.cmpx_softmax_product_plan(ctypes.byref(d), stats, y, buf, 128)
+    return st, buf.value.decode()
+
+
+def test_fused_softmax_plans_for_the_einsum_attention_scores():
+    for dtype, tag in ((2, "bf16"), (1, "f16")):
+        st, name = _rsplan(_bmm(64, 2048, 2048, 64, dtype=dtype, bt=True))
+        assert st == 0 and name == f"bmm_sm100<{tag},128x128x64,A:k-major,B:k-major,4st,persistent,rowstats>"
+        st, name = _spplan(_bmm(64, 2048, 2048, 64, dtype=dtype, bt=True))
+        assert st == 0 and name == f"softmax_product_sm100<{tag},128x128,k64,rowstats>", name
+    st, name = _spplan(_bmm(4, 300, 1000, 128, bt=True))
+    assert st == 0 and ",k128," in name
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(bt=False), "ERR_MISALIGNED"),        # B contiguous along n: the statistics need K-major B
+    (dict(dtype=0), "ERR_UNSUPPORTED_DTYPE"),  # 16-bit only
+    (dict(k=30), "ERR_MISALIGNED"),            # 60-byte A rows
+])
+def test_rowstats_plan_rejects(kw, status):
+    args = dict(nb=2, m=256, n=256, k=64, bt=True)
+    args.update(kw)
+    assert _rsplan(_bmm(**args))[0] == getattr(N, status)
+    assert _rsplan(_bmm(2, 256, 256, 64, bt=True), stats=0x20004)[0] == N.ERR_INVALID_ARGUMENT  # 4-byte aligned
+    assert _rsplan(_bmm(2, 256, 256, 64, bt=True), stats=0)[0] == N.ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(k=136), "ERR_UNSUPPORTED_SHAPE"),    # head dims up to 128
+    (dict(bt=False), "ERR_MISALIGNED"),
+    (dict(dtype=0), "ERR_UNSUPPORTED_DTYPE"),
+    (dict(ptr=0x10008), "ERR_MISALIGNED"),
+])
+def test_softmax_product_plan_rejects(kw, status):
+    args = dict(nb=2, m=256, n=256, k=64, bt=True)
+    args.update(kw)
+    assert _spplan(_bmm(**args))[0] == getattr(N, status)
+    assert _spplan(_bmm(2, 256, 256, 64, bt=True), stats=0)[0] == N.ERR_INVALID_ARGUMENT
+    assert _spplan(_bmm(2, 256, 256, 64, bt=True), y=0x30008)[0] == N.ERR_MISALIGNED
 
 
 @pytest.mark.parametrize("kw,status", [

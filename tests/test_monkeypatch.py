@@ -355,6 +355,67 @@ class TestSoftmax:
         F.softmax(s)  # implicit dim: stock (with torch's warning)
         native.softmax.assert_not_called()
 
+    def _bf16_scores(self, native):
+        # einsum scores of 16-bit q, k with a 32-wide head dim and 256 keys: the planner's bmm
+        # operands are contiguous along the head dim, so the product is computed with its row
+        # statistics and its operands are recorded
+        q = torch.randn(1, 2, 64, 32).to(torch.bfloat16)
+        k = torch.randn(1, 2, 256, 32).to(torch.bfloat16)
+        self.stats = []
+
+        def rowstats(a, b):
+            st = torch.zeros(a.shape[0], (b.shape[2] + 63) // 64, a.shape[1], 2)
+            self.stats.append(st)
+            return torch.zeros(a.shape[0], a.shape[1], b.shape[2], dtype=a.dtype), st
+        native.bmm_rowstats.side_effect = rowstats
+        return q, k, torch.einsum("bhid,bhjd->bhij", q, k)
+
+    def test_softmax_of_recorded_scores_recomputes_them_from_the_operands(self, patched, native, monkeypatch):
+        force_eligible(monkeypatch)
+        q, k, s = self._bf16_scores(native)
+        native.bmm.assert_not_called()
+        assert native.bmm_rowstats.call_count == 1
+        native.softmax_product.return_value = torch.full((2, 64, 256), 0.5, dtype=torch.bfloat16)
+        got = torch.softmax(s, -1)
+        native.softmax.assert_not_called()
+        assert native.softmax_product.call_count == 1
+        a, b, stats = native.softmax_product.call_args[0]
+        assert torch.equal(a, q.reshape(2, 64, 32)) and torch.equal(b, k.reshape(2, 256, 32).transpose(1, 2))
+        assert stats is self.stats[0]  # the statistics the scores product returned
+        assert got.shape == s.shape and "softmax_product" in cmpext3.autoselect_report()
+
+    def test_scores_changed_in_place_are_read_not_recomputed(self, patched, native, monkeypatch):
+        force_eligible(monkeypatch)
+        _, _, s = self._bf16_scores(native)
+        s.mul_(2)  # the recorded operands no longer describe s
+        native.softmax.return_value = torch.ones(1, 2, 64, 256, dtype=torch.bfloat16)
+        torch.softmax(s, -1)
+        native.softmax_product.assert_not_called()
+        assert native.softmax.call_count == 1
+
+    def test_operand_changed_in_place_is_not_recomputed(self, patched, native, monkeypatch):
+        force_eligible(monkeypatch)
+        q, _, s = self._bf16_scores(native)
+        q.add_(1)
+        native.softmax.return_value = torch.ones(1, 2, 64, 256, dtype=torch.bfloat16)
+        torch.softmax(s, -1)
+        native.softmax_product.assert_not_called()
+
+    def test_only_attention_shaped_products_carry_row_statistics(self, patched, native, monkeypatch):
+        force_eligible(monkeypatch)
+        native.bmm.side_effect = lambda a, b: torch.zeros(a.shape[0], a.shape[1], b.shape[2], dtype=a.dtype)
+        native.bmm_rowstats.side_effect = lambda a, b: (
+            torch.zeros(a.shape[0], a.shape[1], b.shape[2], dtype=a.dtype),
+            torch.zeros(a.shape[0], (b.shape[2] + 63) // 64, a.shape[1], 2))
+        bf = torch.bfloat16
+        torch.bmm(torch.randn(2, 64, 64).to(bf), torch.randn(2, 256, 64).to(bf).transpose(1, 2))
+        assert native.bmm_rowstats.call_count == 1 and native.bmm.call_count == 0
+        torch.bmm(torch.randn(2, 64, 64), torch.randn(2, 256, 64).transpose(1, 2))  # fp32
+        torch.bmm(torch.randn(2, 64, 256).to(bf), torch.randn(2, 256, 256).to(bf))  # k > 128
+        torch.bmm(torch.randn(2, 64, 64).to(bf), torch.randn(2, 64, 256).to(bf))  # B contiguous along n
+        torch.bmm(torch.randn(2, 64, 64).to(bf), torch.randn(2, 96, 64).to(bf).transpose(1, 2))  # n < 128
+        assert native.bmm_rowstats.call_count == 1 and native.bmm.call_count == 4
+
     def test_declined_native_softmax_falls_back_to_stock(self, patched, native, monkeypatch):
         force_eligible(monkeypatch)
         native.bmm.return_value = torch.randn(2, 64, 64)  # M*K*N above the small-matrix route

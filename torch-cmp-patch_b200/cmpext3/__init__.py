@@ -229,10 +229,27 @@ def _patched_bmm(input, mat2, *, out=None):
                          lambda: _small_bmm(input, mat2),
                          lambda: orig(input, mat2),
                          lambda: _C.bmm_small_plan(input, mat2))
-    return _note_product(_dispatch("bmm", input, (input.shape, input.dtype, mat2.shape),
-                                   lambda: _C.bmm(input, mat2),
-                                   lambda: orig(input, mat2),
-                                   lambda: _C.bmm_plan(input, mat2)))
+    made = {}
+    if _fusable(input, mat2):
+        # a product a softmax may follow: the same product, with its row statistics
+        def native():
+            made["native"], made["stats"] = _C.bmm_rowstats(input, mat2)
+            return made["native"]
+
+        def plan():
+            return _C.bmm_rowstats_plan(input, mat2)
+    else:
+        def native():
+            made["native"] = r = _C.bmm(input, mat2)
+            return r
+
+        def plan():
+            return _C.bmm_plan(input, mat2)
+    c = _note_product(_dispatch("bmm", input, (input.shape, input.dtype, mat2.shape), native,
+                                lambda: orig(input, mat2), plan))
+    if made.get("native") is c and "stats" in made:
+        _note_operands(c, input, mat2, made["stats"])
+    return c
 
 
 # Tensors returned by the patched einsum / bmm / matmul, keyed by id and held weakly: a softmax
@@ -257,6 +274,44 @@ def _is_product(t: Any) -> bool:
     return ref is not None and ref() is t
 
 
+# Operands and row statistics of a product the native bmm kernel computed, kept (with the in-place
+# version counters) while the product lives, when a softmax over the product's last dimension can be
+# recomputed from them instead of reading the product back: 16-bit, both operands contiguous along
+# the contracted dimension, k <= 128, a product row of at least 128 elements (what attention scores
+# look like).
+_OPERANDS: dict[int, tuple] = {}
+
+
+def _fusable(a: torch.Tensor, b: torch.Tensor) -> bool:
+    return (a.dtype in (torch.float16, torch.bfloat16) and a.dim() == 3 and b.dim() == 3
+            and 1 <= a.shape[2] <= 128 and b.shape[2] >= 128 and b.shape[2] % 8 == 0
+            and a.stride(2) == 1 and b.stride(1) == 1)
+
+
+def _note_operands(t: torch.Tensor, a: torch.Tensor, b: torch.Tensor, stats: torch.Tensor) -> None:
+    if not _fusable(a, b):
+        return
+    key = id(t)
+
+    def _forget(ref, key=key):
+        rec = _OPERANDS.get(key)
+        if rec is not None and rec[0] is ref:
+            del _OPERANDS[key]
+    _OPERANDS[key] = (weakref.ref(t, _forget), a, b, stats, t._version, a._version, b._version)
+
+
+def _operands_of(t: torch.Tensor):
+    """(a, b, stats) with t == a @ b unchanged since it was computed (t contiguous, [.., m, n] rows
+    of the [batch, m, n] product) and stats its row statistics, or None."""
+    rec = _OPERANDS.get(id(t))
+    if rec is None or rec[0]() is not t or not t.is_contiguous():
+        return None
+    _, a, b, stats, tv, av, bv = rec
+    if t._version != tv or a._version != av or b._version != bv:
+        return None
+    return a, b, stats
+
+
 def _patched_einsum(*args, **kwargs):
     """torch.einsum planned as batched matmuls (einsum_ops) so the bmm patch applies."""
     orig = _ORIGINALS[(torch, "einsum")]
@@ -272,18 +327,41 @@ def _patched_einsum(*args, **kwargs):
         return orig(*args)
     if einsum_ops.supported(eq, operands) is not None:
         return orig(*args)
-    return _note_product(_dispatch("einsum", operands[0],
-                                   (eq.replace(" ", ""), tuple(tuple(t.shape) for t in operands)),
-                                   lambda: einsum_ops.einsum(eq, operands, bmm=torch.bmm),
-                                   lambda: orig(*args)))
+    last = {}
+
+    def bmm_noting(x, y):  # the planner's products go through the patched bmm; keep the last one
+        last["r"] = r = torch.bmm(x, y)
+        return r
+    out = _note_product(_dispatch("einsum", operands[0],
+                                  (eq.replace(" ", ""), tuple(tuple(t.shape) for t in operands)),
+                                  lambda: einsum_ops.einsum(eq, operands, bmm=bmm_noting),
+                                  lambda: orig(*args)))
+    # An output that is the last product itself, reshaped (same memory, same rows), keeps that
+    # product's operands: e.g. 'bhid,bhjd->bhij' returns bmm([bh,i,d], [bh,d,j]).view(b,h,i,j).
+    r = last.get("r")
+    if (r is not None and isinstance(out, torch.Tensor) and out is not r and out.is_contiguous()
+            and r.is_contiguous() and out.data_ptr() == r.data_ptr() and out.numel() == r.numel()
+            and out.dim() > 0 and r.dim() > 0 and out.shape[-1] == r.shape[-1]):
+        ops = _operands_of(r)
+        if ops is not None:
+            _note_operands(out, *ops)
+    return out
 
 
 def _softmax(input, dim, dtype, stock_call: Callable):
-    """Native row softmax for the last dimension of a tensor a patched einsum / bmm / matmul
-    returned (same dtype out); stock otherwise."""
+    """Native softmax for the last dimension of a tensor a patched einsum / bmm / matmul returned
+    (same dtype out): recomputed from the product's operands and row statistics when they describe
+    it, else the row kernel reading it; stock otherwise."""
     if (isinstance(input, torch.Tensor) and dim is not None and (dtype is None or dtype == input.dtype)
             and input.dim() > 0 and isinstance(dim, int) and dim in (-1, input.dim() - 1)
             and _is_product(input) and _grad_safe(input) and _usable(input)):
+        ops = _operands_of(input)
+        if ops is not None:
+            # the scores are recomputed from the product's operands instead of read back
+            a, b, stats = ops
+            return _dispatch("softmax_product", input, (tuple(input.shape), input.dtype, tuple(a.shape)),
+                             lambda: _C.softmax_product(a, b, stats).view(input.shape), stock_call,
+                             lambda: _C.softmax_product_plan(a, b, stats))
         return _dispatch("softmax", input, (tuple(input.shape), input.dtype),
                          lambda: _C.softmax(input, -1), stock_call)
     return stock_call()

@@ -94,7 +94,7 @@ class SoftmaxDesc(ctypes.Structure):
 
 
 # CMPX_ABI_VERSION of include/cmpx_b200.h that the ctypes structures above mirror.
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 
 def _load() -> ctypes.CDLL:
@@ -125,6 +125,15 @@ def _load() -> ctypes.CDLL:
     L.cmpx_linear_plan.restype = ctypes.c_int
     L.cmpx_softmax_rows.argtypes = [ctypes.POINTER(SoftmaxDesc), ctypes.c_void_p]
     L.cmpx_softmax_rows.restype = ctypes.c_int
+    L.cmpx_bmm_rowstats.argtypes = [ctypes.POINTER(BmmDesc), ctypes.c_void_p, ctypes.c_void_p]
+    L.cmpx_bmm_rowstats.restype = ctypes.c_int
+    L.cmpx_bmm_rowstats_plan.argtypes = [ctypes.POINTER(BmmDesc), ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t]
+    L.cmpx_bmm_rowstats_plan.restype = ctypes.c_int
+    L.cmpx_softmax_product.argtypes = [ctypes.POINTER(BmmDesc), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    L.cmpx_softmax_product.restype = ctypes.c_int
+    L.cmpx_softmax_product_plan.argtypes = [ctypes.POINTER(BmmDesc), ctypes.c_void_p, ctypes.c_void_p,
+                                            ctypes.c_char_p, ctypes.c_size_t]
+    L.cmpx_softmax_product_plan.restype = ctypes.c_int
     L.cmpx_status_str.argtypes = [ctypes.c_int]
     L.cmpx_status_str.restype = ctypes.c_char_p
     L.cmpx_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint)]
@@ -632,6 +641,83 @@ def softmax(input, dim=-1):
         raise CmpxError("softmax", st)
     _post_check()
     return y
+
+
+def _prepare_rowstats(input, mat2):
+    _check_bmm_args(input, mat2)
+    if input.dtype == torch.float32:
+        raise RuntimeError("bmm_rowstats: 16-bit operands only")
+    nb, m, _ = input.shape
+    n = mat2.shape[2]
+    c = _out_rows(nb, m, n, input.dtype, input.device)
+    stats = torch.empty((nb, (n + 63) // 64, m, 2), dtype=torch.float32, device=input.device)
+    return _bmm_desc(input, mat2, c), c, stats
+
+
+@_traced("bmm_rowstats")
+def bmm_rowstats(input, mat2):
+    """(c, stats): ``bmm(input, mat2)`` bit for bit (16-bit, both operands contiguous along k), and
+    the row statistics of c: stats [batch, ceil(n / 64), m, 2] fp32, for every row and 64-column run
+    the max of the stored values and the sum of exp(value - max) over the run."""
+    d, c, stats = _prepare_rowstats(input, mat2)
+    if c.numel():
+        with torch.cuda.device(input.device):
+            st = lib.cmpx_bmm_rowstats(ctypes.byref(d), stats.data_ptr(), _stream_handle(input.device))
+        if st != OK:
+            raise CmpxError("bmm_rowstats", st)
+        _post_check()
+    return c, stats
+
+
+def bmm_rowstats_plan(input, mat2) -> str:
+    """Name of the kernel ``bmm_rowstats`` runs for these operands."""
+    d, _, stats = _prepare_rowstats(input, mat2)
+    buf = ctypes.create_string_buffer(128)
+    st = lib.cmpx_bmm_rowstats_plan(ctypes.byref(d), stats.data_ptr(), buf, 128)
+    if st != OK:
+        raise CmpxError("bmm_rowstats plan", st)
+    return buf.value.decode()
+
+
+def _prepare_softmax_product(a, b, stats):
+    _check_bmm_args(a, b)
+    if a.dtype == torch.float32:
+        raise RuntimeError("softmax_product: 16-bit operands only")
+    runs = (b.shape[2] + 63) // 64
+    if (not isinstance(stats, torch.Tensor) or stats.dtype != torch.float32 or stats.device != a.device
+            or tuple(stats.shape) != (a.shape[0], runs, a.shape[1], 2) or not stats.is_contiguous()):
+        raise RuntimeError("softmax_product: stats must be the contiguous fp32 [batch, ceil(n / 64), m, 2] "
+                           "row statistics of a @ b (bmm_rowstats)")
+    y = torch.empty((a.shape[0], a.shape[1], b.shape[2]), dtype=a.dtype, device=a.device)
+    d = _bmm_desc(a, b, y)
+    d.c = None
+    return d, y
+
+
+@_traced("softmax_product")
+def softmax_product(a, b, stats):
+    """softmax(a @ b, dim=-1) computed from the operands (16-bit, a [batch, m, k] and b
+    [batch, k, n] both contiguous along k, k <= 128) and the product's row statistics as
+    ``bmm_rowstats`` returned them: the scores are recomputed on the tensor cores exactly as ``bmm``
+    computes and rounds them, and never read back from memory."""
+    d, y = _prepare_softmax_product(a, b, stats)
+    if y.numel():
+        with torch.cuda.device(a.device):
+            st = lib.cmpx_softmax_product(ctypes.byref(d), stats.data_ptr(), y.data_ptr(), _stream_handle(a.device))
+        if st != OK:
+            raise CmpxError("softmax_product", st)
+        _post_check()
+    return y
+
+
+def softmax_product_plan(a, b, stats) -> str:
+    """Name of the kernel ``softmax_product`` runs for these operands."""
+    d, y = _prepare_softmax_product(a, b, stats)
+    buf = ctypes.create_string_buffer(128)
+    st = lib.cmpx_softmax_product_plan(ctypes.byref(d), stats.data_ptr(), y.data_ptr(), buf, 128)
+    if st != OK:
+        raise CmpxError("softmax_product plan", st)
+    return buf.value.decode()
 
 
 def selftest_wait_timeout(timeout_ns: int, device=None) -> None:

@@ -29,6 +29,7 @@
 
 #include "cmpx_internal.h"
 #include "cmpx_ptx.cuh"
+#include "rowstats.cuh"
 
 namespace cmpx {
 
@@ -52,12 +53,16 @@ struct BmmCfg {
   static constexpr int B_FULL = 0, B_EMPTY = STAGES;                 // [STAGES] each
   static constexpr int B_ACCF = 2 * STAGES, B_ACCE = 2 * STAGES + 2;  // [2] each
   static constexpr int B_DRAIN = 2 * STAGES + 4;
-  static constexpr int NBAR = 2 * STAGES + 5;
+  // row statistics (STATS): staging slots of [buffer][epilogue warp] written / read by the stats warp
+  static constexpr int B_SFULL = 2 * STAGES + 5, B_SFREE = B_SFULL + 16;  // [2][8] each
+  static constexpr int NBAR = B_SFREE + 16;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static constexpr int TMEM_COLS = 2 * BN;          // two accumulators (128 / 256 / 512 columns)
   static constexpr int THREADS = 320;               // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+  static constexpr int STATS_THREADS = 576;         // + warps 10-17: row statistics of the staged tile
   static constexpr int EPI_WARPS = 8;
+  static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
 
 struct BmmParams {
@@ -67,6 +72,10 @@ struct BmmParams {
   unsigned long long timeout_ns;
   unsigned int* dev_flags;
   const uint16_t* bias;  // [n], same 16-bit type as C, added to every row in fp32 (linear); or null
+  // STATS: per row and 64-column run of C, (max, sum) of the stored values (rowstats.cuh), as
+  // float2 [batch][ceil(n / 64)][m] (a run's rows contiguous: one 256-byte store per warp)
+  float2* stats;
+  int stats_runs;
 };
 
 // Adds bias[col0 .. col0+31] (16-bit, converted to fp32) to the 32 fp32 accumulator columns of one
@@ -99,8 +108,8 @@ __device__ __forceinline__ void add_bias32(uint32_t (&acc)[32], const uint16_t* 
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, bool BF16>
-__global__ void __launch_bounds__(320, 1)
+template <int BN, bool A_MN, bool B_MN, bool BF16, bool STATS = false>
+__global__ void __launch_bounds__(STATS ? BmmCfg<BN>::STATS_THREADS : BmmCfg<BN>::THREADS, 1)
     bmm_sm100_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                      const __grid_constant__ CUtensorMap tm_c, const BmmParams p) {
   using C = BmmCfg<BN>;
@@ -141,6 +150,12 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(bar(C::B_ACCE + b), C::EPI_WARPS);
     }
     mbar_init(bar(C::B_DRAIN), 1);
+    if (STATS) {
+      for (int i = 0; i < 16; ++i) {
+        mbar_init(bar(C::B_SFULL + i), 1);
+        mbar_init(bar(C::B_SFREE + i), 1);
+      }
+    }
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -226,7 +241,7 @@ __global__ void __launch_bounds__(320, 1)
       }
       if (ok) umma_commit_w(bar(C::B_ACCF + b));
     }
-  } else {
+  } else if (warp < 2 + C::EPI_WARPS) {
     // ------------------------------------------------------------------ epilogue (warps 2..9)
     // Warp w reads TMEM lane quarter w % 4 (rows quarter*32 ..) and the 64-column chunks
     // c = half, half + 2, ... of each tile; each (quarter, chunk) has its own staging slot, stored
@@ -290,6 +305,10 @@ __global__ void __launch_bounds__(320, 1)
       if (i > 1) {  // this buffer's slots: tile i-2's stores (one group per tile) must have read them
         if (lane == 0) bulk_wait_group_read1();
         __syncwarp();
+        // ... and (STATS) tile i-2's statistics warp
+        if (STATS && !(ok = mbar_wait_all(bar(C::B_SFREE + b * 8 + (warp - 2)),
+                                          static_cast<uint32_t>((i >> 1) - 1) & 1u, ctl)))
+          break;
       }
 #pragma unroll 1
       for (int c = half; c < C::CHUNKS; c += 2) {
@@ -313,6 +332,10 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
       }
+      if (STATS) {  // the staged rows are complete: the statistics warp may read them
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(C::B_SFULL + b * 8 + (warp - 2)));
+      }
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(C::B_ACCE + b));  // accumulator b read: tile i+2 may reuse it
@@ -330,6 +353,42 @@ __global__ void __launch_bounds__(320, 1)
       __syncwarp();
     }
     if (lane == 0) bulk_wait_group0();  // every store of this warp complete before exit
+  } else if (STATS) {
+    // ------------------------------------------------------------------ row statistics (10..17)
+    // Warp 10 + e reads the staging slots epilogue warp 2 + e wrote (same rows, same chunks) and
+    // writes, per row and 64-column run, (max, sum of exp) of the stored 16-bit values.
+    static_assert(!STATS || !C::ONE_SLOT, "row statistics with the two-buffer staging only");
+    const int e = warp - 10;
+    const int quarter = warp & 3;
+    const int half = e >> 2;
+    bool ok = true;
+    for (int t = blockIdx.x, i = 0; ok && t < p.n_tiles; t += gridDim.x, ++i) {
+      const int b = i & 1;
+      int z, m0, n0;
+      decode(t, z, m0, n0);
+      if (!(ok = mbar_wait_all(bar(C::B_SFULL + b * 8 + e), static_cast<uint32_t>(i >> 1) & 1u, ctl))) break;
+      const uint32_t staging = base + C::OFF_STAGING + b * C::STAGING_BYTES;
+      const int r = m0 + quarter * 32 + lane;
+      for (int c = half; c < C::CHUNKS; c += 2) {
+        const uint32_t row_addr = staging + (quarter * C::CHUNKS + c) * C::SLOT_BYTES + lane * 128;
+        float cm = -INFINITY, cs = 0.f;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t w[16];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int chunk = hh * 4 + q;
+            ld_shared_v4(row_addr + ((chunk ^ (lane & 7)) << 4), w[q * 4], w[q * 4 + 1], w[q * 4 + 2], w[q * 4 + 3]);
+          }
+          rowstats32<BF16>(w, n0 + c * 64 + hh * 32, p.n, cm, cs);
+        }
+        const int run = (n0 >> 6) + c;
+        if (r < p.m && run < p.stats_runs)
+          p.stats[(static_cast<size_t>(z) * p.stats_runs + run) * p.m + r] = make_float2(cm, cs);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(C::B_SFREE + b * 8 + e));
+    }
   }
 
   tc_fence_before_sync();
@@ -422,8 +481,8 @@ const char* bmm_sm100_plan(const cmpx_bmm_desc* d, int* status) {
 
 namespace {
 
-template <int BN, bool A_MN, bool B_MN, bool BF16>
-int launch_bmm_typed(const cmpx_bmm_desc* d, const LaunchCtx& ctx, const void* bias) {
+template <int BN, bool A_MN, bool B_MN, bool BF16, bool STATS = false>
+int launch_bmm_typed(const cmpx_bmm_desc* d, const LaunchCtx& ctx, const void* bias, float2* stats = nullptr) {
   using C = BmmCfg<BN>;
   const CUtensorMapDataType dt =
       BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -456,7 +515,7 @@ int launch_bmm_typed(const cmpx_bmm_desc* d, const LaunchCtx& ctx, const void* b
   cudaError_t attr_err = cudaSuccess;
   std::call_once(once[dev & 63], [&] {
     attr_err = cudaFuncSetAttribute(
-        reinterpret_cast<const void*>(&bmm_sm100_kernel<BN, A_MN, B_MN, BF16>),
+        reinterpret_cast<const void*>(&bmm_sm100_kernel<BN, A_MN, B_MN, BF16, STATS>),
         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   });
   if (attr_err != cudaSuccess) return CMPX_ERR_LAUNCH;
@@ -473,8 +532,11 @@ int launch_bmm_typed(const cmpx_bmm_desc* d, const LaunchCtx& ctx, const void* b
   p.timeout_ns = ctx.timeout_ns;
   p.dev_flags = ctx.dev_flags;
   p.bias = static_cast<const uint16_t*>(bias);
+  p.stats = stats;
+  p.stats_runs = static_cast<int>((N + 63) / 64);
   const int grid = static_cast<int>(std::min<int64_t>(n_tiles, std::max(1, ctx.num_sms)));
-  bmm_sm100_kernel<BN, A_MN, B_MN, BF16><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(ta, tb, tc, p);
+  bmm_sm100_kernel<BN, A_MN, B_MN, BF16, STATS>
+      <<<grid, STATS ? C::STATS_THREADS : C::THREADS, C::SMEM_BYTES, ctx.stream>>>(ta, tb, tc, p);
   return cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
 }
 
@@ -495,6 +557,35 @@ int launch_bmm_dt(const cmpx_bmm_desc* d, const LaunchCtx& ctx, int am, int bm, 
 }
 
 }  // namespace
+
+// The product with its row statistics (rowstats.cuh): the 128-column tile, both operands K-major
+// (the attention-score product Q K^T of a head dim <= 128 is this case), stats float2
+// [batch][ceil(n / 64)][m].
+const char* bmm_rowstats_plan(const cmpx_bmm_desc* d, const void* stats, int* status) {
+  bmm_sm100_plan(d, status);
+  if (*status != CMPX_OK) return "none";
+  if (a_major(d) != 0 || b_major(d) != 0) {
+    *status = CMPX_ERR_MISALIGNED;
+    return "none";
+  }
+  if (!stats || (reinterpret_cast<uintptr_t>(stats) & 7u) != 0 ||
+      d->batch * ((d->n + 63) / 64) * d->m > (1ll << 40)) {
+    *status = CMPX_ERR_INVALID_ARGUMENT;
+    return "none";
+  }
+  return d->dtype == CMPX_BF16 ? "bmm_sm100<bf16,128x128x64,A:k-major,B:k-major,4st,persistent,rowstats>"
+                               : "bmm_sm100<f16,128x128x64,A:k-major,B:k-major,4st,persistent,rowstats>";
+}
+
+int launch_bmm_rowstats(const cmpx_bmm_desc* d, float* stats, const LaunchCtx& ctx) {
+  int st = CMPX_OK;
+  bmm_rowstats_plan(d, stats, &st);
+  if (st != CMPX_OK) return st;
+  if (d->m == 0 || d->n == 0 || d->batch == 0) return CMPX_OK;
+  float2* s2 = reinterpret_cast<float2*>(stats);
+  return d->dtype == CMPX_BF16 ? launch_bmm_typed<128, false, false, true, true>(d, ctx, nullptr, s2)
+                               : launch_bmm_typed<128, false, false, false, true>(d, ctx, nullptr, s2);
+}
 
 // The GEMM a linear layer is: x [m, k] (rows ld_x apart) times W^T, W [n, k] (rows ld_w apart) --
 // a K-major B operand read in place -- into y [m, n].

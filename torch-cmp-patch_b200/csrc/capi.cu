@@ -335,6 +335,43 @@ int cmpx_softmax_rows(const cmpx_softmax_desc* desc, void* stream) {
   return launch_softmax_rows(desc, ctx);
 }
 
+int cmpx_bmm_rowstats(const cmpx_bmm_desc* desc, float* stats, void* stream) {
+  int st = CMPX_OK;
+  bmm_rowstats_plan(desc, stats, &st);
+  if (st != CMPX_OK) return st;
+  if (desc->batch == 0 || desc->m == 0 || desc->n == 0) return CMPX_OK;
+  LaunchCtx ctx;
+  st = device_ctx(&ctx, static_cast<cudaStream_t>(stream));
+  if (st != CMPX_OK) return st;
+  return launch_bmm_rowstats(desc, stats, ctx);
+}
+
+int cmpx_bmm_rowstats_plan(const cmpx_bmm_desc* desc, const float* stats, char* buf, size_t buf_len) {
+  int st = CMPX_OK;
+  const char* name = bmm_rowstats_plan(desc, stats, &st);
+  copy_name(st == CMPX_OK ? name : "none", buf, buf_len);
+  return st;
+}
+
+int cmpx_softmax_product(const cmpx_bmm_desc* desc, const float* stats, void* y, void* stream) {
+  int st = CMPX_OK;
+  softmax_product_plan(desc, stats, y, &st);
+  if (st != CMPX_OK) return st;
+  if (desc->batch == 0 || desc->m == 0) return CMPX_OK;
+  LaunchCtx ctx;
+  st = device_ctx(&ctx, static_cast<cudaStream_t>(stream));
+  if (st != CMPX_OK) return st;
+  return launch_softmax_product(desc, stats, y, ctx);
+}
+
+int cmpx_softmax_product_plan(const cmpx_bmm_desc* desc, const float* stats, const void* y, char* buf,
+                              size_t buf_len) {
+  int st = CMPX_OK;
+  const char* name = softmax_product_plan(desc, stats, y, &st);
+  copy_name(st == CMPX_OK ? name : "none", buf, buf_len);
+  return st;
+}
+
 int cmpx_device_status(unsigned int* flags) {
   if (!flags) return CMPX_ERR_INVALID_ARGUMENT;
   LaunchCtx ctx;

@@ -84,6 +84,13 @@ int launch_linear_x3(const cmpx_linear_desc* d, const LaunchCtx& ctx);
 // ---- row softmax (einsum-attention chain) ----
 const char* softmax_rows_plan(const cmpx_softmax_desc* d, int* status);
 int launch_softmax_rows(const cmpx_softmax_desc* d, const LaunchCtx& ctx);
+// the 16-bit product with per-row, per-64-column (max, sum) statistics (rowstats.cuh)
+const char* bmm_rowstats_plan(const cmpx_bmm_desc* d, const void* stats, int* status);
+int launch_bmm_rowstats(const cmpx_bmm_desc* d, float* stats, const LaunchCtx& ctx);
+// softmax over the last dimension of a 16-bit product A B, recomputed from A and B (K-major,
+// k <= 128) and the product's row statistics
+const char* softmax_product_plan(const cmpx_bmm_desc* d, const void* stats, const void* y, int* status);
+int launch_softmax_product(const cmpx_bmm_desc* d, const float* stats, void* y, const LaunchCtx& ctx);
 
 // ---- self test ----
 int launch_wait_selftest(uint64_t timeout_ns, const LaunchCtx& ctx);
