@@ -581,9 +581,10 @@ def main() -> int:
             s = torch.einsum("bhid,bhjd->bhij", q, k)
             p = torch.softmax(s, dim=-1)
             return torch.einsum("bhij,bhjd->bhid", p, v)
-        launches_per_step = 3  # scores bmm (with row statistics), fused softmax, values bmm
-        kernel_name = N.bmm_rowstats_plan(q.reshape(-1, w["Lq"], w["D"]),
-                                          k.reshape(-1, w["Lk"], w["D"]).transpose(1, 2))
+        launches_per_step = 3  # scores bmm, softmax (row kernel, or the fused one), values bmm
+        fused = cmpext3._FUSED_SOFTMAX
+        qa, kb = q.reshape(-1, w["Lq"], w["D"]), k.reshape(-1, w["Lk"], w["D"]).transpose(1, 2)
+        kernel_name = N.bmm_rowstats_plan(qa, kb) if fused else N.bmm_plan(qa, kb)
 
     # C5 (the scaling workload) is timed at its sustained, power-capped clock at every N: the
     # warm-up runs at least 1.5 s of device work, whatever the per-GPU step length.
@@ -624,19 +625,23 @@ def main() -> int:
                                    peak_src, kernel_name)
         else:
             # C3 is HBM-bound on the score tensor, which the user holds twice (scores s and
-            # probabilities p, both materialised tensors of the chain): the scores bmm writes s
-            # and its row statistics, the softmax recomputes the scores from q, k and writes p,
-            # the values bmm reads p.
+            # probabilities p, both materialised tensors of the chain): the scores bmm writes s,
+            # the softmax reads s and writes p (or, fused, recomputes the scores from q, k and the
+            # row statistics the scores bmm also wrote), the values bmm reads p.
             es = 2
             score = nb * w["H"] * w["Lq"] * w["Lk"] * es
             opnd = nb * w["H"] * w["Lq"] * w["D"] * es
-            stats = nb * w["H"] * w["Lq"] * ((w["Lk"] + 63) // 64) * 8
-            algo_bytes = (2 * opnd + score + stats) + (2 * opnd + stats + score) + (score + 2 * opnd)
+            if fused:
+                stats = nb * w["H"] * w["Lq"] * ((w["Lk"] + 63) // 64) * 8
+                algo_bytes = (2 * opnd + score + stats) + (2 * opnd + stats + score) + (score + 2 * opnd)
+            else:
+                algo_bytes = (2 * opnd + score) + (2 * score) + (score + 2 * opnd)
             mean_s = statistics.mean(per_step_ms) * 1e-3
             achieved = algo_bytes / mean_s / 1e9
             peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
             roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                    "frac": round(achieved / peak, 4), "kernel": kernel_name + " + softmax_product",
+                    "frac": round(achieved / peak, 4),
+                    "kernel": kernel_name + (" + softmax_product" if fused else " + softmax_rows"),
                     "algorithmic_bytes_per_step": algo_bytes,
                     # any chain that hands s and p back as tensors writes both once, reads q, k, v
                     # and writes o

@@ -355,6 +355,21 @@ class TestSoftmax:
         F.softmax(s)  # implicit dim: stock (with torch's warning)
         native.softmax.assert_not_called()
 
+    @pytest.fixture
+    def fused(self, monkeypatch):
+        monkeypatch.setattr(cmpext3, "_FUSED_SOFTMAX", True)
+
+    def test_fused_softmax_is_off_by_default(self, patched, native, monkeypatch):
+        force_eligible(monkeypatch)
+        native.bmm.side_effect = lambda a, b: torch.zeros(a.shape[0], a.shape[1], b.shape[2], dtype=a.dtype)
+        bf = torch.bfloat16
+        s = torch.einsum("bhid,bhjd->bhij", torch.randn(1, 2, 64, 32).to(bf), torch.randn(1, 2, 256, 32).to(bf))
+        native.softmax.return_value = torch.ones(1, 2, 64, 256, dtype=bf)
+        torch.softmax(s, -1)
+        native.bmm_rowstats.assert_not_called()
+        native.softmax_product.assert_not_called()
+        assert native.bmm.call_count == 1 and native.softmax.call_count == 1
+
     def _bf16_scores(self, native):
         # einsum scores of 16-bit q, k with a 32-wide head dim and 256 keys: the planner's bmm
         # operands are contiguous along the head dim, so the product is computed with its row
@@ -370,7 +385,7 @@ class TestSoftmax:
         native.bmm_rowstats.side_effect = rowstats
         return q, k, torch.einsum("bhid,bhjd->bhij", q, k)
 
-    def test_softmax_of_recorded_scores_recomputes_them_from_the_operands(self, patched, native, monkeypatch):
+    def test_softmax_of_recorded_scores_recomputes_them_from_the_operands(self, patched, native, monkeypatch, fused):
         force_eligible(monkeypatch)
         q, k, s = self._bf16_scores(native)
         native.bmm.assert_not_called()
@@ -384,7 +399,7 @@ class TestSoftmax:
         assert stats is self.stats[0]  # the statistics the scores product returned
         assert got.shape == s.shape and "softmax_product" in cmpext3.autoselect_report()
 
-    def test_scores_changed_in_place_are_read_not_recomputed(self, patched, native, monkeypatch):
+    def test_scores_changed_in_place_are_read_not_recomputed(self, patched, native, monkeypatch, fused):
         force_eligible(monkeypatch)
         _, _, s = self._bf16_scores(native)
         s.mul_(2)  # the recorded operands no longer describe s
@@ -393,7 +408,7 @@ class TestSoftmax:
         native.softmax_product.assert_not_called()
         assert native.softmax.call_count == 1
 
-    def test_operand_changed_in_place_is_not_recomputed(self, patched, native, monkeypatch):
+    def test_operand_changed_in_place_is_not_recomputed(self, patched, native, monkeypatch, fused):
         force_eligible(monkeypatch)
         q, _, s = self._bf16_scores(native)
         q.add_(1)
@@ -401,7 +416,7 @@ class TestSoftmax:
         torch.softmax(s, -1)
         native.softmax_product.assert_not_called()
 
-    def test_only_attention_shaped_products_carry_row_statistics(self, patched, native, monkeypatch):
+    def test_only_attention_shaped_products_carry_row_statistics(self, patched, native, monkeypatch, fused):
         force_eligible(monkeypatch)
         native.bmm.side_effect = lambda a, b: torch.zeros(a.shape[0], a.shape[1], b.shape[2], dtype=a.dtype)
         native.bmm_rowstats.side_effect = lambda a, b: (

@@ -11,9 +11,9 @@ checked against the caller's scores, not against scores recomputed on the CPU: a
 -- N(0,1) inputs, k = 64, scores with a standard deviation of 8 -- one rounding step of a 16-bit
 score moves its probability by tens of percent, so two different products of the same inputs give
 different softmaxes by design; the end of the chain, the attention output, is compared with the
-full CPU chain.)  The einsum-attention chain (cmpext3/einsum_ops.py:69-121 in the reference) routes
-its softmax here when the scores are untouched since the einsum; a change in place to the scores or
-to an operand falls back to the row-softmax kernel that reads the scores.
+full CPU chain.)  With CMPEXT3_FUSED_SOFTMAX=1 the einsum-attention chain (cmpext3/einsum_ops.py:69-121
+in the reference) routes its softmax here when the scores are untouched since the einsum; a change in
+place to the scores or to an operand falls back to the row-softmax kernel that reads the scores.
 """
 from __future__ import annotations
 
@@ -106,7 +106,8 @@ def test_rows_of_infinite_scores(cuda_device):
     check(y[ok], ref[ok], torch.bfloat16, "rows without infinities", attention=False)
 
 
-def test_einsum_chain_recomputes_the_scores(cuda_device, patched):
+def test_einsum_chain_recomputes_the_scores(cuda_device, patched, monkeypatch):
+    monkeypatch.setattr(cmpext3, "_FUSED_SOFTMAX", True)  # off by default
     g = torch.Generator().manual_seed(4)
     q, k, v = (torch.randn(2, 4, 512, 64, generator=g).to(torch.bfloat16) for _ in range(3))
     qd, kd, vd = q.to(cuda_device), k.to(cuda_device), v.to(cuda_device)
@@ -127,7 +128,8 @@ def test_einsum_chain_recomputes_the_scores(cuda_device, patched):
     check(o, ref_o, torch.bfloat16, "attention output vs the CPU chain")
 
 
-def test_scores_changed_in_place_are_read_back(cuda_device, patched):
+def test_scores_changed_in_place_are_read_back(cuda_device, patched, monkeypatch):
+    monkeypatch.setattr(cmpext3, "_FUSED_SOFTMAX", True)
     g = torch.Generator().manual_seed(5)
     q, k = (torch.randn(1, 2, 256, 64, generator=g).to(torch.bfloat16).to(cuda_device) for _ in range(2))
     with torch.no_grad():

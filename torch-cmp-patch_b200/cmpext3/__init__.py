@@ -278,12 +278,16 @@ def _is_product(t: Any) -> bool:
 # version counters) while the product lives, when a softmax over the product's last dimension can be
 # recomputed from them instead of reading the product back: 16-bit, both operands contiguous along
 # the contracted dimension, k <= 128, a product row of at least 128 elements (what attention scores
-# look like).
+# look like).  Off by default (CMPEXT3_FUSED_SOFTMAX=1 turns it on): on a B200 the statistics cost
+# the scores product one exponential per element, which takes longer than the softmax's read of the
+# score tensor that the recompute saves (the C3 chain: 0.401 ms fused against 0.393 ms with the
+# row-softmax kernel).
+_FUSED_SOFTMAX = os.environ.get("CMPEXT3_FUSED_SOFTMAX", "0") not in ("0", "", "false", "False")
 _OPERANDS: dict[int, tuple] = {}
 
 
 def _fusable(a: torch.Tensor, b: torch.Tensor) -> bool:
-    return (a.dtype in (torch.float16, torch.bfloat16) and a.dim() == 3 and b.dim() == 3
+    return (_FUSED_SOFTMAX and a.dtype in (torch.float16, torch.bfloat16) and a.dim() == 3 and b.dim() == 3
             and 1 <= a.shape[2] <= 128 and b.shape[2] >= 128 and b.shape[2] % 8 == 0
             and a.stride(2) == 1 and b.stride(1) == 1)
 

@@ -372,16 +372,11 @@ __global__ void __launch_bounds__(STATS ? BmmCfg<BN>::STATS_THREADS : BmmCfg<BN>
       for (int c = half; c < C::CHUNKS; c += 2) {
         const uint32_t row_addr = staging + (quarter * C::CHUNKS + c) * C::SLOT_BYTES + lane * 128;
         float cm = -INFINITY, cs = 0.f;
+        uint32_t w[32];
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t w[16];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int chunk = hh * 4 + q;
-            ld_shared_v4(row_addr + ((chunk ^ (lane & 7)) << 4), w[q * 4], w[q * 4 + 1], w[q * 4 + 2], w[q * 4 + 3]);
-          }
-          rowstats32<BF16>(w, n0 + c * 64 + hh * 32, p.n, cm, cs);
-        }
+        for (int q = 0; q < 8; ++q)
+          ld_shared_v4(row_addr + ((q ^ (lane & 7)) << 4), w[q * 4], w[q * 4 + 1], w[q * 4 + 2], w[q * 4 + 3]);
+        rowstats64<BF16>(w, n0 + c * 64, p.n, cm, cs);
         const int run = (n0 >> 6) + c;
         if (r < p.m && run < p.stats_runs)
           p.stats[(static_cast<size_t>(z) * p.stats_runs + run) * p.m + r] = make_float2(cm, cs);

@@ -255,10 +255,8 @@ __global__ void __launch_bounds__(64 + 4 * 128, 1)
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            float v0, v1, x0, x1;
-            unpack16<BF16>(pack16<BF16>(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1])), v0, v1);
-            f2_unpack(f2_fma(f2_pack(v0, v1), l2e2, off2), x0, x1);
-            pk[e] = pack16<BF16>(ex2_approx(x0), ex2_approx(x1));
+            const uint32_t s16 = pack16<BF16>(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+            pk[e] = pack16x2<BF16>(ex2x2(f2_fma(unpack16x2<BF16>(s16), l2e2, off2)));
           }
           // 32 16-bit columns into the half of the staging box they belong to (128-byte
           // swizzle: row lane at lane * 128, 16-byte unit u at (u ^ (lane & 7)) * 16)
