@@ -467,6 +467,9 @@ def parse_args():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the extra C4 record of the default (C5, one GPU) run")
+    ap.add_argument("--shard-of", type=int, default=1,
+                    help="on one GPU, run the first rank's shard of an N-GPU run (the per-GPU work of "
+                         "--gpus N): the per-GPU throughput the N-GPU line is compared with")
     ap.add_argument("--warmup-seconds", type=float, default=None,
                     help="extend the warm-up to this much device work (default 1.5 s for the "
                          "tensor-bound c4/c5, 0 for the others)")
@@ -543,9 +546,10 @@ def main() -> int:
     distributed = world > 1
     if distributed:
         sharding.init_process_group("nccl", timeout_s=300)
-    if w["B"] % world != 0:
-        raise SystemExit(f"workload {args.workload} has B={w['B']}, not divisible by {world} GPUs")
-    b0, b1 = sharding.shard_range(w["B"], rank, world)
+    split = world if world > 1 else max(1, args.shard_of)
+    if w["B"] % split != 0:
+        raise SystemExit(f"workload {args.workload} has B={w['B']}, not divisible by {split} GPUs")
+    b0, b1 = sharding.shard_range(w["B"], rank, split)
     nb = b1 - b0
 
     def barrier():
@@ -697,7 +701,8 @@ def main() -> int:
                 "warmup_s": round(warm_elapsed, 2),
                 "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic",
-                "config": config_block(w, args.workload, world, nb),
+                "config": dict(config_block(w, args.workload, world, nb),
+                               **({"parallelism": f"the first shard of dp{split}, on one GPU"} if split > world else {})),
                 "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clock_info,
                 "gpu_launches": launches_per_step * args.steps,
                 "mean_launch_ms": round(mean_launch_ms, 4), "kernel": kernel_name,
