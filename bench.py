@@ -368,6 +368,13 @@ def time_steps(step, steps: int, warmup: int, warm_s: float, dev, stream, flush=
     warm-up steps run, warm-up seconds)."""
     import torch
     out = None
+    # Everything the timed region needs is set up before the warm-up ends, so that the GPU does not
+    # idle between the two: an idle gap of even ~100 ms lets the power capper's average fall, and
+    # a short timed region would then run at a boost clock the sustained run never sees.
+    clocks = ClockSampler(gpu_uuid(dev))
+    clocks.start()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.perf_counter()
     n_warm = 0
     while n_warm < max(3, warmup) or (warm_s > 0 and time.perf_counter() - t0 < warm_s):
@@ -375,12 +382,7 @@ def time_steps(step, steps: int, warmup: int, warm_s: float, dev, stream, flush=
         n_warm += 1
         if n_warm % 8 == 0:
             torch.cuda.synchronize(dev)
-    torch.cuda.synchronize(dev)
     warm_elapsed = time.perf_counter() - t0
-    clocks = ClockSampler(gpu_uuid(dev))
-    clocks.start()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
-    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if barrier:
         barrier()
     torch.cuda.synchronize(dev)
