@@ -146,13 +146,16 @@ typedef struct cmpx_bmm_desc {
 /* Attention forward.  Replaces cmpext3.ops.attention (src/main.cpp:2353-2358). */
 CMPX_API int cmpx_attn_fwd(const cmpx_attn_desc* desc, void* stream);
 
-/* Bytes of device workspace for the fastest schedule of this problem on the current device (0 for
- * fp32, which needs none).  The 16-bit kernels keep the two work counters of their persistent
- * schedule in the first 256 bytes; a non-causal call whose last wave of (256-row, head) items would
- * leave most SMs idle also splits those items into key ranges, whose partial results (fp32 O rows
- * and per-row max / sum) take the bytes after the counters and are merged by a second kernel.  Any
- * 16-bit call accepts a workspace of at least 256 bytes: one smaller than this size runs unsplit,
- * with the same results up to fp32 summation order.  The workspace must be 16-byte aligned and its
+/* Bytes of device workspace for the fastest schedule of this problem on the current device.  The
+ * 16-bit kernels keep the two work counters of their persistent schedule in the first 256 bytes; a
+ * non-causal call whose last wave of (256-row, head) items would leave most SMs idle also splits
+ * those items into key ranges, whose partial results (fp32 O rows and per-row max / sum) take the
+ * bytes after the counters and are merged by a second kernel.  Any 16-bit call accepts a workspace
+ * of at least 256 bytes: one smaller than this size runs unsplit, with the same results up to fp32
+ * summation order.  An fp32 call needs a workspace only for the same kind of split (its last wave's
+ * 128-row items cut into key ranges, 8-bit per-item arrival counters in the first 256 bytes, the
+ * partial rows after them, merged by the last range to finish); 0 when it runs unsplit, and given
+ * less than this size it runs unsplit.  The workspace must be 16-byte aligned and its
  * first 256 bytes zero-filled before the first call; every call leaves them zeroed on return (the
  * rest is scratch, written before it is read), so a workspace can be reused by calls that do not
  * overlap on the GPU (one per stream).

@@ -436,6 +436,36 @@ def test_workspace_size_without_split(cfg):
     assert N.lib.cmpx_attn_workspace_size(ctypes.byref(_attn(**cfg))) == 256
 
 
+def _f32_split_bytes(items, tiles, dp, sms=148):
+    """fp32 tail split: 256 bytes of 8-bit item counters, then per key range 128 rows of
+    (O [dp], m, l, 2 pad) fp32."""
+    rem = items % sms
+    if items <= sms or rem == 0 or 2 * rem > sms:
+        return 0
+    split = min(sms // rem, 8, tiles)
+    return 256 + rem * split * 128 * (dp + 4) * 4 if split >= 2 else 0
+
+
+@pytest.mark.parametrize("cfg,split", [
+    (dict(B=2, H=8, Lq=4096, Lk=4096, D=40, dtype=0), True),     # C1: 512 items, 68 cut 2 ways
+    (dict(B=1, H=150, Lq=128, Lk=4096, D=64, dtype=0), True),    # 2 tail items cut 8 ways
+    (dict(B=1, H=75, Lq=512, Lk=1024, D=128, dtype=0), True),    # D = 128, 32-key tiles
+    (dict(B=2, H=8, Lq=4096, Lk=4096, D=40, dtype=0, causal=1), False),  # causal: never split
+    (dict(B=1, H=248, Lq=128, Lk=4096, D=64, dtype=0), False),   # 100 tail items: more than half a wave
+    (dict(B=1, H=148, Lq=256, Lk=4096, D=64, dtype=0), False),   # full waves only
+])
+def test_fp32_workspace_covers_its_tail_split(cfg, split):
+    d = _attn(**cfg)
+    dp = 64 if cfg["D"] <= 64 else 128
+    items = (cfg["Lq"] + 127) // 128 * cfg["H"] * cfg["B"]
+    want = 0 if cfg.get("causal") else _f32_split_bytes(
+        items, (cfg["Lk"] + (63 if dp == 64 else 31)) // (64 if dp == 64 else 32), dp)
+    assert (want > 0) == split
+    assert N.lib.cmpx_attn_workspace_size(ctypes.byref(d)) == want
+    st, name = _plan(d)
+    assert st == 0 and name.endswith("+tail-split>") == split, name
+
+
 @pytest.mark.skipif(__import__("torch").cuda.is_available(),
                     reason="fake pointers: on a GPU host this call would launch a kernel")
 def test_minimum_workspace_is_accepted_for_split_shapes():

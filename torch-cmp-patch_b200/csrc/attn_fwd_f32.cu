@@ -29,13 +29,21 @@ const char* attn_f32_plan(const cmpx_attn_desc* d, int* status) {
     return "none";
   }
   if (attn_tf32x3_eligible(d)) {
-    static const char* const names[2][3] = {
-        {"attn_tf32x3_sm100<D64,128q,64kv,persistent>", "attn_tf32x3_sm100<D64,128q,64kv,persistent+mask>",
-         "attn_tf32x3_sm100<D64,128q,64kv,persistent+addmask>"},
-        {"attn_tf32x3_sm100<D128,128q,32kv,persistent>", "attn_tf32x3_sm100<D128,128q,32kv,persistent+mask>",
-         "attn_tf32x3_sm100<D128,128q,32kv,persistent+addmask>"}};
+    // "+tail-split": the schedule a call given cmpx_attn_workspace_size() bytes runs
+    static const char* const names[2][2][3] = {
+        {{"attn_tf32x3_sm100<D64,128q,64kv,persistent>", "attn_tf32x3_sm100<D64,128q,64kv,persistent+mask>",
+          "attn_tf32x3_sm100<D64,128q,64kv,persistent+addmask>"},
+         {"attn_tf32x3_sm100<D128,128q,32kv,persistent>", "attn_tf32x3_sm100<D128,128q,32kv,persistent+mask>",
+          "attn_tf32x3_sm100<D128,128q,32kv,persistent+addmask>"}},
+        {{"attn_tf32x3_sm100<D64,128q,64kv,persistent+tail-split>",
+          "attn_tf32x3_sm100<D64,128q,64kv,persistent+mask+tail-split>",
+          "attn_tf32x3_sm100<D64,128q,64kv,persistent+addmask+tail-split>"},
+         {"attn_tf32x3_sm100<D128,128q,32kv,persistent+tail-split>",
+          "attn_tf32x3_sm100<D128,128q,32kv,persistent+mask+tail-split>",
+          "attn_tf32x3_sm100<D128,128q,32kv,persistent+addmask+tail-split>"}}};
     const int mk = !d->mask ? 0 : d->mask_kind == CMPX_MASK_BOOL ? 1 : 2;
-    return names[d->head_dim <= 64 ? 0 : 1][mk];
+    const int split = attn_tf32x3_workspace_bytes(d, current_num_sms()) > 0 ? 1 : 0;
+    return names[split][d->head_dim <= 64 ? 0 : 1][mk];
   }
   // Operands the 3xTF32 kernel cannot read with TMA (strides or pointers not 16-byte aligned; the
   // ctypes binding copies such inputs to padded buffers before it gets here).

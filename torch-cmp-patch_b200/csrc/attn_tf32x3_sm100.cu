@@ -72,7 +72,9 @@ struct X3Cfg {
   static constexpr int B_PVD = B_PREADY + 2;        // [2] P V of buffer b's tile done
   static constexpr int B_OFREE = B_PVD + 2;         // count 128
   static constexpr int B_VREAD = B_OFREE + 1;      // converter threads have read a stage's raw V (128)
-  static constexpr int B_DRAIN = B_VREAD + 1;
+  static constexpr int B_EPI = B_VREAD + 1;         // tail split: the CTA's partial rows written (count 128)
+  static constexpr int B_EPI2 = B_EPI + 1;          // tail split: the range's arrival counted
+  static constexpr int B_DRAIN = B_EPI2 + 1;
   static constexpr int NBAR = B_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
@@ -88,6 +90,14 @@ struct X3Cfg {
 struct X3Params {
   int heads, len_q, len_k, head_dim;
   int n_qt, n_items;
+  // Tail split (non-causal): work items 0 .. n_whole-1 are whole (128-row tile, head) items; each
+  // of the last n_items - n_whole items is cut into `split` key ranges, one work item each
+  // (n_work in all), whose partial (O, m, l) rows go to part and are merged by the CTA of the
+  // item's last range to arrive (cnt: one 8-bit arrival counter per tail item, four to a word, in
+  // the workspace's first 256 bytes, left at 0).
+  int n_whole, split, n_work;
+  unsigned int* cnt;
+  float* part;
   int qk_steps;   // ceil(head_dim / 8): K=8 steps of Q K^T
   int causal, neg_scale;
   int group;      // query heads per key/value head (grouped-query attention)
@@ -174,15 +184,24 @@ __global__ void __launch_bounds__(320, 1)
   const uint32_t sQ = base + C::OFF_Q;
   auto stage = [&](int load) -> uint32_t { return base + C::OFF_ST + (load % C::NS) * C::STAGE_BYTES; };
 
-  // Item w -> (b, h, q0, number of 64-key tiles); causal items heaviest-first within a head.
-  auto geometry = [&](int w, int& b, int& h, int& q0, int& n_kv) {
-    const int bh = w / p.n_qt;
-    const int qt = w - bh * p.n_qt;
+  // Work item w -> (b, h, q0, first key tile j0, number of key tiles); causal items heaviest-first
+  // within a head.  A tail work item takes key tiles [j0, j0 + n_kv) of its (row tile, head).
+  auto geometry = [&](int w, int& b, int& h, int& q0, int& j0, int& n_kv) {
+    int item = w, part = 0;
+    if (w >= p.n_whole) {
+      const int u = w - p.n_whole;
+      item = p.n_whole + u / p.split;
+      part = u - (u / p.split) * p.split;
+    }
+    const int bh = item / p.n_qt;
+    const int qt = item - bh * p.n_qt;
     b = bh / p.heads;
     h = bh - b * p.heads;
     q0 = (p.causal ? p.n_qt - 1 - qt : qt) * C::BM;
     const int kv_len = p.causal ? min(p.len_k, q0 + C::BM) : p.len_k;
-    n_kv = (kv_len + C::BN - 1) / C::BN;
+    const int tiles = (kv_len + C::BN - 1) / C::BN;
+    j0 = w >= p.n_whole ? part * tiles / p.split : 0;
+    n_kv = w >= p.n_whole ? (part + 1) * tiles / p.split - j0 : tiles;
   };
 
   if (threadIdx.x == 0) {
@@ -202,6 +221,8 @@ __global__ void __launch_bounds__(320, 1)
     }
     mbar_init(bar(C::B_OFREE), 128);
     mbar_init(bar(C::B_VREAD), 128);
+    mbar_init(bar(C::B_EPI), 128);
+    mbar_init(bar(C::B_EPI2), 1);
     mbar_init(bar(C::B_DRAIN), 1);
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -226,9 +247,9 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       int load = 0;
       bool ok = true;
-      for (int k = 0, w = blockIdx.x; ok && w < p.n_items; ++k, w += gridDim.x) {
-        int b, h, q0, n_kv;
-        geometry(w, b, h, q0, n_kv);
+      for (int k = 0, w = blockIdx.x; ok && w < p.n_work; ++k, w += gridDim.x) {
+        int b, h, q0, j0, n_kv;
+        geometry(w, b, h, q0, j0, n_kv);
         // the staging tile is free once the converter has read the previous item's Q
         if (k > 0 && !(ok = mbar_wait(bar(C::B_QFREE), static_cast<uint32_t>(k - 1) & 1u, ctl))) break;
         mbar_arrive_expect_tx(bar(C::B_QFULL), C::Q_BYTES);
@@ -239,8 +260,10 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t sb = stage(load);
           mbar_arrive_expect_tx(bar(C::B_FULL + st), 2 * C::T_BYTES);
           for (int c = 0; c < C::NQC; ++c) {
-            tma_load_4d(sb + C::ST_K + c * C::KCH, &tm_k, bar(C::B_FULL + st), c * 32, j * C::BN, h / p.group, b);
-            tma_load_4d(sb + C::ST_B + c * C::KCH, &tm_v, bar(C::B_FULL + st), c * 32, j * C::BN, h / p.group, b);
+            tma_load_4d(sb + C::ST_K + c * C::KCH, &tm_k, bar(C::B_FULL + st), c * 32, (j0 + j) * C::BN,
+                        h / p.group, b);
+            tma_load_4d(sb + C::ST_B + c * C::KCH, &tm_v, bar(C::B_FULL + st), c * 32, (j0 + j) * C::BN,
+                        h / p.group, b);
           }
         }
       }
@@ -276,10 +299,10 @@ __global__ void __launch_bounds__(320, 1)
     auto ready = [&](uint32_t b, uint32_t parity) -> bool {
       return __all_sync(0xffffffffu, mbar_test_wait(b, parity));
     };
-    for (int k = 0, w = blockIdx.x; ok && w < p.n_items; ++k, w += gridDim.x) {
-      int b, h, q0, n_kv;
-      geometry(w, b, h, q0, n_kv);
-      (void)b; (void)h; (void)q0;
+    for (int k = 0, w = blockIdx.x; ok && w < p.n_work; ++k, w += gridDim.x) {
+      int b, h, q0, j0, n_kv;
+      geometry(w, b, h, q0, j0, n_kv);
+      (void)b; (void)h; (void)q0; (void)j0;
       if (!(ok = mbar_wait_all(bar(C::B_QCONV), static_cast<uint32_t>(k) & 1u, ctl))) break;
       // Issue S(nq) and PV(np) in whichever order their inputs become ready.
       int nq = 0, np = 0;
@@ -341,9 +364,9 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     int load = 0;
     bool ok = true;
-    for (int k = 0, w = blockIdx.x; ok && w < p.n_items; ++k, w += gridDim.x) {
-      int b, h, q0, n_kv;
-      geometry(w, b, h, q0, n_kv);
+    for (int k = 0, w = blockIdx.x; ok && w < p.n_work; ++k, w += gridDim.x) {
+      int b, h, q0, j0, n_kv;
+      geometry(w, b, h, q0, j0, n_kv);
       // Q: this thread's row from the staging tile -> hi / lo -> TMEM, one 32-column chunk at a
       // time.  TMEM Q is free once the previous item's last S product is done.
       if (!(ok = mbar_wait_all(bar(C::B_QFULL), static_cast<uint32_t>(k) & 1u, ctl))) break;
@@ -419,11 +442,12 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const float sl2 = p.scale_log2;
     const float masked = p.neg_scale ? INFINITY : -INFINITY;
-    int g = 0;
+    volatile int* last_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
+    int g = 0, nsp = 0;  // nsp: tail ranges this CTA has finished (barrier phases)
     bool ok = true;
-    for (int k = 0, w = blockIdx.x; ok && w < p.n_items; ++k, w += gridDim.x) {
-      int b, h, q0, n_kv;
-      geometry(w, b, h, q0, n_kv);
+    for (int k = 0, w = blockIdx.x; ok && w < p.n_work; ++k, w += gridDim.x) {
+      int b, h, q0, j0, n_kv;
+      geometry(w, b, h, q0, j0, n_kv);
       const int qrow = q0 + row;
       float m_run = -INFINITY, l_run = 0.f;
       for (int j = 0; j < n_kv; ++j) {
@@ -437,7 +461,7 @@ __global__ void __launch_bounds__(320, 1)
           tmem_ld32(lane_base + (bs ? C::TM_S1 : C::TM_S0), sr);
         float* s = reinterpret_cast<float*>(sr);
         tc_fence_before_sync();
-        const int kv0 = j * C::BN;
+        const int kv0 = (j0 + j) * C::BN;
         if constexpr (MK != 0) {
           if (qrow < p.len_q) {
             const long long roff = b * p.mk_b + h * p.mk_h + static_cast<long long>(qrow) * p.mk_q + kv0;
@@ -566,8 +590,67 @@ __global__ void __launch_bounds__(320, 1)
       const int glast = g + n_kv - 1;
       if (!(ok = mbar_wait_all(bar(C::B_PVD + (glast & 1)), static_cast<uint32_t>(glast >> 1) & 1u, ctl))) break;
       tc_fence_after_sync();
-      const float inv_l = (MK != 0 && !(l_run > 0.f)) ? 0.f : 1.f / l_run;  // no key: output 0
       float* dst = p.o + b * p.os_b + h * p.os_h + static_cast<long long>(qrow) * p.os_s;
+      if (w >= p.n_whole) {
+        // A key range of a tail item: park this row's (O, m, l); the CTA of the item's last range
+        // to arrive merges them all.
+        const int u = w - p.n_whole, ti = u / p.split;
+        float* mine = p.part + (static_cast<size_t>(u) * C::BM + row) * (DP + 4);
+#pragma unroll
+        for (int hh = 0; hh < C::NQC; ++hh) {
+          uint32_t o[32];
+          tmem_ld32(lane_base + C::TM_O + hh * 32, o);
+          if (hh + 1 == C::NQC) {
+            tc_fence_before_sync();
+            mbar_arrive(bar(C::B_OFREE));
+          }
+#pragma unroll
+          for (int c = 0; c < 32; c += 4)
+            __stcg(reinterpret_cast<float4*>(mine + hh * 32 + c),
+                   make_float4(__uint_as_float(o[c]), __uint_as_float(o[c + 1]), __uint_as_float(o[c + 2]),
+                               __uint_as_float(o[c + 3])));
+        }
+        __stcg(reinterpret_cast<float4*>(mine + DP), make_float4(m_run, l_run, 0.f, 0.f));
+        __threadfence();  // this row's partial is visible device-wide before the range's arrival is
+        mbar_arrive(bar(C::B_EPI));
+        if (warp == 6) {  // one thread counts the range once all 128 rows are parked
+          if (!(ok = mbar_wait_all(bar(C::B_EPI), static_cast<uint32_t>(nsp) & 1u, ctl))) break;
+          if (lane == 0) {
+            const unsigned sh = 8u * static_cast<unsigned>(ti & 3);
+            unsigned* word = p.cnt + (ti >> 2);
+            const unsigned old = atomicAdd(word, 1u << sh);
+            const bool last = ((old >> sh) & 0xffu) == static_cast<unsigned>(p.split - 1);
+            if (last) atomicSub(word, static_cast<unsigned>(p.split) << sh);  // left at 0
+            *last_flag = last ? 1 : 0;
+            mbar_arrive(bar(C::B_EPI2));
+          }
+          __syncwarp();
+        }
+        if (!(ok = mbar_wait_all(bar(C::B_EPI2), static_cast<uint32_t>(nsp) & 1u, ctl))) break;
+        ++nsp;
+        if (*last_flag && qrow < p.len_q) {  // every range of the item has parked: merge this row
+          __threadfence();
+          const float* first = p.part + (static_cast<size_t>(ti) * p.split * C::BM + row) * (DP + 4);
+          const size_t step = static_cast<size_t>(C::BM) * (DP + 4);
+          float mall = -INFINITY;
+          for (int r = 0; r < p.split; ++r) mall = fmaxf(mall, __ldcg(first + r * step + DP));
+          float wgt[8], lsum = 0.f;
+          for (int r = 0; r < p.split; ++r) {
+            const float mr = __ldcg(first + r * step + DP);
+            wgt[r] = mr == -INFINITY ? 0.f : ex2_approx(mr - mall);
+            lsum += wgt[r] * __ldcg(first + r * step + DP + 1);
+          }
+          const float inv_l = (MK != 0 && !(lsum > 0.f)) ? 0.f : 1.f / lsum;  // no key: output 0
+          for (int c = 0; c < p.head_dim; ++c) {
+            float acc = 0.f;
+            for (int r = 0; r < p.split; ++r) acc += wgt[r] * __ldcg(first + r * step + c);
+            dst[c] = acc * inv_l;
+          }
+        }
+        g += n_kv;
+        continue;
+      }
+      const float inv_l = (MK != 0 && !(l_run > 0.f)) ? 0.f : 1.f / l_run;  // no key: output 0
       const bool vec = (p.head_dim & 3) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
 #pragma unroll
       for (int hh = 0; hh < C::NQC; ++hh) {  // O / l, 32 columns at a time
@@ -652,6 +735,36 @@ bool attn_tf32x3_eligible(const cmpx_attn_desc* d) {
 
 namespace {
 
+// Tail split of a non-causal launch: with n_items = waves * grid + rem (0 < rem <= grid / 2), the
+// rem items of the partial last wave are cut into split = min(grid / rem, 8, key tiles) key
+// ranges, so that the last wave holds rem * split <= grid ranges of 1/split of an item each.
+// The counters take the workspace's first 256 bytes (zero before and after every call, the same
+// bytes the 16-bit kernels' counters use), the partial rows the bytes after them.
+struct X3Split {
+  int n_whole = 0, split = 1;
+  size_t cnt_bytes = 0, bytes = 0;
+};
+
+template <int DP>
+X3Split x3_split_plan(const cmpx_attn_desc* d, int num_sms) {
+  using C = X3Cfg<DP>;
+  X3Split sp;
+  if (d->causal) return sp;
+  const int64_t n_qt = (d->len_q + C::BM - 1) / C::BM;
+  const int64_t n_items = n_qt * d->heads * d->batch;
+  const int64_t grid = std::min<int64_t>(n_items, std::max(1, num_sms));
+  const int64_t rem = n_items % grid, tiles = (d->len_k + C::BN - 1) / C::BN;
+  if (n_items <= grid || rem == 0 || 2 * rem > grid) return sp;
+  const int64_t split = std::min<int64_t>({grid / rem, 8, tiles});
+  if (split < 2) return sp;
+  sp.n_whole = static_cast<int>(n_items - rem);
+  sp.split = static_cast<int>(split);
+  if (rem > 256) return sp;  // one 8-bit counter per tail item in the first 256 bytes
+  sp.cnt_bytes = 256;
+  sp.bytes = sp.cnt_bytes + static_cast<size_t>(rem) * split * C::BM * (DP + 4) * 4;
+  return sp;
+}
+
 template <int DP>
 int launch_tf32x3_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   using C = X3Cfg<DP>;
@@ -697,6 +810,20 @@ int launch_tf32x3_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   p.timeout_ns = ctx.timeout_ns;
   p.dev_flags = ctx.dev_flags;
   const int grid = std::min(p.n_items, std::max(1, ctx.num_sms));
+  const X3Split sp = x3_split_plan<DP>(d, ctx.num_sms);
+  p.n_whole = p.n_items;
+  p.split = 1;
+  p.n_work = p.n_items;
+  p.cnt = nullptr;
+  p.part = nullptr;
+  if (sp.split > 1 && d->workspace && d->workspace_bytes >= sp.bytes &&
+      (reinterpret_cast<uintptr_t>(d->workspace) & 255u) == 0) {
+    p.n_whole = sp.n_whole;
+    p.split = sp.split;
+    p.n_work = sp.n_whole + (p.n_items - sp.n_whole) * sp.split;
+    p.cnt = static_cast<unsigned int*>(d->workspace);
+    p.part = reinterpret_cast<float*>(static_cast<char*>(d->workspace) + sp.cnt_bytes);
+  }
   if (!d->mask)
     attn_tf32x3_sm100_kernel<DP, 0><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, p);
   else if (d->mask_kind == CMPX_MASK_BOOL)
@@ -707,6 +834,11 @@ int launch_tf32x3_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
 }
 
 }  // namespace
+
+size_t attn_tf32x3_workspace_bytes(const cmpx_attn_desc* d, int num_sms) {
+  if (!attn_tf32x3_eligible(d)) return 0;
+  return d->head_dim <= 64 ? x3_split_plan<64>(d, num_sms).bytes : x3_split_plan<128>(d, num_sms).bytes;
+}
 
 int launch_attn_tf32x3(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   return d->head_dim <= 64 ? launch_tf32x3_typed<64>(d, ctx) : launch_tf32x3_typed<128>(d, ctx);

@@ -240,8 +240,11 @@ const char* cmpx_status_str(int status) {
 
 size_t cmpx_attn_workspace_size(const cmpx_attn_desc* desc) {
   // The persistent 16-bit kernels keep two work counters (next item, CTAs finished); a non-causal
-  // call whose last wave of items is partial also parks the split items' partial results.
-  if (!desc || (desc->dtype != CMPX_F16 && desc->dtype != CMPX_BF16)) return 0;
+  // call whose last wave of items is partial also parks the split items' partial results.  An fp32
+  // call needs workspace only for such a split (and runs without it when given none).
+  if (!desc) return 0;
+  if (desc->dtype == CMPX_F32) return attn_tf32x3_workspace_bytes(desc, current_num_sms());
+  if (desc->dtype != CMPX_F16 && desc->dtype != CMPX_BF16) return 0;
   return fmha_workspace_bytes(desc, current_num_sms());
 }
 
