@@ -391,7 +391,9 @@ def test_mask_plans_on_the_16bit_and_fp32_kernels():
 def test_workspace_contract():
     assert N.lib.cmpx_attn_workspace_size(ctypes.byref(_attn(dtype=2))) == 256
     assert N.lib.cmpx_attn_workspace_size(ctypes.byref(_attn(dtype=1))) == 256
-    assert N.lib.cmpx_attn_workspace_size(ctypes.byref(_attn(dtype=0))) == 0
+    # fp32: no split here, but two 128-row items per head share split K / V^T operands
+    assert N.lib.cmpx_attn_workspace_size(ctypes.byref(_attn(dtype=0))) == 1024 + 4 * 2 * 256 * 128 * 4
+    assert N.lib.cmpx_attn_workspace_size(ctypes.byref(_attn(Lq=128, dtype=0))) == 0  # one item per head
     assert N.lib.cmpx_attn_workspace_size(None) == 0
     d = _attn(dtype=2)  # valid shape, no workspace: rejected before any device work
     assert N.lib.cmpx_attn_fwd(ctypes.byref(d), None) == N.ERR_WORKSPACE
@@ -446,6 +448,16 @@ def _f32_split_bytes(items, tiles, dp, sms=148):
     return 256 + rem * split * 128 * (dp + 4) * 4 if split >= 2 else 0
 
 
+def _f32_workspace(cfg, split_bytes, dp):
+    """The split's bytes, then (when every (b, h) has two or more 128-row items) K hi / lo and
+    V^T hi / lo, fp32, B * H * lk_pad * dp each, from the next 1024-byte boundary."""
+    if (cfg["Lq"] + 127) // 128 < 2:
+        return split_bytes
+    lk_pad = (cfg["Lk"] + 63) // 64 * 64
+    off = (max(256, split_bytes) + 1023) // 1024 * 1024
+    return off + 4 * cfg["B"] * cfg["H"] * lk_pad * dp * 4
+
+
 @pytest.mark.parametrize("cfg,split", [
     (dict(B=2, H=8, Lq=4096, Lk=4096, D=40, dtype=0), True),     # C1: 512 items, 68 cut 2 ways
     (dict(B=1, H=150, Lq=128, Lk=4096, D=64, dtype=0), True),    # 2 tail items cut 8 ways
@@ -458,10 +470,10 @@ def test_fp32_workspace_covers_its_tail_split(cfg, split):
     d = _attn(**cfg)
     dp = 64 if cfg["D"] <= 64 else 128
     items = (cfg["Lq"] + 127) // 128 * cfg["H"] * cfg["B"]
-    want = 0 if cfg.get("causal") else _f32_split_bytes(
+    sb = 0 if cfg.get("causal") else _f32_split_bytes(
         items, (cfg["Lk"] + (63 if dp == 64 else 31)) // (64 if dp == 64 else 32), dp)
-    assert (want > 0) == split
-    assert N.lib.cmpx_attn_workspace_size(ctypes.byref(d)) == want
+    assert (sb > 0) == split
+    assert N.lib.cmpx_attn_workspace_size(ctypes.byref(d)) == _f32_workspace(cfg, sb, dp)
     st, name = _plan(d)
     assert st == 0 and name.endswith("+tail-split>") == split, name
 

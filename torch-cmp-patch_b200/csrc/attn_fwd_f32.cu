@@ -42,7 +42,7 @@ const char* attn_f32_plan(const cmpx_attn_desc* d, int* status) {
           "attn_tf32x3_sm100<D128,128q,32kv,persistent+mask+tail-split>",
           "attn_tf32x3_sm100<D128,128q,32kv,persistent+addmask+tail-split>"}}};
     const int mk = !d->mask ? 0 : d->mask_kind == CMPX_MASK_BOOL ? 1 : 2;
-    const int split = attn_tf32x3_workspace_bytes(d, current_num_sms()) > 0 ? 1 : 0;
+    const int split = attn_tf32x3_tail_split(d, current_num_sms()) ? 1 : 0;
     return names[split][d->head_dim <= 64 ? 0 : 1][mk];
   }
   // Operands the 3xTF32 kernel cannot read with TMA (strides or pointers not 16-byte aligned; the

@@ -5,17 +5,19 @@
 // x = x_hi + x_lo, x_hi the value truncated to TF32 (exactly representable) and x_lo = x - x_hi
 // (exact in fp32), a b ~= a_hi b_hi + a_hi b_lo + a_lo b_hi, dropping only a_lo b_lo (~2^-22
 // relative).  It replaces the reference's fp32 attention (attention_fp32_strict_kernel,
-// src/cuda/fp32_attention.cu:35-198: one thread per query row on the CUDA cores) for head dims
-// <= 64 (SD1.5's fp32 attention has D = 40); larger head dims keep the CUDA-core kernel of
-// attn_fwd_f32.cu.
+// src/cuda/fp32_attention.cu:35-198: one thread per query row on the CUDA cores) for every head dim
+// of that kernel (D <= 128; SD1.5's fp32 attention has D = 40).
 //
 //   * a CTA owns a 128-row Q tile of one (batch, head) at a time (persistent, items strided over
-//     the grid); keys stream in 64-key tiles;
-//   * warp 0: TMA of Q (once per item, into a staging tile) and K, V tiles (fp32, 128-byte
-//     swizzle, OOB zero-filled) into a 3-stage ring;
+//     the grid); keys stream in 64-key tiles (D <= 64) or 32-key tiles (D <= 128);
+//   * K hi / lo and V^T hi / lo: made once per call by x3_kv_split_kernel into the workspace when
+//     every (batch, head) has two or more Q tiles to share them, and then loaded by TMA as they
+//     are; otherwise the converter warps make them per stage from raw K / V tiles;
+//   * warp 0: TMA of Q (once per item, into a staging tile) and of the K / V operand tiles (fp32,
+//     128-byte swizzle, OOB zero-filled) into a ring of stages;
 //   * warps 2-5 ("converter", thread = row for Q): Q split into hi / lo and written to TMEM (the
-//     QK products read A from TMEM); V transposed into V^T hi / lo (the K-major B operand of P V),
-//     then K split in place into hi and lo (lo over the raw V, already consumed) -- 64 KB a stage;
+//     QK products read A from TMEM); without the split operands also V transposed into V^T hi / lo
+//     (the K-major B operand of P V) and K split in place into hi and lo;
 //   * warp 1: tcgen05.mma kind::tf32 -- S = Qh Kh^T + Qh Kl^T + Ql Kh^T into one of two TMEM S
 //     buffers, O += Ph Vh + Ph Vl + Pl Vh with P read from TMEM.  The warp polls the inputs of the
 //     next S and of the pending P V and issues whichever is ready first, so neither waits behind
@@ -24,10 +26,13 @@
 //     it by more than 2^64 (fp32 keeps p = 2^(x - m) exact far beyond that; O, l and P share m,
 //     so the result is the same), p in fp32, split into Ph (written over the tile's own S buffer)
 //     and Pl (one of two buffers); the epilogue writes O / l.  Tile j's S buffer is reused by tile
-//     j+2 only after PV(j) is done, so storing P never waits for a PV.
+//     j+2 only after PV(j) is done, so storing P never waits for a PV;
+//   * tail split (non-causal): when the last wave holds at most half a wave of Q tiles, those are
+//     cut into key ranges whose (O, m, l) rows are parked in the workspace and merged by the CTA
+//     of each tile's last range to finish.
 //
-// TMEM columns: S0 / Ph0 [0,64), S1 / Ph1 [64,128), Pl0 [128,192), Pl1 [192,256), O [256,320),
-// Qh [320,384), Ql [384,448).
+// TMEM columns (D <= 64): S0 / Ph0 [0,64), S1 / Ph1 [64,128), Pl0 [128,192), Pl1 [192,256),
+// O [256,320), Qh [320,384), Ql [384,448) (D <= 128: 32-column S / P buffers, 128-column O, Qh, Ql).
 // Every wait is bounded (cmpx_ptx.cuh); a CTA that gives up drains its copies and MMAs, frees
 // TMEM, raises the device status word and returns.
 #include <cuda.h>
@@ -98,6 +103,10 @@ struct X3Params {
   int n_whole, split, n_work;
   unsigned int* cnt;
   float* part;
+  // Split operands (pre = 1): K hi / lo and V^T hi / lo made once per call by x3_kv_split_kernel
+  // (in the workspace) and loaded by TMA as they are, so the converter warps only split Q.
+  int pre;
+  int heads_kv;
   int qk_steps;   // ceil(head_dim / 8): K=8 steps of Q K^T
   int causal, neg_scale;
   int group;      // query heads per key/value head (grouped-query attention)
@@ -170,7 +179,10 @@ template <int DP, int MK>
 __global__ void __launch_bounds__(320, 1)
     attn_tf32x3_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                              const __grid_constant__ CUtensorMap tm_k,
-                             const __grid_constant__ CUtensorMap tm_v, const X3Params p) {
+                             const __grid_constant__ CUtensorMap tm_v,
+                             const __grid_constant__ CUtensorMap tm_kh, const __grid_constant__ CUtensorMap tm_kl,
+                             const __grid_constant__ CUtensorMap tm_vh, const __grid_constant__ CUtensorMap tm_vl,
+                             const X3Params p) {
   using C = X3Cfg<DP>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
@@ -233,8 +245,15 @@ __global__ void __launch_bounds__(320, 1)
   }
   if (warp == C::W_TMA && lane == 0) {
     tma_prefetch_desc(&tm_q);
-    tma_prefetch_desc(&tm_k);
-    tma_prefetch_desc(&tm_v);
+    if (p.pre) {
+      tma_prefetch_desc(&tm_kh);
+      tma_prefetch_desc(&tm_kl);
+      tma_prefetch_desc(&tm_vh);
+      tma_prefetch_desc(&tm_vl);
+    } else {
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+    }
   }
   tc_fence_before_sync();
   __syncthreads();
@@ -258,12 +277,25 @@ __global__ void __launch_bounds__(320, 1)
           const int st = load % C::NS;
           if (!(ok = mbar_wait(bar(C::B_EMPTY + st), (static_cast<uint32_t>(load / C::NS) & 1u) ^ 1u, ctl))) break;
           const uint32_t sb = stage(load);
-          mbar_arrive_expect_tx(bar(C::B_FULL + st), 2 * C::T_BYTES);
-          for (int c = 0; c < C::NQC; ++c) {
-            tma_load_4d(sb + C::ST_K + c * C::KCH, &tm_k, bar(C::B_FULL + st), c * 32, (j0 + j) * C::BN,
-                        h / p.group, b);
-            tma_load_4d(sb + C::ST_B + c * C::KCH, &tm_v, bar(C::B_FULL + st), c * 32, (j0 + j) * C::BN,
-                        h / p.group, b);
+          if (p.pre) {  // the four split operand tiles, as the MMAs read them
+            const int bhkv = b * p.heads_kv + h / p.group, key0 = (j0 + j) * C::BN;
+            mbar_arrive_expect_tx(bar(C::B_FULL + st), 4 * C::T_BYTES);
+            for (int c = 0; c < C::NQC; ++c) {
+              tma_load_3d(sb + C::ST_K + c * C::KCH, &tm_kh, bar(C::B_FULL + st), c * 32, key0, bhkv);
+              tma_load_3d(sb + C::ST_B + c * C::KCH, &tm_kl, bar(C::B_FULL + st), c * 32, key0, bhkv);
+            }
+            for (int u = 0; u < C::BN / 32; ++u) {
+              tma_load_3d(sb + C::ST_VTH + u * C::VCH, &tm_vh, bar(C::B_FULL + st), key0 + u * 32, 0, bhkv);
+              tma_load_3d(sb + C::ST_VTL + u * C::VCH, &tm_vl, bar(C::B_FULL + st), key0 + u * 32, 0, bhkv);
+            }
+          } else {
+            mbar_arrive_expect_tx(bar(C::B_FULL + st), 2 * C::T_BYTES);
+            for (int c = 0; c < C::NQC; ++c) {
+              tma_load_4d(sb + C::ST_K + c * C::KCH, &tm_k, bar(C::B_FULL + st), c * 32, (j0 + j) * C::BN,
+                          h / p.group, b);
+              tma_load_4d(sb + C::ST_B + c * C::KCH, &tm_v, bar(C::B_FULL + st), c * 32, (j0 + j) * C::BN,
+                          h / p.group, b);
+            }
           }
         }
       }
@@ -312,7 +344,7 @@ __global__ void __launch_bounds__(320, 1)
         if (nq < n_kv) {
           const int ld = load_base + nq, gq = g + nq, bs = gq & 1;
           // K/V tile converted; buffer bs (tile gq-2's S, then P) consumed by PV(gq-2).
-          if (ready(bar(C::B_CONV + ld % C::NS), static_cast<uint32_t>(ld / C::NS) & 1u) &&
+          if (ready(bar((p.pre ? C::B_FULL : C::B_CONV) + ld % C::NS), static_cast<uint32_t>(ld / C::NS) & 1u) &&
               (gq < 2 || ready(bar(C::B_PVD + bs), static_cast<uint32_t>((gq - 2) >> 1) & 1u))) {
             tc_fence_after_sync();
             issue_qk(stage(ld), tmem + (bs ? C::TM_S1 : C::TM_S0));
@@ -395,6 +427,7 @@ __global__ void __launch_bounds__(320, 1)
       tmem_st_wait();
       tc_fence_before_sync();
       mbar_arrive(bar(C::B_QCONV));
+      if (p.pre) continue;  // the K / V tiles arrive split
       for (int j = 0; ok && j < n_kv; ++j, ++load) {
         const int st = load % C::NS;
         if (!(ok = mbar_wait_all(bar(C::B_FULL + st), static_cast<uint32_t>(load / C::NS) & 1u, ctl))) break;
@@ -693,6 +726,49 @@ __global__ void __launch_bounds__(320, 1)
   }
 }
 
+// K and V of every (batch, kv head) split once per call into the layouts the MMAs read: K hi / lo
+// [bh][key][d] and V^T hi / lo [bh][d][key] (fp32, hi = TF32-truncated, lo = the exact remainder),
+// padded with zeros to DP columns / rows and to lk_pad keys.  One block per 32 keys of one (b, h):
+// K goes straight through (reads and writes contiguous along d), V through a shared-memory tile so
+// that V^T's writes are contiguous along the keys.
+struct X3SplitParams {
+  const float* k;
+  const float* v;
+  long long ks_b, ks_h, ks_s, vs_b, vs_h, vs_s;
+  int heads_kv, len_k, head_dim, dp, lk_pad;
+  float* kh;
+  float* kl;
+  float* vh;
+  float* vl;
+};
+
+__global__ void __launch_bounds__(256) x3_kv_split_kernel(const X3SplitParams p) {
+  __shared__ float tile[32][129];
+  const int bh = blockIdx.y, b = bh / p.heads_kv, h = bh - b * p.heads_kv;
+  const int key0 = blockIdx.x * 32;
+  const float* kin = p.k + b * p.ks_b + h * p.ks_h;
+  const float* vin = p.v + b * p.vs_b + h * p.vs_h;
+  for (int e = threadIdx.x; e < 32 * p.dp; e += 256) {
+    const int r = e / p.dp, d = e - r * p.dp, key = key0 + r;
+    const bool in = key < p.len_k && d < p.head_dim;
+    const float x = in ? __ldg(kin + static_cast<long long>(key) * p.ks_s + d) : 0.f;
+    const float hi = __uint_as_float(tf32_trunc(__float_as_uint(x)));
+    const size_t o = (static_cast<size_t>(bh) * p.lk_pad + key) * p.dp + d;
+    p.kh[o] = hi;
+    p.kl[o] = x - hi;
+    tile[r][d] = in ? __ldg(vin + static_cast<long long>(key) * p.vs_s + d) : 0.f;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < 32 * p.dp; e += 256) {
+    const int d = e >> 5, r = e & 31;
+    const float x = tile[r][d];
+    const float hi = __uint_as_float(tf32_trunc(__float_as_uint(x)));
+    const size_t o = (static_cast<size_t>(bh) * p.dp + d) * p.lk_pad + key0 + r;
+    p.vh[o] = hi;
+    p.vl[o] = x - hi;
+  }
+}
+
 // --------------------------------------------------------------------------------------------
 // Host side
 // --------------------------------------------------------------------------------------------
@@ -765,6 +841,27 @@ X3Split x3_split_plan(const cmpx_attn_desc* d, int num_sms) {
   return sp;
 }
 
+// Split operands (pre): four fp32 buffers of B * heads_kv * lk_pad * DP, after the split's bytes
+// (1024-aligned), worth it when every (b, h) has two or more 128-row items to share them.
+struct X3Pre {
+  bool use = false;
+  int lk_pad = 0;
+  size_t off = 0, each = 0, bytes = 0;  // bytes: the whole workspace with them
+};
+
+template <int DP>
+X3Pre x3_pre_plan(const cmpx_attn_desc* d, const X3Split& sp) {
+  using C = X3Cfg<DP>;
+  X3Pre pr;
+  if ((d->len_q + C::BM - 1) / C::BM < 2) return pr;
+  pr.use = true;
+  pr.lk_pad = static_cast<int>((d->len_k + 63) / 64 * 64);
+  pr.off = (std::max<size_t>(256, sp.bytes) + 1023) & ~static_cast<size_t>(1023);
+  pr.each = static_cast<size_t>(d->batch) * attn_heads_kv(d) * pr.lk_pad * DP * 4;
+  pr.bytes = pr.off + 4 * pr.each;
+  return pr;
+}
+
 template <int DP>
 int launch_tf32x3_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   using C = X3Cfg<DP>;
@@ -824,12 +921,55 @@ int launch_tf32x3_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
     p.cnt = static_cast<unsigned int*>(d->workspace);
     p.part = reinterpret_cast<float*>(static_cast<char*>(d->workspace) + sp.cnt_bytes);
   }
+  // Split operands, when the workspace holds them: one pre-pass launch, then TMA maps over them.
+  const X3Pre pr = x3_pre_plan<DP>(d, sp);
+  p.pre = 0;
+  p.heads_kv = static_cast<int>(attn_heads_kv(d));
+  CUtensorMap tkh = tk, tkl = tk, tvh = tv, tvl = tv;
+  if (pr.use && d->workspace && d->workspace_bytes >= pr.bytes &&
+      (reinterpret_cast<uintptr_t>(d->workspace) & 255u) == 0) {
+    char* base = static_cast<char*>(d->workspace) + pr.off;
+    X3SplitParams xp;
+    xp.k = static_cast<const float*>(d->k);
+    xp.v = static_cast<const float*>(d->v);
+    xp.ks_b = d->k_stride[0];
+    xp.ks_h = d->k_stride[1];
+    xp.ks_s = d->k_stride[2];
+    xp.vs_b = d->v_stride[0];
+    xp.vs_h = d->v_stride[1];
+    xp.vs_s = d->v_stride[2];
+    xp.heads_kv = p.heads_kv;
+    xp.len_k = p.len_k;
+    xp.head_dim = p.head_dim;
+    xp.dp = DP;
+    xp.lk_pad = pr.lk_pad;
+    xp.kh = reinterpret_cast<float*>(base);
+    xp.kl = reinterpret_cast<float*>(base + pr.each);
+    xp.vh = reinterpret_cast<float*>(base + 2 * pr.each);
+    xp.vl = reinterpret_cast<float*>(base + 3 * pr.each);
+    const uint64_t bhkv = static_cast<uint64_t>(d->batch) * p.heads_kv;
+    const uint64_t kdims[3] = {static_cast<uint64_t>(DP), static_cast<uint64_t>(pr.lk_pad), bhkv};
+    const uint64_t kst[2] = {static_cast<uint64_t>(DP) * 4, static_cast<uint64_t>(pr.lk_pad) * DP * 4};
+    const uint32_t kbox[3] = {32, static_cast<uint32_t>(C::BN), 1};
+    const uint64_t vdims[3] = {static_cast<uint64_t>(pr.lk_pad), static_cast<uint64_t>(DP), bhkv};
+    const uint64_t vst[2] = {static_cast<uint64_t>(pr.lk_pad) * 4, static_cast<uint64_t>(DP) * pr.lk_pad * 4};
+    const uint32_t vbox[3] = {32, static_cast<uint32_t>(DP), 1};
+    const CUtensorMapDataType f32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    if (!encode_tmap(&tkh, f32, 3, xp.kh, kdims, kst, kbox, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap(&tkl, f32, 3, xp.kl, kdims, kst, kbox, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap(&tvh, f32, 3, xp.vh, vdims, vst, vbox, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap(&tvl, f32, 3, xp.vl, vdims, vst, vbox, CU_TENSOR_MAP_SWIZZLE_128B))
+      return CMPX_ERR_LAUNCH;
+    const dim3 sgrid(static_cast<unsigned>(pr.lk_pad / 32), static_cast<unsigned>(bhkv));
+    x3_kv_split_kernel<<<sgrid, 256, 0, ctx.stream>>>(xp);
+    p.pre = 1;
+  }
   if (!d->mask)
-    attn_tf32x3_sm100_kernel<DP, 0><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, p);
+    attn_tf32x3_sm100_kernel<DP, 0><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, tkh, tkl, tvh, tvl, p);
   else if (d->mask_kind == CMPX_MASK_BOOL)
-    attn_tf32x3_sm100_kernel<DP, 1><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, p);
+    attn_tf32x3_sm100_kernel<DP, 1><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, tkh, tkl, tvh, tvl, p);
   else
-    attn_tf32x3_sm100_kernel<DP, 2><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, p);
+    attn_tf32x3_sm100_kernel<DP, 2><<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(tq, tk, tv, tkh, tkl, tvh, tvl, p);
   return cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
 }
 
@@ -837,7 +977,19 @@ int launch_tf32x3_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
 
 size_t attn_tf32x3_workspace_bytes(const cmpx_attn_desc* d, int num_sms) {
   if (!attn_tf32x3_eligible(d)) return 0;
-  return d->head_dim <= 64 ? x3_split_plan<64>(d, num_sms).bytes : x3_split_plan<128>(d, num_sms).bytes;
+  if (d->head_dim <= 64) {
+    const X3Split sp = x3_split_plan<64>(d, num_sms);
+    const X3Pre pr = x3_pre_plan<64>(d, sp);
+    return pr.use ? pr.bytes : sp.bytes;
+  }
+  const X3Split sp = x3_split_plan<128>(d, num_sms);
+  const X3Pre pr = x3_pre_plan<128>(d, sp);
+  return pr.use ? pr.bytes : sp.bytes;
+}
+
+bool attn_tf32x3_tail_split(const cmpx_attn_desc* d, int num_sms) {
+  if (!attn_tf32x3_eligible(d)) return false;
+  return (d->head_dim <= 64 ? x3_split_plan<64>(d, num_sms).split : x3_split_plan<128>(d, num_sms).split) > 1;
 }
 
 int launch_attn_tf32x3(const cmpx_attn_desc* d, const LaunchCtx& ctx) {

@@ -63,6 +63,7 @@ bool attn_tf32x3_eligible(const cmpx_attn_desc* d);
 int launch_attn_tf32x3(const cmpx_attn_desc* d, const LaunchCtx& ctx);
 // workspace of an fp32 call's tail split (0: the call runs without one)
 size_t attn_tf32x3_workspace_bytes(const cmpx_attn_desc* d, int num_sms);
+bool attn_tf32x3_tail_split(const cmpx_attn_desc* d, int num_sms);
 
 // ---- batched matmul ----
 const char* bmm_sm100_plan(const cmpx_bmm_desc* d, int* status);
