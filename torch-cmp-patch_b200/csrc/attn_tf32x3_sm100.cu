@@ -139,37 +139,50 @@ __device__ __forceinline__ void split_v4(uint32_t addr_in, uint32_t addr_hi, uin
 // S = Qh Kh^T + Qh Kl^T + Ql Kh^T over the first `steps` K=8 steps of the head dim (Q hi / lo from
 // TMEM, K hi / lo in shared memory, KCH bytes per 32-column chunk).  The step count is dispatched
 // once to a straight-line sequence of exactly that many MMAs per part: measured on B200, a runtime
-// guard around each MMA raised the issue cost from ~30-40 to ~70-90 clk per MMA.
-template <int S, int KCH>
+// guard around each MMA raised the issue cost from ~30-40 to ~70-90 clk per MMA.  Q4: each whole
+// 32-column chunk goes as one four-MMA statement under one election (D = 128: measured 1046 ->
+// 974 us on [2,8,4096,128]; with D <= 64 it measured 1-3 % slower, so those keep one per MMA).
+template <int S, int KCH, bool Q4>
 __device__ __forceinline__ void x3_issue_qk(int steps, uint32_t s_tmem, uint32_t qh, uint32_t ql, uint64_t dkh,
                                             uint64_t dkl, uint32_t idesc) {
   if (steps == S) {
 #pragma unroll
     for (int part = 0; part < 3; ++part) {
+      const uint32_t qa = part == 2 ? ql : qh;
+      const uint64_t kb = part == 1 ? dkl : dkh;
+      constexpr int S4 = Q4 ? (S & ~3) : 0;  // steps issued four at a time
 #pragma unroll
-      for (int s = 0; s < S; ++s) {
+      for (int s = 0; s < S4; s += 4)
+        umma_ts_tf32_x4_w(s_tmem, qa + s * 8, kb + static_cast<uint64_t>(((s >> 2) * KCH) >> 4), idesc,
+                          (part > 0 || s > 0) ? 1u : 0u);
+#pragma unroll
+      for (int s = S4; s < S; ++s) {
         const uint64_t koff = static_cast<uint64_t>(((s >> 2) * KCH + (s & 3) * 32) >> 4);
-        umma_ts_tf32_w(s_tmem, (part == 2 ? ql : qh) + s * 8, (part == 1 ? dkl : dkh) + koff, idesc,
-                       (part > 0 || s > 0) ? 1u : 0u);
+        umma_ts_tf32_w(s_tmem, qa + s * 8, kb + koff, idesc, (part > 0 || s > 0) ? 1u : 0u);
       }
     }
   } else if constexpr (S > 1) {
-    x3_issue_qk<S - 1, KCH>(steps, s_tmem, qh, ql, dkh, dkl, idesc);
+    x3_issue_qk<S - 1, KCH, Q4>(steps, s_tmem, qh, ql, dkh, dkl, idesc);
   }
 }
 
 // O (+)= Ph Vh + Ph Vl + Pl Vh over a tile's BN keys (BN / 8 K-steps of 8; V^T in 32-key chunks of
-// VCH bytes), P hi / lo from TMEM.
-template <int BN, int VCH>
+// VCH bytes), P hi / lo from TMEM.  Q4 as for x3_issue_qk.
+template <int BN, int VCH, bool Q4>
 __device__ __forceinline__ void x3_issue_pv(uint32_t o_tmem, uint32_t ph, uint32_t pl, uint64_t dvh, uint64_t dvl,
                                             uint32_t idesc, uint32_t acc0) {
 #pragma unroll
   for (int part = 0; part < 3; ++part) {
+    const uint32_t pa = part == 2 ? pl : ph;
+    const uint64_t vb = part == 1 ? dvl : dvh;
 #pragma unroll
-    for (int s = 0; s < BN / 8; ++s) {
+    for (int s = 0; s < BN / 8; s += Q4 ? 4 : 1) {
       const uint64_t voff = static_cast<uint64_t>(((s >> 2) * VCH + (s & 3) * 32) >> 4);
-      umma_ts_tf32_w(o_tmem, (part == 2 ? pl : ph) + s * 8, (part == 1 ? dvl : dvh) + voff, idesc,
-                     (part > 0 || s > 0) ? 1u : acc0);
+      const uint32_t acc = (part > 0 || s > 0) ? 1u : acc0;
+      if constexpr (Q4)
+        umma_ts_tf32_x4_w(o_tmem, pa + s * 8, vb + voff, idesc, acc);
+      else
+        umma_ts_tf32_w(o_tmem, pa + s * 8, vb + voff, idesc, acc);
     }
   }
 }
@@ -318,14 +331,14 @@ __global__ void __launch_bounds__(320, 1)
     auto issue_qk = [&](uint32_t sb, uint32_t s_tmem) {
       const uint64_t dkh = smem_desc_sw128(sb + C::ST_K, 16, 1024);
       const uint64_t dkl = smem_desc_sw128(sb + C::ST_B, 16, 1024);
-      x3_issue_qk<DP / 8, C::KCH>(p.qk_steps, s_tmem, tmem + C::TM_QH, tmem + C::TM_QL, dkh, dkl, kIdesc);
+      x3_issue_qk<DP / 8, C::KCH, DP == 128>(p.qk_steps, s_tmem, tmem + C::TM_QH, tmem + C::TM_QL, dkh, dkl, kIdesc);
     };
     // O (+)= Ph Vh + Ph Vl + Pl Vh over the tile's 64 keys (8 K-steps of 8); P of buffer pb.
     auto issue_pv = [&](uint32_t sb, int pb, bool acc) {
       const uint64_t dvh = smem_desc_sw128(sb + C::ST_VTH, 16, 1024);
       const uint64_t dvl = smem_desc_sw128(sb + C::ST_VTL, 16, 1024);
       const uint32_t ph = tmem + (pb ? C::TM_S1 : C::TM_S0), pl = tmem + (pb ? C::TM_PL1 : C::TM_PL0);
-      x3_issue_pv<C::BN, C::VCH>(tmem + C::TM_O, ph, pl, dvh, dvl, kIdescPV, acc ? 1u : 0u);
+      x3_issue_pv<C::BN, C::VCH, DP == 128>(tmem + C::TM_O, ph, pl, dvh, dvl, kIdescPV, acc ? 1u : 0u);
     };
     // Warp-uniform non-blocking test of one barrier phase.
     auto ready = [&](uint32_t b, uint32_t parity) -> bool {

@@ -322,6 +322,26 @@ __device__ __forceinline__ void umma_ts_tf32_w(uint32_t d_tmem, uint32_t a_tmem,
       : "memory");
 }
 
+// Four TS tf32 MMAs along K under one election, in one asm statement: the k-th reads A at
+// a_tmem + 8k (columns) and B at b_desc + 2k (32 bytes further along the 128-byte swizzled rows);
+// `accumulate` applies to the first, the other three accumulate.
+__device__ __forceinline__ void umma_ts_tf32_x4_w(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                                  uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred e, p, t;\n\t.reg .b64 d1, d2, d3;\n\t.reg .b32 a1, a2, a3;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.eq.u32 t, 1, 1;\n\t"
+      "add.s64 d1, %2, 2;\n\tadd.s64 d2, %2, 4;\n\tadd.s64 d3, %2, 6;\n\t"
+      "add.u32 a1, %1, 8;\n\tadd.u32 a2, %1, 16;\n\tadd.u32 a3, %1, 24;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [a1], d1, %3, t;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [a2], d2, %3, t;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [a3], d3, %3, t;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 __device__ __forceinline__ void umma_commit_w(uint32_t bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\t"
