@@ -422,6 +422,32 @@ def tensor_roofline(flops_per_launch: float, mean_ms: float, region_ms: float, c
             "algorithmic_flops_per_launch": flops_per_launch}
 
 
+def tf32_peak_here(dev) -> float:
+    """cuBLAS's TF32 GEMM rate on this GPU, timed here (MEASURED_PEAKS.json holds bf16 and HBM
+    figures only): 8192^3 fp32 products with TF32 allowed, 3 untimed then 10 timed, CUDA events.
+    The fp32 attention kernel runs three TF32 products per algorithmic product, so a third of this
+    is its roofline."""
+    import torch
+    n = 8192
+    a = torch.randn(n, n, device=dev)
+    b = torch.randn(n, n, device=dev)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        for _ in range(3):
+            a @ b
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(10):
+            a @ b
+        e1.record()
+        torch.cuda.synchronize(dev)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    del a, b
+    return 2.0 * n ** 3 / (e0.elapsed_time(e1) / 10 * 1e-3) / 1e12
+
+
 def extra_sdpa_record(key: str, steps: int, warmup: int, warm_s: float, dev, stream, peaks, peak_src) -> dict:
     """One more single-GPU SDPA workload timed in the same process (after the main one, with its
     own warm-up, CUDA events and clock samples): the C4 prefill config beside the C5 headline."""
@@ -629,6 +655,11 @@ def main() -> int:
         elif w["kind"] == "sdpa":
             roof = tensor_roofline(step_flops_rank, statistics.mean(per_step_ms), region_ms, clock_info, peaks,
                                    peak_src, kernel_name)
+            if w["dtype"] == "f32":
+                # the fp32 kernel's own ceiling: three TF32 products per product, at cuBLAS's TF32 rate
+                tf32 = tf32_peak_here(dev)
+                roof["tf32_cublas_tflops_here"] = round(tf32, 1)
+                roof["frac_of_3xtf32"] = round(roof["achieved"] / (tf32 / 3.0), 4)
         else:
             # C3 is HBM-bound on the score tensor, which the user holds twice (scores s and
             # probabilities p, both materialised tensors of the chain): the scores bmm writes s,
