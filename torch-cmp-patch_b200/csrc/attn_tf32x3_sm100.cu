@@ -18,10 +18,12 @@
 //   * warps 2-5 ("converter", thread = row for Q): Q split into hi / lo and written to TMEM (the
 //     QK products read A from TMEM); without the split operands also V transposed into V^T hi / lo
 //     (the K-major B operand of P V) and K split in place into hi and lo;
-//   * warp 1: tcgen05.mma kind::tf32 -- S = Qh Kh^T + Qh Kl^T + Ql Kh^T into one of two TMEM S
-//     buffers, O += Ph Vh + Ph Vl + Pl Vh with P read from TMEM.  The warp polls the inputs of the
-//     next S and of the pending P V and issues whichever is ready first, so neither waits behind
-//     the other's loads;
+//   * warps 1 and 10: tcgen05.mma kind::tf32 -- warp 1 issues S = Qh Kh^T + Qh Kl^T + Ql Kh^T into
+//     one of two TMEM S buffers, warp 10 issues O += Ph Vh + Ph Vl + Pl Vh with P read from TMEM.
+//     Two issuers on two SMSPs, each waiting only for its own inputs: one warp that polled the
+//     inputs of both products and issued whichever was ready measured 348 us on C1 against 318
+//     (its MMA issue, a few instructions per MMA on an SMSP shared with a softmax warp, left the
+//     tensor pipe idle about half of each tile);
 //   * warps 6-9 (thread = row): exact tile max, running max moved only when a tile's max exceeds
 //     it by more than 2^64 (fp32 keeps p = 2^(x - m) exact far beyond that; O, l and P share m,
 //     so the result is the same), p in fp32, split into Ph (written over the tile's own S buffer)
@@ -79,8 +81,8 @@ struct X3Cfg {
   static constexpr int B_VREAD = B_OFREE + 1;      // converter threads have read a stage's raw V (128)
   static constexpr int B_EPI = B_VREAD + 1;         // tail split: the CTA's partial rows written (count 128)
   static constexpr int B_EPI2 = B_EPI + 1;          // tail split: the range's arrival counted
-  static constexpr int B_DRAIN = B_EPI2 + 1;
-  static constexpr int NBAR = B_DRAIN + 1;
+  static constexpr int B_DRAIN = B_EPI2 + 1;        // [2] the two MMA issuers' drains on abort
+  static constexpr int NBAR = B_DRAIN + 2;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static_assert(SMEM_BYTES <= 232448, "shared memory");
@@ -88,8 +90,8 @@ struct X3Cfg {
                        TM_QH = 4 * BN + DP, TM_QL = 4 * BN + 2 * DP;
   static constexpr int TMEM_COLS = 512;
   static_assert(TM_QL + DP <= TMEM_COLS, "TMEM columns");
-  static constexpr int THREADS = 320;
-  static constexpr int W_TMA = 0, W_MMA = 1;
+  static constexpr int THREADS = 352;
+  static constexpr int W_TMA = 0, W_MMA = 1, W_PV = 10;
 };
 
 struct X3Params {
@@ -189,7 +191,7 @@ __device__ __forceinline__ void x3_issue_pv(uint32_t o_tmem, uint32_t ph, uint32
 
 // MK: no mask (0), a boolean mask (1), an additive fp32 mask (2) -- separate instantiations.
 template <int DP, int MK>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(352, 1)
     attn_tf32x3_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                              const __grid_constant__ CUtensorMap tm_k,
                              const __grid_constant__ CUtensorMap tm_v,
@@ -249,6 +251,7 @@ __global__ void __launch_bounds__(320, 1)
     mbar_init(bar(C::B_EPI), 128);
     mbar_init(bar(C::B_EPI2), 1);
     mbar_init(bar(C::B_DRAIN), 1);
+    mbar_init(bar(C::B_DRAIN + 1), 1);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -318,85 +321,65 @@ __global__ void __launch_bounds__(320, 1)
       }
     }
   } else if (warp == C::W_MMA) {
-    // ------------------------------------------------------------------ MMA issuer (warp-uniform)
+    // ------------------------------------------------------------------ S issuer (warp-uniform)
+    // S_b = Qh Kh^T + Qh Kl^T + Ql Kh^T (Q from TMEM), qk_steps K-steps of 8.  Issue loops are
+    // fully unrolled with compile-time offsets added to descriptors built once per product (the
+    // start address sits in the low bits: no carry for shared-memory addresses), so each MMA costs
+    // the issuing warp about one MMA slot.
     constexpr uint32_t kIdesc = idesc_tf32(128, C::BN, 0, 0);    // S: K-major A (TMEM) and B
-    constexpr uint32_t kIdescPV = idesc_tf32(128, DP, 0, 0);     // O: K-major A (TMEM) and B (V^T)
     int load_base = 0;  // ring position of the item's first K/V tile
     int g = 0;          // tiles of all earlier items (S buffer and barrier phase bookkeeping)
     bool ok = true;
-    // Issue loops are fully unrolled with compile-time offsets added to descriptors built once
-    // per product (the start address sits in the low bits: no carry for shared-memory
-    // addresses), so each MMA costs the issuing warp about one MMA slot.
-    // One S product: S_b = Qh Kh^T + Qh Kl^T + Ql Kh^T (Q from TMEM), qk_steps K-steps of 8.
-    auto issue_qk = [&](uint32_t sb, uint32_t s_tmem) {
-      const uint64_t dkh = smem_desc_sw128(sb + C::ST_K, 16, 1024);
-      const uint64_t dkl = smem_desc_sw128(sb + C::ST_B, 16, 1024);
-      x3_issue_qk<DP / 8, C::KCH, DP == 128>(p.qk_steps, s_tmem, tmem + C::TM_QH, tmem + C::TM_QL, dkh, dkl, kIdesc);
-    };
-    // O (+)= Ph Vh + Ph Vl + Pl Vh over the tile's 64 keys (8 K-steps of 8); P of buffer pb.
-    auto issue_pv = [&](uint32_t sb, int pb, bool acc) {
-      const uint64_t dvh = smem_desc_sw128(sb + C::ST_VTH, 16, 1024);
-      const uint64_t dvl = smem_desc_sw128(sb + C::ST_VTL, 16, 1024);
-      const uint32_t ph = tmem + (pb ? C::TM_S1 : C::TM_S0), pl = tmem + (pb ? C::TM_PL1 : C::TM_PL0);
-      x3_issue_pv<C::BN, C::VCH, DP == 128>(tmem + C::TM_O, ph, pl, dvh, dvl, kIdescPV, acc ? 1u : 0u);
-    };
-    // Warp-uniform non-blocking test of one barrier phase.
-    auto ready = [&](uint32_t b, uint32_t parity) -> bool {
-      return __all_sync(0xffffffffu, mbar_test_wait(b, parity));
-    };
     for (int k = 0, w = blockIdx.x; ok && w < p.n_work; ++k, w += gridDim.x) {
       int b, h, q0, j0, n_kv;
       geometry(w, b, h, q0, j0, n_kv);
       (void)b; (void)h; (void)q0; (void)j0;
       if (!(ok = mbar_wait_all(bar(C::B_QCONV), static_cast<uint32_t>(k) & 1u, ctl))) break;
-      // Issue S(nq) and PV(np) in whichever order their inputs become ready.
-      int nq = 0, np = 0;
-      uint64_t t_idle = global_timer_ns();
-      while (np < n_kv) {
-        bool progress = false;
-        if (nq < n_kv) {
-          const int ld = load_base + nq, gq = g + nq, bs = gq & 1;
-          // K/V tile converted; buffer bs (tile gq-2's S, then P) consumed by PV(gq-2).
-          if (ready(bar((p.pre ? C::B_FULL : C::B_CONV) + ld % C::NS), static_cast<uint32_t>(ld / C::NS) & 1u) &&
-              (gq < 2 || ready(bar(C::B_PVD + bs), static_cast<uint32_t>((gq - 2) >> 1) & 1u))) {
-            tc_fence_after_sync();
-            issue_qk(stage(ld), tmem + (bs ? C::TM_S1 : C::TM_S0));
-            umma_commit_w(bar(C::B_SFULL + bs));
-            if (nq + 1 == n_kv) umma_commit_w(bar(C::B_QEMPTY));  // last product reading Q
-            ++nq;
-            progress = true;
-          }
-        }
-        if (np < nq) {
-          const int gp = g + np, pb = gp & 1;
-          // P written; the item's first PV overwrites O: the previous epilogue must have read it.
-          if (ready(bar(C::B_PREADY + pb), static_cast<uint32_t>(gp >> 1) & 1u) &&
-              (np > 0 || k == 0 || ready(bar(C::B_OFREE), static_cast<uint32_t>(k - 1) & 1u))) {
-            tc_fence_after_sync();
-            issue_pv(stage(load_base + np), pb, np > 0);
-            umma_commit_w(bar(C::B_PVD + pb));
-            umma_commit_w(bar(C::B_EMPTY + (load_base + np) % C::NS));
-            ++np;
-            progress = true;
-          }
-        }
-        if (progress) {
-          t_idle = global_timer_ns();
-        } else {
-          if (*abort_flag) {
-            ok = false;
-            break;
-          }
-          if (global_timer_ns() - t_idle > p.timeout_ns) {
-            if (lane == 0) {
-              *abort_flag = 1;
-              atomicOr(p.dev_flags, 1u /* CMPX_DEVFLAG_WAIT_TIMEOUT */);
-            }
-            ok = false;
-            break;
-          }
-          __nanosleep(64);
-        }
+      for (int j = 0; j < n_kv; ++j) {
+        const int ld = load_base + j, gq = g + j, bs = gq & 1;
+        // K/V tile ready; buffer bs (tile gq-2's S, then P) consumed by PV(gq-2)
+        if (!(ok = mbar_wait_all(bar((p.pre ? C::B_FULL : C::B_CONV) + ld % C::NS),
+                                 static_cast<uint32_t>(ld / C::NS) & 1u, ctl)))
+          break;
+        if (gq >= 2 && !(ok = mbar_wait_all(bar(C::B_PVD + bs), static_cast<uint32_t>((gq - 2) >> 1) & 1u, ctl)))
+          break;
+        tc_fence_after_sync();
+        const uint32_t sb = stage(ld);
+        const uint64_t dkh = smem_desc_sw128(sb + C::ST_K, 16, 1024);
+        const uint64_t dkl = smem_desc_sw128(sb + C::ST_B, 16, 1024);
+        x3_issue_qk<DP / 8, C::KCH, DP == 128>(p.qk_steps, tmem + (bs ? C::TM_S1 : C::TM_S0), tmem + C::TM_QH,
+                                               tmem + C::TM_QL, dkh, dkl, kIdesc);
+        umma_commit_w(bar(C::B_SFULL + bs));
+        if (j + 1 == n_kv) umma_commit_w(bar(C::B_QEMPTY));  // last product reading Q
+      }
+      g += n_kv;
+      load_base += n_kv;
+    }
+  } else if (warp == C::W_PV) {
+    // ------------------------------------------------------------------ P V issuer (warp-uniform)
+    // O (+)= Ph Vh + Ph Vl + Pl Vh over the tile's keys; P of buffer pb (hi over its S, lo in Pl).
+    // Separate from the S issuer, on another SMSP: each waits only for its own inputs.
+    constexpr uint32_t kIdescPV = idesc_tf32(128, DP, 0, 0);     // O: K-major A (TMEM) and B (V^T)
+    int load_base = 0, g = 0;
+    bool ok = true;
+    for (int k = 0, w = blockIdx.x; ok && w < p.n_work; ++k, w += gridDim.x) {
+      int b, h, q0, j0, n_kv;
+      geometry(w, b, h, q0, j0, n_kv);
+      (void)b; (void)h; (void)q0; (void)j0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int gp = g + j, pb = gp & 1;
+        if (!(ok = mbar_wait_all(bar(C::B_PREADY + pb), static_cast<uint32_t>(gp >> 1) & 1u, ctl))) break;
+        // the item's first PV overwrites O: the previous epilogue must have read it
+        if (j == 0 && k > 0 && !(ok = mbar_wait_all(bar(C::B_OFREE), static_cast<uint32_t>(k - 1) & 1u, ctl)))
+          break;
+        tc_fence_after_sync();
+        const uint32_t sb = stage(load_base + j);
+        const uint64_t dvh = smem_desc_sw128(sb + C::ST_VTH, 16, 1024);
+        const uint64_t dvl = smem_desc_sw128(sb + C::ST_VTL, 16, 1024);
+        const uint32_t ph = tmem + (pb ? C::TM_S1 : C::TM_S0), pl = tmem + (pb ? C::TM_PL1 : C::TM_PL0);
+        x3_issue_pv<C::BN, C::VCH, DP == 128>(tmem + C::TM_O, ph, pl, dvh, dvl, kIdescPV, j > 0 ? 1u : 0u);
+        umma_commit_w(bar(C::B_PVD + pb));
+        umma_commit_w(bar(C::B_EMPTY + (load_base + j) % C::NS));  // PV(j) is the stage's last reader
       }
       g += n_kv;
       load_base += n_kv;
@@ -481,7 +464,7 @@ __global__ void __launch_bounds__(320, 1)
         mbar_arrive(bar(C::B_CONV + st));
       }
     }
-  } else {
+  } else if (warp < C::W_PV) {
     // ------------------------------------------------------------------ softmax / epilogue (6-9)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
@@ -727,13 +710,17 @@ __global__ void __launch_bounds__(320, 1)
 
   tc_fence_before_sync();
   __syncthreads();
+  if ((warp == C::W_MMA || warp == C::W_PV) && *abort_flag) {
+    // each issuer waits for its own MMAs (a commit tracks the issuing thread's operations)
+    const uint32_t drain = bar(C::B_DRAIN + (warp == C::W_PV ? 1 : 0));
+    __syncwarp();
+    umma_commit_w(drain);
+    if (lane == 0) mbar_wait_drain(drain, 0, p.timeout_ns);
+    __syncwarp();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
   if (warp == C::W_MMA) {
-    if (*abort_flag) {
-      __syncwarp();
-      umma_commit_w(bar(C::B_DRAIN));
-      if (lane == 0) mbar_wait_drain(bar(C::B_DRAIN), 0, p.timeout_ns);
-      __syncwarp();
-    }
     tc_fence_after_sync();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
