@@ -359,7 +359,9 @@ __global__ void __launch_bounds__(352, 1)
     // ------------------------------------------------------------------ P V issuer (warp-uniform)
     // O (+)= Ph Vh + Ph Vl + Pl Vh over the tile's keys; P of buffer pb (hi over its S, lo in Pl).
     // Separate from the S issuer, on another SMSP: each waits only for its own inputs.
-    constexpr uint32_t kIdescPV = idesc_tf32(128, DP, 0, 0);     // O: K-major A (TMEM) and B (V^T)
+    // O: K-major A (TMEM) and B (V^T); N = the head dim rounded up to 16 (D = 40: 48 of the 64 O
+    // columns; the rest are never read for the output)
+    const uint32_t kIdescPV = idesc_tf32(128, DP == 64 ? max(16, (p.head_dim + 15) & ~15) : DP, 0, 0);
     int load_base = 0, g = 0;
     bool ok = true;
     for (int k = 0, w = blockIdx.x; ok && w < p.n_work; ++k, w += gridDim.x) {
