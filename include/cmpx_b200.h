@@ -39,10 +39,11 @@
 extern "C" {
 #endif
 
-#define CMPX_ABI_VERSION 6  /* 2: cmpx_attn_desc.heads_kv (grouped-query attention); 3: cmpx_linear;
+#define CMPX_ABI_VERSION 7  /* 2: cmpx_attn_desc.heads_kv (grouped-query attention); 3: cmpx_linear;
                                4: cmpx_attn_desc.mask / mask_kind (boolean or additive attention mask);
                                5: cmpx_bmm_small / cmpx_bmm_small_plan;
-                               6: cmpx_bmm_rowstats(_plan), cmpx_softmax_product(_plan) */
+                               6: cmpx_bmm_rowstats(_plan), cmpx_softmax_product(_plan);
+                               7: cmpx_bmm_ws / cmpx_linear_ws and their workspace sizes */
 
 /* Element type of every operand of one call (inputs and output share it, as in the reference:
  * dtype in == dtype out, src/main.cpp:1623-1627, :366-369). */
@@ -214,6 +215,23 @@ typedef struct cmpx_linear_desc {
 } cmpx_linear_desc;
 
 CMPX_API int cmpx_linear(const cmpx_linear_desc* desc, void* stream);
+
+/* cmpx_bmm / cmpx_linear with a device workspace, for the fp32 (3xTF32) products: given at least
+ * cmpx_*_workspace_size bytes (16-byte aligned), a pass before the GEMM writes the low parts
+ * (x - x truncated to TF32) of A and B, or of x and W, into the workspace once per call, and the
+ * GEMM loads them beside the operands instead of splitting every shared-memory tile again (the
+ * split's shared-memory traffic is what bounds the GEMM: 4096^3 measured 1.0 -> 0.6 ms).  The size
+ * is 0 when the product is too small for the pass to pay, and for fp16 / bf16 (which need none).
+ * The results are the same as without a workspace, bit for bit.  Bytes [0, 256) of the workspace
+ * are neither read nor written, so the workspace of the attention calls (whose first 256 bytes
+ * must stay zero) can be passed as it is; the rest is scratch, written before it is read.  Calls
+ * that share a workspace must not overlap on the GPU.  A smaller or NULL workspace runs the
+ * product as cmpx_bmm / cmpx_linear do.
+ * No reference counterpart (the reference allocates nothing but the output). */
+CMPX_API size_t cmpx_bmm_workspace_size(const cmpx_bmm_desc* desc);
+CMPX_API int cmpx_bmm_ws(const cmpx_bmm_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
+CMPX_API size_t cmpx_linear_workspace_size(const cmpx_linear_desc* desc);
+CMPX_API int cmpx_linear_ws(const cmpx_linear_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Row softmax over the last dimension:  y[r, :] = softmax(x[r, :]) for r < rows, computed in
  * fp32 (max, exp, sum) and rounded once to the output dtype (dtype in == dtype out), which is what

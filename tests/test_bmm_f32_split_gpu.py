@@ -1,0 +1,143 @@
+"""fp32 bmm / linear with split operands (needs a B200; marked gpu).
+
+For products large enough to pay (m n / (m + n) >= 512 per batch item) the binding passes a
+workspace to cmpx_bmm_ws / cmpx_linear_ws: a pass writes the low TF32 parts of A and B once per call
+and the GEMM loads them beside the operands.  Checked here: the result bit for bit against the same
+product without a workspace (the converter path, which splits every shared-memory tile), against
+the reference's CPU path within the fp32 contract and against float64; operands with inf, NaN and a
+NaN whose payload sits only in the bits TF32 drops (the pass flags it and the GEMM falls back to the
+converter path, which rewrites it); K chunks; and the workspace's first 256 bytes left as they were.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+import torch
+
+import cmpext3
+from cmpext3 import _native as N
+from oracle import reference_path as RP
+from tests.test_parity_gpu import check
+
+pytestmark = pytest.mark.gpu
+
+
+def _no_workspace(a, b):
+    """The same product through cmpx_bmm (no workspace): the converter path."""
+    a2, b2, c = N._prepare_bmm(a, b)
+    desc = N._bmm_desc(a2, b2, c)
+    st = N.lib.cmpx_bmm(ctypes.byref(desc), N._stream_handle(a.device))
+    assert st == 0, N.lib.cmpx_status_str(st)
+    return c
+
+
+def _ws_size(a, b):
+    a2, b2, c = N._prepare_bmm(a, b)
+    return N.lib.cmpx_bmm_workspace_size(ctypes.byref(N._bmm_desc(a2, b2, c)))
+
+
+def _rel64(got, a, b):
+    ref = torch.bmm(a.double().cpu(), b.double().cpu())
+    return ((got.double().cpu() - ref).abs().max() / ref.abs().max()).item()
+
+
+# (nb, m, k, n, B transposed)
+SHAPES = [(1, 1024, 512, 1024, True), (2, 1536, 260, 1100, False), (1, 1024, 9000, 1024, True),
+          (3, 768, 100, 2000, True), (1, 4096, 64, 4096, False)]
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=["x".join(map(str, s[:4])) + ("t" if s[4] else "") for s in SHAPES])
+def test_split_operands_match_the_converter_path(cuda_device, shape):
+    nb, m, k, n, bt = shape
+    g = torch.Generator().manual_seed(m + k + n)
+    a = torch.randn(nb, m, k, generator=g)
+    b = torch.randn(nb, n, k, generator=g).transpose(1, 2) if bt else torch.randn(nb, k, n, generator=g)
+    ad, bd = a.to(cuda_device), b.to(cuda_device)
+    assert _ws_size(ad, bd) > 0
+    got = cmpext3.ops.bmm(ad, bd)
+    plain = _no_workspace(ad, bd)
+    torch.cuda.synchronize()
+    assert torch.equal(got, plain)
+    check(got, RP.bmm(a, b), torch.float32, f"split fp32 bmm {shape}", attention=False)
+    assert _rel64(got, a, b) <= 5e-5
+    assert N.device_status() == 0
+
+
+@pytest.mark.parametrize("where", ["A", "B"])
+def test_special_values_with_split_operands(cuda_device, where):
+    g = torch.Generator().manual_seed(11)
+    a = torch.randn(1, 1024, 256, generator=g)
+    b = torch.randn(1, 256, 1024, generator=g)
+    low_nan = torch.tensor([0x7F800001], dtype=torch.int32).view(torch.float32)[0]
+    if where == "A":
+        a[0, 3, 10] = float("inf")
+        a[0, 5, 11] = float("nan")
+        a[0, 7, 20] = low_nan  # read as inf through TF32: the GEMM must fall back and rewrite it
+    else:
+        b[0, 10, 3] = float("inf")
+        b[0, 11, 5] = float("nan")
+        b[0, 20, 7] = low_nan
+    ad, bd = a.to(cuda_device), b.to(cuda_device)
+    got = cmpext3.ops.bmm(ad, bd)
+    plain = _no_workspace(ad, bd)
+    torch.cuda.synchronize()
+    assert torch.equal(got.isnan(), plain.isnan())
+    assert torch.equal(torch.nan_to_num(got), torch.nan_to_num(plain))
+    nan_line = got[0, 7] if where == "A" else got[0, :, 7]
+    assert torch.isnan(nan_line).all()
+    # without the low-payload NaN the split path runs, with the same results
+    if where == "A":
+        a[0, 7, 20] = 0.0
+    else:
+        b[0, 20, 7] = 0.0
+    ad, bd = a.to(cuda_device), b.to(cuda_device)
+    got = cmpext3.ops.bmm(ad, bd)
+    plain = _no_workspace(ad, bd)
+    torch.cuda.synchronize()
+    assert torch.equal(torch.nan_to_num(got), torch.nan_to_num(plain))
+    assert torch.equal(got.isnan(), plain.isnan()) and torch.equal(got.isinf(), plain.isinf())
+
+
+def test_split_leaves_the_first_256_workspace_bytes_alone(cuda_device):
+    g = torch.Generator().manual_seed(12)
+    a = torch.randn(1, 1024, 128, generator=g).to(cuda_device)
+    b = torch.randn(1, 128, 1024, generator=g).to(cuda_device)
+    a2, b2, c = N._prepare_bmm(a, b)
+    desc = N._bmm_desc(a2, b2, c)
+    need = N.lib.cmpx_bmm_workspace_size(ctypes.byref(desc))
+    assert need > 0
+    ws = torch.zeros(need, dtype=torch.uint8, device=cuda_device)
+    ws[:256] = torch.arange(256, dtype=torch.uint8, device=cuda_device)
+    st = N.lib.cmpx_bmm_ws(ctypes.byref(desc), ws.data_ptr(), ws.numel(), N._stream_handle(a.device))
+    assert st == 0
+    torch.cuda.synchronize()
+    assert torch.equal(ws[:256].cpu(), torch.arange(256, dtype=torch.uint8))
+    assert torch.equal(c, _no_workspace(a, b))
+    # a workspace one byte short runs the converter path: same result
+    c2 = torch.empty_like(c)
+    desc2 = N._bmm_desc(a2, b2, c2)
+    st = N.lib.cmpx_bmm_ws(ctypes.byref(desc2), ws.data_ptr(), need - 1, N._stream_handle(a.device))
+    assert st == 0
+    torch.cuda.synchronize()
+    assert torch.equal(c2, c)
+
+
+@pytest.mark.parametrize("bias", [True, False], ids=["bias", "nobias"])
+def test_fp32_linear_split_operands(cuda_device, bias):
+    g = torch.Generator().manual_seed(13)
+    x = torch.randn(2048, 1024, generator=g)
+    w = torch.randn(1536, 1024, generator=g)
+    bb = torch.randn(1536, generator=g) if bias else None
+    xd, wd = x.to(cuda_device), w.to(cuda_device)
+    bd = bb.to(cuda_device) if bias else None
+    x2, w2, b2, y = N._prepare_linear(xd, wd, bd)
+    desc = N._linear_desc(x2, w2, b2, y)
+    assert N.lib.cmpx_linear_workspace_size(ctypes.byref(desc)) > 0
+    got = cmpext3.ops.linear(xd, wd, bd)
+    st = N.lib.cmpx_linear(ctypes.byref(desc), N._stream_handle(xd.device))  # no workspace, into y
+    assert st == 0
+    torch.cuda.synchronize()
+    assert torch.equal(got, y)
+    ref = torch.nn.functional.linear(x.double(), w.double(), bb.double() if bias else None)
+    assert ((got.double().cpu() - ref).abs().max() / ref.abs().max()).item() <= 5e-5

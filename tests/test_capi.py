@@ -42,7 +42,7 @@ def test_library_exports_nothing_undeclared():
 
 
 def test_abi_version_and_status_strings():
-    assert N.lib.cmpx_abi_version() == 6
+    assert N.lib.cmpx_abi_version() == 7
     header = HEADER.read_text()
     m = re.search(r"#define CMPX_ABI_VERSION (\d+)", header)
     assert m and int(m.group(1)) == N.ABI_VERSION == N.lib.cmpx_abi_version()
@@ -261,6 +261,46 @@ def test_bmm_tile_width(shape, width):
     nb, m, n, k = shape  # 128x256 only for wide N with K >= 512 (compute-bound); 128x128 / 128x64 else
     st, name = _bplan(_bmm(nb, m, n, k, bt=True))
     assert st == 0 and width in name, name
+
+
+def _x3_ws(nb, m, n, k):
+    """The fp32 split-operand workspace: 512 bytes (256 left alone, a 16-byte flag at 256), then
+    lo(A) [nb][m][k4] and lo(B) [nb][n][k4] fp32, each rounded up to 256 bytes (k4 = k rounded to 4)."""
+    k4 = (k + 3) // 4 * 4
+    up = lambda x: (x + 255) // 256 * 256  # noqa: E731
+    return 512 + up(nb * m * k4 * 4) + up(nb * n * k4 * 4)
+
+
+@pytest.mark.parametrize("shape,split", [((1, 4096, 4096, 4096), True), ((8, 2048, 2048, 2048), True),
+                                         ((64, 2048, 2048, 64), True), ((2, 1024, 1024, 20000), True),
+                                         ((4, 512, 512, 64), False), ((1, 8192, 256, 4096), False),
+                                         ((16, 128, 128, 128), False)])
+def test_fp32_bmm_workspace_size(shape, split):
+    # split operands when m n / (m + n) >= 512 per item: every operand tile feeds enough outputs
+    nb, m, n, k = shape
+    d = _bmm(nb, m, n, k, dtype=0, bt=True)
+    assert _bplan(d)[0] == 0
+    assert N.lib.cmpx_bmm_workspace_size(ctypes.byref(d)) == (_x3_ws(nb, m, n, k) if split else 0)
+
+
+def test_bmm_workspace_size_is_zero_for_16bit_and_rejected_calls():
+    assert N.lib.cmpx_bmm_workspace_size(ctypes.byref(_bmm(1, 4096, 4096, 4096, dtype=2, bt=True))) == 0
+    assert N.lib.cmpx_bmm_workspace_size(ctypes.byref(_bmm(2, 4096, 4096, 30, dtype=0, bt=True))) == 0  # misaligned
+    assert N.lib.cmpx_bmm_workspace_size(None) == 0
+
+
+def test_linear_workspace_size():
+    d = _linear(m=8192, n=4096, k=4096, dtype=0)
+    assert N.lib.cmpx_linear_workspace_size(ctypes.byref(d)) == _x3_ws(1, 8192, 4096, 4096)
+    assert N.lib.cmpx_linear_workspace_size(ctypes.byref(_linear(m=8192, n=4096, k=4096, dtype=2))) == 0
+    assert N.lib.cmpx_linear_workspace_size(ctypes.byref(_linear(m=64, n=128, k=256, dtype=0))) == 0
+
+
+def test_workspace_entry_points_validate_before_launch():
+    # the same plan checks as cmpx_bmm / cmpx_linear, before any device work
+    assert N.lib.cmpx_bmm_ws(ctypes.byref(_bmm(2, 256, 256, 0, dtype=0, bt=True)), None, 0, None) == \
+        N.ERR_UNSUPPORTED_SHAPE
+    assert N.lib.cmpx_linear_ws(ctypes.byref(_linear(k=100)), None, 0, None) == N.ERR_MISALIGNED
 
 
 def _linear(m=64, n=128, k=256, dtype=2, bias=True, ptr=0x10000, ldx=None, ldw=None, ldy=None):

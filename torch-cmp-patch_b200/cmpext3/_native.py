@@ -94,7 +94,7 @@ class SoftmaxDesc(ctypes.Structure):
 
 
 # CMPX_ABI_VERSION of include/cmpx_b200.h that the ctypes structures above mirror.
-ABI_VERSION = 6
+ABI_VERSION = 7
 
 
 def _load() -> ctypes.CDLL:
@@ -120,6 +120,14 @@ def _load() -> ctypes.CDLL:
     L.cmpx_bmm_small_plan.argtypes = [ctypes.POINTER(BmmDesc), ctypes.c_char_p, ctypes.c_size_t]
     L.cmpx_bmm_small_plan.restype = ctypes.c_int
     L.cmpx_linear.argtypes = [ctypes.POINTER(LinearDesc), ctypes.c_void_p]
+    L.cmpx_bmm_workspace_size.restype = ctypes.c_size_t
+    L.cmpx_bmm_workspace_size.argtypes = [ctypes.POINTER(BmmDesc)]
+    L.cmpx_bmm_ws.restype = ctypes.c_int
+    L.cmpx_bmm_ws.argtypes = [ctypes.POINTER(BmmDesc), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    L.cmpx_linear_workspace_size.restype = ctypes.c_size_t
+    L.cmpx_linear_workspace_size.argtypes = [ctypes.POINTER(LinearDesc)]
+    L.cmpx_linear_ws.restype = ctypes.c_int
+    L.cmpx_linear_ws.argtypes = [ctypes.POINTER(LinearDesc), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
     L.cmpx_linear.restype = ctypes.c_int
     L.cmpx_linear_plan.argtypes = [ctypes.POINTER(LinearDesc), ctypes.c_char_p, ctypes.c_size_t]
     L.cmpx_linear_plan.restype = ctypes.c_int
@@ -473,7 +481,14 @@ def bmm(input, mat2):
         return c.zero_()
     desc = _bmm_desc(a, b, c)
     with torch.cuda.device(a.device):
-        st = lib.cmpx_bmm(ctypes.byref(desc), _stream_handle(a.device))
+        stream = _stream_handle(a.device)
+        # fp32: the split-operand schedule when the product is large enough (same results)
+        nbytes = lib.cmpx_bmm_workspace_size(ctypes.byref(desc))
+        if nbytes:
+            ws = _workspace(a.device, stream, nbytes)
+            st = lib.cmpx_bmm_ws(ctypes.byref(desc), ws.data_ptr(), ws.numel(), stream)
+        else:
+            st = lib.cmpx_bmm(ctypes.byref(desc), stream)
     if st != OK:
         raise CmpxError("bmm", st)
     _post_check()
@@ -588,11 +603,19 @@ def linear(input, weight, bias=None):
         return (y.zero_() if b is None else y.copy_(b.expand_as(y))).contiguous().view(out_shape)
     desc = _linear_desc(x, w, b, y)
     dev = x.device
+
+    def run():
+        stream = _stream_handle(dev)
+        nbytes = lib.cmpx_linear_workspace_size(ctypes.byref(desc))  # fp32 split operands (same results)
+        if nbytes:
+            ws = _workspace(dev, stream, nbytes)
+            return lib.cmpx_linear_ws(ctypes.byref(desc), ws.data_ptr(), ws.numel(), stream)
+        return lib.cmpx_linear(ctypes.byref(desc), stream)
     if dev.index == torch.cuda.current_device():
-        st = lib.cmpx_linear(ctypes.byref(desc), _stream_handle(dev))
+        st = run()
     else:
         with torch.cuda.device(dev):
-            st = lib.cmpx_linear(ctypes.byref(desc), _stream_handle(dev))
+            st = run()
     if st != OK:
         raise CmpxError("linear", st)
     _post_check()

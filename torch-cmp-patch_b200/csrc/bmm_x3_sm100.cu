@@ -74,6 +74,12 @@ struct X3GemmParams {
   int tiles_m, tiles_n, n_tiles;
   const float* bias;  // [n] added to every row (linear), or null
   int accumulate;     // 1: add the product into C (a later K chunk), 0: store it
+  // Split operands (pre = 1): the lo parts of A and B were written once per call by x3_lo_kernel
+  // and are loaded by TMA beside the operands, so the converter warps have nothing to do; unless
+  // that pass raised *special (a NaN the tensor core would read as inf), in which case the
+  // converter path runs (it rewrites such words in shared memory).
+  int pre;
+  const unsigned int* special;
   unsigned long long timeout_ns;
   unsigned int* dev_flags;
 };
@@ -87,10 +93,54 @@ __device__ __forceinline__ uint32_t x3_lo(uint32_t bits) {
 __device__ __forceinline__ uint32_t x3_hi_special(uint32_t bits) {
   return x3_special(bits) && (bits & 0x007FFFFFu) ? 0x7FC00000u : bits;
 }
+// A NaN whose payload sits only in the 13 bits TF32 drops: the tensor core would read it as inf.
+__device__ __forceinline__ bool x3_nan_low(uint32_t bits) {
+  return x3_special(bits) && (bits & 0x007FFFFFu) != 0u && (bits & 0x007FE000u) == 0u;
+}
+
+// The lo parts of one K-major operand, once per call: x is `batch` items of `rows` rows of k
+// elements (row_stride / batch_stride elements apart, contiguous along k, 16-byte aligned rows);
+// lo is [batch][rows][k_pad] packed, x3_lo of each element and zero past k.  The hi part is the
+// operand itself, as the converter path uses it.  A block walks whole rows, a thread one float4.
+struct X3LoParams {
+  const float* x;
+  long long batch_stride, row_stride;
+  int rows, k, k_pad, batch;
+  float* lo;
+  unsigned int* special;
+};
+
+__global__ void __launch_bounds__(256) x3_lo_kernel(const X3LoParams p) {
+  const int quads = p.k_pad >> 2;
+  const long long n_rows = static_cast<long long>(p.batch) * p.rows;
+  bool bad = false;
+  for (long long rr = blockIdx.x; rr < n_rows; rr += gridDim.x) {
+    const long long z = rr / p.rows, r = rr - z * p.rows;
+    const float* src = p.x + z * p.batch_stride + r * p.row_stride;
+    float4* dst = reinterpret_cast<float4*>(p.lo + rr * p.k_pad);
+    for (int q = threadIdx.x; q < quads; q += blockDim.x) {
+      const int k0 = q * 4;
+      uint32_t w[4];
+      if (k0 + 4 <= p.k) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(src + k0));
+        w[0] = __float_as_uint(v.x); w[1] = __float_as_uint(v.y); w[2] = __float_as_uint(v.z); w[3] = __float_as_uint(v.w);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) w[e] = k0 + e < p.k ? __float_as_uint(__ldg(src + k0 + e)) : 0u;
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) bad |= x3_nan_low(w[e]);
+      dst[q] = make_float4(__uint_as_float(x3_lo(w[0])), __uint_as_float(x3_lo(w[1])), __uint_as_float(x3_lo(w[2])),
+                           __uint_as_float(x3_lo(w[3])));
+    }
+  }
+  if (bad) atomicOr(p.special, 1u);
+}
 
 __global__ void __launch_bounds__(576, 1)
     bmm_x3_sm100_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                        const __grid_constant__ CUtensorMap tm_c, const X3GemmParams p) {
+                        const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_alo,
+                        const __grid_constant__ CUtensorMap tm_blo, const X3GemmParams p) {
   using C = X3GemmCfg;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
@@ -136,10 +186,15 @@ __global__ void __launch_bounds__(576, 1)
     tmem_alloc(smem_u32(tmem_holder), C::TMEM_COLS);
     tmem_relinquish();
   }
+  const bool pre = p.pre != 0 && p.special[0] == 0u;  // (written by the previous kernel on this stream)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_a);
     tma_prefetch_desc(&tm_b);
     tma_prefetch_desc(&tm_c);
+    if (pre) {
+      tma_prefetch_desc(&tm_alo);
+      tma_prefetch_desc(&tm_blo);
+    }
   }
   tc_fence_before_sync();
   __syncthreads();
@@ -159,9 +214,13 @@ __global__ void __launch_bounds__(576, 1)
           const int st = it % C::STAGES;
           if (!(ok = mbar_wait(bar(C::B_EMPTY + st), (static_cast<uint32_t>(it / C::STAGES) & 1u) ^ 1u, ctl))) break;
           const uint32_t s = stage(it);
-          mbar_arrive_expect_tx(bar(C::B_FULL + st), 2 * C::TILE);
+          mbar_arrive_expect_tx(bar(C::B_FULL + st), (pre ? 4 : 2) * C::TILE);
           tma_load_3d(s + C::A_HI, &tm_a, bar(C::B_FULL + st), kb * C::BK, m0, z);
           tma_load_3d(s + C::B_HI, &tm_b, bar(C::B_FULL + st), kb * C::BK, n0, z);
+          if (pre) {
+            tma_load_3d(s + C::A_LO, &tm_alo, bar(C::B_FULL + st), kb * C::BK, m0, z);
+            tma_load_3d(s + C::B_LO, &tm_blo, bar(C::B_FULL + st), kb * C::BK, n0, z);
+          }
         }
       }
       if (*abort_flag) {
@@ -183,7 +242,9 @@ __global__ void __launch_bounds__(576, 1)
       const uint32_t d_main = tmem + b * 2 * C::BN, d_cross = d_main + C::BN;
       for (int kb = 0; kb < p.n_kblocks; ++kb, ++it) {
         const int st = it % C::STAGES;
-        if (!(ok = mbar_wait_all(bar(C::B_CONV + st), static_cast<uint32_t>(it / C::STAGES) & 1u, ctl))) break;
+        if (!(ok = mbar_wait_all(bar((pre ? C::B_FULL : C::B_CONV) + st), static_cast<uint32_t>(it / C::STAGES) & 1u,
+                                 ctl)))
+          break;
         tc_fence_after_sync();
         const uint32_t s = stage(it);
         const uint64_t dah = smem_desc_sw128(s + C::A_HI, 16, 1024);
@@ -209,7 +270,7 @@ __global__ void __launch_bounds__(576, 1)
     const int tid = threadIdx.x - 64;
     int it = 0;
     bool ok = true;
-    for (int t = blockIdx.x; ok && t < p.n_tiles; t += gridDim.x) {
+    for (int t = blockIdx.x; ok && !pre && t < p.n_tiles; t += gridDim.x) {  // (split operands: idle)
       for (int kb = 0; kb < p.n_kblocks; ++kb, ++it) {
         const int st = it % C::STAGES;
         if (!(ok = mbar_wait_all(bar(C::B_FULL + st), static_cast<uint32_t>(it / C::STAGES) & 1u, ctl))) break;
@@ -322,6 +383,31 @@ inline uint64_t unit_stride(int64_t s, int64_t extent, int64_t fallback_elems) {
 constexpr const char* kX3Name = "bmm_x3tf32_sm100<f32,128x128x32,3st,persistent>";
 constexpr const char* kX3ChunkName = "bmm_x3tf32_sm100<f32,128x128x32,3st,persistent+k-chunks>";
 
+// Workspace of the split-operand schedule: bytes [0, 256) are left as they are (the attention
+// calls' zero-kept counters, so one workspace serves both), the pass's special-value flag at 256,
+// lo(A) from 512, lo(B) after it, each [batch][rows][k_pad] fp32 with k_pad = k rounded up to 4.
+struct X3Ws {
+  size_t bytes = 0, off_alo = 0, off_blo = 0;
+  int64_t k_pad = 0;
+};
+
+inline size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+// Split operands pay when each operand tile is read by enough output tiles: the pass moves every
+// element of A and B three more times (read, lo written, lo read by the GEMM), and on a B200 the
+// converter path costs about 0.75x the split one per product; with m n / (m + n) >= 512 per batch
+// item the saving is at least about three times the pass.
+inline X3Ws x3_ws_layout(const cmpx_bmm_desc* d) {
+  X3Ws w;
+  const double m = static_cast<double>(d->m), n = static_cast<double>(d->n);
+  if (d->m < 1 || d->n < 1 || m * n / (m + n) < 512.0) return w;
+  w.k_pad = (d->k + 3) / 4 * 4;
+  w.off_alo = 512;
+  w.off_blo = w.off_alo + align256(static_cast<size_t>(d->batch) * d->m * w.k_pad * 4);
+  w.bytes = w.off_blo + align256(static_cast<size_t>(d->batch) * d->n * w.k_pad * 4);
+  return w;
+}
+
 }  // namespace
 
 const char* bmm_x3_plan(const cmpx_bmm_desc* d, int* status) {
@@ -356,10 +442,19 @@ const char* bmm_x3_plan(const cmpx_bmm_desc* d, int* status) {
 
 namespace {
 
-int launch_x3_once(const cmpx_bmm_desc* d, const LaunchCtx& ctx, const float* bias, int accumulate) {
+// The split operands of one launch: lo(A) and lo(B) (already offset to the launch's first k) with
+// their row pitch, and the pass's flag; null lo pointers: the converter path.
+struct X3Pre {
+  const float* lo_a = nullptr;
+  const float* lo_b = nullptr;
+  int64_t k_pad = 0;
+  const unsigned int* special = nullptr;
+};
+
+int launch_x3_once(const cmpx_bmm_desc* d, const LaunchCtx& ctx, const float* bias, int accumulate, const X3Pre& pre) {
   using C = X3GemmCfg;
   const uint64_t M = d->m, N = d->n, K = d->k, Z = d->batch;
-  CUtensorMap ta, tb, tc;
+  CUtensorMap ta, tb, tc, talo, tblo;
   {
     const uint64_t dims[3] = {K, M, Z};
     const uint64_t st[2] = {unit_stride(d->a_stride[1], d->m, d->k),
@@ -384,6 +479,18 @@ int launch_x3_once(const cmpx_bmm_desc* d, const LaunchCtx& ctx, const float* bi
     if (!encode_tmap(&tc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, d->c, dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B))
       return CMPX_ERR_LAUNCH;
   }
+  const bool use_pre = pre.lo_a != nullptr;
+  if (use_pre) {
+    const uint32_t box[3] = {32, 128, 1};
+    const uint64_t da[3] = {K, M, Z}, sa[2] = {static_cast<uint64_t>(pre.k_pad) * 4, M * pre.k_pad * 4};
+    const uint64_t db[3] = {K, N, Z}, sb[2] = {static_cast<uint64_t>(pre.k_pad) * 4, N * pre.k_pad * 4};
+    if (!encode_tmap(&talo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, pre.lo_a, da, sa, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap(&tblo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, pre.lo_b, db, sb, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return CMPX_ERR_LAUNCH;
+  } else {
+    talo = ta;  // (not read)
+    tblo = tb;
+  }
   static std::once_flag once[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -405,10 +512,12 @@ int launch_x3_once(const cmpx_bmm_desc* d, const LaunchCtx& ctx, const float* bi
   p.n_tiles = static_cast<int>(n_tiles);
   p.bias = bias;
   p.accumulate = accumulate;
+  p.pre = use_pre ? 1 : 0;
+  p.special = use_pre ? pre.special : ctx.dev_flags;  // (read only when pre = 1)
   p.timeout_ns = ctx.timeout_ns;
   p.dev_flags = ctx.dev_flags;
   const int grid = static_cast<int>(std::min<int64_t>(n_tiles, std::max(1, ctx.num_sms)));
-  bmm_x3_sm100_kernel<<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(ta, tb, tc, p);
+  bmm_x3_sm100_kernel<<<grid, C::THREADS, C::SMEM_BYTES, ctx.stream>>>(ta, tb, tc, talo, tblo, p);
   return cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
 }
 
@@ -416,9 +525,47 @@ int launch_x3_once(const cmpx_bmm_desc* d, const LaunchCtx& ctx, const float* bi
 // chunk on the caller's stream, the first storing C (and adding the bias), the others adding into
 // it.  A and B are K-major, so a chunk is the same operand from element k0 on: its pointers move
 // by k0 elements (16-byte aligned, k0 being a multiple of 32).
-int launch_x3(const cmpx_bmm_desc* d, const LaunchCtx& ctx, const float* bias) {
+int launch_x3_lo(const float* x, long long batch_stride, long long row_stride, int64_t rows, const cmpx_bmm_desc* d,
+                 int64_t k_pad, float* lo, unsigned int* special, const LaunchCtx& ctx) {
+  X3LoParams q;
+  q.x = x;
+  q.batch_stride = batch_stride;
+  q.row_stride = row_stride;
+  q.rows = static_cast<int>(rows);
+  q.k = static_cast<int>(d->k);
+  q.k_pad = static_cast<int>(k_pad);
+  q.batch = static_cast<int>(d->batch);
+  q.lo = lo;
+  q.special = special;
+  const int64_t n_rows = rows * d->batch;
+  const int threads = static_cast<int>(std::min<int64_t>(256, std::max<int64_t>(32, (k_pad / 4 + 31) / 32 * 32)));
+  const int grid = static_cast<int>(std::min<int64_t>(n_rows, std::max(1, ctx.num_sms) * 32));
+  x3_lo_kernel<<<grid, threads, 0, ctx.stream>>>(q);
+  return cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
+}
+
+int launch_x3(const cmpx_bmm_desc* d, const LaunchCtx& ctx, const float* bias, void* ws, size_t ws_bytes) {
   using C = X3GemmCfg;
-  if (d->k <= C::MAX_K) return launch_x3_once(d, ctx, bias, 0);
+  X3Pre pre;
+  const X3Ws lay = x3_ws_layout(d);
+  if (lay.bytes > 0 && ws && ws_bytes >= lay.bytes && (reinterpret_cast<uintptr_t>(ws) & 15u) == 0) {
+    uint8_t* w = static_cast<uint8_t*>(ws);
+    unsigned int* special = reinterpret_cast<unsigned int*>(w + 256);
+    float* lo_a = reinterpret_cast<float*>(w + lay.off_alo);
+    float* lo_b = reinterpret_cast<float*>(w + lay.off_blo);
+    if (cudaMemsetAsync(special, 0, 16, ctx.stream) != cudaSuccess) return CMPX_ERR_LAUNCH;
+    int st = launch_x3_lo(static_cast<const float*>(d->a), d->a_stride[0], d->a_stride[1], d->m, d, lay.k_pad, lo_a,
+                          special, ctx);
+    if (st == CMPX_OK)
+      st = launch_x3_lo(static_cast<const float*>(d->b), d->b_stride[0], d->b_stride[2], d->n, d, lay.k_pad, lo_b,
+                        special, ctx);
+    if (st != CMPX_OK) return st;
+    pre.lo_a = lo_a;
+    pre.lo_b = lo_b;
+    pre.k_pad = lay.k_pad;
+    pre.special = special;
+  }
+  if (d->k <= C::MAX_K) return launch_x3_once(d, ctx, bias, 0, pre);
   const int64_t chunks = (d->k + C::MAX_K - 1) / C::MAX_K;
   const int64_t kc = ((d->k + chunks - 1) / chunks + C::BK - 1) / C::BK * C::BK;
   for (int64_t k0 = 0; k0 < d->k; k0 += kc) {
@@ -426,7 +573,12 @@ int launch_x3(const cmpx_bmm_desc* d, const LaunchCtx& ctx, const float* bias) {
     c.a = static_cast<const float*>(d->a) + k0;
     c.b = static_cast<const float*>(d->b) + k0;
     c.k = std::min<int64_t>(kc, d->k - k0);
-    const int st = launch_x3_once(&c, ctx, k0 == 0 ? bias : nullptr, k0 == 0 ? 0 : 1);
+    X3Pre pc = pre;
+    if (pre.lo_a) {
+      pc.lo_a = pre.lo_a + k0;
+      pc.lo_b = pre.lo_b + k0;
+    }
+    const int st = launch_x3_once(&c, ctx, k0 == 0 ? bias : nullptr, k0 == 0 ? 0 : 1, pc);
     if (st != CMPX_OK) return st;
   }
   return CMPX_OK;
@@ -434,12 +586,19 @@ int launch_x3(const cmpx_bmm_desc* d, const LaunchCtx& ctx, const float* bias) {
 
 }  // namespace
 
-int launch_bmm_x3(const cmpx_bmm_desc* d, const LaunchCtx& ctx) {
+size_t bmm_x3_workspace_bytes(const cmpx_bmm_desc* d) {
+  int st = CMPX_OK;
+  bmm_x3_plan(d, &st);
+  if (st != CMPX_OK || d->batch == 0) return 0;
+  return x3_ws_layout(d).bytes;
+}
+
+int launch_bmm_x3(const cmpx_bmm_desc* d, const LaunchCtx& ctx, void* ws, size_t ws_bytes) {
   int st = CMPX_OK;
   bmm_x3_plan(d, &st);
   if (st != CMPX_OK) return st;
   if (d->m == 0 || d->n == 0 || d->batch == 0) return CMPX_OK;
-  return launch_x3(d, ctx, nullptr);
+  return launch_x3(d, ctx, nullptr, ws, ws_bytes);
 }
 
 const char* linear_x3_plan(const cmpx_linear_desc* d, int* status) {
@@ -457,13 +616,21 @@ const char* linear_x3_plan(const cmpx_linear_desc* d, int* status) {
   return bmm_x3_plan(&b, status);
 }
 
-int launch_linear_x3(const cmpx_linear_desc* d, const LaunchCtx& ctx) {
+size_t linear_x3_workspace_bytes(const cmpx_linear_desc* d) {
+  int st = CMPX_OK;
+  linear_x3_plan(d, &st);
+  if (st != CMPX_OK || d->m == 0) return 0;
+  const cmpx_bmm_desc b = linear_as_bmm(d);
+  return x3_ws_layout(&b).bytes;
+}
+
+int launch_linear_x3(const cmpx_linear_desc* d, const LaunchCtx& ctx, void* ws, size_t ws_bytes) {
   int st = CMPX_OK;
   linear_x3_plan(d, &st);
   if (st != CMPX_OK) return st;
   if (d->m == 0) return CMPX_OK;
   const cmpx_bmm_desc b = linear_as_bmm(d);
-  return launch_x3(&b, ctx, static_cast<const float*>(d->bias));
+  return launch_x3(&b, ctx, static_cast<const float*>(d->bias), ws, ws_bytes);
 }
 
 }  // namespace cmpx

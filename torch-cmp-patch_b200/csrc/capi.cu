@@ -309,6 +309,40 @@ int cmpx_bmm(const cmpx_bmm_desc* desc, void* stream) {
   return launch_bmm_sm100(desc, ctx);
 }
 
+size_t cmpx_bmm_workspace_size(const cmpx_bmm_desc* desc) {
+  if (!desc || desc->dtype != CMPX_F32) return 0;
+  return bmm_x3_workspace_bytes(desc);
+}
+
+int cmpx_bmm_ws(const cmpx_bmm_desc* desc, void* workspace, size_t workspace_bytes, void* stream) {
+  int st = CMPX_OK;
+  bmm_plan_impl(desc, &st);
+  if (st != CMPX_OK) return st;
+  if (desc->batch == 0 || desc->m == 0 || desc->n == 0) return CMPX_OK;
+  LaunchCtx ctx;
+  st = device_ctx(&ctx, static_cast<cudaStream_t>(stream));
+  if (st != CMPX_OK) return st;
+  if (desc->dtype == CMPX_F32) return launch_bmm_x3(desc, ctx, workspace, workspace_bytes);
+  return launch_bmm_sm100(desc, ctx);
+}
+
+size_t cmpx_linear_workspace_size(const cmpx_linear_desc* desc) {
+  if (!desc || desc->dtype != CMPX_F32) return 0;
+  return linear_x3_workspace_bytes(desc);
+}
+
+int cmpx_linear_ws(const cmpx_linear_desc* desc, void* workspace, size_t workspace_bytes, void* stream) {
+  int st = CMPX_OK;
+  linear_plan_impl(desc, &st);
+  if (st != CMPX_OK) return st;
+  if (desc->m == 0) return CMPX_OK;
+  LaunchCtx ctx;
+  st = device_ctx(&ctx, static_cast<cudaStream_t>(stream));
+  if (st != CMPX_OK) return st;
+  if (desc->dtype == CMPX_F32) return launch_linear_x3(desc, ctx, workspace, workspace_bytes);
+  return launch_linear_sm100(desc, ctx);
+}
+
 int cmpx_bmm_small(const cmpx_bmm_desc* desc, void* stream) {
   int st = CMPX_OK;
   bmm_small_plan(desc, &st);

@@ -70,7 +70,9 @@ const char* bmm_sm100_plan(const cmpx_bmm_desc* d, int* status);
 int launch_bmm_sm100(const cmpx_bmm_desc* d, const LaunchCtx& ctx);
 // fp32 on the tensor cores (3xTF32), K-major operands.
 const char* bmm_x3_plan(const cmpx_bmm_desc* d, int* status);
-int launch_bmm_x3(const cmpx_bmm_desc* d, const LaunchCtx& ctx);
+// ws: the split-operand workspace (bmm_x3_workspace_bytes); null or smaller: the converter path.
+int launch_bmm_x3(const cmpx_bmm_desc* d, const LaunchCtx& ctx, void* ws = nullptr, size_t ws_bytes = 0);
+size_t bmm_x3_workspace_bytes(const cmpx_bmm_desc* d);
 // Many tiny products (the reference's M*K*N <= 32768 route): one thread or warp per output element.
 const char* bmm_small_plan(const cmpx_bmm_desc* d, int* status);
 int launch_bmm_small(const cmpx_bmm_desc* d, const LaunchCtx& ctx);
@@ -82,7 +84,8 @@ cmpx_bmm_desc linear_as_bmm(const cmpx_linear_desc* d);
 const char* linear_sm100_plan(const cmpx_linear_desc* d, int* status);
 int launch_linear_sm100(const cmpx_linear_desc* d, const LaunchCtx& ctx);
 const char* linear_x3_plan(const cmpx_linear_desc* d, int* status);
-int launch_linear_x3(const cmpx_linear_desc* d, const LaunchCtx& ctx);
+int launch_linear_x3(const cmpx_linear_desc* d, const LaunchCtx& ctx, void* ws = nullptr, size_t ws_bytes = 0);
+size_t linear_x3_workspace_bytes(const cmpx_linear_desc* d);
 
 // ---- row softmax (einsum-attention chain) ----
 const char* softmax_rows_plan(const cmpx_softmax_desc* d, int* status);
