@@ -221,7 +221,8 @@ CMPX_API int cmpx_linear(const cmpx_linear_desc* desc, void* stream);
  * (x - x truncated to TF32) of A and B, or of x and W, into the workspace once per call, and the
  * GEMM loads them beside the operands instead of splitting every shared-memory tile again (the
  * split's shared-memory traffic is what bounds the GEMM: 4096^3 measured 1.0 -> 0.6 ms).  The size
- * is 0 when the product is too small for the pass to pay, and for fp16 / bf16 (which need none).
+ * is 0 when the pass does not pay (m n / (m + n) < 512 per batch item, or k < 512), and for
+ * fp16 / bf16 (which need none).
  * The results are the same as without a workspace, bit for bit.  Bytes [0, 256) of the workspace
  * are neither read nor written, so the workspace of the attention calls (whose first 256 bytes
  * must stay zero) can be passed as it is; the rest is scratch, written before it is read.  Calls

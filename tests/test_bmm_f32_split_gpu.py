@@ -1,6 +1,6 @@
 """fp32 bmm / linear with split operands (needs a B200; marked gpu).
 
-For products large enough to pay (m n / (m + n) >= 512 per batch item) the binding passes a
+For products large enough to pay (m n / (m + n) >= 512 per batch item, k >= 512) the binding passes a
 workspace to cmpx_bmm_ws / cmpx_linear_ws: a pass writes the low TF32 parts of A and B once per call
 and the GEMM loads them beside the operands.  Checked here: the result bit for bit against the same
 product without a workspace (the converter path, which splits every shared-memory tile), against
@@ -43,8 +43,8 @@ def _rel64(got, a, b):
 
 
 # (nb, m, k, n, B transposed)
-SHAPES = [(1, 1024, 512, 1024, True), (2, 1536, 260, 1100, False), (1, 1024, 9000, 1024, True),
-          (3, 768, 100, 2000, True), (1, 4096, 64, 4096, False)]
+SHAPES = [(1, 1024, 512, 1024, True), (2, 1536, 520, 1100, False), (1, 1024, 9000, 1024, True),
+          (3, 768, 600, 2000, True), (1, 2048, 516, 2048, False)]
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=["x".join(map(str, s[:4])) + ("t" if s[4] else "") for s in SHAPES])
@@ -67,8 +67,8 @@ def test_split_operands_match_the_converter_path(cuda_device, shape):
 @pytest.mark.parametrize("where", ["A", "B"])
 def test_special_values_with_split_operands(cuda_device, where):
     g = torch.Generator().manual_seed(11)
-    a = torch.randn(1, 1024, 256, generator=g)
-    b = torch.randn(1, 256, 1024, generator=g)
+    a = torch.randn(1, 1024, 512, generator=g)
+    b = torch.randn(1, 512, 1024, generator=g)
     low_nan = torch.tensor([0x7F800001], dtype=torch.int32).view(torch.float32)[0]
     if where == "A":
         a[0, 3, 10] = float("inf")
@@ -101,8 +101,8 @@ def test_special_values_with_split_operands(cuda_device, where):
 
 def test_split_leaves_the_first_256_workspace_bytes_alone(cuda_device):
     g = torch.Generator().manual_seed(12)
-    a = torch.randn(1, 1024, 128, generator=g).to(cuda_device)
-    b = torch.randn(1, 128, 1024, generator=g).to(cuda_device)
+    a = torch.randn(1, 1024, 512, generator=g).to(cuda_device)
+    b = torch.randn(1, 512, 1024, generator=g).to(cuda_device)
     a2, b2, c = N._prepare_bmm(a, b)
     desc = N._bmm_desc(a2, b2, c)
     need = N.lib.cmpx_bmm_workspace_size(ctypes.byref(desc))
@@ -141,3 +141,14 @@ def test_fp32_linear_split_operands(cuda_device, bias):
     assert torch.equal(got, y)
     ref = torch.nn.functional.linear(x.double(), w.double(), bb.double() if bias else None)
     assert ((got.double().cpu() - ref).abs().max() / ref.abs().max()).item() <= 5e-5
+
+
+def test_released_workspaces_are_allocated_again(cuda_device):
+    a = torch.randn(1, 1024, 512, device=cuda_device)
+    b = torch.randn(1, 512, 1024, device=cuda_device)
+    first = cmpext3.ops.bmm(a, b)
+    N.release_workspaces()
+    assert not N._WORKSPACES
+    again = cmpext3.ops.bmm(a, b)
+    torch.cuda.synchronize()
+    assert torch.equal(first, again) and N._WORKSPACES

@@ -272,11 +272,13 @@ def _x3_ws(nb, m, n, k):
 
 
 @pytest.mark.parametrize("shape,split", [((1, 4096, 4096, 4096), True), ((8, 2048, 2048, 2048), True),
-                                         ((64, 2048, 2048, 64), True), ((2, 1024, 1024, 20000), True),
-                                         ((4, 512, 512, 64), False), ((1, 8192, 256, 4096), False),
+                                         ((1, 1024, 1024, 512), True), ((2, 1024, 1024, 20000), True),
+                                         ((64, 2048, 2048, 64), False), ((4, 1024, 1024, 256), False),
+                                         ((4, 512, 512, 1024), False), ((1, 8192, 256, 4096), False),
                                          ((16, 128, 128, 128), False)])
 def test_fp32_bmm_workspace_size(shape, split):
-    # split operands when m n / (m + n) >= 512 per item: every operand tile feeds enough outputs
+    # split operands when m n / (m + n) >= 512 per item (every operand tile feeds enough outputs)
+    # and k >= 512 (enough K blocks per tile for the converter to be what bounds it)
     nb, m, n, k = shape
     d = _bmm(nb, m, n, k, dtype=0, bt=True)
     assert _bplan(d)[0] == 0

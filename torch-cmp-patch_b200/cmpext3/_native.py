@@ -338,6 +338,12 @@ def _prepare_attention(query, key, value, scale, causal):
 _WORKSPACES: dict = {}
 
 
+def release_workspaces() -> None:
+    """Drop the cached per-stream workspaces (they grow to the largest call seen: an fp32 GEMM's
+    split operands take 4 (m + n) k bytes per batch item).  The next call allocates afresh."""
+    _WORKSPACES.clear()
+
+
 def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
     key = (device.index, stream)
     ws = _WORKSPACES.get(key)

@@ -393,14 +393,16 @@ struct X3Ws {
 
 inline size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
-// Split operands pay when each operand tile is read by enough output tiles: the pass moves every
-// element of A and B three more times (read, lo written, lo read by the GEMM), and on a B200 the
-// converter path costs about 0.75x the split one per product; with m n / (m + n) >= 512 per batch
-// item the saving is at least about three times the pass.
+// Split operands pay when each operand tile is read by enough output tiles and the product is long
+// enough for the converter's shared-memory traffic to be what bounds a tile: the pass moves every
+// element of A and B three more times (read, lo written, lo read by the GEMM).  Measured on a B200
+// (converter -> split, TFLOP/s): 1024^3 48 -> 63, 16384 x 1024 x 1024 135 -> 195, 4096^3 136 -> 226;
+// but 4 x 1024 x 256 x 1024 83 -> 70 and 64 x 2048 x 64 x 2048 121 -> 112 (a few K blocks per tile:
+// the epilogue, not the converter, sets the pace).  Hence m n / (m + n) >= 512 and k >= 512.
 inline X3Ws x3_ws_layout(const cmpx_bmm_desc* d) {
   X3Ws w;
   const double m = static_cast<double>(d->m), n = static_cast<double>(d->n);
-  if (d->m < 1 || d->n < 1 || m * n / (m + n) < 512.0) return w;
+  if (d->m < 1 || d->n < 1 || d->k < 512 || m * n / (m + n) < 512.0) return w;
   w.k_pad = (d->k + 3) / 4 * 4;
   w.off_alo = 512;
   w.off_blo = w.off_alo + align256(static_cast<size_t>(d->batch) * d->m * w.k_pad * 4);
