@@ -152,3 +152,26 @@ def test_released_workspaces_are_allocated_again(cuda_device):
     again = cmpext3.ops.bmm(a, b)
     torch.cuda.synchronize()
     assert torch.equal(first, again) and N._WORKSPACES
+
+
+def test_split_operands_in_a_graph(cuda_device):
+    # the pass, the flag's memset and the GEMM are all captured; the workspace of the capture
+    # stream is allocated by the warm-up call on that stream, before the capture
+    g = torch.Generator(device=cuda_device).manual_seed(14)
+    a = torch.randn(2, 1024, 512, device=cuda_device, generator=g)
+    b = torch.randn(2, 512, 1024, device=cuda_device, generator=g)
+    assert _ws_size(a, b) > 0
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        cmpext3.ops.bmm(a, b)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        out = cmpext3.ops.bmm(a, b)
+    for trial in range(2):
+        a.copy_(torch.randn(a.shape, device=cuda_device, generator=g))
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, _no_workspace(a, b)), trial
+    del graph
