@@ -223,7 +223,10 @@ CMPX_API int cmpx_linear(const cmpx_linear_desc* desc, void* stream);
  * split's shared-memory traffic is what bounds the GEMM: 4096^3 measured 1.0 -> 0.6 ms).  The size
  * is 0 when the pass does not pay (m n / (m + n) < 512 per batch item, or k < 512), and for
  * fp16 / bf16 (which need none).
- * The results are the same as without a workspace, bit for bit.  Bytes [0, 256) of the workspace
+ * The results are the same as without a workspace, bit for bit.  cmpx_bmm_ws also takes an fp32 B
+ * stored MN-major (a row-major [k, n] matrix: b_stride[2] == 1, rows 16-byte aligned), which
+ * cmpx_bmm declines: the pass then writes B's hi and lo parts K-major into the workspace
+ * (cmpx_bmm_workspace_size counts them), so no transposed copy of B is needed.  Bytes [0, 256) of the workspace
  * are neither read nor written, so the workspace of the attention calls (whose first 256 bytes
  * must stay zero) can be passed as it is; the rest is scratch, written before it is read.  Calls
  * that share a workspace must not overlap on the GPU.  A smaller or NULL workspace runs the

@@ -175,3 +175,29 @@ def test_split_operands_in_a_graph(cuda_device):
         torch.cuda.synchronize()
         assert torch.equal(out, _no_workspace(a, b)), trial
     del graph
+
+
+def test_mn_major_b_through_the_workspace(cuda_device):
+    # a row-major [k, n] B goes to cmpx_bmm_ws as it is: the pass transposes it into the workspace
+    g = torch.Generator().manual_seed(15)
+    a = torch.randn(2, 1024, 1000, generator=g).to(cuda_device)
+    b = torch.randn(2, 1000, 1028, generator=g).to(cuda_device)
+    a2, b2, c = N._prepare_bmm(a, b, keep_mn_b=True)
+    assert b2.data_ptr() == b.data_ptr() and b2.stride(2) == 1  # not copied
+    desc = N._bmm_desc(a2, b2, c)
+    need = N.lib.cmpx_bmm_workspace_size(ctypes.byref(desc))
+    assert need > 0
+    ws = torch.empty(need, dtype=torch.uint8, device=cuda_device)
+    st = N.lib.cmpx_bmm_ws(ctypes.byref(desc), ws.data_ptr(), ws.numel(), N._stream_handle(a.device))
+    assert st == 0, N.lib.cmpx_status_str(st)
+    plain = _no_workspace(a, b)
+    torch.cuda.synchronize()
+    assert torch.equal(c, plain)
+    assert torch.equal(cmpext3.ops.bmm(a, b), plain)
+    # a low-payload NaN in B: the flag sends the GEMM to the converter path over the copy of B
+    b[1, 7, 3] = torch.tensor([0x7F800001], dtype=torch.int32, device=cuda_device).view(torch.float32)[0]
+    got = cmpext3.ops.bmm(a, b)
+    plain = _no_workspace(a, b)
+    torch.cuda.synchronize()
+    assert torch.isnan(got[1, :, 3]).all()
+    assert torch.equal(torch.nan_to_num(got), torch.nan_to_num(plain))

@@ -285,6 +285,19 @@ def test_fp32_bmm_workspace_size(shape, split):
     assert N.lib.cmpx_bmm_workspace_size(ctypes.byref(d)) == (_x3_ws(nb, m, n, k) if split else 0)
 
 
+def test_fp32_mn_major_b_is_served_through_the_workspace():
+    # cmpx_bmm declines an MN-major fp32 B; with a workspace the pass writes B K-major (hi and lo)
+    nb, m, n, k = 1, 4096, 4096, 4096
+    d = _bmm(nb, m, n, k, dtype=0, bt=False)
+    assert _bplan(d)[0] == N.ERR_MISALIGNED
+    k4 = (k + 3) // 4 * 4
+    assert N.lib.cmpx_bmm_workspace_size(ctypes.byref(d)) == _x3_ws(nb, m, n, k) + nb * n * k4 * 4
+    # below the split rule there is no workspace schedule for it either
+    assert N.lib.cmpx_bmm_workspace_size(ctypes.byref(_bmm(4, 512, 512, 1024, dtype=0, bt=False))) == 0
+    # a workspace entry call without enough workspace keeps the plan's answer
+    assert N.lib.cmpx_bmm_ws(ctypes.byref(d), None, 0, None) == N.ERR_MISALIGNED
+
+
 def test_bmm_workspace_size_is_zero_for_16bit_and_rejected_calls():
     assert N.lib.cmpx_bmm_workspace_size(ctypes.byref(_bmm(1, 4096, 4096, 4096, dtype=2, bt=True))) == 0
     assert N.lib.cmpx_bmm_workspace_size(ctypes.byref(_bmm(2, 4096, 4096, 30, dtype=0, bt=True))) == 0  # misaligned

@@ -450,14 +450,24 @@ def _out_rows(nb: int, m: int, n: int, dtype, device) -> torch.Tensor:
     return torch.empty((nb, m, (n + 3) // 4 * 4), dtype=dtype, device=device)[..., :n]
 
 
-def _prepare_bmm(a, b):
+def _mn_f32_ok(b: torch.Tensor) -> bool:
+    """An fp32 [batch, k, n] B stored contiguous along n with 16-byte aligned rows: cmpx_bmm_ws reads
+    it through its workspace pass (no transposed copy)."""
+    nb, k, _ = b.shape
+    s0, s1, s2 = b.stride()
+    return (b.data_ptr() % 16 == 0 and s2 == 1 and (k == 1 or (s1 > 0 and s1 % 4 == 0))
+            and (nb == 1 or (s0 > 0 and s0 % 4 == 0)))
+
+
+def _prepare_bmm(a, b, keep_mn_b=False):
     _check_bmm_args(a, b)
     if a.dtype != torch.float32:
         a = a if _mat_ok(a) else a.contiguous()
         b = b if _mat_ok(b) else b.contiguous()
     else:  # K-major A and B (B as the transpose of a k-contiguous [batch, n, k] buffer)
         a = _kmajor_f32(a)
-        b = _kmajor_f32(b.transpose(1, 2)).transpose(1, 2)
+        if not (keep_mn_b and _mn_f32_ok(b)):
+            b = _kmajor_f32(b.transpose(1, 2)).transpose(1, 2)
     nb, m, _ = a.shape
     n = b.shape[2]
     c = _out_rows(nb, m, n, a.dtype, a.device)
@@ -480,12 +490,17 @@ def _bmm_desc(a, b, c) -> BmmDesc:
 @_traced("bmm")
 def bmm(input, mat2):
     """Batched matmul on the sm_100a kernels.  Same contract as the reference's ops.bmm."""
-    a, b, c = _prepare_bmm(input, mat2)
+    # fp32 with B stored MN-major: kept as it is when the workspace schedule takes it (its pass
+    # writes B K-major), copied K-major otherwise
+    a, b, c = _prepare_bmm(input, mat2, keep_mn_b=True)
     if c.numel() == 0:
         return c
     if a.shape[2] == 0:
         return c.zero_()
     desc = _bmm_desc(a, b, c)
+    if a.dtype == torch.float32 and b.stride(1) != 1 and lib.cmpx_bmm_workspace_size(ctypes.byref(desc)) == 0:
+        a, b, c = _prepare_bmm(input, mat2)
+        desc = _bmm_desc(a, b, c)
     with torch.cuda.device(a.device):
         stream = _stream_handle(a.device)
         # fp32: the split-operand schedule when the product is large enough (same results)

@@ -110,6 +110,43 @@ struct X3LoParams {
   unsigned int* special;
 };
 
+// The same for a B stored MN-major (element (z, kk, j) at x + z * batch_stride + kk * row_stride + j,
+// contiguous along n): both parts written K-major, hi = the word itself, through a shared-memory
+// 32 x 32 transpose, so the GEMM reads B from the workspace and no transposed copy of B is made.
+struct X3LoTParams {
+  const float* x;
+  long long batch_stride, row_stride;
+  int n, k, k_pad, tiles_j, tiles_k;
+  float* hi;
+  float* lo;
+  unsigned int* special;
+};
+
+__global__ void __launch_bounds__(256) x3_lo_t_kernel(const X3LoTParams p) {
+  __shared__ uint32_t t[32][33];
+  const int z = blockIdx.y;
+  const int tile = blockIdx.x, tj = tile % p.tiles_j, tk = tile / p.tiles_j;
+  const int j0 = tj * 32, kk0 = tk * 32;
+  const float* src = p.x + z * p.batch_stride;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int kk = kk0 + i, j = j0 + threadIdx.x;
+    t[i][threadIdx.x] = (kk < p.k && j < p.n) ? __float_as_uint(__ldg(src + kk * p.row_stride + j)) : 0u;
+  }
+  __syncthreads();
+  bool bad = false;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int j = j0 + i, kk = kk0 + threadIdx.x;
+    if (j < p.n && kk < p.k_pad) {
+      const uint32_t w = t[threadIdx.x][i];
+      const size_t o = (static_cast<size_t>(z) * p.n + j) * p.k_pad + kk;
+      p.hi[o] = __uint_as_float(w);
+      p.lo[o] = __uint_as_float(x3_lo(w));
+      bad |= x3_nan_low(w);
+    }
+  }
+  if (bad) atomicOr(p.special, 1u);
+}
+
 __global__ void __launch_bounds__(256) x3_lo_kernel(const X3LoParams p) {
   const int quads = p.k_pad >> 2;
   const long long n_rows = static_cast<long long>(p.batch) * p.rows;
@@ -387,7 +424,7 @@ constexpr const char* kX3ChunkName = "bmm_x3tf32_sm100<f32,128x128x32,3st,persis
 // calls' zero-kept counters, so one workspace serves both), the pass's special-value flag at 256,
 // lo(A) from 512, lo(B) after it, each [batch][rows][k_pad] fp32 with k_pad = k rounded up to 4.
 struct X3Ws {
-  size_t bytes = 0, off_alo = 0, off_blo = 0;
+  size_t bytes = 0, off_alo = 0, off_blo = 0, off_bhi = 0;  // off_bhi: MN-major B only
   int64_t k_pad = 0;
 };
 
@@ -399,7 +436,7 @@ inline size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 // (converter -> split, TFLOP/s): 1024^3 48 -> 63, 16384 x 1024 x 1024 135 -> 195, 4096^3 136 -> 226;
 // but 4 x 1024 x 256 x 1024 83 -> 70 and 64 x 2048 x 64 x 2048 121 -> 112 (a few K blocks per tile:
 // the epilogue, not the converter, sets the pace).  Hence m n / (m + n) >= 512 and k >= 512.
-inline X3Ws x3_ws_layout(const cmpx_bmm_desc* d) {
+inline X3Ws x3_ws_layout(const cmpx_bmm_desc* d, bool b_mn = false) {
   X3Ws w;
   const double m = static_cast<double>(d->m), n = static_cast<double>(d->n);
   if (d->m < 1 || d->n < 1 || d->k < 512 || m * n / (m + n) < 512.0) return w;
@@ -407,7 +444,28 @@ inline X3Ws x3_ws_layout(const cmpx_bmm_desc* d) {
   w.off_alo = 512;
   w.off_blo = w.off_alo + align256(static_cast<size_t>(d->batch) * d->m * w.k_pad * 4);
   w.bytes = w.off_blo + align256(static_cast<size_t>(d->batch) * d->n * w.k_pad * 4);
+  if (b_mn) {
+    w.off_bhi = w.bytes;
+    w.bytes = w.off_bhi + align256(static_cast<size_t>(d->batch) * d->n * w.k_pad * 4);
+  }
   return w;
+}
+
+// An fp32 product whose only departure from the plan's layouts is an MN-major B (a row-major
+// [k, n] matrix, contiguous along n, rows 16-byte aligned): served through the workspace, where the
+// pass writes B's hi and lo parts K-major.
+inline bool x3_b_mn_ok(const cmpx_bmm_desc* d) {
+  if (d->dtype != CMPX_F32 || d->k < 1 || d->m > (int64_t)128 * 65535 || d->n > (1ll << 31) - 256 ||
+      d->batch > 65535 || d->k > (1ll << 31) - 64)
+    return false;
+  const void* ptrs[3] = {d->a, d->b, d->c};
+  for (const void* ptr : ptrs)
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15u) != 0) return false;
+  const bool a_ok = d->a_stride[2] == 1 && (d->m == 1 || s16f(d->a_stride[1]));
+  const bool b_ok = d->b_stride[2] == 1 && (d->k == 1 || s16f(d->b_stride[1]));
+  const bool c_ok = d->c_stride[2] == 1 && (d->m == 1 || s16f(d->c_stride[1]));
+  const bool batch_ok = d->batch == 1 || (s16f(d->a_stride[0]) && s16f(d->b_stride[0]) && s16f(d->c_stride[0]));
+  return a_ok && b_ok && c_ok && batch_ok;
 }
 
 }  // namespace
@@ -546,10 +604,13 @@ int launch_x3_lo(const float* x, long long batch_stride, long long row_stride, i
   return cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
 }
 
-int launch_x3(const cmpx_bmm_desc* d, const LaunchCtx& ctx, const float* bias, void* ws, size_t ws_bytes) {
+int launch_x3(const cmpx_bmm_desc* d_in, const LaunchCtx& ctx, const float* bias, void* ws, size_t ws_bytes,
+              bool b_mn = false) {
   using C = X3GemmCfg;
   X3Pre pre;
-  const X3Ws lay = x3_ws_layout(d);
+  cmpx_bmm_desc dd = *d_in;  // (MN-major B: B is read from the workspace, K-major)
+  const cmpx_bmm_desc* d = &dd;
+  const X3Ws lay = x3_ws_layout(d, b_mn);
   if (lay.bytes > 0 && ws && ws_bytes >= lay.bytes && (reinterpret_cast<uintptr_t>(ws) & 15u) == 0) {
     uint8_t* w = static_cast<uint8_t*>(ws);
     unsigned int* special = reinterpret_cast<unsigned int*>(w + 256);
@@ -558,14 +619,41 @@ int launch_x3(const cmpx_bmm_desc* d, const LaunchCtx& ctx, const float* bias, v
     if (cudaMemsetAsync(special, 0, 16, ctx.stream) != cudaSuccess) return CMPX_ERR_LAUNCH;
     int st = launch_x3_lo(static_cast<const float*>(d->a), d->a_stride[0], d->a_stride[1], d->m, d, lay.k_pad, lo_a,
                           special, ctx);
-    if (st == CMPX_OK)
+    if (st == CMPX_OK && !b_mn)
       st = launch_x3_lo(static_cast<const float*>(d->b), d->b_stride[0], d->b_stride[2], d->n, d, lay.k_pad, lo_b,
                         special, ctx);
+    if (st == CMPX_OK && b_mn) {
+      float* hi_b = reinterpret_cast<float*>(w + lay.off_bhi);
+      X3LoTParams q;
+      q.x = static_cast<const float*>(d->b);
+      q.batch_stride = d->b_stride[0];
+      q.row_stride = d->b_stride[1];
+      q.n = static_cast<int>(d->n);
+      q.k = static_cast<int>(d->k);
+      q.k_pad = static_cast<int>(lay.k_pad);
+      q.tiles_j = static_cast<int>((d->n + 31) / 32);
+      q.tiles_k = static_cast<int>((lay.k_pad + 31) / 32);
+      q.hi = hi_b;
+      q.lo = lo_b;
+      q.special = special;
+      const int64_t tiles = static_cast<int64_t>(q.tiles_j) * q.tiles_k;
+      if (tiles > (1ll << 31) - 1) return CMPX_ERR_UNSUPPORTED_SHAPE;
+      x3_lo_t_kernel<<<dim3(static_cast<unsigned>(tiles), static_cast<unsigned>(d->batch)), dim3(32, 8), 0,
+                       ctx.stream>>>(q);
+      st = cudaGetLastError() == cudaSuccess ? CMPX_OK : CMPX_ERR_LAUNCH;
+      // from here on B is the K-major copy in the workspace
+      dd.b = hi_b;
+      dd.b_stride[0] = d->n * lay.k_pad;
+      dd.b_stride[1] = 1;
+      dd.b_stride[2] = lay.k_pad;
+    }
     if (st != CMPX_OK) return st;
     pre.lo_a = lo_a;
     pre.lo_b = lo_b;
     pre.k_pad = lay.k_pad;
     pre.special = special;
+  } else if (b_mn) {
+    return CMPX_ERR_WORKSPACE;
   }
   if (d->k <= C::MAX_K) return launch_x3_once(d, ctx, bias, 0, pre);
   const int64_t chunks = (d->k + C::MAX_K - 1) / C::MAX_K;
@@ -591,16 +679,20 @@ int launch_x3(const cmpx_bmm_desc* d, const LaunchCtx& ctx, const float* bias, v
 size_t bmm_x3_workspace_bytes(const cmpx_bmm_desc* d) {
   int st = CMPX_OK;
   bmm_x3_plan(d, &st);
-  if (st != CMPX_OK || d->batch == 0) return 0;
-  return x3_ws_layout(d).bytes;
+  if (d->batch == 0) return 0;
+  if (st == CMPX_OK) return x3_ws_layout(d).bytes;
+  if (st == CMPX_ERR_MISALIGNED && x3_b_mn_ok(d)) return x3_ws_layout(d, true).bytes;
+  return 0;
 }
 
 int launch_bmm_x3(const cmpx_bmm_desc* d, const LaunchCtx& ctx, void* ws, size_t ws_bytes) {
   int st = CMPX_OK;
   bmm_x3_plan(d, &st);
-  if (st != CMPX_OK) return st;
+  const bool b_mn = st == CMPX_ERR_MISALIGNED && x3_b_mn_ok(d) && x3_ws_layout(d, true).bytes > 0 && ws &&
+                    ws_bytes >= x3_ws_layout(d, true).bytes;
+  if (st != CMPX_OK && !b_mn) return st;
   if (d->m == 0 || d->n == 0 || d->batch == 0) return CMPX_OK;
-  return launch_x3(d, ctx, nullptr, ws, ws_bytes);
+  return launch_x3(d, ctx, nullptr, ws, ws_bytes, b_mn);
 }
 
 const char* linear_x3_plan(const cmpx_linear_desc* d, int* status) {
