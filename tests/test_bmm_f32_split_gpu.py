@@ -201,3 +201,18 @@ def test_mn_major_b_through_the_workspace(cuda_device):
     torch.cuda.synchronize()
     assert torch.isnan(got[1, :, 3]).all()
     assert torch.equal(torch.nan_to_num(got), torch.nan_to_num(plain))
+
+
+def test_mn_major_b_with_k_chunks(cuda_device):
+    # K > 8192 runs as K chunks; B row-major goes through the transposing pass, every chunk reading
+    # its slice of the workspace copy
+    g = torch.Generator().manual_seed(16)
+    a = torch.randn(1, 1024, 8200, generator=g)
+    b = torch.randn(1, 8200, 1024, generator=g)
+    ad, bd = a.to(cuda_device), b.to(cuda_device)
+    assert N.bmm_plan(ad, bd).endswith("+k-chunks>")
+    got = cmpext3.ops.bmm(ad, bd)
+    plain = _no_workspace(ad, bd)
+    torch.cuda.synchronize()
+    assert torch.equal(got, plain)
+    check(got, RP.bmm(a, b), torch.float32, "split fp32 bmm, row-major B, K chunks", attention=False)
