@@ -13,10 +13,16 @@
 //   * operands are K-major (A rows and B columns contiguous along K, read in place through rank-3
 //     TMA maps); 32-element (128-byte) K blocks stream through a 3-stage ring of 64 KB stages:
 //     A and B as loaded (their hi parts) and their lo parts;
-//   * warp 0: TMA; warps 2-9 ("converter"): per stage, lo = x - trunc(x) for both tiles.  The hi
-//     part is the word as loaded: the tensor core's TF32 read of an fp32 word keeps its top 19 bits
-//     (measured: the same results as explicitly truncated operands).  Only an inf / NaN word is
-//     rewritten in place (a NaN whose payload sits in the dropped bits would read as inf);
+//   * split operands (a caller workspace, cmpx_bmm_ws / cmpx_linear_ws): x3_lo_kernel writes lo(A)
+//     and lo(B) once per call, K-major (x3_lo_t_kernel also hi(B) for a B stored MN-major), and
+//     warp 0 loads them beside A and B, four tiles per stage; the converter warps then idle.  The
+//     split done per stage in shared memory (below) is what bounds the GEMM otherwise: 4096^3 runs
+//     at 226 TFLOP/s split against 136;
+//   * warp 0: TMA; warps 2-9 ("converter", without a workspace or after the pass flagged a NaN it
+//     cannot keep): per stage, lo = x - trunc(x) for both tiles.  The hi part is the word as
+//     loaded: the tensor core's TF32 read of an fp32 word keeps its top 19 bits (measured: the same
+//     results as explicitly truncated operands).  Only an inf / NaN word is rewritten in place (a
+//     NaN whose payload sits in the dropped bits would read as inf);
 //     warp 1: 12 tcgen05.mma kind::tf32 per stage (4 K-steps of 8 x 3 products) into
 //     one of two TMEM tile buffers, so tile i+1's products overlap tile i's epilogue.  A buffer is
 //     two accumulators: hi*hi, and the two cross terms, ~2^-11 smaller.  The tensor core's fp32
