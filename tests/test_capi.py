@@ -499,14 +499,16 @@ def _f32_split_bytes(items, tiles, dp, sms=148):
     rem = items % sms
     if items <= sms or rem == 0 or 2 * rem > sms:
         return 0
-    split = min(sms // rem, 8, tiles)
+    split = min(sms // rem, 8, tiles // 4)  # at least 4 key tiles per range
     return 256 + rem * split * 128 * (dp + 4) * 4 if split >= 2 else 0
 
 
 def _f32_workspace(cfg, split_bytes, dp):
-    """The split's bytes, then (when every (b, h) has two or more 128-row items) K hi / lo and
-    V^T hi / lo, fp32, B * H * lk_pad * dp each, from the next 1024-byte boundary."""
-    if (cfg["Lq"] + 127) // 128 < 2:
+    """The split's bytes, then (when every (b, h) has two or more 128-row items and an item reads
+    four or more key tiles) K hi / lo and V^T hi / lo, fp32, B * H * lk_pad * dp each, from the
+    next 1024-byte boundary."""
+    bn = 64 if dp == 64 else 32
+    if (cfg["Lq"] + 127) // 128 < 2 or (cfg["Lk"] + bn - 1) // bn < 4:
         return split_bytes
     lk_pad = (cfg["Lk"] + 63) // 64 * 64
     off = (max(256, split_bytes) + 1023) // 1024 * 1024
@@ -520,6 +522,9 @@ def _f32_workspace(cfg, split_bytes, dp):
     (dict(B=2, H=8, Lq=4096, Lk=4096, D=40, dtype=0, causal=1), False),  # causal: never split
     (dict(B=1, H=248, Lq=128, Lk=4096, D=64, dtype=0), False),   # 100 tail items: more than half a wave
     (dict(B=1, H=148, Lq=256, Lk=4096, D=64, dtype=0), False),   # full waves only
+    (dict(B=2, H=8, Lq=4096, Lk=77, D=40, dtype=0), False),      # 2 key tiles per item: no split, no pre-pass
+    (dict(B=2, H=8, Lq=1024, Lk=77, D=80, dtype=0), False),      # 3 key tiles of 32: neither
+    (dict(B=1, H=218, Lq=128, Lk=256, D=64, dtype=0), False),    # 4 key tiles: pre-pass not used (1 row tile), no split
 ])
 def test_fp32_workspace_covers_its_tail_split(cfg, split):
     d = _attn(**cfg)

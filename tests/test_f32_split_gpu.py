@@ -26,7 +26,7 @@ SPLIT_SHAPES = [
     (1, 218, 128, 640, 40),    # 218 items: 70 tail items cut in 2 key ranges
     (1, 150, 128, 4096, 64),   # 2 tail items cut in 8
     (1, 75, 512, 1024, 128),   # D = 128 (32-key tiles): 4 tail items cut in 8
-    (2, 3, 4500, 300, 24),     # 216 items, a ragged last row tile (4500 rows) and key tile (300 keys)
+    (2, 3, 4500, 556, 24),     # 216 items, a ragged last row tile (4500 rows) and key tile (556 keys)
 ]
 
 

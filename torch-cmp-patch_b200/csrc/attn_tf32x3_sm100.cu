@@ -833,7 +833,10 @@ X3Split x3_split_plan(const cmpx_attn_desc* d, int num_sms) {
   const int64_t grid = std::min<int64_t>(n_items, std::max(1, num_sms));
   const int64_t rem = n_items % grid, tiles = (d->len_k + C::BN - 1) / C::BN;
   if (n_items <= grid || rem == 0 || 2 * rem > grid) return sp;
-  const int64_t split = std::min<int64_t>({grid / rem, 8, tiles});
+  // At least 4 key tiles per range: with fewer, the ranges' park-and-merge costs more than the
+  // idle tail it fills (SD1.5 fp32 cross-attention [2,8,4096,77,40], 2 key tiles per item: 68.6 us
+  // split into single tiles, 35.8 us unsplit).
+  const int64_t split = std::min<int64_t>({grid / rem, 8, tiles / 4});
   if (split < 2) return sp;
   sp.n_whole = static_cast<int>(n_items - rem);
   sp.split = static_cast<int>(split);
@@ -844,7 +847,9 @@ X3Split x3_split_plan(const cmpx_attn_desc* d, int num_sms) {
 }
 
 // Split operands (pre): four fp32 buffers of B * heads_kv * lk_pad * DP, after the split's bytes
-// (1024-aligned), worth it when every (b, h) has two or more 128-row items to share them.
+// (1024-aligned), worth it when every (b, h) has two or more 128-row items to share them and an
+// item reads four or more key tiles: for shorter key sequences the pre-pass launch costs more than
+// the per-stage split it saves ([2,8,1024,77,80]: 31.7 us with it, 20.5 us without).
 struct X3Pre {
   bool use = false;
   int lk_pad = 0;
@@ -855,7 +860,7 @@ template <int DP>
 X3Pre x3_pre_plan(const cmpx_attn_desc* d, const X3Split& sp) {
   using C = X3Cfg<DP>;
   X3Pre pr;
-  if ((d->len_q + C::BM - 1) / C::BM < 2) return pr;
+  if ((d->len_q + C::BM - 1) / C::BM < 2 || (d->len_k + C::BN - 1) / C::BN < 4) return pr;
   pr.use = true;
   pr.lk_pad = static_cast<int>((d->len_k + 63) / 64 * 64);
   pr.off = (std::max<size_t>(256, sp.bytes) + 1023) & ~static_cast<size_t>(1023);
