@@ -461,7 +461,8 @@ def test_workspace_contract():
 def _split_bytes(items, n_kv, dp, sms=148):
     """Workspace of the tail split: work counters, then per range (m, l) and fp32 O for 256 rows."""
     rem = items % sms
-    split = min(sms // rem, n_kv // 4, 8) if rem else 1
+    per_range = 8 if items < sms else 4  # every item cut: at least 8 key tiles a range; else 4
+    split = min(sms // rem, n_kv // per_range, 8) if rem else 1
     if split < 2:
         return 256
     ranges = rem * split
@@ -471,8 +472,8 @@ def _split_bytes(items, n_kv, dp, sms=148):
 
 @pytest.mark.parametrize("cfg", [
     dict(B=2, H=10, Lq=4096, Lk=4096, D=64, dtype=1),    # SD1.5 self-attention: 320 items, 24 split 6 ways
-    dict(B=1, H=1, Lq=512, Lk=4096, D=128, dtype=2),    # 2 items, 8 ranges each
-    dict(B=1, H=2, Lq=1024, Lk=1024, D=96, dtype=2),    # padded head dim: fp32 rows of 128
+    dict(B=1, H=1, Lq=512, Lk=4096, D=128, dtype=2),    # 2 items, 4 ranges of 8 key tiles each
+    dict(B=1, H=2, Lq=1024, Lk=2048, D=96, dtype=2),    # padded head dim: fp32 rows of 128
 ])
 def test_workspace_size_covers_the_tail_split(cfg):
     d = _attn(**cfg)
@@ -488,6 +489,7 @@ def test_workspace_size_covers_the_tail_split(cfg):
     dict(B=2, H=10, Lq=4096, Lk=77, D=64, dtype=1),               # short keys: its own kernel
     dict(B=1, H=2, Lq=256, Lk=256, D=128, dtype=2),               # too few key tiles to split
     dict(B=1, H=148, Lq=256, Lk=4096, D=64, dtype=1),             # full waves only
+    dict(B=2, H=8, Lq=1024, Lk=1024, D=80, dtype=1),              # 64 items < SMs, 8 key tiles: not cut
 ])
 def test_workspace_size_without_split(cfg):
     assert N.lib.cmpx_attn_workspace_size(ctypes.byref(_attn(**cfg))) == 256

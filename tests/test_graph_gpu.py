@@ -51,7 +51,7 @@ def test_attention_in_a_graph(cuda_device, case):
     dev = cuda_device
     if case == "causal":
         shape_q, shape_k, dtype, causal = (2, 4, 700, 128), (2, 4, 700, 128), torch.bfloat16, True
-    elif case == "split":   # 2 items: tail split into 8 key ranges + merge kernel
+    elif case == "split":   # 2 items: tail split into 4 key ranges + merge kernel
         shape_q, shape_k, dtype, causal = (1, 1, 512, 64), (1, 1, 4096, 64), torch.float16, False
     elif case == "mask":
         shape_q, shape_k, dtype, causal = (2, 4, 300, 64), (2, 4, 500, 64), torch.bfloat16, False

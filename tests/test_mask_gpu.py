@@ -83,7 +83,7 @@ def test_rows_with_no_key_output_zero(cuda_device):
 
 
 def test_mask_with_tail_split(cuda_device):
-    # 2 items on 148 SMs: split into 8 key ranges; some rows have no key in some ranges, one in none
+    # 2 items on 148 SMs: split into 4 key ranges; some rows have no key in some ranges, one in none
     q, k, v, g = _qkv(1, 1, 512, 4096, 64, torch.float16, seed=5)
     m = torch.rand(512, 4096, generator=g) > 0.97
     m[10] = False

@@ -23,10 +23,10 @@ NUM_SMS = 148
 
 CASES = [
     # (dtype, B, H, Hkv, Lq, Lk, D)  -- every one splits on a 148-SM B200
-    (torch.float16, 1, 1, 1, 512, 4096, 64),     # 2 items, 8 ranges each (the most)
-    (torch.bfloat16, 1, 2, 2, 1024, 1024, 128),  # 8 items, 2 ranges each
-    (torch.bfloat16, 2, 3, 3, 300, 4000, 64),    # ragged rows and last key tile, 8 ranges
-    (torch.float16, 1, 4, 2, 512, 2048, 128),    # grouped-query heads, 4 ranges
+    (torch.float16, 1, 1, 1, 512, 4096, 64),     # 2 items, 4 ranges of 8 key tiles each
+    (torch.bfloat16, 1, 2, 2, 1024, 2048, 128),  # 8 items, 2 ranges each
+    (torch.bfloat16, 2, 3, 3, 300, 4000, 64),    # ragged rows and last key tile, 4 ranges
+    (torch.float16, 1, 4, 2, 512, 2048, 128),    # grouped-query heads, 2 ranges
     (torch.bfloat16, 2, 10, 10, 4096, 4096, 64),  # the SD1.5 self-attention shape: 24 of 320 items split 6 ways
 ]
 
@@ -36,7 +36,8 @@ def _split_of(B, H, Lq, Lk):
     rem = items % NUM_SMS
     if rem == 0:
         return 1, items
-    return min(NUM_SMS // rem, ((Lk + 127) // 128) // 4, 8), rem
+    per_range = 8 if items < NUM_SMS else 4  # every item cut: at least 8 key tiles a range
+    return min(NUM_SMS // rem, ((Lk + 127) // 128) // per_range, 8), rem
 
 
 def _inputs(case, seed):
