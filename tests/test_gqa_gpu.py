@@ -22,6 +22,12 @@ CASES = [
     (torch.bfloat16, 1, 8, 1, 257, 257, 64, True, "fmha_sm100<"),       # multi-query
     (torch.float16, 2, 10, 5, 500, 77, 64, False, "fmha_sm100_short"),  # short key sequences
     (torch.float32, 1, 8, 2, 300, 300, 40, False, "attn_tf32x3"),        # fp32 tensor cores
+    # one query row (decode): the group's query heads folded into one head of `group` rows
+    (torch.bfloat16, 8, 32, 8, 1, 4096, 128, False, "fmha_sm100<"),
+    (torch.float16, 2, 12, 4, 1, 1000, 64, False, "fmha_sm100<"),
+    (torch.bfloat16, 3, 16, 2, 1, 77, 128, False, "fmha_sm100_short"),   # folded, short keys
+    (torch.float16, 2, 8, 2, 3, 2000, 64, False, "fmha_sm100<"),        # 3 rows: [B, L, H, D] output, not folded
+    (torch.bfloat16, 4, 8, 4, 1, 500, 64, True, "fmha_sm100<"),         # causal: not folded
 ]
 
 

@@ -983,17 +983,53 @@ FmhaSplit fmha_split_plan(const cmpx_attn_desc* d, int num_sms) {
 
 }  // namespace
 
-size_t fmha_workspace_bytes(const cmpx_attn_desc* d, int num_sms) {
+// Grouped-query heads with few query rows (decode steps, short prefills): the `group` query heads
+// of a key/value head are folded into one head of group * len_q rows, so the two 128-row Q tiles of
+// an item hold several heads' rows against one K/V stream -- each K/V tile is read once per
+// key/value head instead of once per query head, and there are `group` times fewer mostly empty
+// items ([8,32,1,4096,128] bf16 with 8 key/value heads: 256 items of one query row each before).
+// Exact (attention treats every query row on its own).  Needs the query and output rows of the
+// group to be one stride apart: always for one query row (the head stride then serves as the row
+// stride), else when a head's rows follow each other (head stride = len_q * row stride); no mask
+// and no causal mask (both are per head and row).
+static bool fmha_gqa_fold(const cmpx_attn_desc* d, cmpx_attn_desc* f) {
+  if (d->causal || d->mask || d->heads_kv <= 0 || d->heads_kv >= d->heads || d->heads % d->heads_kv != 0 ||
+      d->len_q < 1 || d->len_q >= 256)
+    return false;
+  const int64_t group = d->heads / d->heads_kv;
+  const bool one_row = d->len_q == 1;
+  if (!one_row && (d->q_stride[1] != d->len_q * d->q_stride[2] || d->o_stride[1] != d->len_q * d->o_stride[2]))
+    return false;
+  *f = *d;
+  f->heads = d->heads_kv;
+  f->len_q = d->len_q * group;
+  if (one_row) {  // row r of the folded head = query head g * group + r
+    f->q_stride[2] = d->q_stride[1];
+    f->o_stride[2] = d->o_stride[1];
+  }
+  f->q_stride[1] = d->q_stride[1] * group;
+  f->o_stride[1] = d->o_stride[1] * group;
+  f->heads_kv = 0;  // one query head (of group * len_q rows) per key/value head
+  return true;
+}
+
+size_t fmha_workspace_bytes(const cmpx_attn_desc* d_in, int num_sms) {
+  cmpx_attn_desc fd;
+  const cmpx_attn_desc* d = fmha_gqa_fold(d_in, &fd) ? &fd : d_in;
   if (fmha_short_eligible(d)) return kAttnWorkspaceMin;
   return fmha_split_plan(d, num_sms).bytes;
 }
 
-size_t fmha_workspace_min(const cmpx_attn_desc* d) {
+size_t fmha_workspace_min(const cmpx_attn_desc* d_in) {
+  cmpx_attn_desc fd;
+  const cmpx_attn_desc* d = fmha_gqa_fold(d_in, &fd) ? &fd : d_in;
   return kAttnWorkspaceMin + (fmha_short_eligible(d) ? 0 : mask_pack_plan(d).bytes);
 }
 
-const char* fmha_sm100_plan(const cmpx_attn_desc* d, int* status) {
+const char* fmha_sm100_plan(const cmpx_attn_desc* d_in, int* status) {
   *status = CMPX_OK;
+  cmpx_attn_desc fd;
+  const cmpx_attn_desc* d = fmha_gqa_fold(d_in, &fd) ? &fd : d_in;
   if (d->dtype != CMPX_F16 && d->dtype != CMPX_BF16) {
     *status = CMPX_ERR_UNSUPPORTED_DTYPE;
     return "none";
@@ -1191,10 +1227,12 @@ int launch_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
 
 }  // namespace
 
-int launch_fmha_sm100(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
+int launch_fmha_sm100(const cmpx_attn_desc* d_in, const LaunchCtx& ctx) {
   int st = CMPX_OK;
-  fmha_sm100_plan(d, &st);
+  fmha_sm100_plan(d_in, &st);
   if (st != CMPX_OK) return st;
+  cmpx_attn_desc fd;
+  const cmpx_attn_desc* d = fmha_gqa_fold(d_in, &fd) ? &fd : d_in;
   if (d->len_q == 0) return CMPX_OK;
   if (fmha_short_eligible(d)) return launch_fmha_short(d, ctx);
   const bool bf = d->dtype == CMPX_BF16;
