@@ -216,3 +216,23 @@ def test_mn_major_b_with_k_chunks(cuda_device):
     torch.cuda.synchronize()
     assert torch.equal(got, plain)
     check(got, RP.bmm(a, b), torch.float32, "split fp32 bmm, row-major B, K chunks", attention=False)
+
+
+def test_patched_fp32_matmul_and_linear_take_the_split_schedule(cuda_device, patched):
+    # torch.matmul of two row-major fp32 matrices (a row-major B: the transposing pass) and
+    # nn.Linear (the weight read as the K-major operand), both through the patched ops
+    g = torch.Generator().manual_seed(17)
+    x = torch.randn(2048, 1024, generator=g)
+    w = torch.randn(1024, 2048, generator=g)
+    lin = torch.nn.Linear(1024, 1536).to(cuda_device)
+    xd, wd = x.to(cuda_device), w.to(cuda_device)
+    cmpext3.autoselect.reset()
+    with torch.no_grad():
+        got = torch.matmul(xd, wd)
+        got_lin = lin(xd)
+    torch.cuda.synchronize()
+    check(got, RP.bmm(x[None], w[None])[0], torch.float32, "patched fp32 matmul", attention=False)
+    ref_lin = torch.nn.functional.linear(x.double(), lin.weight.detach().double().cpu(), lin.bias.detach().double().cpu())
+    assert ((got_lin.double().cpu() - ref_lin).abs().max() / ref_lin.abs().max()).item() <= 5e-5
+    report = cmpext3.autoselect_report()
+    assert "bmm_x3tf32_sm100" in report
