@@ -462,7 +462,7 @@ def _split_bytes(items, n_kv, dp, sms=148):
     """Workspace of the tail split: work counters, then per range (m, l) and fp32 O for 256 rows."""
     rem = items % sms
     per_range = 8 if items < sms else 4  # every item cut: at least 8 key tiles a range; else 4
-    split = min(sms // rem, n_kv // per_range, 8) if rem else 1
+    split = min(sms // rem, n_kv // per_range, 8) if rem and n_kv >= 16 else 1  # items of < 16 tiles: never
     if split < 2:
         return 256
     ranges = rem * split
@@ -490,6 +490,7 @@ def test_workspace_size_covers_the_tail_split(cfg):
     dict(B=1, H=2, Lq=256, Lk=256, D=128, dtype=2),               # too few key tiles to split
     dict(B=1, H=148, Lq=256, Lk=4096, D=64, dtype=1),             # full waves only
     dict(B=2, H=8, Lq=1024, Lk=1024, D=80, dtype=1),              # 64 items < SMs, 8 key tiles: not cut
+    dict(B=4, H=40, Lq=1024, Lk=1024, D=64, dtype=1),             # 640 items, tail of 48, 8 key tiles: not cut
 ])
 def test_workspace_size_without_split(cfg):
     assert N.lib.cmpx_attn_workspace_size(ctypes.byref(_attn(**cfg))) == 256

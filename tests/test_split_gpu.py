@@ -37,7 +37,8 @@ def _split_of(B, H, Lq, Lk):
     if rem == 0:
         return 1, items
     per_range = 8 if items < NUM_SMS else 4  # every item cut: at least 8 key tiles a range
-    return min(NUM_SMS // rem, ((Lk + 127) // 128) // per_range, 8), rem
+    n_kv = (Lk + 127) // 128
+    return (min(NUM_SMS // rem, n_kv // per_range, 8) if n_kv >= 16 else 1), rem
 
 
 def _inputs(case, seed):

@@ -919,7 +919,8 @@ void* fmha_kernel_ptr() {
 // Tail split of a non-causal launch on num_sms persistent CTAs.  With n items and G CTAs, the
 // first n - n % G items run whole (full waves); the n % G items of the last, partial wave would
 // leave most CTAs idle while they run, so each is cut into split = G / (n % G) key ranges (at most
-// kMaxSplit, and at least 4 key tiles per range; 8 when n < G and every item is cut).  Workspace: the 256-byte work counters, the
+// kMaxSplit, and at least 4 key tiles per range; 8 when n < G and every item is cut; no split
+// for items of fewer than 16 key tiles).  Workspace: the 256-byte work counters, the
 // packed mask if the call has one, then each range's (m, l) per row and its fp32 O rows (scratch:
 // written before they are read).
 struct FmhaSplit {
@@ -964,9 +965,12 @@ FmhaSplit fmha_split_plan(const cmpx_attn_desc* d, int num_sms) {
   const bool add_mask = d->mask && d->mask_kind == CMPX_MASK_ADD;
   const int64_t bn = (d->head_dim <= 128 && !add_mask) ? 128 : 64;
   const int64_t n_kv = (d->len_k + bn - 1) / bn;
-  // A launch of fewer items than SMs splits every item, and every range then parks and merges its
-  // whole 256-row partial: keep at least 8 key tiles a range there ([2,8,1024,1024,80] fp16, 64
-  // items of 8 tiles: 35.8 us in 4-tile ranges, 24.8 us unsplit), 4 for the tail of a longer launch.
+  // Items of fewer than 16 key tiles are not cut: the ranges' park-and-merge then costs more than
+  // the idle tail it fills ([4,40,1024,1024,64] fp16, 8 tiles an item: 91.1 us split, 81.9 us not;
+  // [2,10,2048,2048,64], 16 tiles: 54.2 us split, 63.5 us not).  A launch of fewer items than SMs
+  // splits every item, and every range then parks and merges its whole 256-row partial: at least 8
+  // key tiles a range there, 4 for the tail of a longer launch.
+  if (n_kv < 16) return sp;
   const int64_t per_range = n_items < num_sms ? 8 : 4;
   const int64_t split = std::min<int64_t>({num_sms / rem, n_kv / per_range, kMaxSplit});
   if (split < 2) return sp;
