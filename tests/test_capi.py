@@ -498,9 +498,12 @@ def test_workspace_size_without_split(cfg):
 
 def _f32_split_bytes(items, tiles, dp, sms=148):
     """fp32 tail split: 256 bytes of 8-bit item counters, then per key range 128 rows of
-    (O [dp], m, l, 2 pad) fp32."""
+    (O [dp], m, l, 2 pad) fp32.  Fewer items than SMs: every item cut, ranges of >= 8 key tiles."""
+    if 0 < items < sms:
+        split = min(sms // items, 8, tiles // 8)
+        return 256 + items * split * 128 * (dp + 4) * 4 if split >= 2 else 0
     rem = items % sms
-    if items <= sms or rem == 0 or 2 * rem > sms:
+    if rem == 0 or 2 * rem > sms:
         return 0
     split = min(sms // rem, 8, tiles // 4)  # at least 4 key tiles per range
     return 256 + rem * split * 128 * (dp + 4) * 4 if split >= 2 else 0
@@ -528,6 +531,9 @@ def _f32_workspace(cfg, split_bytes, dp):
     (dict(B=2, H=8, Lq=4096, Lk=77, D=40, dtype=0), False),      # 2 key tiles per item: no split, no pre-pass
     (dict(B=2, H=8, Lq=1024, Lk=77, D=80, dtype=0), False),      # 3 key tiles of 32: neither
     (dict(B=1, H=218, Lq=128, Lk=256, D=64, dtype=0), False),    # 4 key tiles: pre-pass not used (1 row tile), no split
+    (dict(B=2, H=8, Lq=128, Lk=8192, D=64, dtype=0), True),      # 16 items < SMs: every item cut 8 ways
+    (dict(B=1, H=8, Lq=256, Lk=4096, D=128, dtype=0), True),     # 16 items, 32-key tiles: cut 8 ways
+    (dict(B=2, H=8, Lq=1024, Lk=512, D=64, dtype=0), False),     # 128 items < SMs but 8 key tiles: 1 range each
 ])
 def test_fp32_workspace_covers_its_tail_split(cfg, split):
     d = _attn(**cfg)

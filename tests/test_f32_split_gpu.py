@@ -27,6 +27,8 @@ SPLIT_SHAPES = [
     (1, 150, 128, 4096, 64),   # 2 tail items cut in 8
     (1, 75, 512, 1024, 128),   # D = 128 (32-key tiles): 4 tail items cut in 8
     (2, 3, 4500, 556, 24),     # 216 items, a ragged last row tile (4500 rows) and key tile (556 keys)
+    (2, 8, 128, 8192, 64),     # 16 items, fewer than SMs: every item cut into 8 key ranges
+    (1, 8, 256, 4096, 100),    # 16 items, D = 100 (32-key tiles), every item cut 8 ways
 ]
 
 

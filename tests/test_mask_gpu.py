@@ -67,7 +67,7 @@ def test_boolean_mask_sweep(cuda_device, dtype, kind, D, causal, lens):
     q, k, v, g = _qkv(2, 3, lq, lk, D, dtype, seed=lq + 7 * lk + D + causal)
     m = _mask(kind, 2, 3, lq, lk, g)
     assert N.attention_plan(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), None, causal,
-                            m.to(cuda_device)).endswith("+mask>")
+                            m.to(cuda_device)).endswith(("+mask>", "+mask+tail-split>"))
     _run(cuda_device, q, k, v, m, causal, f"{kind} D{D} {lens} causal={causal}")
 
 
@@ -119,8 +119,8 @@ def test_patched_sdpa_boolean_and_additive_masks_native(cuda_device, patched):
     check(got, _ref(q, k, v, m, False), torch.bfloat16, "patched sdpa mask")
     check(got_add, _ref(q, k, v, add.float(), False), torch.bfloat16, "patched sdpa additive mask")
     entries = [d.entry for d in cmpext3.autoselect.report() if d.use_native]
-    assert any((e or "").endswith("+mask>") for e in entries), cmpext3.autoselect_report()
-    assert any((e or "").endswith("+addmask>") for e in entries), cmpext3.autoselect_report()
+    assert any((e or "").endswith(("+mask>", "+mask+tail-split>")) for e in entries), cmpext3.autoselect_report()
+    assert any((e or "").endswith(("+addmask>", "+addmask+tail-split>")) for e in entries), cmpext3.autoselect_report()
 
 
 def _additive(kind, B, H, Lq, Lk, dtype, g):
@@ -145,7 +145,7 @@ def test_additive_mask_sweep(cuda_device, dtype, kind, D, causal, lens):
     q, k, v, g = _qkv(2, 3, lq, lk, D, dtype, seed=lq + 5 * lk + D + causal)
     m = _additive(kind, 2, 3, lq, lk, dtype, g)
     qd, kd, vd, md = (t.to(cuda_device) for t in (q, k, v, m))
-    assert N.attention_plan(qd, kd, vd, None, causal, md).endswith("+addmask>")
+    assert N.attention_plan(qd, kd, vd, None, causal, md).endswith(("+addmask>", "+addmask+tail-split>"))
     got = cmpext3.ops.attention(qd, kd, vd, None, causal, md)
     torch.cuda.synchronize()
     assert torch.isfinite(got.float()).all()
@@ -234,7 +234,7 @@ def test_fp32_boolean_mask_sweep(cuda_device, kind, D, causal, lens):
     m = _mask(kind, 2, 3, lq, lk, g)
     plan = N.attention_plan(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), None, causal,
                             m.to(cuda_device))
-    assert plan.startswith("attn_tf32x3_sm100") and plan.endswith("+mask>"), plan
+    assert plan.startswith("attn_tf32x3_sm100") and plan.endswith(("+mask>", "+mask+tail-split>")), plan
     _run(cuda_device, q, k, v, m, causal, f"fp32 {kind} D{D} {lens} causal={causal}")
 
 
@@ -247,7 +247,7 @@ def test_fp32_additive_mask_sweep(cuda_device, kind, D, causal, lens):
     q, k, v, g = _qkv(2, 3, lq, lk, D, torch.float32, seed=lq + 5 * lk + D + causal)
     m = _additive(kind, 2, 3, lq, lk, torch.float32, g)
     qd, kd, vd, md = (t.to(cuda_device) for t in (q, k, v, m))
-    assert N.attention_plan(qd, kd, vd, None, causal, md).endswith("+addmask>")
+    assert N.attention_plan(qd, kd, vd, None, causal, md).endswith(("+addmask>", "+addmask+tail-split>"))
     got = cmpext3.ops.attention(qd, kd, vd, None, causal, md)
     torch.cuda.synchronize()
     assert torch.isfinite(got).all()
@@ -300,5 +300,5 @@ def test_fp32_patched_sdpa_masks_native(cuda_device, patched):
     check(got, _ref(q, k, v, m, False), torch.float32, "fp32 patched sdpa mask")
     check(got_add, _ref(q, k, v, add, False), torch.float32, "fp32 patched sdpa additive mask")
     entries = [d.entry for d in cmpext3.autoselect.report() if d.use_native]
-    assert any("attn_tf32x3" in (e or "") and (e or "").endswith("+mask>") for e in entries), cmpext3.autoselect_report()
-    assert any("attn_tf32x3" in (e or "") and (e or "").endswith("+addmask>") for e in entries), cmpext3.autoselect_report()
+    assert any("attn_tf32x3" in (e or "") and (e or "").endswith(("+mask>", "+mask+tail-split>")) for e in entries), cmpext3.autoselect_report()
+    assert any("attn_tf32x3" in (e or "") and (e or "").endswith(("+addmask>", "+addmask+tail-split>")) for e in entries), cmpext3.autoselect_report()

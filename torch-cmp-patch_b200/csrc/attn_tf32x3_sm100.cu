@@ -814,8 +814,10 @@ bool attn_tf32x3_eligible(const cmpx_attn_desc* d) {
 namespace {
 
 // Tail split of a non-causal launch: with n_items = waves * grid + rem (0 < rem <= grid / 2), the
-// rem items of the partial last wave are cut into split = min(grid / rem, 8, key tiles) key
-// ranges, so that the last wave holds rem * split <= grid ranges of 1/split of an item each.
+// rem items of the partial last wave are cut into split = min(grid / rem, 8, key tiles / 4) key
+// ranges, so that the last wave holds rem * split <= grid ranges of 1/split of an item each.  A
+// launch of fewer items than SMs cuts every item, into ranges of at least 8 key tiles
+// ([2,8,128,8192,64]: 16 items on 16 of the 148 SMs before).
 // The counters take the workspace's first 256 bytes (zero before and after every call, the same
 // bytes the 16-bit kernels' counters use), the partial rows the bytes after them.
 struct X3Split {
@@ -830,17 +832,28 @@ X3Split x3_split_plan(const cmpx_attn_desc* d, int num_sms) {
   if (d->causal) return sp;
   const int64_t n_qt = (d->len_q + C::BM - 1) / C::BM;
   const int64_t n_items = n_qt * d->heads * d->batch;
-  const int64_t grid = std::min<int64_t>(n_items, std::max(1, num_sms));
-  const int64_t rem = n_items % grid, tiles = (d->len_k + C::BN - 1) / C::BN;
-  if (n_items <= grid || rem == 0 || 2 * rem > grid) return sp;
+  const int64_t sms = std::max(1, num_sms);
+  const int64_t tiles = (d->len_k + C::BN - 1) / C::BN;
+  if (n_items < 1) return sp;
+  if (n_items < sms) {  // every item cut, into ranges of at least 8 key tiles
+    const int64_t split = std::min<int64_t>({sms / n_items, 8, tiles / 8});
+    if (split < 2) return sp;
+    sp.n_whole = 0;
+    sp.split = static_cast<int>(split);
+    sp.cnt_bytes = 256;
+    sp.bytes = sp.cnt_bytes + static_cast<size_t>(n_items) * split * C::BM * (DP + 4) * 4;
+    return sp;
+  }
+  const int64_t grid = sms;
+  const int64_t rem = n_items % grid;
+  if (rem == 0 || 2 * rem > grid) return sp;
   // At least 4 key tiles per range: with fewer, the ranges' park-and-merge costs more than the
   // idle tail it fills (SD1.5 fp32 cross-attention [2,8,4096,77,40], 2 key tiles per item: 68.6 us
   // split into single tiles, 35.8 us unsplit).
   const int64_t split = std::min<int64_t>({grid / rem, 8, tiles / 4});
-  if (split < 2) return sp;
+  if (split < 2 || rem > 256) return sp;  // (one 8-bit counter per tail item in the first 256 bytes)
   sp.n_whole = static_cast<int>(n_items - rem);
   sp.split = static_cast<int>(split);
-  if (rem > 256) return sp;  // one 8-bit counter per tail item in the first 256 bytes
   sp.cnt_bytes = 256;
   sp.bytes = sp.cnt_bytes + static_cast<size_t>(rem) * split * C::BM * (DP + 4) * 4;
   return sp;
@@ -913,7 +926,6 @@ int launch_tf32x3_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
   p.mask_inv_scale = static_cast<float>(1.0 / d->scale);
   p.timeout_ns = ctx.timeout_ns;
   p.dev_flags = ctx.dev_flags;
-  const int grid = std::min(p.n_items, std::max(1, ctx.num_sms));
   const X3Split sp = x3_split_plan<DP>(d, ctx.num_sms);
   p.n_whole = p.n_items;
   p.split = 1;
@@ -928,6 +940,7 @@ int launch_tf32x3_typed(const cmpx_attn_desc* d, const LaunchCtx& ctx) {
     p.cnt = static_cast<unsigned int*>(d->workspace);
     p.part = reinterpret_cast<float*>(static_cast<char*>(d->workspace) + sp.cnt_bytes);
   }
+  const int grid = std::min(p.n_work, std::max(1, ctx.num_sms));
   // Split operands, when the workspace holds them: one pre-pass launch, then TMA maps over them.
   const X3Pre pr = x3_pre_plan<DP>(d, sp);
   p.pre = 0;
