@@ -555,3 +555,31 @@ def test_minimum_workspace_is_accepted_for_split_shapes():
     d = _attn(B=2, H=10, Lq=4096, Lk=4096, D=64, dtype=1)
     d.workspace, d.workspace_bytes = 0x10000, 256
     assert N.lib.cmpx_attn_fwd(ctypes.byref(d), None) == N.ERR_DEVICE
+
+
+def _gqa(B, H, Hkv, Lq, Lk, D, dtype=2, causal=0, blhd_out=False):
+    d = _attn(B=B, H=H, Lq=Lq, Lk=Lk, D=D, dtype=dtype, causal=causal)
+    d.k_stride[:] = (Hkv * Lk * D, Lk * D, D)
+    d.v_stride[:] = (Hkv * Lk * D, Lk * D, D)
+    if blhd_out:  # the binding's [B, L, H, D] output layout
+        d.o_stride[:] = (Lq * H * D, D, H * D)
+    d.heads_kv = Hkv
+    return d
+
+
+def test_one_row_grouped_query_calls_are_folded():
+    # decode [8, 32, 1, 4096, 128] with 8 key/value heads: the 4 query heads of a key/value head
+    # run as one head of 4 rows -- 64 items of 32 key tiles, which (fewer items than SMs) are cut
+    # into 2 ranges of 16 tiles; unfolded, 256 one-row items would not be split at all
+    for blhd in (False, True):  # one query row: any row stride folds
+        d = _gqa(8, 32, 8, 1, 4096, 128, blhd_out=blhd)
+        st, name = _plan(d)
+        assert st == 0 and name.endswith("+tail-split>"), name
+        ranges = 64 * 2
+        up = lambda x: (x + 255) // 256 * 256  # noqa: E731
+        assert N.lib.cmpx_attn_workspace_size(ctypes.byref(d)) == 256 + up(ranges * 256 * 2 * 4) + ranges * 256 * 128 * 4
+    # not folded: causal, several rows in a [B, L, H, D] output, equal head counts
+    for d in (_gqa(8, 32, 8, 1, 4096, 128, causal=1), _gqa(8, 32, 8, 3, 4096, 128, blhd_out=True),
+              _gqa(8, 32, 32, 1, 4096, 128)):
+        st, name = _plan(d)
+        assert st == 0 and not name.endswith("+tail-split>"), name
